@@ -1,0 +1,134 @@
+/* treeattn_b200 - C ABI of the B200 (sm_100a) segment-tree sparse-attention kernels.
+ *
+ * Conventions (every entry point):
+ *   - All pointers are device pointers owned by the caller; the library allocates nothing on these paths.
+ *   - Strides are in ELEMENTS; the innermost (head-dim) stride is 1. Rows read with 16-byte vector loads
+ *     or bulk copies must start 16-byte aligned (checked; violations return TA_ERR_ARG).
+ *   - dtype codes: 0 = float32, 1 = bfloat16, 2 = float16.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Work is only enqueued; nothing synchronizes.
+ *   - Return value: 0 on success, TA_ERR_ARG for rejected arguments, TA_ERR_CUDA for a launch failure.
+ *     ta_last_error() then describes the failure (thread-local string). There is no fallback path.
+ *   - Kernels that detect a bad position/index at run time, or a bounded wait that gave up, record it in a
+ *     device-side error record read (and cleared) by ta_device_error().
+ *
+ * Tree levels ("nodes"): per (b, h) the levels L0..Lm are packed back to back, level l holding cap >> l fp32
+ * rows of dh values (node m covers positions [m*2^l, (m+1)*2^l)); n_sb / n_sh are the strides (in floats)
+ * between batch rows / heads. ta_level_nodes() gives the per-(b, h) node count.
+ */
+#ifndef TREEATTN_B200_H
+#define TREEATTN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TA_OK 0
+#define TA_ERR_ARG 1
+#define TA_ERR_CUDA 2
+
+#define TA_F32 0
+#define TA_BF16 1
+#define TA_F16 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ta_version(void);
+
+/* Description of the last failure on this thread ("" if none). */
+const char* ta_last_error(void);
+
+/* Copy the device-side error record {code, kernel, a, b} of the current device into out4 and clear it.
+ * Synchronizes the device. code 0 = no error, 1 = bounded wait gave up, 2 = position out of range,
+ * 3 = index out of range. */
+int ta_device_error(int* out4);
+
+/* Nodes per (b, h) for a capacity and level range: sum over l in [L0, Lm] of cap >> l. */
+int64_t ta_level_nodes(int cap, int L0, int Lm);
+
+/* Replaces seg.level_sums (seg.py:26-41), fastseg.level_sums_min (fastseg.py:238-251) and the bulk
+ * SegState.fill (engine.py:57-71): node sums of levels L0..Lm from keys k (B, H, T_len, dh), complete nodes
+ * only (m < T_len >> l). zero_sink != 0 counts the key at position 0 as 0 (what select_seg and SegState do,
+ * seg.py:128-130, engine.py:62). fp32, reference pair order (bit-exact). */
+int ta_build_levels(const void* k, int dtype, int B, int H, int T_len, int dh, int64_t k_sb, int64_t k_sh,
+                    int64_t k_st, int cap, int L0, int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh,
+                    void* stream);
+
+/* Replaces seg.tree_pass (seg.py:44-70) / fastseg.tree_pass_fast (fastseg.py:254-271) on the tree of leaf
+ * blocks of 2^L0 tokens: per query (b, h, n) at position tq[b*tq_sb + n*tq_st], the best wmax leaves, best
+ * first. Outputs (B, H, Nq, wl) contiguous: ids (int64, invalid slots 0), vld (uint8), sct (fp32 scores
+ * q.S_L0 / 2^L0, -inf when invalid; may be NULL). q may be float32, bfloat16 or float16 (q_dtype). */
+int ta_select(const void* q, int q_dtype, int B, int H, int Nq, int dh, int64_t q_sb, int64_t q_sh, int64_t q_st,
+              const int64_t* tq, int64_t tq_sb, int64_t tq_st, const float* nodes, int64_t n_sb, int64_t n_sh,
+              int cap, int L0, int Lm, int wmax, int wl, int64_t* ids, uint8_t* vld, float* sct, void* stream);
+
+/* Replaces seg.finish + seg.leaves_to_pos (seg.py:106-119) for Q queries: n_tree from the budget lhat and the
+ * neighbour count nL (NULL = 0); leaf ids -> positions (tree_pos[q, j*wl + i] = ids[q, i]*leaf + j, -1 when
+ * invalid); neighbour leaves likewise (nid/match NULL = no matches). tree_pos / nb_pos may be NULL when only
+ * n_tree and nb_leaves are wanted. */
+int ta_finish(const int64_t* ids, const uint8_t* vld, const int64_t* nid, const uint8_t* match, const int64_t* nL,
+              const int64_t* lhat, int64_t Q, int wl, int nbw, int leaf, int wmax, int64_t* tree_pos,
+              int64_t* nb_pos, int64_t* n_tree, int64_t* nb_leaves, void* stream);
+
+/* Replaces the key assembly + dedupe_fast + sparse_attn of SegAttention.sparse_attend (fastseg.py:367-383)
+ * and DynAttention.sparse_attend (attention_dyn.py:345-366): per query, exact softmax attention (scale,
+ * fp32 accumulation) over the first n_tree valid leaves of ids/vld (each 2^L0 positions), the sink and the
+ * window [t-Lw+1, t], every position once. o has q's dtype; lse (natural log) and nkeys may be NULL.
+ * n_tree NULL -> ntree_const for every query. */
+int ta_seg_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int Nq, int dh,
+                int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const int64_t* tq, int64_t tq_sb,
+                int64_t tq_st, const int64_t* ids, const uint8_t* vld, int wl, const int64_t* n_tree,
+                int ntree_const, int leaf, int Lw, float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st,
+                float* lse, int32_t* nkeys, void* stream);
+
+/* Replaces fastseg.sparse_attn forward (fastseg.py:173-177, _attn_fwd 49-78): cand (B, H, T, Kc) key
+ * positions (int32 if cand64 == 0, else int64), -1 = unused. o (B, H, T, dh) in q's dtype, lse may be NULL. */
+int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int T, int dh,
+                   int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                   int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const void* cand, int cand64, int Kc,
+                   float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st, float* lse, void* stream);
+
+/* Replaces fastseg.gather_dot (fastseg.py:118-130, _gather_dot_kernel 34-47): out (B, H, N, C) fp32 =
+ * scale * q[b,h,n] . S[b,h,cand[b,h,n,c]] with ids clamped to [0, M-1]. q and S share `dtype`. */
+int ta_gather_dot(const void* q, const void* S, int dtype, int B, int H, int N, int M, int C, int dh,
+                  int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t s_sb, int64_t s_sh, int64_t s_st,
+                  const void* cand, int cand64, float scale, float* out, void* stream);
+
+/* Block form of gather_dot for selections made of whole key blocks (config "gather-dot microbenchmark"):
+ * out (B, H, nblk*blk) fp32 = scale * q[b,h] . K[b,h, blocks[b,h,j]*blk + r]; blocks staged into shared
+ * memory with bulk copies, nb_cta blocks per CTA (1..64). */
+int ta_gather_dot_blocks(const void* q, const void* k, int dtype, int B, int H, int T, int dh, int64_t q_sb,
+                         int64_t q_sh, int64_t k_sb, int64_t k_sh, int64_t k_st, const int32_t* blocks, int nblk,
+                         int blk, int nb_cta, float scale, float* out, void* stream);
+
+/* Replaces attention_dyn.dedupe (attention_dyn.py:12-17) / fastseg.dedupe_fast (fastseg.py:227-234):
+ * keep[r, j] = valid[r, j] and no earlier valid entry of row r has the same value. (rows, Kc) contiguous. */
+int ta_dedupe(const int64_t* cand, const uint8_t* valid, uint8_t* keep, int64_t rows, int Kc, void* stream);
+
+/* Replaces SegState.add (engine.py:41-55) for a batch: k, v rows (B, H, dh) of position pos[b] are written
+ * into the caches (B, H, cap, dh) and, when pos[b] completes a leaf block, the leaf node and its complete
+ * right-spine ancestors are formed. */
+int ta_append(const void* k, const void* v, int dtype, int B, int H, int dh, int64_t k_sb, int64_t k_sh,
+              int64_t v_sb, int64_t v_sh, void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
+              float* nodes, int64_t n_sb, int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos,
+              void* stream);
+
+/* Replaces seg_attend (engine.py:84-120) for a batch, fused: tree descent for the new query, attention over
+ * used leaves + sink + window + the new token, append of the new k/v and the incremental tree update.
+ * qkv rows (B, 3*H*dh): q at 0, k at k_ofs, v at v_ofs (elements). out rows (B, H*dh). splits = CTAs per
+ * (b, h) (a thread-block cluster, 1..8; 0 = choose). lse / nkeys / sel (B, H, wmax+1) may be NULL. */
+int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,
+                   void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st, float* nodes, int64_t n_sb,
+                   int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos, int wmax, int n_tree, int Lw,
+                   float scale, void* out, int64_t o_sb, float* lse, int32_t* nkeys, int32_t* sel, int splits,
+                   void* stream);
+
+/* The split count ta_decode_step would choose for B*H (b, h) pairs on the current device. */
+int ta_decode_default_splits(int B, int H);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TREEATTN_B200_H */

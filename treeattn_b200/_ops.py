@@ -1,0 +1,301 @@
+"""Tensor-level wrappers over the C ABI (include/treeattn_b200.h).
+
+Every function here takes CUDA tensors, checks shapes / dtypes / layouts, allocates its outputs with torch (the
+library itself allocates nothing) and enqueues the kernel on the current torch stream of the tensors' device.
+CPU tensors are rejected: there is no CPU, Triton or eager-PyTorch fallback.
+"""
+import math
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _code(t):
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError('unsupported dtype %s (float32, bfloat16, float16)' % t.dtype) from None
+
+
+def _need_cuda(name, *ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError('%s: tensors must be CUDA tensors (this package has no CPU path)' % name)
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _unit_inner(name, *ts):
+    for t in ts:
+        if t is not None and t.stride(-1) != 1:
+            raise ValueError('%s: the innermost (head) dimension must be contiguous' % name)
+
+
+def log2_exact(n, what='value'):
+    n = int(n)
+    if n < 1 or (n & (n - 1)):
+        raise ValueError('%s must be a power of two (got %d)' % (what, n))
+    return n.bit_length() - 1
+
+
+def output_width(n_levels, wmax):
+    """Slots the reference's tree_pass returns (seg.py:66: min(wmax, #candidates) at the last level)."""
+    w = min(wmax, 1)
+    for _ in range(n_levels - 1):
+        w = min(wmax, 2 * w + 1)
+    return w
+
+
+def level_counts(cap, L0, Lm):
+    """{l: (offset, count)} of the packed level layout."""
+    out, o = {}, 0
+    for l in range(L0, Lm + 1):
+        out[l] = (o, cap >> l)
+        o += cap >> l
+    return out
+
+
+class Levels:
+    """Packed segment-tree levels L0..Lm for a batch of (b, h) trees.
+
+    `nodes` is (B, H, n_nodes, dh) fp32; level l occupies nodes[:, :, off_l:off_l + (cap >> l)], node m covering
+    positions [m*2^l, (m+1)*2^l)."""
+
+    def __init__(self, nodes, cap, L0, Lm):
+        self.nodes, self.cap, self.L0, self.Lm = nodes, int(cap), int(L0), int(Lm)
+        self.counts = level_counts(self.cap, self.L0, self.Lm)
+
+    @classmethod
+    def empty(cls, B, H, dh, cap, L0, Lm, device):
+        n = sum(c for _, c in level_counts(cap, L0, Lm).values())
+        return cls(torch.zeros(B, H, max(n, 1), dh, device=device, dtype=torch.float32), cap, L0, Lm)
+
+    def level(self, l):
+        o, c = self.counts[l]
+        return self.nodes[:, :, o:o + c]
+
+    def as_dict(self):
+        return LevelDict({l: self.level(l) for l in range(self.L0, self.Lm + 1)}, self)
+
+
+class LevelDict(dict):
+    """{level: tensor view} as the reference's level_sums returns, carrying the packed storage."""
+
+    def __init__(self, d, packed):
+        super().__init__(d)
+        self.packed = packed
+
+
+def build_levels(k, cap, L0, Lm, zero_sink=True, out=None):
+    """Levels L0..Lm from keys k (B, H, T, dh) (any strides, contiguous head dim). Returns Levels."""
+    _need_cuda('build_levels', k)
+    _unit_inner('build_levels', k)
+    B, H, T, dh = k.shape
+    if out is None:
+        out = Levels.empty(B, H, dh, cap, L0, Lm, k.device)
+    nd = out.nodes
+    _lib.call('ta_build_levels', _p(k), _code(k), B, H, T, dh, k.stride(0), k.stride(1), k.stride(2), out.cap,
+              out.L0, out.Lm, 1 if zero_sink else 0, _p(nd), nd.stride(0), nd.stride(1), _stream(k))
+    return out
+
+
+def _tq_strides(tq, B, Nq):
+    if tq.dim() == 1:
+        if tq.shape[0] == Nq:
+            return 0, tq.stride(0)
+        if Nq == 1 and tq.shape[0] == B:
+            return tq.stride(0), 0
+    elif tq.dim() == 2 and tuple(tq.shape) == (B, Nq):
+        return tq.stride(0), tq.stride(1)
+    raise ValueError('query positions must have shape (Nq,), (B,) with Nq == 1, or (B, Nq)')
+
+
+def select(q, levels, tq, wmax, wl=None):
+    """Tree descent (seg.tree_pass) for queries q (B, H, Nq, dh) at positions tq.
+
+    Returns ids (int64), vld (bool), sct (fp32), each (B, H, Nq, wl), best first."""
+    _need_cuda('select', q, tq, levels.nodes)
+    _unit_inner('select', q)
+    B, H, Nq, dh = q.shape
+    if wl is None:
+        wl = output_width(levels.Lm - levels.L0 + 1, wmax)
+    tq = tq.to(torch.int64)
+    sb, st = _tq_strides(tq, B, Nq)
+    ids = torch.empty(B, H, Nq, wl, device=q.device, dtype=torch.int64)
+    vld = torch.empty(B, H, Nq, wl, device=q.device, dtype=torch.bool)
+    sct = torch.empty(B, H, Nq, wl, device=q.device, dtype=torch.float32)
+    nd = levels.nodes
+    _lib.call('ta_select', _p(q), _code(q), B, H, Nq, dh, q.stride(0), q.stride(1), q.stride(2), _p(tq), sb, st,
+              _p(nd), nd.stride(0), nd.stride(1), levels.cap, levels.L0, levels.Lm, wmax, wl, _p(ids), _p(vld),
+              _p(sct), _stream(q))
+    return ids, vld, sct
+
+
+def finish(ids, vld, lhat, wmax, leaf, nid=None, match=None, nL=None, positions=True):
+    """seg.finish: returns dict(tree_pos, leaf_ok, nb_pos, n_tree, nb_leaves) (positions=False: n_tree only)."""
+    _need_cuda('finish', ids, vld, lhat)
+    shp = ids.shape[:-1]
+    wl = ids.shape[-1]
+    Q = int(torch.Size(shp).numel())
+    ids = ids.contiguous()
+    vld = vld.contiguous()
+    lhat = lhat.to(torch.int64).expand(shp).contiguous()
+    nbw = nid.shape[-1] if nid is not None else 0
+    if nid is not None:
+        nid = nid.to(torch.int64).contiguous()
+        match = match.contiguous()
+    if nL is not None:
+        nL = nL.to(torch.int64).contiguous()
+    dev = ids.device
+    n_tree = torch.empty(shp, device=dev, dtype=torch.int64)
+    nb_leaves = torch.empty(shp, device=dev, dtype=torch.int64)
+    tree_pos = torch.empty(shp + (leaf * wl,), device=dev, dtype=torch.int64) if positions else None
+    nb_pos = torch.empty(shp + (leaf * nbw,), device=dev, dtype=torch.int64) if positions else None
+    _lib.call('ta_finish', _p(ids), _p(vld), _p(nid), _p(match), _p(nL), _p(lhat), Q, wl, nbw, leaf, wmax,
+              _p(tree_pos), _p(nb_pos), _p(n_tree), _p(nb_leaves), _stream(ids))
+    return dict(tree_pos=tree_pos, leaf_ok=vld, nb_pos=nb_pos, n_tree=n_tree, nb_leaves=nb_leaves)
+
+
+def seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_lse=False, want_nkeys=True):
+    """Attention of each query over its used leaves (first n_tree valid of ids/vld), sink and window.
+
+    q (B, H, Nq, dh), k / v (B, H, T_kv, dh): any strides with a contiguous head dim. n_tree: int or (B, H, Nq).
+    `out` (B, H, Nq, dh) may be a strided view (e.g. of a (B, Nq, H, dh) buffer). Returns (out, lse, nkeys)."""
+    _need_cuda('seg_attn', q, k, v, tq, ids, vld)
+    _unit_inner('seg_attn', q, k, v)
+    B, H, Nq, dh = q.shape
+    T_kv = k.shape[2]
+    if q.dtype != k.dtype or k.dtype != v.dtype:
+        raise TypeError('seg_attn: q, k and v must share a dtype')
+    if out is None:
+        out = torch.empty(B, H, Nq, dh, device=q.device, dtype=q.dtype)
+    _unit_inner('seg_attn', out)
+    tq = tq.to(torch.int64)
+    sb, st = _tq_strides(tq, B, Nq)
+    wl = ids.shape[-1]
+    ids = ids.contiguous()
+    vld = vld.contiguous()
+    if torch.is_tensor(n_tree):
+        ntp, ntc = n_tree.to(torch.int64).expand(B, H, Nq).contiguous(), 0
+    else:
+        ntp, ntc = None, int(n_tree)
+    lse = torch.empty(B, H, Nq, device=q.device, dtype=torch.float32) if want_lse else None
+    nkeys = torch.empty(B, H, Nq, device=q.device, dtype=torch.int32) if want_nkeys else None
+    _lib.call('ta_seg_attn', _p(q), _p(k), _p(v), _code(q), B, H, Nq, dh, q.stride(0), q.stride(1), q.stride(2),
+              k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), T_kv, _p(tq), sb, st,
+              _p(ids), _p(vld), wl, _p(ntp), ntc, leaf, Lw, float(scale), _p(out), out.stride(0), out.stride(1),
+              out.stride(2), _p(lse), _p(nkeys), _stream(q))
+    return out, lse, nkeys
+
+
+def sparse_attn_fwd(q, k, v, cand, scale):
+    """fastseg sparse_attn forward: cand (B, H, T, Kc) positions, -1 unused. Returns (o, lse)."""
+    _need_cuda('sparse_attn', q, k, v, cand)
+    _unit_inner('sparse_attn', q, k, v)
+    B, H, T, dh = q.shape
+    if q.dtype != k.dtype or k.dtype != v.dtype:
+        raise TypeError('sparse_attn: q, k and v must share a dtype')
+    if cand.dtype not in (torch.int32, torch.int64):
+        cand = cand.to(torch.int64)
+    cand = cand.contiguous()
+    Kc = cand.shape[-1]
+    o = torch.empty(B, H, T, dh, device=q.device, dtype=q.dtype)
+    lse = torch.empty(B, H, T, device=q.device, dtype=torch.float32)
+    _lib.call('ta_sparse_attn', _p(q), _p(k), _p(v), _code(q), B, H, T, dh, q.stride(0), q.stride(1), q.stride(2),
+              k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), k.shape[2], _p(cand),
+              1 if cand.dtype == torch.int64 else 0, Kc, float(scale), _p(o), o.stride(0), o.stride(1), o.stride(2),
+              _p(lse), _stream(q))
+    return o, lse
+
+
+def gather_dot(q, S, cand, scale):
+    """fastseg.gather_dot: (B, H, N, C) fp32 = scale * q . S[cand] (ids clamped to [0, M-1])."""
+    _need_cuda('gather_dot', q, S, cand)
+    _unit_inner('gather_dot', q, S)
+    if q.dtype != S.dtype:
+        S = S.to(q.dtype)
+    B, H, N, dh = q.shape
+    M = S.shape[2]
+    C = cand.shape[-1]
+    if cand.dtype not in (torch.int32, torch.int64):
+        cand = cand.to(torch.int64)
+    cand = cand.contiguous()
+    out = torch.empty(B, H, N, C, device=q.device, dtype=torch.float32)
+    _lib.call('ta_gather_dot', _p(q), _p(S), _code(q), B, H, N, M, C, dh, q.stride(0), q.stride(1), q.stride(2),
+              S.stride(0), S.stride(1), S.stride(2), _p(cand), 1 if cand.dtype == torch.int64 else 0, float(scale),
+              _p(out), _stream(q))
+    return out
+
+
+def gather_dot_blocks(q, k, blocks, blk, scale, nb_cta=2, out=None):
+    """Block form: q (B, H, dh), k (B, H, T, dh) with contiguous rows, blocks (B, H, nblk) int32 block ids.
+    Returns (B, H, nblk*blk) fp32 scores."""
+    _need_cuda('gather_dot_blocks', q, k, blocks)
+    B, H, T, dh = k.shape
+    nblk = blocks.shape[-1]
+    blocks = blocks.to(torch.int32).contiguous()
+    if out is None:
+        out = torch.empty(B, H, nblk * blk, device=q.device, dtype=torch.float32)
+    _lib.call('ta_gather_dot_blocks', _p(q), _p(k), _code(k), B, H, T, dh, q.stride(0), q.stride(1), k.stride(0),
+              k.stride(1), k.stride(2), _p(blocks), nblk, blk, nb_cta, float(scale), _p(out), _stream(q))
+    return out
+
+
+def dedupe(cand, valid):
+    """Keep the first valid copy of every value along the last dim (attention_dyn.dedupe)."""
+    _need_cuda('dedupe', cand, valid)
+    shp = cand.shape
+    Kc = shp[-1]
+    c = cand.to(torch.int64).contiguous()
+    vv = valid.to(torch.bool).contiguous()
+    keep = torch.empty(shp, device=cand.device, dtype=torch.bool)
+    rows = c.numel() // max(Kc, 1)
+    _lib.call('ta_dedupe', _p(c), _p(vv), _p(keep), rows, Kc, _stream(cand))
+    return keep
+
+
+def append(k, v, kc, vc, levels, pos):
+    """SegState.add for a batch: k, v (B, H, dh) at positions pos (B,) int32."""
+    _need_cuda('append', k, v, kc, vc, pos)
+    B, H, dh = k.shape
+    pos = pos.to(torch.int32)
+    nd = levels.nodes
+    _lib.call('ta_append', _p(k), _p(v), _code(kc), B, H, dh, k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+              _p(kc), _p(vc), kc.stride(0), kc.stride(1), kc.stride(2), _p(nd), nd.stride(0), nd.stride(1),
+              levels.cap, levels.L0, levels.Lm, _p(pos), _stream(kc))
+
+
+def decode_step(qkv, kc, vc, levels, pos, H, wmax, n_tree, Lw, scale, out, lse=None, nkeys=None, sel=None,
+                splits=0):
+    """Fused decode step of one layer (seg_attend): qkv (B, 3*H*dh) rows, caches (B, H, cap, dh), pos (B,) int32.
+    Writes out (B, H*dh) and appends k/v + updates the tree in place."""
+    B = qkv.shape[0]
+    dh = kc.shape[-1]
+    C = H * dh
+    nd = levels.nodes
+    _lib.call('ta_decode_step', _p(qkv), _code(qkv), B, H, dh, qkv.stride(0), C, 2 * C, _p(kc), _p(vc),
+              kc.stride(0), kc.stride(1), kc.stride(2), _p(nd), nd.stride(0), nd.stride(1), levels.cap, levels.L0,
+              levels.Lm, _p(pos), wmax, n_tree, Lw, float(scale), _p(out), out.stride(0), _p(lse), _p(nkeys),
+              _p(sel), int(splits), _stream(qkv))
+
+
+def default_splits(B, H):
+    return _lib.load().ta_decode_default_splits(B, H)
+
+
+def device_error():
+    return _lib.device_error()
+
+
+def lm_of(T):
+    """Top tree level for a sequence / capacity T (seg.py:127, engine.py:24): round(log2 T) - 1."""
+    return int(round(math.log2(T))) - 1

@@ -1,0 +1,484 @@
+// Exact softmax attention over selected keys, gather-dot and duplicate removal.
+//
+// Reference: fastseg.py:134-141 sparse_attn_ref / fastseg.py:49-78 _attn_fwd (online softmax over the kept
+// keys, scale 1/sqrt(dh), fp32 accumulation, -1 = unused slot); fastseg.py:118-130 gather_dot;
+// fastseg.py:227-234 dedupe_fast and attention_dyn.py:12-17 dedupe (keep the first valid copy).
+//
+// Lane layout shared by all warp-per-query kernels here: one key row of DH elements is read as DH/VEC
+// 16-byte chunks by LPR = DH/VEC consecutive lanes, so a warp covers RPW = 32/LPR rows per pass with fully
+// coalesced 128-bit loads. Row scores are reduced across the LPR lanes with shuffles.
+#pragma once
+#include "select.cuh"
+
+namespace ta {
+
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+template <typename T, int DH>
+struct WarpAttn {
+  static constexpr int VEC = TypeInfo<T>::VEC;
+  static constexpr int LPR = DH / VEC;
+  static constexpr int RPW = 32 / LPR;
+  static_assert(LPR >= 1 && LPR <= 32 && (LPR & (LPR - 1)) == 0, "unsupported head dim");
+
+  float q[VEC];    // this lane's query chunk, pre-multiplied by scale*log2(e)
+  float acc[VEC];  // running sum of p * v for this lane's rows and dims
+  float m;         // running max of the (log2-domain) scores, warp-uniform
+  float l;         // running sum of p over this lane's rows
+  int sub, c;
+
+  __device__ __forceinline__ void init(const T* __restrict__ qrow, float scale_log2, int lane) {
+    sub = lane / LPR;
+    c = lane - sub * LPR;
+    float tmp[VEC];
+    load_vec_f32<T>(qrow + c * VEC, tmp);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      q[i] = tmp[i] * scale_log2;
+      acc[i] = 0.f;
+    }
+    m = -INFINITY;
+    l = 0.f;
+  }
+
+  // Score one K chunk (already widened) -> full-row score on every lane of the row group.
+  __device__ __forceinline__ float row_score(const float (&kf)[VEC]) const {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) s = fmaf(q[i], kf[i], s);
+    return warp_sum_sub(s, LPR);
+  }
+
+  // Online-softmax update with U row groups at once (scores s[u], values vf[u]; invalid rows have s = -inf).
+  template <int U>
+  __device__ __forceinline__ void update(const float (&s)[U], const float (&vf)[U][VEC]) {
+    float mx = s[0];
+#pragma unroll
+    for (int u = 1; u < U; ++u) mx = fmaxf(mx, s[u]);
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float m_new = fmaxf(m, mx);
+    if (m_new == -INFINITY) return;  // nothing valid yet (warp-uniform)
+    const float alpha = exp2f(m - m_new);
+    l *= alpha;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] *= alpha;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float p = (s[u] == -INFINITY) ? 0.f : exp2f(s[u] - m_new);
+      l += p;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] = fmaf(p, vf[u][i], acc[i]);
+    }
+    m = m_new;
+  }
+
+  // Process U row groups read from global memory (row pointers for this lane; null = invalid row).
+  template <int U>
+  __device__ __forceinline__ void rows_global(const T* const (&kr)[U], const T* const (&vr)[U]) {
+    float kf[U][VEC], vf[U][VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (kr[u]) {
+        ldg_vec_f32<T>(kr[u] + c * VEC, kf[u]);
+        ldg_vec_f32<T>(vr[u] + c * VEC, vf[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) kf[u][i] = vf[u][i] = 0.f;
+      }
+    }
+    float s[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float x = row_score(kf[u]);
+      s[u] = kr[u] ? x : -INFINITY;
+    }
+    update<U>(s, vf);
+  }
+
+  // Sum l and acc over the row groups; afterwards every lane holds the warp totals for its dim chunk c.
+  __device__ __forceinline__ void reduce_rows() {
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1) {
+      l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    }
+  }
+};
+
+// Merge partial softmax state b into a (both in the log2 domain).
+__device__ __forceinline__ void merge_state(float& ma, float& la, float* acca, float mb, float lb, const float* accb,
+                                            int n) {
+  const float m = fmaxf(ma, mb);
+  if (m == -INFINITY) return;
+  const float fa = exp2f(ma - m), fb = exp2f(mb - m);
+  la = la * fa + lb * fb;
+  for (int i = 0; i < n; ++i) acca[i] = acca[i] * fa + accb[i] * fb;
+  ma = m;
+}
+
+// ------------------------------------------------------------------------------------------------ key ranges
+// The key set of one query of the segment-tree path, as disjoint position ranges (no duplicate positions):
+// every used leaf block [m*leaf, (m+1)*leaf) cut at the window start w0, the sink {0} unless a used leaf or the
+// window already holds it, and the local window [w0, t] (fastseg.py:372-381 static keys + dedupe_fast).
+constexpr int MAX_RANGES = WMAX_LIMIT + 2;
+
+struct RangeList {
+  int start[MAX_RANGES];
+  int pref[MAX_RANGES + 1];  // prefix sums of the lengths
+  int n;
+};
+
+// Build the ranges of one query with a warp. `leaf_of(i)` returns the leaf id of slot i or -1 when the slot is
+// not used. `t_end` = one past the last window position (t+1 when position t is read from the cache, t when
+// the caller handles position t itself). Returns the total number of keys in the ranges.
+template <typename LeafFn>
+__device__ __forceinline__ int build_ranges(RangeList& rl, int nslots, LeafFn leaf_of, int leaf, int t, int Lw,
+                                            int t_end, int lane) {
+  const int w0 = max(t - Lw + 1, 0);
+  int cnt = 0;
+  bool leaf0 = false;
+  for (int base = 0; base < nslots; base += 32) {
+    const int i = base + lane;
+    int st = 0, len = 0;
+    if (i < nslots) {
+      const int m = leaf_of(i);
+      if (m >= 0) {
+        st = m * leaf;
+        const int en = min(st + leaf, w0);
+        len = max(en - st, 0);
+        if (m == 0) leaf0 = true;
+      }
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, len > 0);
+    if (len > 0) {
+      const int idx = cnt + __popc(mask & ((1u << lane) - 1u));
+      rl.start[idx] = st;
+      rl.pref[idx + 1] = len;  // lengths for now
+    }
+    cnt += __popc(mask);
+  }
+  leaf0 = __any_sync(0xffffffffu, leaf0);
+  if (lane == 0) {
+    if (w0 > 0 && !leaf0) {
+      rl.start[cnt] = 0;
+      rl.pref[cnt + 1] = 1;
+      ++cnt;
+    }
+    if (t_end > w0) {
+      rl.start[cnt] = w0;
+      rl.pref[cnt + 1] = t_end - w0;
+      ++cnt;
+    }
+    rl.pref[0] = 0;
+    for (int r = 0; r < cnt; ++r) rl.pref[r + 1] += rl.pref[r];
+    rl.n = cnt;
+  }
+  __syncwarp();
+  return rl.pref[rl.n];
+}
+
+// ------------------------------------------------------------------------------------------------ seg attention
+// One warp per query: key set from the selected leaves (best first, the first n_tree valid ones are used),
+// the sink and the local window; exact online-softmax attention over it, K/V read straight from HBM/L2.
+struct SegAttnParams {
+  const void *q, *k, *v;
+  int64_t q_sb, q_sh, q_st;
+  int64_t k_sb, k_sh, k_st;
+  int64_t v_sb, v_sh, v_st;
+  const int64_t* tq;
+  int64_t tq_sb, tq_st;
+  const int64_t* ids;     // (B,H,Nq,wl)
+  const uint8_t* vld;     // (B,H,Nq,wl)
+  const int64_t* n_tree;  // (B,H,Nq) or null -> ntree_const
+  int ntree_const;
+  int B, H, Nq, wl, leaf, Lw, T_kv;
+  float scale;
+  void* o;                // (B,H,Nq,dh) with strides
+  int64_t o_sb, o_sh, o_st;
+  float* lse;             // (B,H,Nq) natural-log LSE, may be null
+  int32_t* nkeys;         // (B,H,Nq) keys attended, may be null
+};
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(128) seg_attn_kernel(SegAttnParams p) {
+  __shared__ RangeList s_rl[4];
+  using WA = WarpAttn<T, DH>;
+  constexpr int U = (WA::RPW >= 8) ? 2 : 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qid = (int64_t)blockIdx.x * 4 + warp;
+  if (qid >= (int64_t)p.B * p.H * p.Nq) return;
+  const int n = (int)(qid % p.Nq);
+  const int bh = (int)(qid / p.Nq);
+  const int b = bh / p.H, h = bh % p.H;
+  const int64_t tt = p.tq[b * p.tq_sb + n * p.tq_st];
+  RangeList& rl = s_rl[warp];
+  if (tt < 0 || tt >= p.T_kv) {
+    if (lane == 0) record_error(DEV_POS_RANGE, K_SEG_ATTN, (int)tt, p.T_kv);
+    return;
+  }
+  const int t = (int)tt;
+  const int ntree = p.n_tree ? (int)p.n_tree[qid] : p.ntree_const;
+  const int64_t sbase = qid * p.wl;
+  const int total = build_ranges(
+      rl, p.wl,
+      [&](int i) -> int {
+        return (p.vld[sbase + i] && i < ntree) ? (int)p.ids[sbase + i] : -1;
+      },
+      p.leaf, t, p.Lw, t + 1, lane);
+
+  const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st;
+  const T* kb = reinterpret_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+  const T* vb = reinterpret_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+  WA wa;
+  wa.init(qrow, p.scale * LOG2E, lane);
+  int ri = 0;  // this lane's current range
+  for (int base = 0; base < total; base += WA::RPW * U) {
+    const T* kr[U];
+    const T* vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = base + u * WA::RPW + wa.sub;
+      kr[u] = vr[u] = nullptr;
+      if (g < total) {
+        while (g >= rl.pref[ri + 1]) ++ri;
+        const int pos = rl.start[ri] + (g - rl.pref[ri]);
+        kr[u] = kb + pos * p.k_st;
+        vr[u] = vb + pos * p.v_st;
+      }
+    }
+    wa.template rows_global<U>(kr, vr);
+  }
+  wa.reduce_rows();
+  const float inv = wa.l > 0.f ? 1.f / wa.l : 0.f;
+  if (wa.sub == 0) {
+    float outv[WA::VEC];
+#pragma unroll
+    for (int i = 0; i < WA::VEC; ++i) outv[i] = wa.acc[i] * inv;
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + n * p.o_st;
+    store_vec_from_f32<T>(orow + wa.c * WA::VEC, outv);
+  }
+  if (lane == 0) {
+    if (p.lse) p.lse[qid] = wa.l > 0.f ? (wa.m + log2f(wa.l)) * LN2 : -INFINITY;
+    if (p.nkeys) p.nkeys[qid] = total;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ sparse_attn
+// fastseg.py:173 sparse_attn forward: candidate positions per query (int32 or int64), -1 = unused.
+struct SparseAttnParams {
+  const void *q, *k, *v;
+  int64_t q_sb, q_sh, q_st;
+  int64_t k_sb, k_sh, k_st;
+  int64_t v_sb, v_sh, v_st;
+  const void* cand;       // (B,H,T,Kc) contiguous
+  int cand64;             // 1: int64, 0: int32
+  int B, H, T, Kc, T_kv;
+  float scale;
+  void* o;
+  int64_t o_sb, o_sh, o_st;
+  float* lse;
+};
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(128) sparse_attn_kernel(SparseAttnParams p) {
+  using WA = WarpAttn<T, DH>;
+  constexpr int U = (WA::RPW >= 8) ? 2 : 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qid = (int64_t)blockIdx.x * 4 + warp;
+  if (qid >= (int64_t)p.B * p.H * p.T) return;
+  const int n = (int)(qid % p.T);
+  const int bh = (int)(qid / p.T);
+  const int b = bh / p.H, h = bh % p.H;
+  const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st;
+  const T* kb = reinterpret_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+  const T* vb = reinterpret_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+  const int64_t cbase = qid * p.Kc;
+  WA wa;
+  wa.init(qrow, p.scale * LOG2E, lane);
+  for (int base = 0; base < p.Kc; base += WA::RPW * U) {
+    const T* kr[U];
+    const T* vr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = base + u * WA::RPW + wa.sub;
+      kr[u] = vr[u] = nullptr;
+      if (g < p.Kc) {
+        const int64_t pos = p.cand64 ? reinterpret_cast<const int64_t*>(p.cand)[cbase + g]
+                                     : (int64_t)reinterpret_cast<const int32_t*>(p.cand)[cbase + g];
+        if (pos >= 0 && pos < p.T_kv) {
+          kr[u] = kb + pos * p.k_st;
+          vr[u] = vb + pos * p.v_st;
+        } else if (pos >= p.T_kv) {
+          record_error(DEV_INDEX_RANGE, K_SPARSE_ATTN, (int)pos, p.T_kv);
+        }
+      }
+    }
+    wa.template rows_global<U>(kr, vr);
+  }
+  wa.reduce_rows();
+  const float inv = wa.l > 0.f ? 1.f / wa.l : 0.f;
+  if (wa.sub == 0) {
+    float outv[WA::VEC];
+#pragma unroll
+    for (int i = 0; i < WA::VEC; ++i) outv[i] = wa.acc[i] * inv;
+    T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + n * p.o_st;
+    store_vec_from_f32<T>(orow + wa.c * WA::VEC, outv);
+  }
+  if (lane == 0 && p.lse) p.lse[qid] = wa.l > 0.f ? (wa.m + log2f(wa.l)) * LN2 : -INFINITY;
+}
+
+// ------------------------------------------------------------------------------------------------ gather_dot
+// fastseg.py:118-130: out[b,h,n,c] = scale * q[b,h,n] . S[b,h,cand[b,h,n,c]] in fp32; ids clamped to [0, M-1]
+// as the reference does. One warp per query row.
+struct GatherDotParams {
+  const void* q;
+  int64_t q_sb, q_sh, q_st;
+  const void* S;
+  int64_t s_sb, s_sh, s_st;
+  const void* cand;  // (B,H,N,C) contiguous, int32 or int64
+  int cand64;
+  int B, H, N, C, M;
+  float scale;
+  float* out;        // (B,H,N,C)
+};
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(128) gather_dot_kernel(GatherDotParams p) {
+  using WA = WarpAttn<T, DH>;
+  constexpr int VEC = WA::VEC, LPR = WA::LPR, RPW = WA::RPW;
+  constexpr int U = (RPW >= 8) ? 2 : 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qid = (int64_t)blockIdx.x * 4 + warp;
+  if (qid >= (int64_t)p.B * p.H * p.N) return;
+  const int n = (int)(qid % p.N);
+  const int bh = (int)(qid / p.N);
+  const int b = bh / p.H, h = bh % p.H;
+  const int sub = lane / LPR, c = lane % LPR;
+  float qv[VEC];
+  load_vec_f32<T>(reinterpret_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st + c * VEC, qv);
+  const T* sb = reinterpret_cast<const T*>(p.S) + b * p.s_sb + h * p.s_sh;
+  const int64_t cbase = qid * p.C;
+  for (int base = 0; base < p.C; base += RPW * U) {
+    float kf[U][VEC];
+    int gi[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = base + u * RPW + sub;
+      gi[u] = g;
+      if (g < p.C) {
+        int64_t id = p.cand64 ? reinterpret_cast<const int64_t*>(p.cand)[cbase + g]
+                              : (int64_t)reinterpret_cast<const int32_t*>(p.cand)[cbase + g];
+        id = id < 0 ? 0 : (id >= p.M ? p.M - 1 : id);
+        ldg_vec_f32<T>(sb + id * p.s_st + c * VEC, kf[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) kf[u][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) s = fmaf(qv[i], kf[u][i], s);
+      s = warp_sum_sub(s, LPR);
+      if (c == 0 && gi[u] < p.C) p.out[cbase + gi[u]] = s * p.scale;
+    }
+  }
+}
+
+// Block form (selected key blocks of `blk` contiguous rows): each CTA stages NB_CTA blocks of one (b, h) into
+// shared memory with 1-D bulk copies (one mbarrier), then 4 warps score the rows from shared memory.
+struct GatherDotBlocksParams {
+  const void* q;            // (B,H,dh) query rows (strides)
+  int64_t q_sb, q_sh;
+  const void* k;            // (B,H,T,dh) keys (strides; rows must be 16-byte aligned)
+  int64_t k_sb, k_sh, k_st;
+  const int32_t* blocks;    // (B,H,nblk) block ids
+  int B, H, T, nblk, blk, nb_cta;
+  float scale;
+  float* out;               // (B,H,nblk*blk)
+};
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(128) gather_dot_blocks_kernel(GatherDotBlocksParams p) {
+  using WA = WarpAttn<T, DH>;
+  constexpr int VEC = WA::VEC, LPR = WA::LPR, RPW = WA::RPW;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t bar;
+  T* rows = reinterpret_cast<T*>(smem_raw);
+  const int groups = ceil_div(p.nblk, p.nb_cta);
+  const int bh = blockIdx.x / groups, grp = blockIdx.x % groups;
+  const int b = bh / p.H, h = bh % p.H;
+  const int j0 = grp * p.nb_cta;
+  const int nb = min(p.nb_cta, p.nblk - j0);
+  const int row_bytes = DH * (int)sizeof(T);
+  const int32_t* bl = p.blocks + (int64_t)bh * p.nblk + j0;
+  const T* kbase = reinterpret_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t pol = l2_policy_evict_first();
+    uint32_t bytes = 0;
+    int okb[64];
+    for (int j = 0; j < nb; ++j) {
+      const int id = bl[j];
+      okb[j & 63] = (id >= 0 && (int64_t)(id + 1) * p.blk <= p.T);
+      if (okb[j & 63]) bytes += (uint32_t)(p.blk * row_bytes);
+      else record_error(DEV_INDEX_RANGE, K_GATHER_DOT_BLOCKS, id, p.T / p.blk);
+    }
+    mbar_arrive_expect_tx(&bar, bytes);
+    for (int j = 0; j < nb; ++j) {
+      if (!okb[j & 63]) continue;
+      bulk_g2s_hint(rows + (size_t)j * p.blk * DH, kbase + (int64_t)bl[j] * p.blk * p.k_st,
+                    (uint32_t)(p.blk * row_bytes), &bar, pol);
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / LPR, c = lane % LPR;
+  float qv[VEC];
+  load_vec_f32<T>(reinterpret_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh + c * VEC, qv);
+  const bool ok = mbar_wait_bounded(&bar, 0, K_GATHER_DOT_BLOCKS, 0);
+  if (!ok) return;  // the wait gave up; an error is recorded (copies may still land in this CTA's smem)
+  const int nrows = nb * p.blk;
+  float* outp = p.out + (int64_t)bh * p.nblk * p.blk + (int64_t)j0 * p.blk;
+  for (int base = warp * RPW; base < nrows; base += 4 * RPW) {
+    const int r = base + sub;
+    float s = 0.f;
+    if (r < nrows) {
+      float kf[VEC];
+      load_vec_f32<T>(rows + (size_t)r * DH + c * VEC, kf);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) s = fmaf(qv[i], kf[i], s);
+    }
+    s = warp_sum_sub(s, LPR);
+    if (c == 0 && r < nrows) outp[r] = s * p.scale;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ dedupe
+// keep[r, j] = valid[r, j] and no earlier valid entry of row r holds the same value. One CTA per row.
+__global__ void dedupe_kernel(const int64_t* __restrict__ cand, const uint8_t* __restrict__ valid, uint8_t* keep,
+                              int64_t rows, int Kc) {
+  extern __shared__ int64_t s_key[];
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  for (int j = threadIdx.x; j < Kc; j += blockDim.x) {
+    const bool v = valid[r * Kc + j] != 0;
+    s_key[j] = v ? cand[r * Kc + j] : INT64_MIN;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < Kc; j += blockDim.x) {
+    const int64_t x = s_key[j];
+    bool kp = x != INT64_MIN;
+    for (int i = 0; i < j && kp; ++i) kp = (s_key[i] != x);
+    keep[r * Kc + j] = kp ? 1 : 0;
+  }
+}
+
+}  // namespace ta

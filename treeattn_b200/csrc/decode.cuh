@@ -1,0 +1,470 @@
+// Fused segment-tree decode step for one layer (reference: engine.py:84-120 seg_attend with the incremental
+// tree update of engine.py:41-55 SegState.add), batched over (b, h) and split across a thread-block cluster.
+//
+// One cluster of S CTAs per (b, h). Every CTA of the cluster runs the tree descent for the new query (warp 0;
+// the node rows come from L2 after the first CTA), while a producer warp already streams the local-window
+// rows. The key set - used leaf blocks cut at the window, the sink, the window, and the new token - is cut
+// into stages of <= CH rows; stage c belongs to CTA c % S. A producer warp fills a ring of NST shared-memory
+// stages with 1-D bulk copies (cp.async.bulk, no multicast) and mbarriers; NCW consumer warps run the online
+// softmax from shared memory. Partial (max, sum, acc) states are merged across the cluster through
+// distributed shared memory, rank 0 writes the output, appends the new K/V rows and, when the new token
+// completes a leaf block, forms that leaf node and its right-spine ancestors (fp32, adjacent-pair order).
+//
+// Position t itself is not read from the cache: rank 0 takes the new token's key/value straight from the
+// qkv rows of this step, so no CTA reads a cache row that is written in the same launch. The tree nodes
+// written here (node t>>l at each level where (t+1) % 2^l == 0) are not complete before t, so no descent of
+// this launch reads them either.
+#pragma once
+#include "attn.cuh"
+
+namespace ta {
+
+struct DecodeParams {
+  const void* qkv;        // (B, 3*H*DH) rows of this step: q | k | v
+  int64_t qkv_sb;         // row stride (elements)
+  int64_t k_ofs, v_ofs;   // element offsets of the k and v parts inside a row
+  void* kc;               // key cache (B, H, cap, DH) with strides below
+  void* vc;               // value cache
+  int64_t c_sb, c_sh, c_st;
+  float* nodes;           // tree levels (mutable), layout of LevelView
+  LevelView lv;
+  const int32_t* pos;     // (B) position t of this step
+  int B, H, wmax, n_tree, Lw;
+  float scale;
+  void* out;              // (B, H*DH) attention output rows
+  int64_t o_sb;
+  float* lse;             // (B, H) natural-log LSE, may be null
+  int32_t* nkeys;         // (B, H) keys attended, may be null
+  int32_t* sel;           // (B, H, wmax + 1): [count, leaf ids...] of the descent, may be null
+  int splits;             // cluster size S (grid.x)
+};
+
+template <typename T, int DH, int CH, int NST, int NCW>
+struct DecodeCfg {
+  static constexpr int NTHREADS = (NCW + 1) * 32;
+  static constexpr int STAGE_ELEMS = 2 * CH * DH;  // K rows then V rows
+  static constexpr size_t RING_BYTES = (size_t)NST * STAGE_ELEMS * sizeof(T);
+};
+
+struct DecodeShared {
+  uint64_t full[8];
+  uint64_t empty[8];
+  int nrows[8];
+  int consumed;
+  int rows_cta;
+  int nsel;
+  int abort_flag;
+  RangeList rl;
+  DescentScratch ds;
+  float part_m[8], part_l[8];
+  float cta_m, cta_l;
+  int cta_rows;
+};
+
+// Dynamic shared memory: [DecodeShared][pad to 128][ring][descent stage rows][part_acc NCW*DH][cta_acc DH]
+template <typename T, int DH, int CH, int NST, int NCW>
+__host__ __device__ inline size_t decode_smem_bytes(int wmax) {
+  size_t off = (sizeof(DecodeShared) + 127) & ~(size_t)127;
+  off += DecodeCfg<T, DH, CH, NST, NCW>::RING_BYTES;
+  off += (size_t)(2 * wmax + 1) * DH * sizeof(float);
+  off += (size_t)NCW * DH * sizeof(float);
+  off += (size_t)DH * sizeof(float);
+  return off;
+}
+
+// Form the leaf node of the block that position t completes ((t+1) % 2^L0 == 0) and its right-spine
+// ancestors. Leaf node = adjacent-pair fp32 sums of rows [n*2^L0, t] (the sink as 0; row t = knew, not yet
+// readable from the cache), reduced in shared memory `xs` (xs_floats >= 2^L0) in dim slices. All `nthreads`
+// threads of the CTA must call this; it ends with the node rows written.
+template <typename T, int DH>
+__device__ void tree_update_block(const T* __restrict__ kbase, int64_t c_st, const T* __restrict__ knew, int t,
+                                  float* __restrict__ nodes_bh, const LevelView& lv, float* xs, int xs_floats,
+                                  int tid, int nthreads) {
+  const int L0 = lv.L0, leaf = 1 << L0;
+  const int DS = min(DH, xs_floats / leaf);
+  const int n_blk = t >> L0;
+  const int p0 = n_blk * leaf;
+  float my_node = 0.f;  // this thread's dim of the new leaf node (tid < DH)
+  for (int d0 = 0; d0 < DH; d0 += DS) {
+    const int dn = min(DS, DH - d0);
+    for (int x = tid; x < leaf * dn; x += nthreads) {
+      const int i = x / dn, d = d0 + (x - (x / dn) * dn);
+      const int pp = p0 + i;
+      float v;
+      if (pp == 0) v = 0.f;
+      else if (pp == t) v = to_f32(knew[d]);
+      else v = to_f32(kbase[(int64_t)pp * c_st + d]);
+      xs[i * dn + (d - d0)] = v;
+    }
+    __syncthreads();
+    for (int st = 1; st < leaf; st <<= 1) {
+      const int pairs = leaf / (2 * st);
+      for (int x = tid; x < pairs * dn; x += nthreads) {
+        const int pi = x / dn, d = x - (x / dn) * dn;
+        const int i = pi * 2 * st;
+        xs[i * dn + d] = xs[i * dn + d] + xs[(i + st) * dn + d];
+      }
+      __syncthreads();
+    }
+    if (tid >= d0 && tid < d0 + dn) my_node = xs[tid - d0];
+    __syncthreads();
+  }
+  if (tid < DH) {
+    nodes_bh[(int64_t)(lv.off[L0] + n_blk) * DH + tid] = my_node;
+    // node m = t >> l at level l is complete when (t+1) % 2^l == 0; the node just formed at level l-1 is its
+    // right child, so parent = S[l-1][2m] (stored earlier) + S[l-1][2m+1] (just formed)
+    float cur = my_node;
+    for (int l = L0 + 1; l <= lv.Lm; ++l) {
+      if (((t + 1) & ((1 << l) - 1)) != 0) break;
+      const int m = t >> l;
+      if (m >= (lv.cap >> l)) break;
+      const float left = nodes_bh[(int64_t)(lv.off[l - 1] + 2 * m) * DH + tid];
+      cur = left + cur;
+      nodes_bh[(int64_t)(lv.off[l] + m) * DH + tid] = cur;
+    }
+  }
+}
+
+template <typename T, int DH, int CH, int NST, int NCW>
+__global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) {
+  using Cfg = DecodeCfg<T, DH, CH, NST, NCW>;
+  using WA = WarpAttn<T, DH>;
+  constexpr int VEC = WA::VEC, RPW = WA::RPW;
+  constexpr int ROWB = DH * (int)sizeof(T);
+  static_assert(NST <= 8 && NCW <= 8, "ring too deep");
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  DecodeShared& sh = *reinterpret_cast<DecodeShared*>(smem_raw);
+  size_t off = (sizeof(DecodeShared) + 127) & ~(size_t)127;
+  T* ring = reinterpret_cast<T*>(smem_raw + off);
+  off += Cfg::RING_BYTES;
+  float* dstage = reinterpret_cast<float*>(smem_raw + off);
+  off += (size_t)(2 * p.wmax + 1) * DH * sizeof(float);
+  float* part_acc = reinterpret_cast<float*>(smem_raw + off);
+  off += (size_t)NCW * DH * sizeof(float);
+  float* cta_acc = reinterpret_cast<float*>(smem_raw + off);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = p.splits;
+  const int rank = (S > 1) ? (int)cluster_ctarank() : 0;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int leaf = 1 << p.lv.L0;
+
+  int t = p.pos[b];
+  bool active = true;
+  if (t < 0 || t >= p.lv.cap) {
+    if (tid == 0 && rank == 0) record_error(DEV_POS_RANGE, K_DECODE, t, p.lv.cap);
+    active = false;
+    t = 0;
+  }
+  const int w0 = max(t - p.Lw + 1, 0);
+  const int nwin = active ? t - w0 : 0;   // window rows read from the cache: [w0, t)
+  const int nA = ceil_div(nwin, CH);      // window stages
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], NCW);
+    }
+    sh.consumed = 0;
+    sh.rows_cta = 0;
+    sh.abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const T* kbase = reinterpret_cast<const T*>(p.kc) + b * p.c_sb + h * p.c_sh;
+  const T* vbase = reinterpret_cast<const T*>(p.vc) + b * p.c_sb + h * p.c_sh;
+  const T* qkv_row = reinterpret_cast<const T*>(p.qkv) + b * p.qkv_sb;
+
+  if (warp == NCW) {
+    // ------------------------------------------------------------------ producer warp (lane 0 issues)
+    const uint64_t pol = l2_policy_evict_first();
+    int it = 0;  // stages issued by this CTA (lane 0)
+    bool ok = true;
+    auto acquire = [&](int& s) -> bool {
+      s = it % NST;
+      if (it >= NST) return mbar_wait_bounded(&sh.empty[s], ((it / NST) - 1) & 1, K_DECODE, 1);
+      return true;
+    };
+    if (lane == 0) {
+      // phase A: the window rows [w0, t), CH rows per stage
+      for (int c = 0; c < nA && ok; ++c) {
+        if (c % S != rank) continue;
+        int s;
+        if (!(ok = acquire(s))) break;
+        const int r0 = w0 + c * CH;
+        const int n = min(CH, t - r0);
+        sh.nrows[s] = n;
+        T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
+        mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+        bulk_g2s_hint(kd, kbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
+        bulk_g2s_hint(kd + CH * DH, vbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
+        ++it;
+      }
+    }
+    __syncwarp();
+    // wait for the descent's range list (warp 0 arrives on named barrier 1)
+    named_bar_sync(1, 64);
+    if (lane == 0) {
+      // phase B: leaf ranges + sink, packed CH rows per stage; every CTA walks the same packing
+      if (ok && active) {
+        const RangeList& rl = sh.rl;
+        int ri = 0, roff = 0;
+        for (int c = nA; ri < rl.n && ok; ++c) {
+          const bool mine = (c % S) == rank;
+          int s = 0;
+          if (mine && !(ok = acquire(s))) break;
+          T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
+          int n = 0;
+          {  // rows of this stage
+            int ri2 = ri, roff2 = roff;
+            while (n < CH && ri2 < rl.n) {
+              const int len = rl.pref[ri2 + 1] - rl.pref[ri2];
+              const int take = min(CH - n, len - roff2);
+              n += take;
+              roff2 += take;
+              if (roff2 == len) { ++ri2; roff2 = 0; }
+            }
+          }
+          if (mine) {
+            sh.nrows[s] = n;
+            mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+          }
+          int put = 0;
+          while (put < n) {
+            const int len = rl.pref[ri + 1] - rl.pref[ri];
+            const int take = min(n - put, len - roff);
+            if (mine) {
+              const int64_t r0 = rl.start[ri] + roff;
+              bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
+              bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB),
+                            &sh.full[s], pol);
+            }
+            put += take;
+            roff += take;
+            if (roff == len) { ++ri; roff = 0; }
+          }
+          if (mine) ++it;
+        }
+      }
+      // sentinel stage: no copy, only an arrival
+      if (ok) {
+        int s;
+        if ((ok = acquire(s))) {
+          sh.nrows[s] = -1;
+          mbar_arrive(&sh.full[s]);
+        }
+      }
+      if (!ok) atomicExch(&sh.abort_flag, 1);
+    }
+    __syncwarp();
+    // wait until the consumers stopped, then make sure no copy of this CTA is still in flight
+    named_bar_sync(2, Cfg::NTHREADS);
+    if (lane == 0) {
+      for (int i = sh.consumed; i < it; ++i) mbar_wait_bounded(&sh.full[i % NST], (i / NST) & 1, K_DECODE, 2);
+    }
+  } else {
+    // ------------------------------------------------------------------ consumer warps
+    WA wa;
+    wa.init(qkv_row + h * DH, p.scale * LOG2E, lane);
+    if (warp == 0) {
+      int nk = 0;
+      if (active) {
+        float qv[4];
+        load_q4<T, DH>(qkv_row + h * DH, lane, qv);
+        const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
+        const int keep = min(p.n_tree, p.wmax);
+        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, lane);
+        build_ranges(
+            sh.rl, nk, [&](int i) -> int { return sh.ds.kid[i]; }, leaf, t, p.Lw, w0, lane);
+      } else if (lane == 0) {
+        sh.rl.n = 0;
+        sh.rl.pref[0] = 0;
+      }
+      if (lane == 0) sh.nsel = nk;
+      __syncwarp();
+      named_bar_arrive(1, 64);
+      if (rank == 0 && active) {
+        // the new token (position t) from this step's k/v rows
+        const T* kr[1] = {wa.sub == 0 ? qkv_row + p.k_ofs + h * DH : nullptr};
+        const T* vr[1] = {wa.sub == 0 ? qkv_row + p.v_ofs + h * DH : nullptr};
+        wa.template rows_global<1>(kr, vr);
+      }
+    }
+    // stream the ring
+    int it = 0, rows_mine = 0;
+    bool ok = true;
+    while (true) {
+      const int s = it % NST;
+      if (!mbar_wait_bounded(&sh.full[s], (it / NST) & 1, K_DECODE, 3)) {
+        ok = false;
+        break;
+      }
+      const int n = sh.nrows[s];
+      if (n < 0) break;
+      const T* kst = ring + (size_t)s * Cfg::STAGE_ELEMS;
+      const T* vst = kst + CH * DH;
+      const int ngroups = ceil_div(n, RPW);
+      for (int g0 = warp; g0 < ngroups; g0 += 2 * NCW) {
+        float kf[2][VEC], vf[2][VEC];
+        float sc[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int g = g0 + u * NCW;
+          const int r = g * RPW + wa.sub;
+          const bool valid = (g < ngroups) && (r < n);
+          if (valid) {
+            load_vec_f32<T>(kst + (size_t)r * DH + wa.c * VEC, kf[u]);
+            load_vec_f32<T>(vst + (size_t)r * DH + wa.c * VEC, vf[u]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) kf[u][i] = vf[u][i] = 0.f;
+          }
+          const float x = wa.row_score(kf[u]);
+          sc[u] = valid ? x : -INFINITY;
+        }
+        wa.template update<2>(sc, vf);
+      }
+      if (warp == 0) rows_mine += n;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.empty[s]);
+      ++it;
+    }
+    if (!ok) atomicExch(&sh.abort_flag, 1);
+    if (warp == 0 && lane == 0) {
+      sh.consumed = it;
+      sh.rows_cta = rows_mine + ((rank == 0 && active) ? 1 : 0);
+    }
+    // warp partials
+    wa.reduce_rows();
+    if (lane == 0) {
+      sh.part_m[warp] = wa.m;
+      sh.part_l[warp] = wa.l;
+    }
+    if (wa.sub == 0) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) part_acc[warp * DH + wa.c * VEC + i] = wa.acc[i];
+    }
+    named_bar_sync(2, Cfg::NTHREADS);
+  }
+
+  // ------------------------------------------------------------------ CTA partial (threads < DH)
+  __syncthreads();
+  if (tid < DH) {
+    float m = -INFINITY, l = 0.f, a = 0.f;
+    for (int w = 0; w < NCW; ++w) {
+      const float mw = sh.part_m[w];
+      const float mn = fmaxf(m, mw);
+      if (mn == -INFINITY) continue;
+      const float fa = exp2f(m - mn), fb = exp2f(mw - mn);
+      l = l * fa + sh.part_l[w] * fb;
+      a = a * fa + part_acc[w * DH + tid] * fb;
+      m = mn;
+    }
+    cta_acc[tid] = a;
+    if (tid == 0) {
+      sh.cta_m = m;
+      sh.cta_l = l;
+      sh.cta_rows = sh.rows_cta;
+    }
+  }
+  // ------------------------------------------------------------------ cluster merge
+  if (S > 1) cluster_sync_all();
+  else __syncthreads();
+  if (rank == 0) {
+    if (tid < DH) {
+      float m = sh.cta_m, l = sh.cta_l, a = cta_acc[tid];
+      for (int r = 1; r < S; ++r) {
+        const DecodeShared* rs = cluster_map(&sh, (uint32_t)r);
+        const float* racc = cluster_map(cta_acc, (uint32_t)r);
+        const float mr = rs->cta_m;
+        const float mn = fmaxf(m, mr);
+        if (mn == -INFINITY) continue;
+        const float fa = exp2f(m - mn), fb = exp2f(mr - mn);
+        l = l * fa + rs->cta_l * fb;
+        a = a * fa + racc[tid] * fb;
+        m = mn;
+      }
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      cta_acc[tid] = a * inv;  // reuse as the normalised output
+      if (tid == 0) {
+        int rows = sh.cta_rows;
+        for (int r = 1; r < S; ++r) rows += cluster_map(&sh, (uint32_t)r)->cta_rows;
+        if (p.lse) p.lse[bh] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
+        if (p.nkeys) p.nkeys[bh] = rows;
+        if (p.sel) {
+          int32_t* so = p.sel + (int64_t)bh * (p.wmax + 1);
+          so[0] = sh.nsel;
+          for (int i = 0; i < p.wmax; ++i) so[1 + i] = i < sh.nsel ? sh.ds.kid[i] : -1;
+        }
+      }
+    }
+  }
+  if (S > 1) cluster_sync_all();  // remote shared memory stays alive until rank 0 has read it
+  if (rank != 0 || !active) return;
+  __syncthreads();
+  // ------------------------------------------------------------------ output + append (rank 0)
+  T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
+  T* kdst = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh + (int64_t)t * p.c_st;
+  T* vdst = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh + (int64_t)t * p.c_st;
+  if (tid < DH / VEC) {
+    store_vec_from_f32<T>(orow + tid * VEC, cta_acc + tid * VEC);
+    *reinterpret_cast<uint4*>(kdst + tid * VEC) = *reinterpret_cast<const uint4*>(qkv_row + p.k_ofs + h * DH + tid * VEC);
+    *reinterpret_cast<uint4*>(vdst + tid * VEC) = *reinterpret_cast<const uint4*>(qkv_row + p.v_ofs + h * DH + tid * VEC);
+  }
+  // ------------------------------------------------------------------ incremental tree update
+  if (((t + 1) & (leaf - 1)) != 0) return;
+  constexpr int RING_FLOATS = (int)(Cfg::RING_BYTES / sizeof(float));
+  tree_update_block<T, DH>(kbase, p.c_st, qkv_row + p.k_ofs + h * DH, t,
+                           p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, reinterpret_cast<float*>(ring), RING_FLOATS,
+                           tid, Cfg::NTHREADS);
+}
+
+// ------------------------------------------------------------------------------------------------ append
+// SegState.add (engine.py:41-55) for a batch: write k, v of position pos[b] into the caches and, when that
+// position completes a leaf block, form the leaf node and its right-spine ancestors. One CTA per (b, h).
+struct AppendParams {
+  const void* k;          // (B, H, DH) new key rows, strides k_sb, k_sh
+  const void* v;
+  int64_t k_sb, k_sh, v_sb, v_sh;
+  void* kc;
+  void* vc;
+  int64_t c_sb, c_sh, c_st;
+  float* nodes;
+  LevelView lv;
+  const int32_t* pos;
+  int B, H;
+};
+
+constexpr int APPEND_THREADS = 128;
+constexpr int APPEND_SMEM_FLOATS = 8192;
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(APPEND_THREADS) append_kernel(AppendParams p) {
+  extern __shared__ __align__(16) float xs[];
+  const int bh = blockIdx.x;
+  const int b = bh / p.H, h = bh % p.H;
+  const int tid = threadIdx.x;
+  const int t = p.pos[b];
+  if (t < 0 || t >= p.lv.cap) {
+    if (tid == 0) record_error(DEV_POS_RANGE, K_APPEND, t, p.lv.cap);
+    return;
+  }
+  constexpr int VEC = TypeInfo<T>::VEC;
+  const T* kr = reinterpret_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+  const T* vr = reinterpret_cast<const T*>(p.v) + b * p.v_sb + h * p.v_sh;
+  T* kbase = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh;
+  T* vbase = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh;
+  if (tid < DH / VEC) {
+    *reinterpret_cast<uint4*>(kbase + (int64_t)t * p.c_st + tid * VEC) = *reinterpret_cast<const uint4*>(kr + tid * VEC);
+    *reinterpret_cast<uint4*>(vbase + (int64_t)t * p.c_st + tid * VEC) = *reinterpret_cast<const uint4*>(vr + tid * VEC);
+  }
+  const int leaf = 1 << p.lv.L0;
+  if (((t + 1) & (leaf - 1)) != 0) return;
+  tree_update_block<T, DH>(kbase, p.c_st, kr, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, xs,
+                           APPEND_SMEM_FLOATS, tid, APPEND_THREADS);
+}
+
+}  // namespace ta

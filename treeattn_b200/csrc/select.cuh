@@ -1,0 +1,263 @@
+// Past-only beam descent over the segment tree (reference: seg.py:44-70 tree_pass, fastseg.py:254-271
+// tree_pass_fast), one warp per query.
+//
+// Reference rule, per level l from Lm down to the leaf level L0: the candidates are the children of the
+// nodes kept at level l+1 plus the newly available past-only subtree (t>>l)-1 when bit l of t is set;
+// each is scored q . S_l[c] / 2^l and the best `wmax` are kept; at the leaf level the kept leaves are
+// returned best first. (With leaf blocks of 2^L0 tokens this is the reference's tree_pass on the level-
+// shifted tree S'[l'] = S[l'+L0-1]: all candidates of a level share one scale, so the order is unchanged.)
+//
+// Two facts let the kernel skip work without changing the result:
+//  * While a level's reachable set R(l) has at most wmax nodes, every node of it is kept, whatever the
+//    scores. R(l) is then the contiguous range [a_l, t>>l) with a_l = ((t>>Lm) - bit_Lm(t)) << (Lm-l), so
+//    the first level that needs a real top-k, l*, has R(l*) = a contiguous range of <= 2*wmax+1 nodes.
+//  * Below l* the candidates are the 2 adjacent children of each kept node plus the injected node.
+// Ties are broken by the smaller node id (torch.topk leaves the tie order undefined; parity tests exclude
+// queries whose reference scores tie at a cut).
+#pragma once
+#include "levels.cuh"
+
+namespace ta {
+
+constexpr int WMAX_LIMIT = 64;                  // largest supported wmax
+constexpr int CAND_LIMIT = 2 * WMAX_LIMIT + 1;  // largest candidate list of one level
+
+// Per-warp shared scratch of one descent (the staged node rows live in a separate, host-sized buffer of
+// (2*wmax+1) * DH floats).
+struct DescentScratch {
+  int cid[CAND_LIMIT];
+  float csc[CAND_LIMIT];
+  int kid[WMAX_LIMIT];
+  float ksc[WMAX_LIMIT];
+};
+
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Exact 2^-l as a float (l < 127).
+__device__ __forceinline__ float pow2_neg(int l) { return __int_as_float((127 - l) << 23); }
+
+template <int DH>
+struct Descent {
+  static constexpr int G = DH / 4;    // lanes per node row (float4 each)
+  static constexpr int NPP = 32 / G;  // node rows per warp pass
+
+  // Score the n candidates sc.cid[0..n) of level `lvl` (base pointer of that level for this (b,h)).
+  static __device__ __forceinline__ void score(const float* __restrict__ lvl, int n, float scale,
+                                               const float (&qv)[4], DescentScratch& sc, float* stage, int lane) {
+    const int chunks = n * G;
+    for (int x = lane; x < chunks; x += 32) {
+      const int j = x / G, cc = x - (x / G) * G;
+      cp_async16(stage + j * DH + cc * 4, lvl + (int64_t)sc.cid[j] * DH + cc * 4);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    const int sub = lane / G, c = lane - (lane / G) * G;
+    for (int base = 0; base < n; base += NPP) {
+      const int j = base + sub;
+      float s = 0.f;
+      if (j < n) {
+        const float4 v = *reinterpret_cast<const float4*>(stage + j * DH + c * 4);
+        s = qv[0] * v.x;
+        s = fmaf(qv[1], v.y, s);
+        s = fmaf(qv[2], v.z, s);
+        s = fmaf(qv[3], v.w, s);
+      }
+      s = warp_sum_sub(s, G);
+      if (c == 0 && j < n) sc.csc[j] = s * scale;
+    }
+    __syncwarp();
+  }
+
+  // Keep the best `keep` of the n scored candidates, best first, into sc.kid / sc.ksc. Returns the count.
+  static __device__ __forceinline__ int topk(int n, int keep, DescentScratch& sc, int lane) {
+    for (int j = lane; j < n; j += 32) {
+      const float sj = rank_key(sc.csc[j]);
+      const int ij = sc.cid[j];
+      int r = 0;
+      for (int i = 0; i < n; ++i) r += better(rank_key(sc.csc[i]), sc.cid[i], sj, ij) ? 1 : 0;
+      if (r < keep) {
+        sc.kid[r] = ij;
+        sc.ksc[r] = sc.csc[j];
+      }
+    }
+    __syncwarp();
+    return n < keep ? n : keep;
+  }
+
+  // Full descent for query position t. Returns the number of kept leaves; sc.kid[0..nk) holds the leaf ids.
+  // If `sorted_out` or if more leaves are reachable than `keep_last`, the leaf level is scored and the ids are
+  // best first with scores in sc.ksc; otherwise (everything reachable is kept) they are in ascending order
+  // and sc.ksc is not written.
+  static __device__ int run(const float* __restrict__ nodes_bh, const LevelView& lv, int t, int wmax, int keep_last,
+                            bool sorted_out, const float (&qv)[4], DescentScratch& sc, float* stage, int lane) {
+    const int Lm = lv.Lm, L0 = lv.L0;
+    const int eLm = t >> Lm;
+    const int aLm = eLm - (eLm & 1);
+    int lstar = -1;
+    for (int l = Lm; l >= L0; --l) {
+      const int e = t >> l, a = aLm << (Lm - l);
+      if (e - a > wmax) {
+        lstar = l;
+        break;
+      }
+    }
+    if (lstar < 0) {
+      const int a = aLm << (Lm - L0), e = t >> L0;
+      const int n = e - a;
+      for (int j = lane; j < n; j += 32) sc.cid[j] = a + j;
+      __syncwarp();
+      if (n > 0 && (sorted_out || n > keep_last)) {
+        score(nodes_bh + (int64_t)lv.off[L0] * DH, n, pow2_neg(L0), qv, sc, stage, lane);
+        return topk(n, keep_last, sc, lane);
+      }
+      for (int j = lane; j < n; j += 32) sc.kid[j] = a + j;
+      __syncwarp();
+      return n;
+    }
+    // first real selection: the whole reachable range of level l*
+    int nk;
+    {
+      const int a = aLm << (Lm - lstar), e = t >> lstar;
+      const int n = e - a;
+      for (int j = lane; j < n; j += 32) sc.cid[j] = a + j;
+      __syncwarp();
+      score(nodes_bh + (int64_t)lv.off[lstar] * DH, n, pow2_neg(lstar), qv, sc, stage, lane);
+      nk = topk(n, lstar == L0 ? keep_last : wmax, sc, lane);
+    }
+    for (int l = lstar - 1; l >= L0; --l) {
+      const int bit = (t >> l) & 1;
+      for (int i = lane; i < nk; i += 32) {
+        const int m = sc.kid[i];
+        sc.cid[2 * i] = 2 * m;
+        sc.cid[2 * i + 1] = 2 * m + 1;
+      }
+      if (bit && lane == 0) sc.cid[2 * nk] = (t >> l) - 1;
+      __syncwarp();
+      const int n = 2 * nk + bit;
+      score(nodes_bh + (int64_t)lv.off[l] * DH, n, pow2_neg(l), qv, sc, stage, lane);
+      nk = topk(n, l == L0 ? keep_last : wmax, sc, lane);
+    }
+    return nk;
+  }
+};
+
+// Load this lane's 4 query dims (c*4 .. c*4+3, c = lane % (DH/4)) as fp32.
+template <typename QT, int DH>
+__device__ __forceinline__ void load_q4(const QT* __restrict__ q, int lane, float (&qv)[4]) {
+  constexpr int G = DH / 4;
+  const int c = lane % G;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qv[i] = to_f32(q[c * 4 + i]);
+}
+
+// ------------------------------------------------------------------------------------------------ select kernel
+struct SelectParams {
+  const void* q;             // (B, H, Nq, dh), element strides below, unit stride in dh
+  int64_t q_sb, q_sh, q_st;
+  const int64_t* tq;         // position of query (b, n) = tq[b*tq_sb + n*tq_st]
+  int64_t tq_sb, tq_st;
+  LevelView lv;
+  int B, H, Nq;
+  int wmax, wl;              // beam width; output slots per query
+  int64_t* ids;              // (B, H, Nq, wl) leaf ids, best first; invalid slots 0
+  uint8_t* vld;              // (B, H, Nq, wl)
+  float* sct;                // (B, H, Nq, wl) scores q.S/2^L0 (-inf in invalid slots); may be null
+};
+
+template <typename QT, int DH>
+__global__ void __launch_bounds__(128) select_kernel(SelectParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int stage_floats = (2 * p.wmax + 1) * DH;
+  DescentScratch* scr = reinterpret_cast<DescentScratch*>(smem_raw);
+  float* stage_base = reinterpret_cast<float*>(smem_raw + sizeof(DescentScratch) * nwarps);
+  DescentScratch& sc = scr[warp];
+  float* stage = stage_base + (size_t)warp * stage_floats;
+
+  const int64_t qid = (int64_t)blockIdx.x * nwarps + warp;
+  const int64_t nq_total = (int64_t)p.B * p.H * p.Nq;
+  if (qid >= nq_total) return;
+  const int n = (int)(qid % p.Nq);
+  const int bh = (int)(qid / p.Nq);
+  const int b = bh / p.H, h = bh % p.H;
+  const int64_t tt = p.tq[b * p.tq_sb + n * p.tq_st];
+  const size_t obase = (size_t)qid * p.wl;
+  if (tt < 0 || tt >= p.lv.cap) {
+    if (lane == 0) record_error(DEV_POS_RANGE, K_SELECT, (int)tt, p.lv.cap);
+    for (int i = lane; i < p.wl; i += 32) {
+      p.ids[obase + i] = 0;
+      p.vld[obase + i] = 0;
+      if (p.sct) p.sct[obase + i] = -INFINITY;
+    }
+    return;
+  }
+  const int t = (int)tt;
+  float qv[4];
+  load_q4<QT, DH>(reinterpret_cast<const QT*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st, lane, qv);
+  const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
+  const int nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, p.wmax, true, qv, sc, stage, lane);
+  for (int i = lane; i < p.wl; i += 32) {
+    const bool ok = i < nk;
+    p.ids[obase + i] = ok ? sc.kid[i] : 0;
+    p.vld[obase + i] = ok ? 1 : 0;
+    if (p.sct) p.sct[obase + i] = ok ? sc.ksc[i] : -INFINITY;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ finish
+// seg.py:106-119 (leaves_to_pos, finish), one thread per query. Leaf m expands to positions
+// [m*leaf, (m+1)*leaf) stored as tree_pos[j*wl + i] = ids[i]*leaf + j (the reference's cat([2*ids, 2*ids+1])
+// at leaf 2); invalid -> -1.
+struct FinishParams {
+  const int64_t* ids;        // (Q, wl)
+  const uint8_t* vld;        // (Q, wl)
+  const int64_t* nid;        // (Q, nbw) neighbour leaf ids, may be null
+  const uint8_t* match;      // (Q, nbw), may be null (no neighbour matches)
+  const int64_t* nL;         // (Q), may be null (0)
+  const int64_t* lhat;       // (Q)
+  int64_t Q;
+  int wl, nbw, leaf, wmax;
+  int64_t* tree_pos;         // (Q, leaf*wl)
+  int64_t* nb_pos;           // (Q, leaf*nbw)
+  int64_t* n_tree;           // (Q)
+  int64_t* nb_leaves;        // (Q)
+};
+
+__device__ __forceinline__ int64_t floor_div2(int64_t x) { return x >= 0 ? x / 2 : -((-x + 1) / 2); }
+
+__global__ void finish_kernel(FinishParams p) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= p.Q) return;
+  const int64_t L = p.lhat[q];
+  const int64_t nL = p.nL ? p.nL[q] : 0;
+  const int64_t lo = floor_div2(L + 1);
+  int64_t need = L - nL;
+  if (need < 0) need = 0;
+  const int64_t floor_b = nL < lo ? 2 : 1;
+  int64_t bt = nL >= L ? 0 : (need > floor_b ? need : floor_b);
+  if (bt > p.wmax) bt = p.wmax;
+  p.n_tree[q] = bt;
+  p.nb_leaves[q] = nL;
+  if (p.tree_pos == nullptr) return;
+  for (int i = 0; i < p.wl; ++i) {
+    const bool ok = p.vld[q * p.wl + i] != 0;
+    const int64_t m = p.ids[q * p.wl + i];
+    for (int j = 0; j < p.leaf; ++j)
+      p.tree_pos[q * (int64_t)p.leaf * p.wl + (int64_t)j * p.wl + i] = ok ? m * p.leaf + j : -1;
+  }
+  if (p.nb_pos == nullptr) return;
+  for (int i = 0; i < p.nbw; ++i) {
+    const bool ok = p.match ? p.match[q * p.nbw + i] != 0 : false;
+    const int64_t m = p.nid ? p.nid[q * p.nbw + i] : 0;
+    for (int j = 0; j < p.leaf; ++j)
+      p.nb_pos[q * (int64_t)p.leaf * p.nbw + (int64_t)j * p.nbw + i] = ok ? m * p.leaf + j : -1;
+  }
+}
+
+}  // namespace ta

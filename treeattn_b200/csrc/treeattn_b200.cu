@@ -1,0 +1,505 @@
+// C ABI of the treeattn_b200 kernels: argument checks, launch shapes, dispatch over dtype x head dim.
+// Single translation unit: every kernel header is included here.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/treeattn_b200.h"
+#include "decode.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return TA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// a row of dh elements of `esize` bytes read in 16-byte chunks: base and every stride must keep 16-byte
+// alignment
+bool rows_aligned(const void* base, int esize, std::initializer_list<int64_t> strides) {
+  if (!aligned16(base)) return false;
+  for (int64_t s : strides)
+    if ((s * esize) % 16 != 0) return false;
+  return true;
+}
+
+int esize_of(int dtype) { return dtype == TA_F32 ? 4 : 2; }
+
+bool valid_dtype(int dtype) { return dtype == TA_F32 || dtype == TA_BF16 || dtype == TA_F16; }
+
+bool valid_dh(int dh) { return dh == 16 || dh == 32 || dh == 64 || dh == 128; }
+
+cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Dispatch F<T, DH>::run(args...) over the runtime dtype and head dim.
+template <template <typename, int> class F, typename T, typename... Args>
+int by_dh(int dh, Args&&... args) {
+  switch (dh) {
+    case 16: return F<T, 16>::run(args...);
+    case 32: return F<T, 32>::run(args...);
+    case 64: return F<T, 64>::run(args...);
+    case 128: return F<T, 128>::run(args...);
+    default: return fail(TA_ERR_ARG, "unsupported head dim %d (16, 32, 64, 128)", dh);
+  }
+}
+
+template <template <typename, int> class F, typename... Args>
+int by_type_dh(int dtype, int dh, Args&&... args) {
+  switch (dtype) {
+    case TA_F32: return by_dh<F, float>(dh, args...);
+    case TA_BF16: return by_dh<F, __nv_bfloat16>(dh, args...);
+    case TA_F16: return by_dh<F, __half>(dh, args...);
+    default: return fail(TA_ERR_ARG, "unsupported dtype code %d", dtype);
+  }
+}
+
+int check_levels(int cap, int L0, int Lm) {
+  if (cap <= 0) return fail(TA_ERR_ARG, "capacity must be positive (got %d)", cap);
+  if (L0 < 1 || L0 > 12) return fail(TA_ERR_ARG, "leaf level L0=%d outside [1, 12]", L0);
+  if (Lm < L0 || Lm > 30) return fail(TA_ERR_ARG, "top level Lm=%d outside [L0=%d, 30]", Lm, L0);
+  return TA_OK;
+}
+
+ta::LevelView make_lv(const float* nodes, int64_t n_sb, int64_t n_sh, int cap, int L0, int Lm) {
+  ta::LevelView lv{};
+  lv.nodes = nodes;
+  lv.s_b = n_sb;
+  lv.s_h = n_sh;
+  lv.cap = cap;
+  lv.L0 = L0;
+  lv.Lm = Lm;
+  ta::level_offsets(cap, L0, Lm, lv.off);
+  return lv;
+}
+
+// ------------------------------------------------------------------------------------------------ launchers
+template <typename T, int DH>
+struct BuildLevels {
+  static int run(const void* k, int B, int H, int T_len, int64_t k_sb, int64_t k_sh, int64_t k_st, int cap, int L0,
+                 int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh, cudaStream_t st) {
+    const ta::LevelView lv = make_lv(nodes, n_sb, n_sh, cap, L0, Lm);
+    const int n_leaf = T_len >> L0;
+    const int64_t total = (int64_t)B * H * n_leaf * DH;
+    if (total > 0) {
+      const int threads = 256;
+      ta::build_leaf_level_kernel<T><<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
+          reinterpret_cast<const T*>(k), k_sb, k_sh, k_st, H, T_len, DH, L0, nodes + (int64_t)lv.off[L0] * DH, n_sb,
+          n_sh, n_leaf, total, zero_sink);
+      if (int r = check_launch("ta_build_levels(leaf)")) return r;
+    }
+    if (Lm > L0 && n_leaf > 1) {
+      const int n = B * H * DH;
+      ta::build_upper_levels_kernel<<<(n + 127) / 128, 128, 0, st>>>(nodes, n_sb, n_sh, H, DH, lv, B * H, T_len);
+      if (int r = check_launch("ta_build_levels(upper)")) return r;
+    }
+    return TA_OK;
+  }
+};
+
+template <typename QT, int DH>
+struct Select {
+  static int run(ta::SelectParams p, cudaStream_t st) {
+    const int warps = 4;
+    const size_t smem = sizeof(ta::DescentScratch) * warps + (size_t)warps * (2 * p.wmax + 1) * DH * sizeof(float);
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(ta::select_kernel<QT, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr_set = true;
+    }
+    const int64_t nq = (int64_t)p.B * p.H * p.Nq;
+    if (nq == 0) return TA_OK;
+    ta::select_kernel<QT, DH><<<(unsigned)((nq + warps - 1) / warps), warps * 32, smem, st>>>(p);
+    return check_launch("ta_select");
+  }
+};
+
+template <typename T, int DH>
+struct SegAttn {
+  static int run(ta::SegAttnParams p, cudaStream_t st) {
+    const int64_t nq = (int64_t)p.B * p.H * p.Nq;
+    if (nq == 0) return TA_OK;
+    ta::seg_attn_kernel<T, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_seg_attn");
+  }
+};
+
+template <typename T, int DH>
+struct SparseAttn {
+  static int run(ta::SparseAttnParams p, cudaStream_t st) {
+    const int64_t nq = (int64_t)p.B * p.H * p.T;
+    if (nq == 0) return TA_OK;
+    ta::sparse_attn_kernel<T, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_sparse_attn");
+  }
+};
+
+template <typename T, int DH>
+struct GatherDot {
+  static int run(ta::GatherDotParams p, cudaStream_t st) {
+    const int64_t nq = (int64_t)p.B * p.H * p.N;
+    if (nq == 0 || p.C == 0) return TA_OK;
+    ta::gather_dot_kernel<T, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_gather_dot");
+  }
+};
+
+template <typename T, int DH>
+struct GatherDotBlocks {
+  static int run(ta::GatherDotBlocksParams p, cudaStream_t st) {
+    const size_t smem = (size_t)p.nb_cta * p.blk * DH * sizeof(T);
+    if (smem > 200 * 1024)
+      return fail(TA_ERR_ARG, "ta_gather_dot_blocks: nb_cta*blk rows need %zu B of shared memory (max 200 KiB)", smem);
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(ta::gather_dot_blocks_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           200 * 1024);
+      attr_set = true;
+    }
+    const int groups = ta::ceil_div(p.nblk, p.nb_cta);
+    const int64_t grid = (int64_t)p.B * p.H * groups;
+    if (grid == 0) return TA_OK;
+    ta::gather_dot_blocks_kernel<T, DH><<<(unsigned)grid, 128, smem, st>>>(p);
+    return check_launch("ta_gather_dot_blocks");
+  }
+};
+
+template <typename T, int DH>
+struct Append {
+  static int run(ta::AppendParams p, cudaStream_t st) {
+    static bool attr_set = false;
+    const size_t smem = ta::APPEND_SMEM_FLOATS * sizeof(float);
+    if (!attr_set) {
+      cudaFuncSetAttribute(ta::append_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_set = true;
+    }
+    if (p.B * p.H == 0) return TA_OK;
+    ta::append_kernel<T, DH><<<p.B * p.H, ta::APPEND_THREADS, smem, st>>>(p);
+    return check_launch("ta_append");
+  }
+};
+
+// Decode ring shape per (dtype, head dim): CH rows per stage, NST stages, 4 consumer warps.
+template <typename T, int DH>
+struct DecodeShape {
+  static constexpr int ROWB = DH * (int)sizeof(T);
+  static constexpr int CH = ROWB <= 128 ? 64 : 32;
+  static constexpr int NST = 3;
+  static constexpr int NCW = 4;
+};
+
+int g_num_sms = 0;
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+int default_splits(int B, int H) {
+  const int pairs = B * H;
+  if (pairs <= 0) return 1;
+  const int target = 4 * num_sms();  // ~4 resident CTAs per SM
+  int s = 1;
+  while (s < 8 && pairs * s < target) s <<= 1;
+  return s;
+}
+
+template <typename T, int DH>
+struct Decode {
+  static int run(ta::DecodeParams p, cudaStream_t st) {
+    using Sh = DecodeShape<T, DH>;
+    auto kern = ta::decode_kernel<T, DH, Sh::CH, Sh::NST, Sh::NCW>;
+    const size_t smem = ta::decode_smem_bytes<T, DH, Sh::CH, Sh::NST, Sh::NCW>(p.wmax);
+    if (smem > 220 * 1024) return fail(TA_ERR_ARG, "ta_decode_step: %zu B of shared memory needed", smem);
+    constexpr int RING_FLOATS = (int)(ta::DecodeCfg<T, DH, Sh::CH, Sh::NST, Sh::NCW>::RING_BYTES / sizeof(float));
+    if ((1 << p.lv.L0) > RING_FLOATS) return fail(TA_ERR_ARG, "ta_decode_step: leaf block too large");
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      attr_set = true;
+    }
+    if (p.B * p.H == 0) return TA_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p.splits, (unsigned)(p.B * p.H), 1);
+    cfg.blockDim = dim3((Sh::NCW + 1) * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.splits > 1 ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_decode_step: launch failed: %s", cudaGetErrorString(e));
+    return check_launch("ta_decode_step");
+  }
+};
+
+}  // namespace
+
+// ================================================================================================== C ABI
+extern "C" {
+
+int ta_version(void) { return 100; }
+
+const char* ta_last_error(void) { return g_err.c_str(); }
+
+int ta_device_error(int* out4) {
+  if (!out4) return fail(TA_ERR_ARG, "ta_device_error: null output");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_device_error: %s", cudaGetErrorString(e));
+  e = cudaMemcpyFromSymbol(out4, ta::g_dev_err, 4 * sizeof(int));
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_device_error: %s", cudaGetErrorString(e));
+  const int zero[4] = {0, 0, 0, 0};
+  e = cudaMemcpyToSymbol(ta::g_dev_err, zero, 4 * sizeof(int));
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_device_error: %s", cudaGetErrorString(e));
+  return TA_OK;
+}
+
+int64_t ta_level_nodes(int cap, int L0, int Lm) {
+  if (cap <= 0 || L0 < 0 || Lm < L0 || Lm > 30) return 0;
+  int off[ta::MAX_LEVELS];
+  return ta::level_offsets(cap, L0, Lm, off);
+}
+
+int ta_build_levels(const void* k, int dtype, int B, int H, int T_len, int dh, int64_t k_sb, int64_t k_sh,
+                    int64_t k_st, int cap, int L0, int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh,
+                    void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_build_levels: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_build_levels: unsupported head dim %d", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if (B < 0 || H <= 0 || T_len < 0 || T_len > cap)
+    return fail(TA_ERR_ARG, "ta_build_levels: bad sizes B=%d H=%d T=%d cap=%d", B, H, T_len, cap);
+  if (!k || !nodes) return fail(TA_ERR_ARG, "ta_build_levels: null pointer");
+  return by_type_dh<BuildLevels>(dtype, dh, k, B, H, T_len, k_sb, k_sh, k_st, cap, L0, Lm, zero_sink, nodes, n_sb,
+                                 n_sh, S(stream));
+}
+
+int ta_select(const void* q, int q_dtype, int B, int H, int Nq, int dh, int64_t q_sb, int64_t q_sh, int64_t q_st,
+              const int64_t* tq, int64_t tq_sb, int64_t tq_st, const float* nodes, int64_t n_sb, int64_t n_sh,
+              int cap, int L0, int Lm, int wmax, int wl, int64_t* ids, uint8_t* vld, float* sct, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(q_dtype)) return fail(TA_ERR_ARG, "ta_select: bad dtype %d", q_dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_select: unsupported head dim %d", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if (wmax < 1 || wmax > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_select: wmax=%d outside [1, 64]", wmax);
+  if (wl < 1 || wl > wmax) return fail(TA_ERR_ARG, "ta_select: wl=%d outside [1, wmax]", wl);
+  if (B < 0 || H <= 0 || Nq < 0) return fail(TA_ERR_ARG, "ta_select: bad sizes");
+  if (!q || !tq || !nodes || !ids || !vld) return fail(TA_ERR_ARG, "ta_select: null pointer");
+  if (!aligned16(nodes) || (n_sb * 4) % 16 || (n_sh * 4) % 16)
+    return fail(TA_ERR_ARG, "ta_select: node rows must be 16-byte aligned");
+  ta::SelectParams p{};
+  p.q = q;
+  p.q_sb = q_sb;
+  p.q_sh = q_sh;
+  p.q_st = q_st;
+  p.tq = tq;
+  p.tq_sb = tq_sb;
+  p.tq_st = tq_st;
+  p.lv = make_lv(nodes, n_sb, n_sh, cap, L0, Lm);
+  p.B = B;
+  p.H = H;
+  p.Nq = Nq;
+  p.wmax = wmax;
+  p.wl = wl;
+  p.ids = ids;
+  p.vld = vld;
+  p.sct = sct;
+  return by_type_dh<Select>(q_dtype, dh, p, S(stream));
+}
+
+int ta_finish(const int64_t* ids, const uint8_t* vld, const int64_t* nid, const uint8_t* match, const int64_t* nL,
+              const int64_t* lhat, int64_t Q, int wl, int nbw, int leaf, int wmax, int64_t* tree_pos,
+              int64_t* nb_pos, int64_t* n_tree, int64_t* nb_leaves, void* stream) {
+  g_err.clear();
+  if (Q < 0 || wl < 0 || nbw < 0 || leaf < 1) return fail(TA_ERR_ARG, "ta_finish: bad sizes");
+  if (!ids || !vld || !lhat || !n_tree || !nb_leaves) return fail(TA_ERR_ARG, "ta_finish: null pointer");
+  if (Q == 0) return TA_OK;
+  ta::FinishParams p{ids, vld, nid, match, nL, lhat, Q, wl, nbw, leaf, wmax, tree_pos, nb_pos, n_tree, nb_leaves};
+  ta::finish_kernel<<<(unsigned)((Q + 127) / 128), 128, 0, S(stream)>>>(p);
+  return check_launch("ta_finish");
+}
+
+int ta_seg_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int Nq, int dh,
+                int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const int64_t* tq, int64_t tq_sb,
+                int64_t tq_st, const int64_t* ids, const uint8_t* vld, int wl, const int64_t* n_tree,
+                int ntree_const, int leaf, int Lw, float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st,
+                float* lse, int32_t* nkeys, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_seg_attn: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_seg_attn: unsupported head dim %d", dh);
+  if (wl < 0 || wl > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_seg_attn: wl=%d outside [0, 64]", wl);
+  if (leaf < 1 || (leaf & (leaf - 1))) return fail(TA_ERR_ARG, "ta_seg_attn: leaf %d not a power of two", leaf);
+  if (Lw < 1) return fail(TA_ERR_ARG, "ta_seg_attn: window %d < 1", Lw);
+  if (!q || !k || !v || !tq || (wl > 0 && (!ids || !vld)) || !o) return fail(TA_ERR_ARG, "ta_seg_attn: null pointer");
+  const int es = esize_of(dtype);
+  if (!rows_aligned(q, es, {q_sb, q_sh, q_st}) || !rows_aligned(k, es, {k_sb, k_sh, k_st}) ||
+      !rows_aligned(v, es, {v_sb, v_sh, v_st}) || !rows_aligned(o, es, {o_sb, o_sh, o_st}))
+    return fail(TA_ERR_ARG, "ta_seg_attn: q/k/v/o rows must be 16-byte aligned");
+  ta::SegAttnParams p{};
+  p.q = q; p.k = k; p.v = v;
+  p.q_sb = q_sb; p.q_sh = q_sh; p.q_st = q_st;
+  p.k_sb = k_sb; p.k_sh = k_sh; p.k_st = k_st;
+  p.v_sb = v_sb; p.v_sh = v_sh; p.v_st = v_st;
+  p.tq = tq; p.tq_sb = tq_sb; p.tq_st = tq_st;
+  p.ids = ids; p.vld = vld; p.n_tree = n_tree; p.ntree_const = ntree_const;
+  p.B = B; p.H = H; p.Nq = Nq; p.wl = wl; p.leaf = leaf; p.Lw = Lw; p.T_kv = T_kv;
+  p.scale = scale;
+  p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
+  p.lse = lse; p.nkeys = nkeys;
+  return by_type_dh<SegAttn>(dtype, dh, p, S(stream));
+}
+
+int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int T, int dh,
+                   int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                   int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const void* cand, int cand64, int Kc,
+                   float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st, float* lse, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_sparse_attn: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_sparse_attn: unsupported head dim %d", dh);
+  if (Kc < 0) return fail(TA_ERR_ARG, "ta_sparse_attn: Kc < 0");
+  if (!q || !k || !v || !o || (Kc > 0 && !cand)) return fail(TA_ERR_ARG, "ta_sparse_attn: null pointer");
+  const int es = esize_of(dtype);
+  if (!rows_aligned(q, es, {q_sb, q_sh, q_st}) || !rows_aligned(k, es, {k_sb, k_sh, k_st}) ||
+      !rows_aligned(v, es, {v_sb, v_sh, v_st}) || !rows_aligned(o, es, {o_sb, o_sh, o_st}))
+    return fail(TA_ERR_ARG, "ta_sparse_attn: q/k/v/o rows must be 16-byte aligned");
+  ta::SparseAttnParams p{};
+  p.q = q; p.k = k; p.v = v;
+  p.q_sb = q_sb; p.q_sh = q_sh; p.q_st = q_st;
+  p.k_sb = k_sb; p.k_sh = k_sh; p.k_st = k_st;
+  p.v_sb = v_sb; p.v_sh = v_sh; p.v_st = v_st;
+  p.cand = cand; p.cand64 = cand64;
+  p.B = B; p.H = H; p.T = T; p.Kc = Kc; p.T_kv = T_kv;
+  p.scale = scale;
+  p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
+  p.lse = lse;
+  return by_type_dh<SparseAttn>(dtype, dh, p, S(stream));
+}
+
+int ta_gather_dot(const void* q, const void* Sn, int dtype, int B, int H, int N, int M, int C, int dh,
+                  int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t s_sb, int64_t s_sh, int64_t s_st,
+                  const void* cand, int cand64, float scale, float* out, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_gather_dot: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_gather_dot: unsupported head dim %d", dh);
+  if (M < 1 || C < 0) return fail(TA_ERR_ARG, "ta_gather_dot: bad sizes M=%d C=%d", M, C);
+  if (!q || !Sn || !out || (C > 0 && !cand)) return fail(TA_ERR_ARG, "ta_gather_dot: null pointer");
+  const int es = esize_of(dtype);
+  if (!rows_aligned(q, es, {q_sb, q_sh, q_st}) || !rows_aligned(Sn, es, {s_sb, s_sh, s_st}))
+    return fail(TA_ERR_ARG, "ta_gather_dot: q/S rows must be 16-byte aligned");
+  ta::GatherDotParams p{q, q_sb, q_sh, q_st, Sn, s_sb, s_sh, s_st, cand, cand64, B, H, N, C, M, scale, out};
+  return by_type_dh<GatherDot>(dtype, dh, p, S(stream));
+}
+
+int ta_gather_dot_blocks(const void* q, const void* k, int dtype, int B, int H, int T, int dh, int64_t q_sb,
+                         int64_t q_sh, int64_t k_sb, int64_t k_sh, int64_t k_st, const int32_t* blocks, int nblk,
+                         int blk, int nb_cta, float scale, float* out, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_gather_dot_blocks: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_gather_dot_blocks: unsupported head dim %d", dh);
+  if (nblk < 0 || blk < 1 || nb_cta < 1 || nb_cta > 64)
+    return fail(TA_ERR_ARG, "ta_gather_dot_blocks: bad sizes nblk=%d blk=%d nb_cta=%d", nblk, blk, nb_cta);
+  if (!q || !k || !out || (nblk > 0 && !blocks)) return fail(TA_ERR_ARG, "ta_gather_dot_blocks: null pointer");
+  const int es = esize_of(dtype);
+  if (!rows_aligned(q, es, {q_sb, q_sh}) || !rows_aligned(k, es, {k_sb, k_sh, k_st}))
+    return fail(TA_ERR_ARG, "ta_gather_dot_blocks: q/k rows must be 16-byte aligned");
+  if (k_st != dh) return fail(TA_ERR_ARG, "ta_gather_dot_blocks: key rows of a block must be contiguous");
+  ta::GatherDotBlocksParams p{q, q_sb, q_sh, k, k_sb, k_sh, k_st, blocks, B, H, T, nblk, blk, nb_cta, scale, out};
+  return by_type_dh<GatherDotBlocks>(dtype, dh, p, S(stream));
+}
+
+int ta_dedupe(const int64_t* cand, const uint8_t* valid, uint8_t* keep, int64_t rows, int Kc, void* stream) {
+  g_err.clear();
+  if (rows < 0 || Kc < 0 || Kc > 6000) return fail(TA_ERR_ARG, "ta_dedupe: bad sizes rows=%lld Kc=%d", (long long)rows, Kc);
+  if (rows == 0 || Kc == 0) return TA_OK;
+  if (!cand || !valid || !keep) return fail(TA_ERR_ARG, "ta_dedupe: null pointer");
+  ta::dedupe_kernel<<<(unsigned)rows, 128, (size_t)Kc * sizeof(int64_t), S(stream)>>>(cand, valid, keep, rows, Kc);
+  return check_launch("ta_dedupe");
+}
+
+int ta_append(const void* k, const void* v, int dtype, int B, int H, int dh, int64_t k_sb, int64_t k_sh,
+              int64_t v_sb, int64_t v_sh, void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st,
+              float* nodes, int64_t n_sb, int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos,
+              void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_append: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_append: unsupported head dim %d", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if ((1 << L0) > ta::APPEND_SMEM_FLOATS) return fail(TA_ERR_ARG, "ta_append: leaf block too large");
+  if (!k || !v || !kc || !vc || !nodes || !pos) return fail(TA_ERR_ARG, "ta_append: null pointer");
+  const int es = esize_of(dtype);
+  if (!rows_aligned(k, es, {k_sb, k_sh}) || !rows_aligned(v, es, {v_sb, v_sh}) ||
+      !rows_aligned(kc, es, {c_sb, c_sh, c_st}) || !rows_aligned(vc, es, {c_sb, c_sh, c_st}))
+    return fail(TA_ERR_ARG, "ta_append: rows must be 16-byte aligned");
+  ta::AppendParams p{};
+  p.k = k; p.v = v; p.k_sb = k_sb; p.k_sh = k_sh; p.v_sb = v_sb; p.v_sh = v_sh;
+  p.kc = kc; p.vc = vc; p.c_sb = c_sb; p.c_sh = c_sh; p.c_st = c_st;
+  p.nodes = nodes;
+  p.lv = make_lv(nodes, n_sb, n_sh, cap, L0, Lm);
+  p.pos = pos; p.B = B; p.H = H;
+  return by_type_dh<Append>(dtype, dh, p, S(stream));
+}
+
+int ta_decode_default_splits(int B, int H) { return default_splits(B, H); }
+
+int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,
+                   void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st, float* nodes, int64_t n_sb,
+                   int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos, int wmax, int n_tree, int Lw,
+                   float scale, void* out, int64_t o_sb, float* lse, int32_t* nkeys, int32_t* sel, int splits,
+                   void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_decode_step: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_decode_step: unsupported head dim %d", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if (wmax < 1 || wmax > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_decode_step: wmax=%d outside [1, 64]", wmax);
+  if (n_tree < 0) return fail(TA_ERR_ARG, "ta_decode_step: n_tree < 0");
+  if (Lw < 1) return fail(TA_ERR_ARG, "ta_decode_step: window %d < 1", Lw);
+  if (splits == 0) splits = default_splits(B, H);
+  if (splits < 1 || splits > 8) return fail(TA_ERR_ARG, "ta_decode_step: splits=%d outside [1, 8]", splits);
+  if (!qkv || !kc || !vc || !nodes || !pos || !out) return fail(TA_ERR_ARG, "ta_decode_step: null pointer");
+  const int es = esize_of(dtype);
+  if (!rows_aligned(qkv, es, {qkv_sb, k_ofs, v_ofs, (int64_t)dh}) || !rows_aligned(kc, es, {c_sb, c_sh, c_st}) ||
+      !rows_aligned(vc, es, {c_sb, c_sh, c_st}) || !rows_aligned(out, es, {o_sb, (int64_t)dh}))
+    return fail(TA_ERR_ARG, "ta_decode_step: rows must be 16-byte aligned");
+  if (!aligned16(nodes) || (n_sb * 4) % 16 || (n_sh * 4) % 16)
+    return fail(TA_ERR_ARG, "ta_decode_step: node rows must be 16-byte aligned");
+  if (B * H > 65535) return fail(TA_ERR_ARG, "ta_decode_step: B*H=%d above 65535", B * H);
+  ta::DecodeParams p{};
+  p.qkv = qkv; p.qkv_sb = qkv_sb; p.k_ofs = k_ofs; p.v_ofs = v_ofs;
+  p.kc = kc; p.vc = vc; p.c_sb = c_sb; p.c_sh = c_sh; p.c_st = c_st;
+  p.nodes = nodes;
+  p.lv = make_lv(nodes, n_sb, n_sh, cap, L0, Lm);
+  p.pos = pos; p.B = B; p.H = H; p.wmax = wmax; p.n_tree = n_tree; p.Lw = Lw;
+  p.scale = scale;
+  p.out = out; p.o_sb = o_sb;
+  p.lse = lse; p.nkeys = nkeys; p.sel = sel;
+  p.splits = splits;
+  return by_type_dh<Decode>(dtype, dh, p, S(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,307 @@
+"""KV-cache decoding with the segment tree (reference engine.py), batched and on B200 kernels.
+
+Reference engine.py is batch 1, fp32, one Python loop over layers and tree levels with a host sync per layer.
+Here a SegState holds a whole batch (B, H, cap, dh) of keys/values (fp32 or bf16/fp16) plus the packed tree
+levels >= the leaf level; one decode step of one layer is ONE fused kernel (ta_decode_step: descent, exact
+attention over used leaves + sink + window + the new token, append, incremental tree update), and the whole
+model step is captured in a CUDA graph. `keys` results are device tensors (no host sync per layer).
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import _ops
+from ._ops import Levels
+from .fastseg import n_tree_fixed
+from .forest import gather_nodes
+
+
+def _ln(x, w):
+    return F.layer_norm(x, (x.shape[-1],), w, None, 1e-5)
+
+
+def _positions(t, B, device):
+    if torch.is_tensor(t):
+        return t.to(device=device, dtype=torch.int32).expand(B).contiguous()
+    return torch.full((B,), int(t), device=device, dtype=torch.int32)
+
+
+class SegState:
+    """Per-layer cache for a batch of sequences: keys, values and the tree levels L0..Lm (reference
+    engine.py:18-71; a node is formed the moment its last position is added).
+
+    Tcap sets the tree height (Lm = round(log2 Tcap) - 1, as the reference); `cap` (default Tcap) is the number
+    of positions actually allocated, so a 4352-token context with Tcap 8192 does not pay for 8192 rows."""
+
+    def __init__(self, cfg, Tcap, H, dh, dev, batch=1, dtype=torch.float32, cap=None):
+        if cfg.gate:
+            raise NotImplementedError('the mean-log gate (cfg.gate=True) is not implemented in treeattn_b200')
+        self.cfg, self.Tcap, self.H, self.dh = cfg, Tcap, H, dh
+        self.Lm = _ops.lm_of(Tcap)
+        self.L0 = _ops.log2_exact(getattr(cfg, 'leaf', 2), 'cfg.leaf')
+        self.cap = int(cap or Tcap)
+        self.batch = batch
+        dev = torch.device(dev)
+        self.K = torch.zeros(batch, H, self.cap, dh, device=dev, dtype=dtype)
+        self.V = torch.zeros(batch, H, self.cap, dh, device=dev, dtype=dtype)
+        self.levels = Levels.empty(batch, H, dh, self.cap, self.L0, self.Lm, dev)
+
+    @property
+    def raw(self):
+        """{level: (B, H, cap >> l, dh)} views of the stored levels (reference SegState.raw, levels >= L0)."""
+        return self.levels.as_dict()
+
+    def getU(self, l, cand):
+        return gather_nodes(self.levels.level(l), cand)
+
+    def add(self, t, k, v):
+        """k, v: (B, H, dh) (or (B, H, 1, dh)) for position t (int or (B,) tensor)."""
+        if k.dim() == 4:
+            k, v = k[:, :, 0], v[:, :, 0]
+        pos = _positions(t, self.batch, self.K.device)
+        _ops.append(k.to(self.K.dtype), v.to(self.V.dtype), self.K, self.V, self.levels, pos)
+
+    def fill(self, K, V):
+        """Load positions [0, T) at once (K, V: (B, H, T, dh)) and build the levels (reference fill)."""
+        T = K.shape[2]
+        if T > self.cap:
+            raise ValueError('fill: %d positions above capacity %d' % (T, self.cap))
+        self.K[:, :, :T].copy_(K)
+        self.V[:, :, :T].copy_(V)
+        _ops.build_levels(self.K[:, :, :T], self.cap, self.L0, self.Lm, zero_sink=True, out=self.levels)
+
+
+@torch.no_grad()
+def seg_attend(state, pw, q, k, v, t, update=True):
+    """One decoding step of segment-tree attention for a batch. q, k, v: (B, H, 1, dh). Returns (out (B, H, 1,
+    dh), keys read per head as a 0-d device tensor)."""
+    cfg = state.cfg
+    if cfg.beam_mode == 'pred':
+        raise NotImplementedError("beam_mode='pred' decoding is not implemented in treeattn_b200")
+    if cfg.neighbors:
+        raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
+    B, H, _, dh = q.shape
+    pos = _positions(t, B, q.device)
+    if update:
+        state.add(pos, k, v)
+    qx = q.to(state.K.dtype)
+    ids, vld, _ = _ops.select(qx, state.levels, pos.to(torch.int64), cfg.wmax)
+    n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
+    out, _, nkeys = _ops.seg_attn(qx, state.K, state.V, pos.to(torch.int64), ids, vld, n_tree,
+                                  1 << state.L0, max(cfg.local, 3), 1.0 / math.sqrt(dh))
+    return out, nkeys.float().mean()
+
+
+def weights_from_ours(sd, cfg):
+    """engine.py:123-134: a GPT state dict -> the decoder's weight dict."""
+    W = dict(wte=sd['wte.weight'], wpe=sd['wpe.weight'], ln_f=sd['ln_f.weight'], layers=[])
+    for i in range(cfg.n_layer):
+        p = 'blocks.%d.' % i
+        L = dict(ln1=sd[p + 'ln1.weight'], c_attn=sd[p + 'attn.c_attn.weight'], c_proj=sd[p + 'attn.c_proj.weight'],
+                 ln2=sd[p + 'ln2.weight'], c_fc=sd[p + 'mlp.c_fc.weight'], c_mlp=sd[p + 'mlp.c_proj.weight'])
+        if cfg.beam_mode == 'pred':
+            L['pw'] = dict(w1=sd[p + 'attn.pred.0.weight'], b1=sd[p + 'attn.pred.0.bias'],
+                           w2=sd[p + 'attn.pred.2.weight'], b2=sd[p + 'attn.pred.2.bias'],
+                           classes=torch.tensor(list(cfg.beam_classes), device=sd['wte.weight'].device))
+        W['layers'].append(L)
+    return W
+
+
+def weights_from_nanogpt(sd, n_layer):
+    """engine.py:137-146: a nanoGPT state dict -> the decoder's weight dict."""
+    sd = {k.replace('_orig_mod.', ''): v for k, v in sd.items()}
+    W = dict(wte=sd['transformer.wte.weight'], wpe=sd['transformer.wpe.weight'],
+             ln_f=sd['transformer.ln_f.weight'], layers=[])
+    for i in range(n_layer):
+        p = 'transformer.h.%d.' % i
+        W['layers'].append(dict(ln1=sd[p + 'ln_1.weight'], c_attn=sd[p + 'attn.c_attn.weight'],
+                                c_proj=sd[p + 'attn.c_proj.weight'], ln2=sd[p + 'ln_2.weight'],
+                                c_fc=sd[p + 'mlp.c_fc.weight'], c_mlp=sd[p + 'mlp.c_proj.weight']))
+    return W
+
+
+class Decoder:
+    """Token-by-token decoding for a batch of sequences (reference engine.py:149-177, mode 'seg').
+
+    Decoder(W, n_layer, n_head, n_embd, Tcap, 'seg', cfg, dev) keeps the reference's arguments; `batch`, `dtype`
+    (weights / cache precision, default: the weights' dtype), `cap` (allocated positions) and `graphs` are
+    additions. The residual stream is kept in fp32; matmuls run in `dtype` on cuBLAS."""
+
+    def __init__(self, W, n_layer, n_head, n_embd, Tcap, mode='seg', cfg=None, dev='cuda', batch=1, dtype=None,
+                 cap=None, graphs=True, splits=0):
+        if mode != 'seg':
+            raise NotImplementedError("Decoder mode '%s' is not implemented in treeattn_b200 (only 'seg')" % mode)
+        if cfg is None:
+            raise ValueError("mode 'seg' needs cfg")
+        if cfg.beam_mode == 'pred':
+            raise NotImplementedError("beam_mode='pred' decoding is not implemented in treeattn_b200")
+        if cfg.neighbors:
+            raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
+        self.dev = torch.device(dev)
+        self.dtype = dtype or W['wte'].dtype
+        cast = lambda t: t.to(device=self.dev, dtype=self.dtype).contiguous()
+        self.W = dict(wte=cast(W['wte']), wpe=cast(W['wpe']), ln_f=W['ln_f'].to(self.dev, torch.float32),
+                      layers=[dict(ln1=L['ln1'].to(self.dev, torch.float32), c_attn=cast(L['c_attn']),
+                                   c_proj=cast(L['c_proj']), ln2=L['ln2'].to(self.dev, torch.float32),
+                                   c_fc=cast(L['c_fc']), c_mlp=cast(L['c_mlp'])) for L in W['layers'][:n_layer]])
+        self.nl, self.H, self.C, self.Tcap = n_layer, n_head, n_embd, Tcap
+        self.dh, self.mode, self.cfg = n_embd // n_head, mode, cfg
+        self.batch = batch
+        self.cap = int(cap or Tcap)
+        self.wmax = cfg.wmax
+        self.n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
+        self.Lw = max(cfg.local, 3)
+        self.scale = 1.0 / math.sqrt(self.dh)
+        self.use_graphs = graphs
+        self.splits = splits or _ops.default_splits(batch, n_head)
+        self.reset()
+
+    # -------------------------------------------------------------- state
+    def reset(self):
+        B, C, dev = self.batch, self.C, self.dev
+        self.states = [SegState(self.cfg, self.Tcap, self.H, self.dh, dev, B, self.dtype, self.cap)
+                       for _ in range(self.nl)]
+        self._tok = torch.zeros(B, device=dev, dtype=torch.int64)
+        self._pos = torch.zeros(B, device=dev, dtype=torch.int32)
+        self._qkv = torch.empty(B, 3 * C, device=dev, dtype=self.dtype)
+        self._att = torch.empty(B, C, device=dev, dtype=self.dtype)
+        self._nkeys = torch.zeros(self.nl, B, self.H, device=dev, dtype=torch.int32)
+        self._logits = None
+        self._graph = None
+        self._graph_greedy = None
+
+    # -------------------------------------------------------------- one model step on the static buffers
+    def _forward_step(self):
+        W, dt = self.W, self.dtype
+        x = W['wte'].index_select(0, self._tok).float() + W['wpe'].index_select(0, self._pos.long()).float()
+        for i, L in enumerate(W['layers']):
+            st = self.states[i]
+            torch.mm(_ln(x, L['ln1']).to(dt), L['c_attn'].t(), out=self._qkv)
+            _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree, self.Lw,
+                             self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits)
+            x = x + F.linear(self._att, L['c_proj']).float()
+            x = x + F.linear(F.gelu(F.linear(_ln(x, L['ln2']).to(dt), L['c_fc'])), L['c_mlp']).float()
+        return F.linear(_ln(x, W['ln_f']).to(dt), W['wte'])
+
+    def _greedy_step(self):
+        logits = self._forward_step()
+        self._tok.copy_(logits.argmax(-1))
+        self._pos.add_(1)
+        return logits
+
+    def _capture(self, fn):
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                out = fn()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        return g, out
+
+    def _snapshot(self):
+        return [(st.K.clone(), st.V.clone(), st.levels.nodes.clone()) for st in self.states], \
+            self._tok.clone(), self._pos.clone()
+
+    def _restore(self, snap):
+        sts, tok, pos = snap
+        for st, (K, V, N) in zip(self.states, sts):
+            st.K.copy_(K)
+            st.V.copy_(V)
+            st.levels.nodes.copy_(N)
+        self._tok.copy_(tok)
+        self._pos.copy_(pos)
+
+    def _ensure_graphs(self):
+        """Capture the step graphs once (a capture runs the kernels, so the state is saved and restored)."""
+        if self._graph is not None or not self.use_graphs:
+            return
+        snap = self._snapshot()
+        self._forward_step()  # warm-up outside capture (library attribute setup, cuBLAS handles)
+        self._restore(snap)
+        self._graph, self._logits = self._capture(self._forward_step)
+        self._restore(snap)
+        self._graph_greedy, _ = self._capture(self._greedy_step)
+        self._restore(snap)
+        del snap
+
+    # -------------------------------------------------------------- public API
+    @torch.no_grad()
+    def step(self, tok, t):
+        """Feed tokens `tok` at positions t. Returns (logits, average keys read per head and layer).
+
+        tok: int (batch 1, as the reference) or (B,) tensor; t: int or (B,) tensor. Logits are (V,) for an int
+        token and (B, V) otherwise; keys is a 0-d device tensor."""
+        scalar = not torch.is_tensor(tok)
+        self._tok.copy_(torch.as_tensor(tok, dtype=torch.int64).reshape(-1).expand(self.batch))
+        self._pos.copy_(_positions(t, self.batch, self.dev))
+        if self.use_graphs:
+            self._ensure_graphs()
+            self._graph.replay()
+            logits = self._logits
+        else:
+            logits = self._forward_step()
+        keys = self._nkeys.float().mean()
+        return (logits[0] if scalar and self.batch == 1 else logits), keys
+
+    @torch.no_grad()
+    def greedy_steps(self, n):
+        """n greedy decode steps entirely on the device, continuing from the current token/position buffers
+        (set by prefill() or step()). The generated tokens end in the token buffer (self.tokens)."""
+        if not self.use_graphs:
+            for _ in range(n):
+                self._greedy_step()
+            return
+        self._ensure_graphs()
+        for _ in range(n):
+            self._graph_greedy.replay()
+
+    @property
+    def tokens(self):
+        return self._tok
+
+    @property
+    def positions(self):
+        return self._pos
+
+    @torch.no_grad()
+    def prefill(self, idx, chunk=16):
+        """Run a prompt idx (B, T0) through the model (the training-mode forward semantics, reference
+        model.py:75 / fastseg.py:338), filling every layer's cache and tree. Sets the token buffer to the greedy
+        next token and the positions to T0. Returns the logits of the last prompt position (B, V)."""
+        B, T0 = idx.shape
+        if B != self.batch:
+            raise ValueError('prefill: batch %d != decoder batch %d' % (B, self.batch))
+        if T0 > self.cap:
+            raise ValueError('prefill: %d positions above capacity %d' % (T0, self.cap))
+        W, dt, H, dh, C = self.W, self.dtype, self.H, self.dh, self.C
+        tq = torch.arange(T0, device=self.dev)
+        last = torch.empty(B, W['wte'].shape[0], device=self.dev, dtype=dt)
+        for b0 in range(0, B, chunk):
+            b1 = min(B, b0 + chunk)
+            ib = idx[b0:b1].to(self.dev)
+            nb = b1 - b0
+            x = W['wte'][ib].float() + W['wpe'][:T0].float()
+            for i, L in enumerate(W['layers']):
+                st = self.states[i]
+                qkv = F.linear(_ln(x, L['ln1']).to(dt), L['c_attn'])
+                q = qkv[..., :C].view(nb, T0, H, dh).transpose(1, 2)
+                k = qkv[..., C:2 * C].view(nb, T0, H, dh).transpose(1, 2)
+                v = qkv[..., 2 * C:].view(nb, T0, H, dh).transpose(1, 2)
+                Kc, Vc = st.K[b0:b1, :, :T0], st.V[b0:b1, :, :T0]
+                Kc.copy_(k)
+                Vc.copy_(v)
+                lv = Levels(st.levels.nodes[b0:b1], st.cap, st.L0, st.Lm)
+                _ops.build_levels(Kc, st.cap, st.L0, st.Lm, zero_sink=True, out=lv)
+                ids, vld, _ = _ops.select(q, lv, tq, self.wmax)
+                o = torch.empty(nb, T0, H, dh, device=self.dev, dtype=dt)
+                _ops.seg_attn(q, Kc, Vc, tq, ids, vld, self.n_tree, 1 << st.L0, self.Lw, self.scale,
+                              out=o.transpose(1, 2), want_nkeys=False)
+                del ids, vld
+                x = x + F.linear(o.view(nb, T0, C), L['c_proj']).float()
+                x = x + F.linear(F.gelu(F.linear(_ln(x, L['ln2']).to(dt), L['c_fc'])), L['c_mlp']).float()
+            last[b0:b1] = F.linear(_ln(x[:, -1], W['ln_f']).to(dt), W['wte'])
+        self._tok.copy_(last.argmax(-1))
+        self._pos.fill_(T0)
+        return last

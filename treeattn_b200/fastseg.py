@@ -1,0 +1,166 @@
+"""Segment-tree sparse attention on B200 (reference fastseg.py): the SegAttention module and the kernels it uses.
+
+Names and signatures follow the reference module. Every function runs a hand-written sm_100a kernel through
+the C ABI; there is no Triton and no PyTorch fallback (CPU tensors are rejected, a missing library raises).
+"""
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib, _ops
+from .seg import finish, gate_apply, neighbor_pass, select_seg, select_tree, tree_pass
+
+FAST = [True]  # kept for callers that toggle it; this package has only the CUDA path
+
+
+def fast_available():
+    """True when the CUDA library is built and a GPU is present (reference fastseg.py:180-223 ran a kernel
+    self-check with a silent fallback; here a failure raises instead)."""
+    if not torch.cuda.is_available():
+        return False
+    _lib.load()
+    return True
+
+
+# ------------------------------------------------------------------ scores of queries against gathered nodes
+def gather_dot(q, S, cand, scale):
+    """q (b,H,N,dh), S (b,H,M,dh), cand (b,H,N,C) node ids -> (b,H,N,C) float32 = scale * q . S[cand]."""
+    return _ops.gather_dot(q, S, cand, scale)
+
+
+# ------------------------------------------------------------------ attention over the selected keys
+class _SparseAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cand, scale):
+        o, lse = _ops.sparse_attn_fwd(q, k, v, cand, scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        raise NotImplementedError('sparse_attn backward is not implemented in treeattn_b200 (inference path)')
+
+
+def sparse_attn(q, k, v, cand, scale):
+    """cand: (b,H,T,K) int, -1 = unused slot. Exact softmax attention over the used keys."""
+    return _SparseAttnFn.apply(q, k, v, cand, scale)
+
+
+# ------------------------------------------------------------------ duplicate removal
+def dedupe_fast(cand, valid):
+    """Keep the first valid copy of every key position (same result as attention_dyn.dedupe)."""
+    return _ops.dedupe(cand, valid)
+
+
+# ------------------------------------------------------------------ key selection (same logic as seg.select_seg)
+@torch.no_grad()
+def level_sums_min(kidx, Lm, gate, gate_q, gate_min):
+    if gate:
+        gate_apply(None, None, None, gate_q)
+    from .seg import level_sums
+    return level_sums(kidx, Lm, False, gate_q)
+
+
+@torch.no_grad()
+def tree_pass_fast(q, S, tq, Lm, wmax):
+    return tree_pass(q, S, tq, Lm, wmax)
+
+
+@torch.no_grad()
+def neighbor_pass_fast(q, S1, st_leaf, st_score, st_ok, tq, cfg):
+    return neighbor_pass(q, S1, st_leaf, st_score, st_ok, tq, cfg)
+
+
+@torch.no_grad()
+def select_seg_fast(q, k, lhat, cfg):
+    return select_seg(q, k, lhat, cfg)
+
+
+def n_tree_fixed(beam, wmax):
+    """seg.finish with no neighbour matches and a fixed budget: min(max(beam, 2), wmax) (0 for beam <= 0)."""
+    return 0 if beam <= 0 else min(max(beam, 2), wmax)
+
+
+# ------------------------------------------------------------------ the module
+class SegAttention(nn.Module):
+    """Reference fastseg.py:318-405: same parameters (c_attn, c_proj, optional pred head), same math.
+
+    Per layer: node sums of the keys (fp32, bit-exact), the past-only top-k descent, then exact attention over
+    the used leaf blocks + the sink + the local window, each position once. The attention output is written
+    straight into the (b, T, H, dh) layout that c_proj consumes."""
+
+    def __init__(self, cfg):
+        super().__init__()
+        self.cfg = cfg
+        C = cfg.n_embd
+        self.H = cfg.n_head
+        self.dh = C // cfg.n_head
+        assert cfg.seq_len % cfg.chunk == 0 and (cfg.seq_len & (cfg.seq_len - 1)) == 0
+        self.c_attn = nn.Linear(C, 3 * C, bias=False)
+        self.c_proj = nn.Linear(C, C, bias=False)
+        if cfg.beam_mode == 'pred':
+            assert max(cfg.beam_classes) <= cfg.wmax
+            fin = self.dh + 1 + self.H + (self.dh if cfg.global_pool else 0)
+            self.pred = nn.Sequential(nn.Linear(fin, 64), nn.ReLU(), nn.Linear(64, len(cfg.beam_classes)))
+            self.register_buffer('classes', torch.tensor(list(cfg.beam_classes)), persistent=False)
+            self.register_buffer('head_eye', torch.eye(self.H), persistent=False)
+        self.aux = {}
+
+    def forward(self, x):
+        b, T, C = x.shape
+        q, k, v = self.c_attn(x).split(C, dim=2)
+        q, k, v = [t.view(b, T, self.H, self.dh).transpose(1, 2) for t in (q, k, v)]
+        out = torch.empty(b, T, self.H, self.dh, device=x.device, dtype=q.dtype)
+        self.sparse_attend(q, k, v, out=out.transpose(1, 2))
+        return self.c_proj(out.view(b, T, C))
+
+    def _lhat(self, q, k):
+        cfg = self.cfg
+        b, H, T, dh = q.shape
+        if cfg.beam_mode != 'pred':
+            return None
+        t = torch.arange(T, device=q.device)
+        qd = q.detach()
+        feats = [qd, torch.log(qd.float().norm(dim=-1, keepdim=True) + 1e-6).to(qd.dtype),
+                 self.head_eye.to(qd.dtype)[None, :, None, :].expand(b, H, T, H)]
+        if cfg.global_pool:
+            kd = k.detach().float()
+            prefix_mean = (kd.cumsum(2) - kd) / t.clamp(min=1).view(1, 1, T, 1).float()
+            feats.append(prefix_mean.to(qd.dtype))
+        plog = self.pred(torch.cat(feats, -1))
+        return self.classes[plog.argmax(-1).detach()]
+
+    def sparse_attend(self, q, k, v, out=None):
+        cfg = self.cfg
+        if cfg.gate:
+            gate_apply(None, None, None, cfg.gate_q)
+        if cfg.neighbors:
+            raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
+        if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
+            raise NotImplementedError('SegAttention backward is not implemented in treeattn_b200 (inference path); '
+                                      'run under torch.no_grad()')
+        b, H, T, dh = q.shape
+        scale = 1.0 / math.sqrt(dh)
+        self.aux = {}
+        with torch.no_grad():
+            lhat = self._lhat(q, k)
+            ids, vld, sct, lv = select_tree(q.detach(), k.detach(), cfg)
+            leaf = 1 << lv.L0
+            wl = ids.shape[-1]
+            if lhat is None:
+                n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
+                used = vld & (torch.arange(wl, device=q.device) < n_tree)
+            else:
+                n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, positions=False)['n_tree']
+                used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
+            Lw = max(cfg.local, 3)
+            tq = torch.arange(T, device=q.device)
+            out, _, nkeys = _ops.seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=out)
+            n_used = used.sum(-1).float()
+            self.aux['keys_total'] = nkeys.float().mean()
+            self.aux['keys_tree'] = (n_used * leaf).mean()
+            self.aux['keys_nb'] = torch.zeros((), device=q.device)
+            self.aux['nb_leaves'] = torch.zeros((), device=q.device)
+            self.aux['leaves_used'] = n_used.mean()
+        return out

@@ -1,0 +1,113 @@
+"""Segment-tree key selection (reference seg.py), backed by the sm_100a kernels.
+
+Same names, arguments and results as the reference module. Differences, all explicit:
+  * tree_pass takes the tree itself (the dict returned by level_sums, a Levels object or a SegState /
+    its bound getU) instead of an arbitrary getU callable: the descent runs inside one CUDA kernel.
+  * Leaf blocks of cfg.leaf tokens (default 2 = the reference) are supported; positions of a leaf block m are
+    [m*leaf, (m+1)*leaf), stored leaf-slot-major as the reference's cat([2*ids, 2*ids+1]) is at leaf 2.
+  * The mean-log gate (cfg.gate) and neighbour borrowing with matches (cfg.neighbors=True) raise
+    NotImplementedError instead of silently changing the result.
+"""
+import torch
+
+from . import _ops
+from ._ops import Levels, LevelDict
+
+
+def _leaf_level(cfg):
+    return _ops.log2_exact(getattr(cfg, 'leaf', 2), 'cfg.leaf') if cfg is not None else 1
+
+
+def gate_apply(raw, lgsum, size, gate_q):
+    """Mean-log dilution gate (seg.py:16-23). Not implemented on this path."""
+    raise NotImplementedError('the mean-log gate (cfg.gate=True) is not implemented in treeattn_b200')
+
+
+@torch.no_grad()
+def level_sums(kidx, Lm, gate, gate_q):
+    """seg.py:26-41: {l: (b, H, T >> l, dh)} fp32 node sums for l = 1..Lm from kidx (b, H, T, dh) as given
+    (select_seg zeroes the sink before calling it). The returned dict carries the packed storage."""
+    if gate:
+        gate_apply(None, None, None, gate_q)
+    T = kidx.shape[2]
+    lv = _ops.build_levels(kidx, T, 1, Lm, zero_sink=False)
+    return lv.as_dict()
+
+
+def _as_levels(getU):
+    if isinstance(getU, Levels):
+        return getU
+    if isinstance(getU, LevelDict):
+        return getU.packed
+    owner = getattr(getU, '__self__', None)
+    if owner is not None and hasattr(owner, 'levels') and isinstance(owner.levels, Levels):
+        return owner.levels
+    if hasattr(getU, 'levels') and isinstance(getU.levels, Levels):
+        return getU.levels
+    raise TypeError('tree_pass needs the tree itself (level_sums() result, Levels, or a SegState / its getU); '
+                    'an arbitrary getU callable cannot run inside the CUDA descent')
+
+
+@torch.no_grad()
+def tree_pass(q, getU, tq, Lm, wmax):
+    """seg.py:44-70: past-only beam descent. q (b, H, Nq, dh); tq (Nq,) positions (or (b,) / (b, Nq)).
+    Returns leaf ids (b, H, Nq, wl), validity and scores (q . S_L0 / 2^L0), best first."""
+    lv = _as_levels(getU)
+    if Lm != lv.Lm:
+        lv = Levels(lv.nodes, lv.cap, lv.L0, Lm) if Lm <= lv.Lm else None
+        if lv is None:
+            raise ValueError('tree_pass: Lm=%d above the stored levels' % Lm)
+    return _ops.select(q, lv, tq.to(q.device), wmax)
+
+
+@torch.no_grad()
+def neighbor_pass(q, getU1, st_leaf, st_score, st_ok, tq, cfg):
+    """seg.py:73-103 with cfg.neighbors=False: the stored ids of the nb_window earlier queries, no matches,
+    nL = 0. Neighbour matching itself raises NotImplementedError."""
+    if cfg.neighbors:
+        raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
+    b, H, Nq, dh = q.shape
+    Wn, NS = cfg.nb_window, cfg.nb_store
+    back = torch.arange(1, Wn + 1, device=q.device).view(1, Wn)
+    jc = (tq.view(Nq, 1) - back).clamp(min=0)
+    ids = st_leaf[:, :, jc].reshape(b, H, Nq, Wn * NS)
+    match = torch.zeros(ids.shape, dtype=torch.bool, device=q.device)
+    nL = torch.zeros(b, H, Nq, dtype=torch.long, device=q.device)
+    return ids, match, nL
+
+
+def leaves_to_pos(ids, ok, leaf=2):
+    """seg.py:106-108 (leaf positions, -1 where not ok)."""
+    lhat = torch.zeros(ids.shape[:-1], dtype=torch.long, device=ids.device)
+    return _ops.finish(ids, ok, lhat, 1, leaf)['tree_pos']
+
+
+def finish(ids, vld, nid, match, nL, lhat, cfg):
+    """seg.py:111-119."""
+    return _ops.finish(ids, vld, lhat, cfg.wmax, getattr(cfg, 'leaf', 2), nid=nid, match=match, nL=nL)
+
+
+def select_tree(q, k, cfg):
+    """Levels + descent for a whole sequence: returns (ids, vld, sct, Levels)."""
+    b, H, T, dh = q.shape
+    Lm = _ops.lm_of(T)
+    L0 = _leaf_level(cfg)
+    if Lm < L0:
+        raise ValueError('sequence length %d too short for leaf blocks of %d' % (T, 1 << L0))
+    lv = _ops.build_levels(k, T, L0, Lm, zero_sink=True)
+    tq = torch.arange(T, device=q.device)
+    ids, vld, sct = _ops.select(q, lv, tq, cfg.wmax)
+    return ids, vld, sct, lv
+
+
+@torch.no_grad()
+def select_seg(q, k, lhat, cfg):
+    """seg.py:122-140: key selection for a whole sequence (levels, descent, neighbour pass, finish)."""
+    if cfg.gate:
+        gate_apply(None, None, None, cfg.gate_q)
+    b, H, T, dh = q.shape
+    ids, vld, sct, lv = select_tree(q, k, cfg)
+    NS = cfg.nb_store
+    tq = torch.arange(T, device=q.device)
+    nid, match, nL = neighbor_pass(q, None, ids[..., :NS], sct[..., :NS], vld[..., :NS], tq, cfg)
+    return _ops.finish(ids, vld, lhat, cfg.wmax, 1 << lv.L0, nid=nid, match=match, nL=nL)
