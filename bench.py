@@ -1,0 +1,353 @@
+"""Decode benchmark: batched greedy KV-cache decoding with segment-tree attention.
+
+Model: 12 layers, d_model 768, 12 heads (dh 64), vocab 50304, random init N(0, 0.02), bf16 weights and cache.
+Input: batch 64 prompts of 4096 uniform-random tokens per GPU (seeded per rank), prefilled untimed, then greedy
+decode steps; tree: 64-token leaves, top-16 leaves, 128-token local window, Tcap 8192.
+
+One step = one greedy decode step of the whole batch through all 12 layers + lm_head (CUDA graph).
+  value    tokens/s over all ranks, device-resident loop (tokens fed back on the device)
+  e2e      tokens/s through Decoder.serve_step: tokens copied host->device from pinned memory and the next tokens
+           device->host every step
+  roofline the fused decode-attention kernel (ta_decode_step) timed alone with CUDA events: selected-KV bytes per
+           launch / launch time vs the measured HBM copy bandwidth
+Multi-GPU: one process per GPU (torchrun), each rank decodes its own 64 sequences; no collective in the timed
+region (weak scaling). `--impl reference` times the CPU oracle (numpy restatement of the reference's engine) on
+the host cores instead.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+V, C, H, NL = 50304, 768, 12, 12
+LEAF, TOPK, WINDOW, TCAP = 64, 16, 128, 8192
+METRIC = 'decode tok/s (config 4: 12x768 bf16 GPT, batch 64/GPU, 4096-token prompts, leaf 64, top-16, window 128)'
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=256)
+    p.add_argument('--warmup', type=int, default=8)
+    p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    p.add_argument('--batch', type=int, default=64)
+    p.add_argument('--prompt', type=int, default=4096)
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--cpu-seconds', type=float, default=12.0)
+    p.add_argument('--splits', type=int, default=0, help='CTAs per (b, h) in the decode kernel (0 = auto)')
+    p.add_argument('--profile-steps', type=int, default=0,
+                   help='profiling mode: after prefill and warm-up run this many eager decode steps between '
+                        'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
+    return p.parse_args()
+
+
+def make_cfg(prompt, steps):
+    from treeattn_b200.config import Config
+    return Config(vocab_size=V, seq_len=TCAP, n_layer=NL, n_head=H, n_embd=C, attn='seg', wmax=TOPK, beam=TOPK,
+                  local=WINDOW, neighbors=False, beam_mode='fixed', leaf=LEAF)
+
+
+def make_weights(device, seed, dtype):
+    """Random-init weights of the configuration-4 architecture (GPT._init: N(0, 0.02), c_proj 0.02/sqrt(2L))."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    n = lambda *s, std=0.02: (torch.randn(*s, generator=g, device=device) * std).to(dtype)
+    sp = 0.02 / math.sqrt(2 * NL)
+    W = dict(wte=n(V, C), wpe=n(TCAP, C), ln_f=torch.ones(C, device=device), layers=[])
+    for _ in range(NL):
+        W['layers'].append(dict(ln1=torch.ones(C, device=device), c_attn=n(3 * C, C), c_proj=n(C, C, std=sp),
+                                ln2=torch.ones(C, device=device), c_fc=n(4 * C, C), c_mlp=n(C, 4 * C, std=sp)))
+    return W
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons; only samples inside [t_begin, t_end] are kept."""
+    Q = ('timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+        self.t_begin = self.t_end = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix='.csv')
+            os.close(fd)
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.index), '--query-gpu=' + self.Q,
+                                          '--format=csv,noheader,nounits', '-lms', '50'],
+                                         stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
+            time.sleep(1.0)  # let the sampler come up before the timed region
+        except Exception:
+            self.proc = None
+
+    def mark_begin(self):
+        self.t_begin = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        from datetime import datetime
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                ts = datetime.strptime(f[0], '%Y/%m/%d %H:%M:%S.%f').timestamp()
+            except ValueError:
+                continue
+            if self.t_begin - 0.05 <= ts <= self.t_end + 0.05:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=[], samples=0)
+        num = lambda x: float(x) if x.replace('.', '', 1).isdigit() else None
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        smax = [v for v in (num(r[2]) for r in rows) if v is not None]
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == 'Active'})
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=max(smax) if smax else None,
+                    reasons=reasons, samples=len(rows))
+
+
+def measured_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
+    except Exception:
+        return None
+
+
+def cpu_decode_sample(seconds, W_dev=None, seed=0):
+    """Time the CPU oracle's decode (numpy, fp32, the reference engine's algorithm: engine.py:149-177 Decoder,
+    batch 1) on the configuration-4 model for a bounded number of steps. The prompt cache (4096 positions per
+    layer) is filled with random keys/values instead of a CPU prefill (the time of a decode step does not depend
+    on the values). Returns (tokens/s, steps, threads)."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(seed)
+    if W_dev is not None:
+        f = lambda t: t.float().cpu().numpy()
+        W = dict(wte=f(W_dev['wte']), wpe=f(W_dev['wpe']), ln_f=f(W_dev['ln_f']),
+                 layers=[{k: f(v) for k, v in L.items()} for L in W_dev['layers']])
+    else:
+        n = lambda *s, std=0.02: (rng.standard_normal(s, dtype=np.float32) * std)
+        W = dict(wte=n(V, C), wpe=n(TCAP, C), ln_f=np.ones(C, np.float32),
+                 layers=[dict(ln1=np.ones(C, np.float32), c_attn=n(3 * C, C), c_proj=n(C, C), ln2=np.ones(C, np.float32),
+                              c_fc=n(4 * C, C), c_mlp=n(C, 4 * C)) for _ in range(NL)])
+    T0 = 4096
+    dec = oracle.DecoderNP(W, H, TCAP, TOPK, TOPK, WINDOW, L0=int(math.log2(LEAF)), cap=T0 + 512)
+    dec.reset(1)
+    for st in dec.states[0]:
+        st.fill(rng.standard_normal((H, T0, C // H), dtype=np.float32),
+                rng.standard_normal((H, T0, C // H), dtype=np.float32))
+    tok = rng.integers(0, V, 1)
+    dec.step(tok, T0)  # warm-up
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        logits, _ = dec.step(tok, T0 + 1 + steps)
+        tok = logits.argmax(-1)
+        steps += 1
+        if time.perf_counter() - t0 > seconds or steps >= 512:
+            break
+    dt = time.perf_counter() - t0
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get('num_threads', 1) for i in threadpool_info()] + [1])
+    except Exception:
+        threads = 1
+    return steps / dt, steps, threads
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return
+    warm = max(0, a.warmup)
+    value, steps, threads = cpu_decode_sample(max(5.0, a.cpu_seconds), seed=1)
+    line = dict(metric=METRIC, value=value, unit='tokens/s', n_gpus=world, steps=a.steps, warmup=warm,
+                ms_per_step=1000.0 / value, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
+                data='synthetic', impl='reference',
+                config=dict(workload='config 4 decode, CPU oracle (numpy restatement of the reference engine), '
+                                     'batch 1 sample', global_batch=1, seq_len=4096, parallelism='none'),
+                cpu_baseline=dict(value=value, unit='tokens/s', cores=threads, kind='port',
+                                  sample='%d greedy decode steps of 1 sequence at t~4096 (12 layers + lm_head), '
+                                         'fp32 numpy, cache filled with random K/V' % steps),
+                e2e=dict(value=value, unit='tokens/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if a.impl == 'reference':
+        run_reference(a, rank, world)
+        return
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=600), device_id=dev)
+    from treeattn_b200 import _ops
+    from treeattn_b200.engine import Decoder
+
+    B, T0, K, Wm = a.batch, a.prompt, a.steps, max(a.warmup, 3)
+    cap = ((T0 + Wm + 2 * K + 8 + LEAF - 1) // LEAF) * LEAF
+    cfg = make_cfg(T0, K)
+    W = make_weights(dev, 1234, torch.bfloat16)
+    dec = Decoder(W, NL, H, C, TCAP, 'seg', cfg, dev, batch=B, dtype=torch.bfloat16, cap=cap, splits=a.splits)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    prompts = torch.randint(0, V, (B, T0), device=dev, generator=g)
+    torch.cuda.synchronize()
+    t_pf = time.time()
+    dec.prefill(prompts)
+    torch.cuda.synchronize()
+    t_pf = time.time() - t_pf
+    if a.profile_steps:
+        with torch.no_grad():
+            for _ in range(Wm):
+                dec._greedy_step()
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStart()
+            for _ in range(a.profile_steps):
+                dec._greedy_step()
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps(dict(profile_steps=a.profile_steps, batch=B, splits=dec.splits,
+                              keys_per_head=float(dec._nkeys.float().mean()))), flush=True)
+        return
+    dec._ensure_graphs()
+
+    # ---------------------------------------------------------------- device-resident timed loop
+    dec.greedy_steps(Wm)
+    clocks = Clocks(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_begin()
+    e0.record()
+    dec.greedy_steps(K)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    ms = e0.elapsed_time(e1)
+    ck = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    keys_mean = float(dec._nkeys.float().mean())
+
+    # ---------------------------------------------------------------- end to end through the public API
+    tok_host = torch.empty(B, dtype=torch.int64, pin_memory=True)
+    tok_host.copy_(dec.tokens.cpu())
+    dec.serve_step(tok_host, out=tok_host)  # warm-up
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K):
+        dec.serve_step(tok_host, out=tok_host)
+    f1.record()
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+
+    # ---------------------------------------------------------------- roofline: the fused decode kernel alone
+    # The 12 per-layer launches (one per layer cache, so consecutive launches read different KV and nothing stays
+    # in L2) are captured in a CUDA graph and replayed, so the events see kernel time, not Python launch time.
+    # Relaunching at the same position is idempotent (same appended row, same tree node).
+    pos = dec.positions.clone()
+    nk = torch.empty(B, H, device=dev, dtype=torch.int32)
+    att = torch.empty(B, C, device=dev, dtype=torch.bfloat16)
+    qkv = dec._qkv
+
+    def layer_launches():
+        for st in dec.states:
+            _ops.decode_step(qkv, st.K, st.V, st.levels, pos, H, TOPK, TOPK, WINDOW, 1 / 8.0, att, nkeys=nk,
+                             splits=dec.splits)
+
+    layer_launches()
+    torch.cuda.synchronize()
+    kg, _ = dec._capture(layer_launches)
+    kg.replay()
+    torch.cuda.synchronize()
+    reps = 10
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record()
+    for _ in range(reps):
+        kg.replay()
+    r1.record()
+    torch.cuda.synchronize()
+    kern_ms = r0.elapsed_time(r1) / (reps * NL)
+    sel_bytes = float(nk.sum()) * (C // H) * 2 * 2  # K and V rows of the selected keys, bf16
+    del kg
+
+    # ---------------------------------------------------------------- reduce over ranks
+    t = torch.tensor([ms, ms_e2e, kern_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        toks = dec.tokens.clone()
+        allt = [torch.empty_like(toks) for _ in range(world)]
+        dist.all_gather(allt, toks)  # generated tokens gathered off the hot path
+    ms, ms_e2e, kern_ms = t.tolist()
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = peaks['hbm_gbs'] if peaks else 6650.0
+        achieved = sel_bytes / (kern_ms * 1e-3) / 1e9
+        tokens = B * K * world
+        line = dict(metric=METRIC, value=tokens / (ms * 1e-3), unit='tokens/s', n_gpus=world, steps=K, warmup=Wm,
+                    ms_per_step=ms / K, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
+                    data='synthetic (uniform random tokens, N(0,0.02) random-init weights)',
+                    config=dict(workload='config 4: KV-cache decode, 12x768 GPT bf16, batch %d/GPU, prompt %d, '
+                                         'leaf %d, top-%d, window %d' % (B, T0, LEAF, TOPK, WINDOW),
+                                global_batch=B * world, seq_len=T0, parallelism='dp%d (batch sharded, no collective)'
+                                % world, l2='inputs larger than L2 (KV cache %.1f GB/GPU)' % (
+                                    2 * NL * B * H * cap * (C // H) * 2 / 1e9),
+                                prefill_s=round(t_pf, 2), keys_per_head=round(keys_mean, 1),
+                                splits=dec.splits),
+                    e2e=dict(value=tokens / (ms_e2e * 1e-3), unit='tokens/s', h2d_bytes_per_step=B * 8,
+                             d2h_bytes_per_step=B * 8),
+                    gpu_launches=NL * K,
+                    roofline=dict(bound='hbm', achieved=achieved, peak=peak, unit='GB/s', frac=achieved / peak,
+                                  traffic=None, kernel='ta_decode_step (decode_kernel<bf16,64>)',
+                                  kernel_us=kern_ms * 1e3, bytes_per_launch=sel_bytes,
+                                  peak_source='MEASURED_PEAKS.json hbm_gbs (burst copy)' if peaks else 'fallback'),
+                    clocks=ck)
+        if world == 1 and not a.no_cpu_baseline:
+            v, steps, threads = cpu_decode_sample(a.cpu_seconds, W_dev=W)
+            line['cpu_baseline'] = dict(value=v, unit='tokens/s', cores=threads, kind='port',
+                                        sample='%d greedy decode steps of 1 sequence at t~4096 on the CPU oracle '
+                                               '(numpy fp32 restatement of the reference engine), same weights, '
+                                               'cache filled with random K/V' % steps)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

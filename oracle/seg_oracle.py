@@ -266,25 +266,31 @@ def weights_from_state_dict(sd, n_layer):
     return W
 
 
-def gpt_forward(W, idx, n_head, wmax, beam, local, L0=1, chunk=64):
+def gpt_forward(W, idx, n_head, wmax, beam, local, L0=1, chunk=64, bf16=False):
     """model.py:75-93 GPT.forward with SegAttention blocks (model.py:34-44, fastseg.py:338-343), fp32.
+
+    bf16=True mirrors a bf16 nn.Module forward: every stored activation (embedding sum, residual stream, layer-norm
+    and matmul outputs, attention output, GELU output, logits) is rounded to bfloat16; arithmetic stays fp32.
     Returns (logits (B, T, V), per-layer-averaged stats)."""
+    r = bf16_round if bf16 else (lambda a: a)
     idx = np.asarray(idx, np.int64)
     B, T = idx.shape
     C = W['wte'].shape[1]
     dh = C // n_head
-    x = (W['wte'][idx] + W['wpe'][np.arange(T)]).astype(F32)
+    x = r((W['wte'][idx] + W['wpe'][np.arange(T)]).astype(F32))
     acc = {}
     for L in W['layers']:
-        h = layer_norm(x, L['ln1'])
-        qkv = (h @ L['c_attn'].T).astype(F32)
+        h = r(layer_norm(x, L['ln1']))
+        qkv = r((h @ L['c_attn'].T).astype(F32))
         q, k, v = [qkv[..., i * C:(i + 1) * C].reshape(B, T, n_head, dh).transpose(0, 2, 1, 3) for i in range(3)]
         o, st = seg_attention(q, k, v, wmax, beam, local, L0=L0, chunk=chunk)
+        o = r(o)
         for name, val in st.items():
             acc[name] = acc.get(name, 0.0) + val
-        x = (x + o.transpose(0, 2, 1, 3).reshape(B, T, C) @ L['c_proj'].T).astype(F32)
-        x = (x + gelu(layer_norm(x, L['ln2']) @ L['c_fc'].T) @ L['c_mlp'].T).astype(F32)
-    logits = (layer_norm(x, W['ln_f']) @ W['wte'].T).astype(F32)
+        x = r(x + r((o.transpose(0, 2, 1, 3).reshape(B, T, C) @ L['c_proj'].T).astype(F32)))
+        f = r(gelu(r(r(layer_norm(x, L['ln2'])) @ L['c_fc'].T)))
+        x = r(x + r((f @ L['c_mlp'].T).astype(F32)))
+    logits = r((r(layer_norm(x, W['ln_f'])) @ W['wte'].T).astype(F32))
     n = len(W['layers'])
     return logits, {name: val / n for name, val in acc.items()}
 
@@ -364,9 +370,13 @@ def seg_attend(state, q, k, v, t, wmax, beam, local, update=True, with_sel=False
 
 
 class DecoderNP:
-    """engine.py:149-177 Decoder ('seg' mode) for a batch of sequences, fp32, token by token."""
+    """engine.py:149-177 Decoder ('seg' mode) for a batch of sequences, fp32, token by token.
 
-    def __init__(self, W, n_head, Tcap, wmax, beam, local, L0=1, cap=None, kv_round=None):
+    bf16=True mirrors a decoder with bf16 weights and cache and an fp32 residual stream: layer-norm outputs,
+    matmul outputs, the attention output, the GELU output and the logits are rounded to bfloat16 (and so are the
+    keys/values entering the cache)."""
+
+    def __init__(self, W, n_head, Tcap, wmax, beam, local, L0=1, cap=None, kv_round=None, bf16=False):
         self.W, self.H = W, n_head
         self.C = W['wte'].shape[1]
         self.dh = self.C // n_head
@@ -374,6 +384,7 @@ class DecoderNP:
         self.L0, self.wmax, self.beam, self.local = L0, wmax, beam, local
         self.cap = cap or Tcap
         self.kv_round = kv_round
+        self.r = bf16_round if bf16 else (lambda a: a)
         self.states = None
 
     def reset(self, batch):
@@ -382,20 +393,21 @@ class DecoderNP:
 
     def step(self, toks, t):
         """toks (B,) token ids at position t (an int or (B,) array). Returns (logits (B, V), keys read)."""
-        W, H, C, dh = self.W, self.H, self.C, self.dh
+        W, H, C, dh, r = self.W, self.H, self.C, self.dh, self.r
         toks = np.asarray(toks, np.int64)
         B = toks.shape[0]
         tt = np.broadcast_to(np.asarray(t, np.int64), (B,))
         x = (W['wte'][toks] + W['wpe'][tt]).astype(F32)
         keys = 0.0
         for i, L in enumerate(W['layers']):
-            qkv = (layer_norm(x, L['ln1']) @ L['c_attn'].T).astype(F32)
+            qkv = r((r(layer_norm(x, L['ln1'])) @ L['c_attn'].T).astype(F32))
             o = np.zeros((B, C), F32)
             for b in range(B):
                 q, k, v = [qkv[b, j * C:(j + 1) * C].reshape(H, dh) for j in range(3)]
                 ob, kr = seg_attend(self.states[b][i], q, k, v, int(tt[b]), self.wmax, self.beam, self.local)
                 o[b] = ob.reshape(C)
                 keys += kr / B
-            x = (x + o @ L['c_proj'].T).astype(F32)
-            x = (x + gelu(layer_norm(x, L['ln2']) @ L['c_fc'].T) @ L['c_mlp'].T).astype(F32)
-        return (layer_norm(x, W['ln_f']) @ W['wte'].T).astype(F32), keys / len(W['layers'])
+            x = (x + r((r(o) @ L['c_proj'].T).astype(F32))).astype(F32)
+            f = r(gelu(r((r(layer_norm(x, L['ln2'])) @ L['c_fc'].T).astype(F32))))
+            x = (x + r((f @ L['c_mlp'].T).astype(F32))).astype(F32)
+        return r((r(layer_norm(x, W['ln_f'])) @ W['wte'].T).astype(F32)), keys / len(W['layers'])

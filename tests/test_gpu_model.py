@@ -1,0 +1,234 @@
+"""Module-level parity on the GPU: SegAttention / GPT / SegState / seg_attend / Decoder against the reference's
+golden outputs and the oracle, plus the reference's own invariant tests (test_seg.py) on this implementation."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests._golden import load
+
+pytestmark = pytest.mark.gpu
+DEV = 'cuda'
+
+
+def tiny(**kw):
+    from treeattn_b200.config import Config
+    base = dict(vocab_size=64, seq_len=64, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=2,
+                beam_classes=(2, 3, 4), nb_window=4, nb_store=2, nb_probe=2, nb_cap_min=1, neighbors=False,
+                beam_mode='fixed')
+    base.update(kw)
+    return Config(**base)
+
+
+def _no_device_error():
+    from treeattn_b200 import _ops
+    assert _ops.device_error()[0] == 0
+
+
+def test_tiny_gpt_forward_golden():
+    from treeattn_b200.model import GPT
+    g = load('tiny_gpt')
+    torch.manual_seed(4)
+    m = GPT(tiny()).eval()
+    m.to(DEV)
+    with torch.no_grad():
+        logits, _, stats = m(torch.as_tensor(g['idx']).to(DEV))
+    np.testing.assert_allclose(logits.cpu().numpy(), g['logits'], atol=1e-4)
+    for k in ('keys_total', 'keys_tree', 'leaves_used'):
+        assert abs(stats[k] - float(g['stat_' + k])) < 1e-4, k
+    _no_device_error()
+
+
+def test_config1_forward_golden():
+    """Configuration 1: GPT 4x256, 4 heads, vocab 4096, T 512, leaf 32, top-4, window 64, fp32, batch 2."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    g = load('config1')
+    L0 = int(g['L0'])
+    cfg = Config(vocab_size=4096, seq_len=512, n_layer=4, n_head=4, n_embd=256, attn='seg', wmax=4, beam=4,
+                 local=64, neighbors=False, beam_mode='fixed', leaf=1 << L0)
+    torch.manual_seed(0)
+    m = GPT(cfg).eval().to(DEV)
+    with torch.no_grad():
+        logits, _, stats = m(torch.as_tensor(g['idx']).to(DEV))
+    lg = logits.cpu().numpy()
+    np.testing.assert_allclose(lg[:, ::32], g['logits_sub'], atol=1e-3)
+    assert (lg.argmax(-1) == g['argmax']).mean() > 0.999
+    lse = torch.logsumexp(logits.double(), -1).cpu().numpy()
+    np.testing.assert_allclose(lse, g['lse'], atol=1e-3)
+    assert abs(stats['keys_total'] - float(g['stat_keys_total'])) < 1e-2
+    _no_device_error()
+
+
+def test_engine_golden_tiny():
+    """Decoder.step token by token (fp32) vs the reference engine's logits and keys."""
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    g = load('tiny_gpt')
+    torch.manual_seed(4)
+    cfg = tiny()
+    m = GPT(cfg).eval()
+    for graphs in (False, True):
+        dec = Decoder(weights_from_ours(m.state_dict(), cfg), cfg.n_layer, cfg.n_head, cfg.n_embd, 64, 'seg', cfg,
+                      DEV, graphs=graphs)
+        got, keys = [], []
+        for t in range(64):
+            lg, kr = dec.step(int(g['idx'][0, t]), t)
+            got.append(lg.clone())
+            keys.append(float(kr))
+        np.testing.assert_allclose(torch.stack(got).cpu().numpy(), g['dec_logits'], atol=1e-4)
+        np.testing.assert_allclose(keys, g['dec_keys'], atol=1e-5)
+    _no_device_error()
+
+
+def test_seg_attend_golden():
+    from treeattn_b200.config import Config
+    from treeattn_b200.engine import SegState, seg_attend
+    g = load('seg_attend')
+    K, V, q = [torch.as_tensor(g[n]).to(DEV) for n in ('K', 'V', 'q')]
+    H, T, dh = K.shape[1:]
+    cfg = Config(seq_len=T, n_head=H, n_embd=H * dh, attn='seg', beam=4, beam_mode='fixed', local=3, neighbors=False)
+    st = SegState(cfg, T, H, dh, DEV)
+    st.fill(K, V)
+    out, keys = seg_attend(st, None, q, None, None, T - 1, update=False)
+    np.testing.assert_allclose(out.cpu().numpy(), g['out'], atol=1e-5)
+    assert abs(float(keys) - float(g['keys'])) < 1e-6
+
+
+@pytest.mark.parametrize('dtype,leaf', [(torch.float32, 8), (torch.float32, 2)])
+def test_engine_matches_forward(dtype, leaf):
+    """Reference test_seg.test_engine_matches_forward with leaf blocks and a batch: prefill of the first half
+    of the sequence, then token-by-token steps, equal the whole-sequence forward (fp32, 1e-4)."""
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    cfg = tiny(seq_len=128, n_embd=64, wmax=4, beam=3, local=16, leaf=leaf)
+    torch.manual_seed(9)
+    m = GPT(cfg).eval().to(DEV)
+    idx = torch.randint(0, 64, (3, 128), device=DEV)
+    with torch.no_grad():
+        ref = m(idx)[0]
+    W = weights_from_ours(m.state_dict(), cfg)
+    dec = Decoder(W, cfg.n_layer, cfg.n_head, cfg.n_embd, 128, 'seg', cfg, DEV, batch=3, dtype=dtype)
+    last = dec.prefill(idx[:, :64])
+    np.testing.assert_allclose(last.float().cpu().numpy(), ref[:, 63].cpu().numpy(), atol=1e-4)
+    for t in range(64, 128):
+        lg, _ = dec.step(idx[:, t], t)
+        np.testing.assert_allclose(lg.float().cpu().numpy(), ref[:, t].cpu().numpy(), atol=1e-4)
+    _no_device_error()
+
+
+def test_bf16_decoder_vs_oracle():
+    """bf16 weights and cache: prefill + token-by-token steps vs the oracle decoder that rounds to bf16 at the
+    same points (max-abs 2e-2 on the logits)."""
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    cfg = tiny(seq_len=256, n_embd=128, n_head=2, vocab_size=128, wmax=8, beam=8, local=32, leaf=16)
+    torch.manual_seed(7)
+    m = GPT(cfg).eval()
+    sd = {k: v.to(torch.bfloat16) for k, v in m.state_dict().items()}
+    W = weights_from_ours(sd, cfg)
+    idx = torch.randint(0, 128, (2, 192))
+    dec = Decoder(W, cfg.n_layer, cfg.n_head, cfg.n_embd, 256, 'seg', cfg, DEV, batch=2, dtype=torch.bfloat16)
+    dec.prefill(idx[:, :128].to(DEV))
+    Wn = oracle.weights_from_state_dict({k: v.float() for k, v in sd.items()}, cfg.n_layer)
+    ref = oracle.DecoderNP(Wn, cfg.n_head, 256, cfg.wmax, cfg.beam, cfg.local, L0=4, kv_round=oracle.bf16_round,
+                           bf16=True)
+    ref.reset(2)
+    worst = 0.0
+    for t in range(192):
+        rl, _ = ref.step(idx[:, t].numpy(), t)
+        if t >= 128:
+            lg, _ = dec.step(idx[:, t].to(DEV), t)
+            worst = max(worst, float(np.abs(lg.float().cpu().numpy() - rl).max()))
+    assert worst < 2e-2, worst
+    _no_device_error()
+
+
+def test_greedy_graph_matches_eager():
+    """The captured greedy loop gives the same tokens as eager steps."""
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    cfg = tiny(seq_len=256, n_embd=64, wmax=4, beam=4, local=16, leaf=8)
+    torch.manual_seed(11)
+    m = GPT(cfg).eval()
+    W = weights_from_ours(m.state_dict(), cfg)
+    idx = torch.randint(0, 64, (4, 100), device=DEV)
+    toks = []
+    for graphs in (False, True):
+        dec = Decoder(W, cfg.n_layer, cfg.n_head, cfg.n_embd, 256, 'seg', cfg, DEV, batch=4, graphs=graphs)
+        dec.prefill(idx)
+        seq = []
+        for _ in range(40):
+            dec.greedy_steps(1)
+            seq.append(dec.tokens.clone())
+        toks.append(torch.stack(seq, 1))
+        assert int(dec.positions[0]) == 140
+    assert torch.equal(toks[0], toks[1])
+
+
+def test_past_is_covered_exactly():
+    """Reference test_seg.test_past_is_covered_exactly: with a wide beam the tree keys plus the static keys
+    cover [0, t] exactly and nothing later."""
+    from treeattn_b200.seg import select_seg
+    torch.manual_seed(1)
+    cfg = tiny(wmax=32, beam=32)
+    T = 64
+    q, k = torch.randn(1, 1, T, 16, device=DEV), torch.randn(1, 1, T, 16, device=DEV)
+    sel = select_seg(q, k, torch.full((1, 1, T), 32, dtype=torch.long, device=DEV), cfg)
+    tp = sel['tree_pos'][0, 0].cpu()
+    for t in range(T):
+        pos = set(tp[t][tp[t] >= 0].tolist())
+        assert all(p < t for p in pos), ('future key selected', t)
+        got = {p for p in pos | {0, t, t - 1, t - 2} if p >= 0}
+        assert got == set(range(t + 1)), t
+
+
+def test_all_keys_matches_dense():
+    """Reference test_seg.test_all_keys_matches_dense on DynAttention(attn='seg')."""
+    from treeattn_b200.attention_dyn import DynAttention
+    torch.manual_seed(2)
+    cfg = tiny(n_layer=1, wmax=32, beam=32)
+    attn = DynAttention(cfg).eval().to(DEV)
+    x = torch.randn(2, 64, 32, device=DEV)
+    with torch.no_grad():
+        out = attn(x)
+        C, H, dh = 32, 2, 16
+        q, k, v = attn.c_attn(x).split(C, 2)
+        q, k, v = [t.view(2, 64, H, dh).transpose(1, 2) for t in (q, k, v)]
+        s = (q @ k.transpose(-1, -2)) / dh ** 0.5
+        s = s.masked_fill(~torch.tril(torch.ones(64, 64, dtype=torch.bool, device=DEV)), float('-inf'))
+        ref = attn.c_proj((torch.softmax(s, -1) @ v).transpose(1, 2).reshape(2, 64, C))
+    assert (out - ref).abs().max().item() < 1e-4
+
+
+def test_causality():
+    """Reference test_seg.test_causality (fixed budget): changing token 37 changes nothing before it."""
+    from treeattn_b200.model import GPT
+    torch.manual_seed(3)
+    model = GPT(tiny()).eval().to(DEV)
+    idx = torch.randint(0, 64, (2, 64), device=DEV)
+    idx2 = idx.clone()
+    idx2[:, 37] = (idx[:, 37] + 1) % 64
+    with torch.no_grad():
+        l1, _, _ = model(idx)
+        l2, _, _ = model(idx2)
+    assert (l1[:, :37] - l2[:, :37]).abs().max().item() < 1e-4
+    assert (l1[:, 37:] - l2[:, 37:]).abs().max().item() > 1e-6
+
+
+def test_bf16_model_vs_oracle():
+    """bf16 weights through SegAttention (bf16 nn.Module forward) vs the oracle forward that rounds to bf16 at the
+    same points (max-abs 2e-2 on the logits)."""
+    from treeattn_b200.model import GPT
+    cfg = tiny(seq_len=256, n_embd=128, n_head=2, wmax=8, beam=8, local=32, leaf=16, vocab_size=128)
+    torch.manual_seed(5)
+    m = GPT(cfg).eval()
+    m = m.to(DEV, torch.bfloat16)
+    idx = torch.randint(0, 128, (2, 256))
+    with torch.no_grad():
+        logits, _, _ = m(idx.to(DEV))
+    W = oracle.weights_from_state_dict({k: v.float() for k, v in m.state_dict().items()}, cfg.n_layer)
+    ref, _ = oracle.gpt_forward(W, idx.numpy(), cfg.n_head, cfg.wmax, cfg.beam, cfg.local, L0=4, bf16=True)
+    assert np.abs(logits.float().cpu().numpy() - ref).max() < 2e-2

@@ -1,0 +1,110 @@
+"""CPU checks of the C-ABI library: it loads, exports every symbol the header declares, and rejects bad
+arguments before touching the GPU. Plus the host-side helpers of the Python layer."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, 'include', 'treeattn_b200.h')
+
+
+def _declared():
+    src = open(HEADER).read()
+    src = re.sub(r'/\*.*?\*/', '', src, flags=re.S)
+    return sorted(set(re.findall(r'\b(ta_[a-z0-9_]+)\s*\(', src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from treeattn_b200 import _lib
+    lib = _lib.load()
+    declared = _declared()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert sorted(_lib.SIGNATURES) == declared
+    assert lib.ta_version() >= 100
+
+
+def test_level_nodes():
+    from treeattn_b200 import _lib, _ops
+    lib = _lib.load()
+    for cap, L0, Lm in [(4352, 6, 12), (65536, 7, 15), (512, 1, 8), (300, 2, 9)]:
+        want = sum(cap >> l for l in range(L0, Lm + 1))
+        assert lib.ta_level_nodes(cap, L0, Lm) == want
+        counts = _ops.level_counts(cap, L0, Lm)
+        assert sum(c for _, c in counts.values()) == want
+
+
+def test_argument_validation_without_gpu():
+    """Rejected arguments return TA_ERR_ARG with a message; no CUDA call is made on these paths."""
+    from treeattn_b200 import _lib
+    lib = _lib.load()
+    # bad head dim
+    rc = lib.ta_build_levels(None, 1, 1, 1, 16, 48, 0, 0, 0, 16, 1, 3, 1, None, 0, 0, None)
+    assert rc == _lib.TA_ERR_ARG and 'head dim' in _lib.last_error()
+    # wmax out of range
+    rc = lib.ta_select(None, 1, 1, 1, 1, 64, 0, 0, 0, None, 0, 0, None, 0, 0, 16, 1, 3, 0, 1, None, None, None, None)
+    assert rc == _lib.TA_ERR_ARG and 'wmax' in _lib.last_error()
+    # top level below the leaf level
+    rc = lib.ta_decode_step(None, 1, 1, 1, 64, 0, 0, 0, None, None, 0, 0, 0, None, 0, 0, 64, 6, 5, None, 16, 16, 128,
+                            ctypes.c_float(0.125), None, 0, None, None, None, 1, None)
+    assert rc == _lib.TA_ERR_ARG and 'Lm' in _lib.last_error()
+    # cluster size limit
+    rc = lib.ta_decode_step(None, 1, 1, 1, 64, 0, 0, 0, None, None, 0, 0, 0, None, 0, 0, 64, 3, 5, None, 16, 16, 128,
+                            ctypes.c_float(0.125), None, 0, None, None, None, 9, None)
+    assert rc == _lib.TA_ERR_ARG and 'splits' in _lib.last_error()
+    # misaligned rows
+    buf = (ctypes.c_char * 256)()
+    addr = ctypes.addressof(buf)
+    addr += (16 - addr % 16) % 16
+    rc = lib.ta_seg_attn(addr + 2, addr, addr, 1, 1, 1, 1, 64, 0, 0, 64, 0, 0, 64, 0, 0, 64, 16, addr, 0, 1, addr,
+                         addr, 1, None, 1, 2, 3, ctypes.c_float(0.125), addr, 0, 0, 64, None, None, None)
+    assert rc == _lib.TA_ERR_ARG and 'aligned' in _lib.last_error()
+
+
+def test_python_layer_rejects_cpu_tensors():
+    import torch
+    from treeattn_b200 import _ops
+    k = torch.randn(1, 2, 16, 64)
+    with pytest.raises(ValueError, match='CUDA'):
+        _ops.build_levels(k, 16, 1, 3)
+
+
+@pytest.mark.parametrize('n_levels,wmax', [(1, 4), (2, 4), (3, 4), (8, 16), (12, 8)])
+def test_output_width_matches_reference_rule(n_levels, wmax):
+    """The slot count the reference's tree_pass returns (min(wmax, #candidates) at the last level)."""
+    from treeattn_b200._ops import output_width
+    T = 1 << (n_levels + 1)
+    q = np.random.default_rng(0).standard_normal((1, 1, 4, 8)).astype(np.float32)
+    k = np.random.default_rng(1).standard_normal((1, 1, T, 8)).astype(np.float32)
+    S = oracle.level_sums(k, 1, n_levels)
+    ids, _, _ = oracle.tree_pass(q, S, np.arange(T - 4, T), 1, n_levels, wmax)
+    assert ids.shape[-1] == output_width(n_levels, wmax)
+
+
+def test_n_tree_fixed_matches_finish():
+    from treeattn_b200.fastseg import n_tree_fixed
+    for wmax in (1, 4, 16):
+        for beam in range(0, 20):
+            r = oracle.finish(np.zeros((1, 1), np.int64), np.ones((1, 1), bool), np.zeros((1, 0), np.int64),
+                              np.zeros((1, 0), bool), np.zeros(1, np.int64), np.array([beam]), wmax)
+            assert n_tree_fixed(beam, wmax) == int(r['n_tree'][0]), (beam, wmax)
+
+
+def test_config_fields_match_reference_defaults():
+    from treeattn_b200.config import Config
+    c = Config()
+    assert (c.wmax, c.beam, c.local, c.nb_window, c.nb_store, c.leaf) == (8, 4, 3, 8, 2, 2)
+    assert Config(**c.to_dict()) == c
+
+
+def test_unsupported_paths_raise():
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    with pytest.raises(NotImplementedError):
+        GPT(Config(attn='block'))

@@ -132,7 +132,7 @@ struct RangeList {
 };
 
 // Build the ranges of one query with a warp. `leaf_of(i)` returns the leaf id of slot i or -1 when the slot is
-// not used. `t_end` = one past the last window position (t+1 when position t is read from the cache, t when
+// not used (ids whose block does not end before the window start are ignored). `t_end` = one past the last window position (t+1 when position t is read from the cache, t when
 // the caller handles position t itself). Returns the total number of keys in the ranges.
 template <typename LeafFn>
 __device__ __forceinline__ int build_ranges(RangeList& rl, int nslots, LeafFn leaf_of, int leaf, int t, int Lw,
@@ -144,9 +144,10 @@ __device__ __forceinline__ int build_ranges(RangeList& rl, int nslots, LeafFn le
     const int i = base + lane;
     int st = 0, len = 0;
     if (i < nslots) {
-      const int m = leaf_of(i);
-      if (m >= 0) {
-        st = m * leaf;
+      const int64_t m = leaf_of(i);
+      // a used leaf lies entirely before the window start; anything else (a bad id) contributes nothing
+      if (m >= 0 && m * (int64_t)leaf < (int64_t)w0) {
+        st = (int)(m * leaf);
         const int en = min(st + leaf, w0);
         len = max(en - st, 0);
         if (m == 0) leaf0 = true;
@@ -161,6 +162,7 @@ __device__ __forceinline__ int build_ranges(RangeList& rl, int nslots, LeafFn le
     cnt += __popc(mask);
   }
   leaf0 = __any_sync(0xffffffffu, leaf0);
+  __syncwarp();
   if (lane == 0) {
     if (w0 > 0 && !leaf0) {
       rl.start[cnt] = 0;
@@ -224,8 +226,8 @@ __global__ void __launch_bounds__(128) seg_attn_kernel(SegAttnParams p) {
   const int64_t sbase = qid * p.wl;
   const int total = build_ranges(
       rl, p.wl,
-      [&](int i) -> int {
-        return (p.vld[sbase + i] && i < ntree) ? (int)p.ids[sbase + i] : -1;
+      [&](int i) -> int64_t {
+        return (p.vld[sbase + i] && i < ntree) ? p.ids[sbase + i] : (int64_t)-1;
       },
       p.leaf, t, p.Lw, t + 1, lane);
 

@@ -278,7 +278,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
         const int keep = min(p.n_tree, p.wmax);
         nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, lane);
         build_ranges(
-            sh.rl, nk, [&](int i) -> int { return sh.ds.kid[i]; }, leaf, t, p.Lw, w0, lane);
+            sh.rl, nk, [&](int i) -> int64_t { return sh.ds.kid[i]; }, leaf, t, p.Lw, w0, lane);
       } else if (lane == 0) {
         sh.rl.n = 0;
         sh.rl.pref[0] = 0;

@@ -116,8 +116,14 @@ struct BuildLevels {
 template <typename QT, int DH>
 struct Select {
   static int run(ta::SelectParams p, cudaStream_t st) {
-    const int warps = 4;
-    const size_t smem = sizeof(ta::DescentScratch) * warps + (size_t)warps * (2 * p.wmax + 1) * DH * sizeof(float);
+    // 4 warps (queries) per CTA unless their staging rows would not fit in shared memory
+    int warps = 4;
+    auto smem_for = [&](int w) {
+      return sizeof(ta::DescentScratch) * w + (size_t)w * (2 * p.wmax + 1) * DH * sizeof(float);
+    };
+    while (warps > 1 && smem_for(warps) > 200 * 1024) warps >>= 1;
+    const size_t smem = smem_for(warps);
+    if (smem > 200 * 1024) return fail(TA_ERR_ARG, "ta_select: wmax %d too large for head dim %d", p.wmax, DH);
     static bool attr_set = false;
     if (!attr_set) {
       cudaFuncSetAttribute(ta::select_kernel<QT, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -257,6 +257,23 @@ class Decoder:
         for _ in range(n):
             self._graph_greedy.replay()
 
+    @torch.no_grad()
+    def serve_step(self, tok_host, out=None):
+        """One greedy step for a serving loop that keeps tokens on the host: copy the current tokens (B,) from
+        host (pinned) memory, run the step, copy the next tokens back to `out` (host) and wait for them.
+        Positions advance by one on the device."""
+        self._ensure_graphs()
+        self._tok.copy_(tok_host, non_blocking=True)
+        if self.use_graphs:
+            self._graph_greedy.replay()
+        else:
+            self._greedy_step()
+        if out is None:
+            out = torch.empty(self.batch, dtype=torch.int64, pin_memory=True)
+        out.copy_(self._tok, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return out
+
     @property
     def tokens(self):
         return self._tok
