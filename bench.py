@@ -45,6 +45,9 @@ def parse():
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
     p.add_argument('--splits', type=int, default=0, help='CTAs per (b, h) in the decode kernel (0 = auto)')
+    p.add_argument('--kernel-only', action='store_true',
+                   help='time only the fused decode kernel on the config-4 shape (random caches of 4 layers, '
+                        'rotated so that no launch finds its KV in L2) and print one JSON line')
     p.add_argument('--profile-steps', type=int, default=0,
                    help='profiling mode: after prefill and warm-up run this many eager decode steps between '
                         'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
@@ -179,6 +182,68 @@ def cpu_decode_sample(seconds, W_dev=None, seed=0):
     return steps / dt, steps, threads
 
 
+def run_kernel_only(a, dev):
+    """Config-4 decode-attention kernel alone: batch a.batch x 12 heads, dh 64, bf16 caches holding a.prompt
+    positions, leaf 64, top-16, window 128, position t = prompt (+ the launch index). With --profile-steps the
+    launches are bracketed by cudaProfilerStart/Stop for ncu."""
+    from treeattn_b200 import _ops
+    from treeattn_b200._ops import Levels
+    B, T0, dh = a.batch, a.prompt, C // H
+    L0, Lm = int(math.log2(LEAF)), int(math.log2(TCAP)) - 1
+    cap = T0 + 64
+    nlay = 4
+    g = torch.Generator(device=dev).manual_seed(7)
+    layers = []
+    for _ in range(nlay):
+        K = (torch.randn(B, H, cap, dh, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        Vv = torch.randn(B, H, cap, dh, device=dev, generator=g).to(torch.bfloat16)
+        lv = Levels.empty(B, H, dh, cap, L0, Lm, dev)
+        _ops.build_levels(K[:, :, :T0], cap, L0, Lm, zero_sink=True, out=lv)
+        layers.append((K, Vv, lv))
+    qkv = torch.randn(B, 3 * C, device=dev, generator=g).to(torch.bfloat16)
+    pos = torch.full((B,), T0, device=dev, dtype=torch.int32)
+    att = torch.empty(B, C, device=dev, dtype=torch.bfloat16)
+    nk = torch.empty(B, H, device=dev, dtype=torch.int32)
+    splits = a.splits or _ops.default_splits(B, H)
+
+    def run_all():
+        for K, Vv, lv in layers:
+            _ops.decode_step(qkv, K, Vv, lv, pos, H, TOPK, TOPK, WINDOW, 1 / 8.0, att, nkeys=nk, splits=splits)
+
+    run_all()
+    torch.cuda.synchronize()
+    if a.profile_steps:
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(a.profile_steps):
+            run_all()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps(dict(kernel_only=True, profile_steps=a.profile_steps, launches=nlay * a.profile_steps)))
+        return
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(gr, stream=s):
+        run_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    gr.replay()
+    torch.cuda.synchronize()
+    reps = 25
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * nlay)
+    byts = float(nk.sum()) * dh * 2 * 2
+    peaks = measured_peaks()
+    peak = peaks['hbm_gbs'] if peaks else 6650.0
+    print(json.dumps(dict(kernel_only=True, batch=B, prompt=T0, splits=splits, kernel_us=us, bytes_per_launch=byts,
+                          achieved_gbs=byts / us / 1e3, frac=byts / us / 1e3 / peak,
+                          keys_per_head=float(nk.float().mean()))), flush=True)
+
+
 def run_reference(a, rank, world):
     if rank != 0:
         return
@@ -212,6 +277,9 @@ def main():
         dist.init_process_group('nccl', timeout=timedelta(seconds=600), device_id=dev)
     from treeattn_b200 import _ops
     from treeattn_b200.engine import Decoder
+    if a.kernel_only:
+        run_kernel_only(a, dev)
+        return
 
     B, T0, K, Wm = a.batch, a.prompt, a.steps, max(a.warmup, 3)
     cap = ((T0 + Wm + 2 * K + 8 + LEAF - 1) // LEAF) * LEAF

@@ -116,15 +116,17 @@ int ta_append(const void* k, const void* v, int dtype, int B, int H, int dh, int
 
 /* Replaces seg_attend (engine.py:84-120) for a batch, fused: tree descent for the new query, attention over
  * used leaves + sink + window + the new token, append of the new k/v and the incremental tree update.
- * qkv rows (B, 3*H*dh): q at 0, k at k_ofs, v at v_ofs (elements). out rows (B, H*dh). splits = CTAs per
- * (b, h) (a thread-block cluster, 1..8; 0 = choose). lse / nkeys / sel (B, H, wmax+1) may be NULL. */
+ * qkv rows (B, 3*H*dh): q at 0, k at k_ofs, v at v_ofs (elements). out rows (B, H*dh). lse / nkeys /
+ * sel (B, H, wmax+1) may be NULL. splits: 0 = choose; -1 = persistent pipelined kernel (a selector warp runs
+ * the descent of the next (b, h) while the current one streams; for B*H >= #SMs); 1..8 = CTAs per (b, h) of
+ * the cluster kernel (split KV merged through distributed shared memory; for small batches). */
 int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,
                    void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st, float* nodes, int64_t n_sb,
                    int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos, int wmax, int n_tree, int Lw,
                    float scale, void* out, int64_t o_sb, float* lse, int32_t* nkeys, int32_t* sel, int splits,
                    void* stream);
 
-/* The split count ta_decode_step would choose for B*H (b, h) pairs on the current device. */
+/* The `splits` value ta_decode_step chooses for B*H (b, h) pairs on the current device (-1 = persistent). */
 int ta_decode_default_splits(int B, int H);
 
 #ifdef __cplusplus

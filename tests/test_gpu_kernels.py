@@ -283,6 +283,9 @@ def test_append_incremental_tree(L0, dt):
 
 # ------------------------------------------------------------------------------------------------ fused decode
 @pytest.mark.parametrize('dt,dh,L0,wmax,beam,local,splits', [
+    (torch.bfloat16, 64, 6, 16, 16, 128, -1),
+    (torch.bfloat16, 128, 7, 32, 32, 256, -1),
+    (torch.float32, 32, 2, 8, 3, 8, -1),
     (torch.bfloat16, 64, 6, 16, 16, 128, 1),
     (torch.bfloat16, 64, 6, 16, 16, 128, 4),
     (torch.bfloat16, 64, 6, 16, 16, 128, 8),
@@ -349,7 +352,6 @@ def test_decode_step_vs_oracle(dt, dh, L0, wmax, beam, local, splits):
                     continue
                 tol = 1e-4 if dt == torch.float32 else 2e-2
                 np.testing.assert_allclose(o_n[b, h * dh:(h + 1) * dh], ro[h], atol=tol)
-                ok = states[b]
                 assert nk_n[b, h] == len(set(
                     [p for p in oracle.leaves_to_pos(rids[h], rused[h], leaf).tolist() if p >= 0] +
                     [0] + list(range(max(0, T0[b] + s_i - Lw + 1), T0[b] + s_i + 1)))), (b, h, s_i)
@@ -359,6 +361,66 @@ def test_decode_step_vs_oracle(dt, dh, L0, wmax, beam, local, splits):
         n = T0[b] + steps
         np.testing.assert_array_equal(kc[b, :, :n].float().cpu().numpy(), states[b].K[:, :n])
         np.testing.assert_array_equal(vc[b, :, :n].float().cpu().numpy(), states[b].V[:, :n])
+        for l in range(L0, Lm + 1):
+            m = n >> l
+            np.testing.assert_array_equal(lv.level(l)[b, :, :m].cpu().numpy(), states[b].levels[l][0, :, :m])
+    _no_device_error()
+
+
+@pytest.mark.parametrize('dt,dh,L0', [(torch.bfloat16, 64, 4), (torch.float16, 128, 5)])
+def test_decode_persistent_many_items(dt, dh, L0):
+    """Persistent kernel with several (b, h) items per CTA (descriptor-slot reuse, partial-state hand-off), ragged
+    positions, steps crossing leaf-block boundaries: outputs, key counts, caches and tree vs the oracle."""
+    ops = _ops()
+    from treeattn_b200._ops import Levels
+    rng = np.random.default_rng(dh)
+    B, H = 40, 16
+    C = H * dh
+    leaf = 1 << L0
+    wmax, beam, local = 8, 8, 2 * leaf
+    T0 = rng.integers(3 * leaf, 12 * leaf, B).tolist()
+    steps = leaf + 3
+    cap = max(T0) + steps + 1
+    Tcap = 1 << int(math.ceil(math.log2(cap)))
+    Lm = int(round(math.log2(Tcap))) - 1
+    rnd = lambda a: torch.as_tensor(a).to(dt).float().numpy()
+    kc = torch.zeros(B, H, cap, dh, device=DEV, dtype=dt)
+    vc = torch.zeros_like(kc)
+    lv = Levels.empty(B, H, dh, cap, L0, Lm, DEV)
+    states = []
+    for b in range(B):
+        K0 = rnd(rng.standard_normal((H, T0[b], dh)).astype(np.float32))
+        V0 = rnd(rng.standard_normal((H, T0[b], dh)).astype(np.float32))
+        kc[b, :, :T0[b]] = torch.as_tensor(K0).to(DEV, dt)
+        vc[b, :, :T0[b]] = torch.as_tensor(V0).to(DEV, dt)
+        st = oracle.SegStateNP(H, dh, cap, L0, Lm)
+        st.fill(K0, V0)
+        states.append(st)
+    ops.build_levels(kc, cap, L0, Lm, zero_sink=True, out=lv)  # complete nodes of each row's own prefix only
+    for b in range(B):  # rows with shorter prompts: clear nodes beyond their own complete prefix
+        for l in range(L0, Lm + 1):
+            lv.level(l)[b, :, T0[b] >> l:] = 0
+    out = torch.empty(B, C, device=DEV, dtype=dt)
+    nkeys = torch.empty(B, H, device=DEV, dtype=torch.int32)
+    ntree = oracle.n_tree_fixed(beam, wmax)
+    worst = 0.0
+    for s_i in range(steps):
+        pos = torch.tensor([T0[b] + s_i for b in range(B)], device=DEV, dtype=torch.int32)
+        qkv_np = rnd(rng.standard_normal((B, 3 * C)).astype(np.float32))
+        ops.decode_step(torch.as_tensor(qkv_np).to(DEV, dt), kc, vc, lv, pos, H, wmax, ntree, local,
+                        1 / math.sqrt(dh), out, nkeys=nkeys, splits=-1)
+        o_n, nk_n = out.float().cpu().numpy(), nkeys.cpu().numpy()
+        for b in range(B):
+            q, k, v = [qkv_np[b, j * C:(j + 1) * C].reshape(H, dh) for j in range(3)]
+            ro, _, (rids, rused, margin) = oracle.seg_attend(states[b], q, k, v, T0[b] + s_i, wmax, beam, local,
+                                                             with_sel=True)
+            ok = margin > 1e-6
+            d = np.abs(o_n[b].reshape(H, dh) - ro).max(-1)
+            worst = max(worst, float(d[ok].max(initial=0)))
+    assert worst < 2e-2, worst
+    for b in range(B):
+        n = T0[b] + steps
+        np.testing.assert_array_equal(kc[b, :, :n].float().cpu().numpy(), states[b].K[:, :n])
         for l in range(L0, Lm + 1):
             m = n >> l
             np.testing.assert_array_equal(lv.level(l)[b, :, :m].cpu().numpy(), states[b].levels[l][0, :, :m])
@@ -377,10 +439,12 @@ def test_decode_bad_position_records_error():
     out = torch.empty(B, H * dh, device=DEV, dtype=torch.bfloat16)
     ops.device_error()
     pos = torch.tensor([5, cap + 10], device=DEV, dtype=torch.int32)
-    ops.decode_step(qkv, kc, vc, lv, pos, H, 4, 4, 8, 0.125, out, splits=1)
-    code = ops.device_error()
-    assert code[0] == 2 and code[2] == cap + 10, code
-    assert kc[0, :, 5].abs().sum() > 0  # the valid sequence was still processed
+    for splits in (1, -1):
+        kc.zero_()
+        ops.decode_step(qkv, kc, vc, lv, pos, H, 4, 4, 8, 0.125, out, splits=splits)
+        code = ops.device_error()
+        assert code[0] == 2 and code[2] == cap + 10, (splits, code)
+        assert kc[0, :, 5].abs().sum() > 0  # the valid sequence was still processed
 
 
 def test_bad_arguments_raise():

@@ -74,12 +74,12 @@ __host__ __device__ inline size_t decode_smem_bytes(int wmax) {
 
 // Form the leaf node of the block that position t completes ((t+1) % 2^L0 == 0) and its right-spine
 // ancestors. Leaf node = adjacent-pair fp32 sums of rows [n*2^L0, t] (the sink as 0; row t = knew, not yet
-// readable from the cache), reduced in shared memory `xs` (xs_floats >= 2^L0) in dim slices. All `nthreads`
-// threads of the CTA must call this; it ends with the node rows written.
+// readable from the cache), reduced in shared memory `xs` (xs_floats >= 2^L0) in dim slices. The `nthreads`
+// threads (tid 0..nthreads-1) synchronizing on named barrier `bar` (0 = the whole CTA) must all call this.
 template <typename T, int DH>
 __device__ void tree_update_block(const T* __restrict__ kbase, int64_t c_st, const T* __restrict__ knew, int t,
                                   float* __restrict__ nodes_bh, const LevelView& lv, float* xs, int xs_floats,
-                                  int tid, int nthreads) {
+                                  int tid, int nthreads, int bar) {
   const int L0 = lv.L0, leaf = 1 << L0;
   const int DS = min(DH, xs_floats / leaf);
   const int n_blk = t >> L0;
@@ -96,7 +96,7 @@ __device__ void tree_update_block(const T* __restrict__ kbase, int64_t c_st, con
       else v = to_f32(kbase[(int64_t)pp * c_st + d]);
       xs[i * dn + (d - d0)] = v;
     }
-    __syncthreads();
+    named_bar_sync(bar, nthreads);
     for (int st = 1; st < leaf; st <<= 1) {
       const int pairs = leaf / (2 * st);
       for (int x = tid; x < pairs * dn; x += nthreads) {
@@ -104,10 +104,10 @@ __device__ void tree_update_block(const T* __restrict__ kbase, int64_t c_st, con
         const int i = pi * 2 * st;
         xs[i * dn + d] = xs[i * dn + d] + xs[(i + st) * dn + d];
       }
-      __syncthreads();
+      named_bar_sync(bar, nthreads);
     }
     if (tid >= d0 && tid < d0 + dn) my_node = xs[tid - d0];
-    __syncthreads();
+    named_bar_sync(bar, nthreads);
   }
   if (tid < DH) {
     nodes_bh[(int64_t)(lv.off[L0] + n_blk) * DH + tid] = my_node;
@@ -276,7 +276,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
         load_q4<T, DH>(qkv_row + h * DH, lane, qv);
         const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
         const int keep = min(p.n_tree, p.wmax);
-        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, lane);
+        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, 2 * p.wmax + 1, lane);
         build_ranges(
             sh.rl, nk, [&](int i) -> int64_t { return sh.ds.kid[i]; }, leaf, t, p.Lw, w0, lane);
       } else if (lane == 0) {
@@ -419,7 +419,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
   constexpr int RING_FLOATS = (int)(Cfg::RING_BYTES / sizeof(float));
   tree_update_block<T, DH>(kbase, p.c_st, qkv_row + p.k_ofs + h * DH, t,
                            p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, reinterpret_cast<float*>(ring), RING_FLOATS,
-                           tid, Cfg::NTHREADS);
+                           tid, Cfg::NTHREADS, 0);
 }
 
 // ------------------------------------------------------------------------------------------------ append
@@ -464,7 +464,435 @@ __global__ void __launch_bounds__(APPEND_THREADS) append_kernel(AppendParams p) 
   const int leaf = 1 << p.lv.L0;
   if (((t + 1) & (leaf - 1)) != 0) return;
   tree_update_block<T, DH>(kbase, p.c_st, kr, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, xs,
-                           APPEND_SMEM_FLOATS, tid, APPEND_THREADS);
+                           APPEND_SMEM_FLOATS, tid, APPEND_THREADS, 0);
+}
+
+// ================================================================================================ persistent
+// Persistent, warp-specialized decode for large batches (B*H >= #SMs). CTA c owns the (b, h) items
+// c, c + G, c + 2G, ... (G = gridDim.x) and pipelines them:
+//   selector warp  : copies item k+1's q/k/v rows into a descriptor slot and runs its tree descent while item k
+//                    streams (descriptor ready -> mbarrier ifull[slot])
+//   producer warp  : 1-D bulk copies (no multicast) of item k's K/V rows into a ring of NST shared-memory stages -
+//                    the window rows first (they need no descent), then the used leaf blocks and the sink - and
+//                    an end-of-item marker stage
+//   consumer warps : online softmax over the ring; at the marker, warps 1.. hand their partial state to warp 0,
+//                    which merges it, writes the output, appends the new k/v rows and, when the new token completes
+//                    a leaf block, forms that leaf node and its right-spine ancestors (fp32, adjacent-pair order)
+// Every wait between warps is a bounded mbarrier wait, so a protocol error ends in a recorded error, not a hang.
+constexpr int PSLOTS = 2;
+constexpr int STAGE_FIRST = 1, STAGE_LAST = 2;
+
+template <typename T, int DH>
+struct __align__(16) PItem {
+  T q[DH], k[DH], v[DH];  // this step's rows of the item's (b, h)
+  RangeList rl;           // used leaf blocks cut at the window start, and the sink; the window is not listed
+  int sel[WMAX_LIMIT];
+  int t, bh, nsel, active;
+};
+
+template <typename T, int DH, int NST, int NCW>
+struct __align__(16) PShared {
+  PItem<T, DH> item[PSLOTS];
+  DescentScratch ds;
+  uint64_t full[NST], empty[NST], ifull[PSLOTS], iempty[PSLOTS], pready[2], pfree[2];
+  int nrows[NST], slot[NST], flags[NST];
+  float part_m[2][NCW], part_l[2][NCW];
+  int part_rows[2];
+  int consumed;
+  int abort_flag;
+};
+
+template <typename T, int DH, int CH, int NST, int NCW>
+struct PCfg {
+  static constexpr int NTHREADS = (NCW + 2) * 32;
+  static constexpr int STAGE_ELEMS = 2 * CH * DH;
+  static constexpr size_t RING_BYTES = (size_t)NST * STAGE_ELEMS * sizeof(T);
+  static constexpr int TU_FLOATS = 2048;
+  static size_t smem_bytes(int stage_rows) {
+    size_t off = (sizeof(PShared<T, DH, NST, NCW>) + 127) & ~(size_t)127;
+    return off + RING_BYTES + (size_t)stage_rows * DH * 4 + (size_t)2 * NCW * DH * 4 + (size_t)TU_FLOATS * 4;
+  }
+};
+
+// One warp forms the leaf node completed by position t and its right-spine ancestors (same arithmetic and order
+// as tree_update_block), reducing in `xs` (xs_floats >= 2^L0) with warp-level synchronization only.
+template <typename T, int DH>
+__device__ void tree_update_warp(const T* __restrict__ kbase, int64_t c_st, const T* knew, int t,
+                                 float* __restrict__ nodes_bh, const LevelView& lv, float* xs, int xs_floats,
+                                 int lane) {
+  const int L0 = lv.L0, leaf = 1 << L0;
+  const int DS = min(DH, xs_floats / leaf);
+  const int n_blk = t >> L0;
+  const int p0 = n_blk * leaf;
+  for (int d0 = 0; d0 < DH; d0 += DS) {
+    const int dn = min(DS, DH - d0);
+    for (int x = lane; x < leaf * dn; x += 32) {
+      const int i = x / dn, d = d0 + (x - (x / dn) * dn);
+      const int pp = p0 + i;
+      float v;
+      if (pp == 0) v = 0.f;
+      else if (pp == t) v = to_f32(knew[d]);
+      else v = to_f32(kbase[(int64_t)pp * c_st + d]);
+      xs[i * dn + (d - d0)] = v;
+    }
+    __syncwarp();
+    for (int st = 1; st < leaf; st <<= 1) {
+      const int pairs = leaf / (2 * st);
+      for (int x = lane; x < pairs * dn; x += 32) {
+        const int pi = x / dn, d = x - (x / dn) * dn;
+        const int i = pi * 2 * st;
+        xs[i * dn + d] = xs[i * dn + d] + xs[(i + st) * dn + d];
+      }
+      __syncwarp();
+    }
+    for (int d = lane; d < dn; d += 32) {
+      float cur = xs[d];
+      const int dd = d0 + d;
+      nodes_bh[(int64_t)(lv.off[L0] + n_blk) * DH + dd] = cur;
+      for (int l = L0 + 1; l <= lv.Lm; ++l) {
+        if (((t + 1) & ((1 << l) - 1)) != 0) break;
+        const int m = t >> l;
+        if (m >= (lv.cap >> l)) break;
+        cur = nodes_bh[(int64_t)(lv.off[l - 1] + 2 * m) * DH + dd] + cur;
+        nodes_bh[(int64_t)(lv.off[l] + m) * DH + dd] = cur;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T, int DH, int CH, int NST, int NCW>
+__global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
+  using Cfg = PCfg<T, DH, CH, NST, NCW>;
+  using Sh = PShared<T, DH, NST, NCW>;
+  using WA = WarpAttn<T, DH>;
+  constexpr int VEC = WA::VEC, RPW = WA::RPW;
+  constexpr int ROWB = DH * (int)sizeof(T);
+  static_assert(NCW >= 2 && NST <= 16, "pipeline shape");
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
+  size_t off = (sizeof(Sh) + 127) & ~(size_t)127;
+  T* ring = reinterpret_cast<T*>(smem_raw + off);
+  off += Cfg::RING_BYTES;
+  float* dstage = reinterpret_cast<float*>(smem_raw + off);
+  off += (size_t)stage_rows * DH * sizeof(float);
+  float* part_acc = reinterpret_cast<float*>(smem_raw + off);  // [2][NCW][DH]
+  off += (size_t)2 * NCW * DH * sizeof(float);
+  float* tu = reinterpret_cast<float*>(smem_raw + off);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  const int n_all = p.B * p.H;
+  const int K = ((int)blockIdx.x < n_all) ? (n_all - (int)blockIdx.x + G - 1) / G : 0;  // items of this CTA
+  const int leaf = 1 << p.lv.L0;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], NCW);
+    }
+    for (int s = 0; s < PSLOTS; ++s) {
+      mbar_init(&sh.ifull[s], 1);
+      mbar_init(&sh.iempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sh.pready[s], NCW - 1);
+      mbar_init(&sh.pfree[s], 1);
+    }
+    sh.consumed = 0;
+    sh.abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == NCW + 1) {
+    // ------------------------------------------------------------------ selector warp
+    const int keep = min(p.n_tree, p.wmax);
+    for (int k = 0; k < K; ++k) {
+      const int slot = k % PSLOTS;
+      if (k >= PSLOTS && !mbar_wait_bounded(&sh.iempty[slot], ((k / PSLOTS) - 1) & 1, K_DECODE, 10)) {
+        if (lane == 0) atomicExch(&sh.abort_flag, 1);
+        break;
+      }
+      PItem<T, DH>& it = sh.item[slot];
+      const int bh = (int)blockIdx.x + k * G;
+      const int b = bh / p.H, h = bh % p.H;
+      int t = p.pos[b];
+      const bool active = t >= 0 && t < p.lv.cap;
+      if (!active) {
+        if (lane == 0) record_error(DEV_POS_RANGE, K_DECODE, t, p.lv.cap);
+        t = 0;
+      }
+      const T* row = reinterpret_cast<const T*>(p.qkv) + b * p.qkv_sb;
+      constexpr int CPR = DH / VEC;  // 16-byte chunks per row
+      for (int x = lane; x < 3 * CPR; x += 32) {
+        const int part = x / CPR, c = x - (x / CPR) * CPR;
+        const int64_t src = (part == 0 ? 0 : (part == 1 ? p.k_ofs : p.v_ofs)) + h * DH + c * VEC;
+        T* dst = (part == 0 ? it.q : (part == 1 ? it.k : it.v)) + c * VEC;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(row + src);
+      }
+      __syncwarp();
+      int nk = 0;
+      if (active) {
+        float qv[4];
+        load_q4<T, DH>(it.q, lane, qv);
+        const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
+        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, stage_rows, lane);
+        build_ranges(
+            it.rl, nk, [&](int i) -> int64_t { return sh.ds.kid[i]; }, leaf, t, p.Lw, max(t - p.Lw + 1, 0), lane);
+        for (int i = lane; i < nk; i += 32) it.sel[i] = sh.ds.kid[i];
+      } else if (lane == 0) {
+        it.rl.n = 0;
+        it.rl.pref[0] = 0;
+      }
+      if (lane == 0) {
+        it.t = t;
+        it.bh = bh;
+        it.nsel = nk;
+        it.active = active ? 1 : 0;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.ifull[slot]);
+    }
+  } else if (warp == NCW) {
+    // ------------------------------------------------------------------ producer warp (lane 0 issues)
+    int it = 0;
+    bool ok = true;
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      auto acquire = [&](int& s) -> bool {
+        s = it % NST;
+        if (it >= NST) return mbar_wait_bounded(&sh.empty[s], ((it / NST) - 1) & 1, K_DECODE, 1);
+        return true;
+      };
+      for (int k = 0; k < K && ok; ++k) {
+        const int slot = k % PSLOTS;
+        const int bh = (int)blockIdx.x + k * G;
+        const int b = bh / p.H, h = bh % p.H;
+        int t = p.pos[b];
+        const bool active = t >= 0 && t < p.lv.cap;
+        if (!active) t = 0;
+        const int w0 = max(t - p.Lw + 1, 0);
+        const T* kbase = reinterpret_cast<const T*>(p.kc) + b * p.c_sb + h * p.c_sh;
+        const T* vbase = reinterpret_cast<const T*>(p.vc) + b * p.c_sb + h * p.c_sh;
+        int first = STAGE_FIRST;
+        for (int r0 = w0; active && r0 < t; r0 += CH) {  // window rows [w0, t)
+          int s;
+          if (!(ok = acquire(s))) break;
+          const int n = min(CH, t - r0);
+          sh.nrows[s] = n;
+          sh.flags[s] = first;
+          sh.slot[s] = slot;
+          first = 0;
+          T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
+          mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+          bulk_g2s_hint(kd, kbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
+          bulk_g2s_hint(kd + CH * DH, vbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
+          ++it;
+        }
+        if (!ok) break;
+        if (!(ok = mbar_wait_bounded(&sh.ifull[slot], (k / PSLOTS) & 1, K_DECODE, 11))) break;
+        const RangeList& rl = sh.item[slot].rl;
+        int ri = 0, roff = 0;
+        while (ri < rl.n) {  // leaf blocks + sink, packed CH rows per stage
+          int s;
+          if (!(ok = acquire(s))) break;
+          int n = 0;
+          {
+            int ri2 = ri, roff2 = roff;
+            while (n < CH && ri2 < rl.n) {
+              const int len = rl.pref[ri2 + 1] - rl.pref[ri2];
+              const int take = min(CH - n, len - roff2);
+              n += take;
+              roff2 += take;
+              if (roff2 == len) { ++ri2; roff2 = 0; }
+            }
+          }
+          sh.nrows[s] = n;
+          sh.flags[s] = first;
+          sh.slot[s] = slot;
+          first = 0;
+          T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
+          mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+          int put = 0;
+          while (put < n) {
+            const int len = rl.pref[ri + 1] - rl.pref[ri];
+            const int take = min(n - put, len - roff);
+            const int64_t r0 = rl.start[ri] + roff;
+            bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
+            bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s],
+                          pol);
+            put += take;
+            roff += take;
+            if (roff == len) { ++ri; roff = 0; }
+          }
+          ++it;
+        }
+        if (!ok) break;
+        int s;  // end-of-item marker
+        if (!(ok = acquire(s))) break;
+        sh.nrows[s] = 0;
+        sh.flags[s] = first | STAGE_LAST;
+        sh.slot[s] = slot;
+        mbar_arrive(&sh.full[s]);
+        ++it;
+      }
+      if (ok) {
+        int s;
+        if ((ok = acquire(s))) {
+          sh.nrows[s] = -1;
+          mbar_arrive(&sh.full[s]);
+        }
+      }
+      if (!ok) atomicExch(&sh.abort_flag, 1);
+    }
+    __syncwarp();
+    named_bar_sync(2, (NCW + 1) * 32);
+    if (lane == 0) {  // no bulk copy of this CTA may still be in flight when it exits
+      for (int i = sh.consumed; i < it; ++i) mbar_wait_bounded(&sh.full[i % NST], (i / NST) & 1, K_DECODE, 2);
+    }
+  } else {
+    // ------------------------------------------------------------------ consumer warps
+    WA wa;
+    int it = 0, k = 0, rows = 0;
+    bool ok = true;
+    while (true) {
+      const int s = it % NST;
+      if (!mbar_wait_bounded(&sh.full[s], (it / NST) & 1, K_DECODE, 3)) {
+        ok = false;
+        break;
+      }
+      const int n = sh.nrows[s];
+      if (n < 0) break;
+      const int fl = sh.flags[s], slot = sh.slot[s];
+      PItem<T, DH>& item = sh.item[slot];
+      if (fl & STAGE_FIRST) {
+        if (!mbar_wait_bounded(&sh.ifull[slot], (k / PSLOTS) & 1, K_DECODE, 4)) {
+          ok = false;
+          break;
+        }
+        wa.init(item.q, p.scale * LOG2E, lane);
+        rows = 0;
+        if (warp == 0 && item.active) {  // the new token, from this step's rows
+          float kf[1][VEC], vf[1][VEC], sc[1];
+          load_vec_f32<T>(item.k + wa.c * VEC, kf[0]);
+          load_vec_f32<T>(item.v + wa.c * VEC, vf[0]);
+          const float x = wa.row_score(kf[0]);
+          sc[0] = wa.sub == 0 ? x : -INFINITY;
+          wa.template update<1>(sc, vf);
+          rows = 1;
+        }
+      }
+      if (n > 0) {
+        const T* kst = ring + (size_t)s * Cfg::STAGE_ELEMS;
+        const T* vst = kst + CH * DH;
+        const int ngroups = ceil_div(n, RPW);
+        for (int g0 = warp; g0 < ngroups; g0 += 2 * NCW) {
+          float kf[2][VEC], vf[2][VEC], sc[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int g = g0 + u * NCW;
+            const int r = g * RPW + wa.sub;
+            const bool valid = (g < ngroups) && (r < n);
+            if (valid) {
+              load_vec_f32<T>(kst + (size_t)r * DH + wa.c * VEC, kf[u]);
+              load_vec_f32<T>(vst + (size_t)r * DH + wa.c * VEC, vf[u]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < VEC; ++i) kf[u][i] = vf[u][i] = 0.f;
+            }
+            const float x = wa.row_score(kf[u]);
+            sc[u] = valid ? x : -INFINITY;
+          }
+          wa.template update<2>(sc, vf);
+        }
+        if (warp == 0) rows += n;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.empty[s]);
+      ++it;
+      if (!(fl & STAGE_LAST)) continue;
+      // ---------------------------------------------------------------- end of item k: merge + finalize
+      const int par = k & 1;
+      wa.reduce_rows();
+      float* pacc = part_acc + (size_t)par * NCW * DH;
+      if (warp > 0) {
+        if (k >= 2 && !mbar_wait_bounded(&sh.pfree[par], ((k >> 1) - 1) & 1, K_DECODE, 5)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          sh.part_m[par][warp] = wa.m;
+          sh.part_l[par][warp] = wa.l;
+        }
+        if (wa.sub == 0) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) pacc[warp * DH + wa.c * VEC + i] = wa.acc[i];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.pready[par]);
+      } else {
+        if (lane == 0) {
+          sh.part_m[par][0] = wa.m;
+          sh.part_l[par][0] = wa.l;
+        }
+        if (wa.sub == 0) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) pacc[wa.c * VEC + i] = wa.acc[i];
+        }
+        __syncwarp();
+        const bool got = mbar_wait_bounded(&sh.pready[par], (k >> 1) & 1, K_DECODE, 6);
+        if (got && item.active) {
+          const int b = item.bh / p.H, h = item.bh % p.H, t = item.t;
+          float m = -INFINITY;
+          for (int w = 0; w < NCW; ++w) m = fmaxf(m, sh.part_m[par][w]);
+          float l = 0.f;
+          for (int w = 0; w < NCW; ++w)
+            if (sh.part_m[par][w] != -INFINITY) l += sh.part_l[par][w] * exp2f(sh.part_m[par][w] - m);
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
+          for (int d = lane; d < DH; d += 32) {
+            float a = 0.f;
+            for (int w = 0; w < NCW; ++w)
+              if (sh.part_m[par][w] != -INFINITY) a += pacc[w * DH + d] * exp2f(sh.part_m[par][w] - m);
+            orow[d] = from_f32<T>(a * inv);
+          }
+          const int bhi = item.bh;
+          if (lane == 0) {
+            if (p.lse) p.lse[bhi] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
+            if (p.nkeys) p.nkeys[bhi] = rows;
+            if (p.sel) {
+              int32_t* so = p.sel + (int64_t)bhi * (p.wmax + 1);
+              so[0] = item.nsel;
+              for (int i = 0; i < p.wmax; ++i) so[1 + i] = i < item.nsel ? item.sel[i] : -1;
+            }
+          }
+          // append this step's k / v rows at position t
+          T* kc = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh;
+          T* vc = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh;
+          for (int c = lane; c < DH / VEC; c += 32) {
+            *reinterpret_cast<uint4*>(kc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.k + c * VEC);
+            *reinterpret_cast<uint4*>(vc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.v + c * VEC);
+          }
+          if (((t + 1) & (leaf - 1)) == 0)
+            tree_update_warp<T, DH>(kc, p.c_st, item.k, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, tu,
+                                    Cfg::TU_FLOATS, lane);
+        }
+        if (!got) ok = false;
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sh.pfree[par]);
+          mbar_arrive(&sh.iempty[slot]);
+        }
+        if (!got) break;
+      }
+      ++k;
+    }
+    if (!ok) atomicExch(&sh.abort_flag, 1);
+    if (warp == 0 && lane == 0) sh.consumed = it;
+    named_bar_sync(2, (NCW + 1) * 32);
+  }
 }
 
 }  // namespace ta

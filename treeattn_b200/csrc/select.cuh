@@ -46,22 +46,33 @@ struct Descent {
   static constexpr int G = DH / 4;    // lanes per node row (float4 each)
   static constexpr int NPP = 32 / G;  // node rows per warp pass
 
-  // Score the n candidates sc.cid[0..n) of level `lvl` (base pointer of that level for this (b,h)).
-  static __device__ __forceinline__ void score(const float* __restrict__ lvl, int n, float scale,
-                                               const float (&qv)[4], DescentScratch& sc, float* stage, int lane) {
-    const int chunks = n * G;
-    for (int x = lane; x < chunks; x += 32) {
+  // Async-copy the contiguous node rows [a, a+n) of one level into stage rows [r0, r0+n).
+  static __device__ __forceinline__ void stage_range(const float* __restrict__ lvl, int a, int n, float* stage,
+                                                     int r0, int lane) {
+    const float* src = lvl + (int64_t)a * DH;
+    float* dst = stage + (size_t)r0 * DH;
+    for (int x = lane; x < n * G; x += 32) cp_async16(dst + x * 4, src + x * 4);
+  }
+
+  // Async-copy the rows of candidates sc.cid[0..n) into stage rows [0, n).
+  static __device__ __forceinline__ void stage_gather(const float* __restrict__ lvl, int n, const DescentScratch& sc,
+                                                      float* stage, int lane) {
+    for (int x = lane; x < n * G; x += 32) {
       const int j = x / G, cc = x - (x / G) * G;
       cp_async16(stage + j * DH + cc * 4, lvl + (int64_t)sc.cid[j] * DH + cc * 4);
     }
-    cp_async_wait_all();
-    __syncwarp();
+  }
+
+  // Score candidates 0..n-1 (candidate j's row = stage + row_of(j) * DH) into sc.csc.
+  template <typename RowFn>
+  static __device__ __forceinline__ void score(int n, float scale, const float (&qv)[4], DescentScratch& sc,
+                                               const float* stage, RowFn row_of, int lane) {
     const int sub = lane / G, c = lane - (lane / G) * G;
     for (int base = 0; base < n; base += NPP) {
       const int j = base + sub;
       float s = 0.f;
       if (j < n) {
-        const float4 v = *reinterpret_cast<const float4*>(stage + j * DH + c * 4);
+        const float4 v = *reinterpret_cast<const float4*>(stage + (size_t)row_of(j) * DH + c * 4);
         s = qv[0] * v.x;
         s = fmaf(qv[1], v.y, s);
         s = fmaf(qv[2], v.z, s);
@@ -93,8 +104,12 @@ struct Descent {
   // If `sorted_out` or if more leaves are reachable than `keep_last`, the leaf level is scored and the ids are
   // best first with scores in sc.ksc; otherwise (everything reachable is kept) they are in ascending order
   // and sc.ksc is not written.
+  // `stage` holds stage_rows node rows (>= 2*wmax+1). From l* downwards, the whole reachable range of as many
+  // levels as fit is fetched in ONE round of async copies (levels below l* only ever hold candidates inside
+  // [a_l* << (l*-l), t >> l)); deeper levels are fetched level by level (children of the kept nodes only).
   static __device__ int run(const float* __restrict__ nodes_bh, const LevelView& lv, int t, int wmax, int keep_last,
-                            bool sorted_out, const float (&qv)[4], DescentScratch& sc, float* stage, int lane) {
+                            bool sorted_out, const float (&qv)[4], DescentScratch& sc, float* stage, int stage_rows,
+                            int lane) {
     const int Lm = lv.Lm, L0 = lv.L0;
     const int eLm = t >> Lm;
     const int aLm = eLm - (eLm & 1);
@@ -112,22 +127,38 @@ struct Descent {
       for (int j = lane; j < n; j += 32) sc.cid[j] = a + j;
       __syncwarp();
       if (n > 0 && (sorted_out || n > keep_last)) {
-        score(nodes_bh + (int64_t)lv.off[L0] * DH, n, pow2_neg(L0), qv, sc, stage, lane);
+        stage_range(nodes_bh + (int64_t)lv.off[L0] * DH, a, n, stage, 0, lane);
+        cp_async_wait_all();
+        __syncwarp();
+        score(n, pow2_neg(L0), qv, sc, stage, [](int j) { return j; }, lane);
         return topk(n, keep_last, sc, lane);
       }
       for (int j = lane; j < n; j += 32) sc.kid[j] = a + j;
       __syncwarp();
       return n;
     }
-    // first real selection: the whole reachable range of level l*
+    // prefetch plan: levels l*, l*-1, ..., lp (reachable ranges [a_l, e_l)), packed from stage row 0
+    const int astar = aLm << (Lm - lstar);
+    int lp = lstar, rows = 0;
+    for (int l = lstar; l >= L0; --l) {
+      const int n_l = (t >> l) - (astar << (lstar - l));
+      if (rows + n_l > stage_rows) break;
+      stage_range(nodes_bh + (int64_t)lv.off[l] * DH, astar << (lstar - l), n_l, stage, rows, lane);
+      rows += n_l;
+      lp = l;
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    // first real selection: the whole reachable range of level l* (stage rows 0..n-1)
     int nk;
+    int seg = 0;  // stage row of the first node of the current prefetched level
     {
-      const int a = aLm << (Lm - lstar), e = t >> lstar;
-      const int n = e - a;
-      for (int j = lane; j < n; j += 32) sc.cid[j] = a + j;
+      const int n = (t >> lstar) - astar;
+      for (int j = lane; j < n; j += 32) sc.cid[j] = astar + j;
       __syncwarp();
-      score(nodes_bh + (int64_t)lv.off[lstar] * DH, n, pow2_neg(lstar), qv, sc, stage, lane);
+      score(n, pow2_neg(lstar), qv, sc, stage, [](int j) { return j; }, lane);
       nk = topk(n, lstar == L0 ? keep_last : wmax, sc, lane);
+      seg = n;
     }
     for (int l = lstar - 1; l >= L0; --l) {
       const int bit = (t >> l) & 1;
@@ -139,7 +170,17 @@ struct Descent {
       if (bit && lane == 0) sc.cid[2 * nk] = (t >> l) - 1;
       __syncwarp();
       const int n = 2 * nk + bit;
-      score(nodes_bh + (int64_t)lv.off[l] * DH, n, pow2_neg(l), qv, sc, stage, lane);
+      const float* lvl = nodes_bh + (int64_t)lv.off[l] * DH;
+      if (l >= lp) {
+        const int base = seg - (astar << (lstar - l));  // row of node m = base + m
+        score(n, pow2_neg(l), qv, sc, stage, [&](int j) { return base + sc.cid[j]; }, lane);
+        seg += (t >> l) - (astar << (lstar - l));
+      } else {
+        stage_gather(lvl, n, sc, stage, lane);
+        cp_async_wait_all();
+        __syncwarp();
+        score(n, pow2_neg(l), qv, sc, stage, [](int j) { return j; }, lane);
+      }
       nk = topk(n, l == L0 ? keep_last : wmax, sc, lane);
     }
     return nk;
@@ -201,7 +242,7 @@ __global__ void __launch_bounds__(128) select_kernel(SelectParams p) {
   float qv[4];
   load_q4<QT, DH>(reinterpret_cast<const QT*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st, lane, qv);
   const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
-  const int nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, p.wmax, true, qv, sc, stage, lane);
+  const int nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, p.wmax, true, qv, sc, stage, 2 * p.wmax + 1, lane);
   for (int i = lane; i < p.wl; i += 32) {
     const bool ok = i < nk;
     p.ids[obase + i] = ok ? sc.kid[i] : 0;

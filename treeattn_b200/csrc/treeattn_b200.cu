@@ -2,6 +2,7 @@
 // Single translation unit: every kernel header is included here.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -222,10 +223,13 @@ int num_sms() {
   return g_num_sms;
 }
 
+// Decode mode for B*H (b, h) pairs: -1 = persistent pipelined kernel (enough pairs for every SM), otherwise the
+// number of CTAs per (b, h) of the cluster kernel (~4 resident CTAs per SM).
 int default_splits(int B, int H) {
   const int pairs = B * H;
   if (pairs <= 0) return 1;
-  const int target = 4 * num_sms();  // ~4 resident CTAs per SM
+  if (pairs >= num_sms()) return -1;
+  const int target = 4 * num_sms();
   int s = 1;
   while (s < 8 && pairs * s < target) s <<= 1;
   return s;
@@ -234,6 +238,8 @@ int default_splits(int B, int H) {
 template <typename T, int DH>
 struct Decode {
   static int run(ta::DecodeParams p, cudaStream_t st) {
+    if (p.B * p.H == 0) return TA_OK;
+    if (p.splits < 0) return persistent(p, st);
     using Sh = DecodeShape<T, DH>;
     auto kern = ta::decode_kernel<T, DH, Sh::CH, Sh::NST, Sh::NCW>;
     const size_t smem = ta::decode_smem_bytes<T, DH, Sh::CH, Sh::NST, Sh::NCW>(p.wmax);
@@ -245,7 +251,6 @@ struct Decode {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
       attr_set = true;
     }
-    if (p.B * p.H == 0) return TA_OK;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)p.splits, (unsigned)(p.B * p.H), 1);
     cfg.blockDim = dim3((Sh::NCW + 1) * 32, 1, 1);
@@ -261,6 +266,32 @@ struct Decode {
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_decode_step: launch failed: %s", cudaGetErrorString(e));
     return check_launch("ta_decode_step");
+  }
+
+  static int persistent(ta::DecodeParams p, cudaStream_t st) {
+    constexpr int ROWB = DH * (int)sizeof(T);
+    constexpr int CH = ROWB <= 128 ? 64 : 32;
+    constexpr int NST = 4, NCW = 4;
+    using Cfg = ta::PCfg<T, DH, CH, NST, NCW>;
+    auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCW>;
+    const int stage_rows = std::max(2 * p.wmax + 1, 32768 / (DH * 4));
+    const size_t smem = Cfg::smem_bytes(stage_rows);
+    if (smem > 220 * 1024) return fail(TA_ERR_ARG, "ta_decode_step: %zu B of shared memory needed", smem);
+    if ((1 << p.lv.L0) > Cfg::TU_FLOATS) return fail(TA_ERR_ARG, "ta_decode_step: leaf block too large");
+    static int per_sm = 0;
+    static size_t per_sm_smem = 0;
+    if (per_sm == 0 || per_sm_smem != smem) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::NTHREADS, smem);
+      if (per_sm < 1) per_sm = 1;
+      per_sm_smem = smem;
+    }
+    const int items = p.B * p.H;
+    const int gmax = per_sm * num_sms();
+    const int per_cta = (items + gmax - 1) / gmax;  // items per CTA (equal for all but the last few)
+    const int grid = (items + per_cta - 1) / per_cta;
+    kern<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
+    return check_launch("ta_decode_step(persistent)");
   }
 };
 
@@ -486,7 +517,7 @@ int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv
   if (n_tree < 0) return fail(TA_ERR_ARG, "ta_decode_step: n_tree < 0");
   if (Lw < 1) return fail(TA_ERR_ARG, "ta_decode_step: window %d < 1", Lw);
   if (splits == 0) splits = default_splits(B, H);
-  if (splits < 1 || splits > 8) return fail(TA_ERR_ARG, "ta_decode_step: splits=%d outside [1, 8]", splits);
+  if (splits < -1 || splits > 8) return fail(TA_ERR_ARG, "ta_decode_step: splits=%d outside [-1, 8]", splits);
   if (!qkv || !kc || !vc || !nodes || !pos || !out) return fail(TA_ERR_ARG, "ta_decode_step: null pointer");
   const int es = esize_of(dtype);
   if (!rows_aligned(qkv, es, {qkv_sb, k_ofs, v_ofs, (int64_t)dh}) || !rows_aligned(kc, es, {c_sb, c_sh, c_st}) ||
