@@ -106,7 +106,230 @@ struct WarpAttn {
       for (int i = 0; i < VEC; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
     }
   }
+
+  // This warp's share (row groups warp, warp + nw, ...) of n staged rows (row stride DH).
+  __device__ __forceinline__ void stage(const T* kst, const T* vst, int n, int warp, int nw) {
+    const int ngroups = ceil_div(n, RPW);
+    for (int g0 = warp; g0 < ngroups; g0 += 2 * nw) {
+      float kf[2][VEC], vf[2][VEC], sc[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int g = g0 + u * nw;
+        const int r = g * RPW + sub;
+        const bool valid = (g < ngroups) && (r < n);
+        if (valid) {
+          load_vec_f32<T>(kst + (size_t)r * DH + c * VEC, kf[u]);
+          load_vec_f32<T>(vst + (size_t)r * DH + c * VEC, vf[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) kf[u][i] = vf[u][i] = 0.f;
+        }
+        const float x = row_score(kf[u]);
+        sc[u] = valid ? x : -INFINITY;
+      }
+      update<2>(sc, vf);
+    }
+  }
+
+  // One row (k, v: DH elements each, any 16-byte aligned memory).
+  __device__ __forceinline__ void one_row(const T* k, const T* v) {
+    float kf[1][VEC], vf[1][VEC], sc[1];
+    load_vec_f32<T>(k + c * VEC, kf[0]);
+    load_vec_f32<T>(v + c * VEC, vf[0]);
+    const float x = row_score(kf[0]);
+    sc[0] = sub == 0 ? x : -INFINITY;
+    update<1>(sc, vf);
+  }
 };
+
+// ------------------------------------------------------------------------------------------------ packed math
+// bf16 / fp16 rows without widening: fma.rn.f32.{bf16,f16} multiplies two 16-bit values exactly and adds in fp32
+// with one rounding, i.e. the same result as widening both and using an fp32 FMA.
+template <typename T> struct Mixed;
+template <> struct Mixed<__nv_bfloat16> {
+  // c += a.lo*b.lo ; c += a.hi*b.hi   (a, b: packed pairs)
+  static __device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float c) {
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, al, bl, %0;\n\tfma.rn.f32.bf16 %0, ah, bh, %0;\n\t}"
+        : "+f"(c) : "r"(a), "r"(b));
+    return c;
+  }
+  // (c0, c1) += p * (v.lo, v.hi)   (p: one 16-bit value in the low half of pp)
+  static __device__ __forceinline__ void axpy2(uint32_t pp, uint32_t v, float& c0, float& c1) {
+    asm("{\n\t.reg .b16 pl, ph, vl, vh;\n\tmov.b32 {pl, ph}, %2;\n\tmov.b32 {vl, vh}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, pl, vl, %0;\n\tfma.rn.f32.bf16 %1, pl, vh, %1;\n\t}"
+        : "+f"(c0), "+f"(c1) : "r"(pp), "r"(v));
+  }
+  static __device__ __forceinline__ uint32_t pack(float p) {
+    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p));
+  }
+  static __device__ __forceinline__ float unpack(uint32_t pp) {
+    return __bfloat162float(__ushort_as_bfloat16((unsigned short)(pp & 0xffffu)));
+  }
+};
+template <> struct Mixed<__half> {
+  static __device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float c) {
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\tfma.rn.f32.f16 %0, ah, bh, %0;\n\t}"
+        : "+f"(c) : "r"(a), "r"(b));
+    return c;
+  }
+  static __device__ __forceinline__ void axpy2(uint32_t pp, uint32_t v, float& c0, float& c1) {
+    asm("{\n\t.reg .b16 pl, ph, vl, vh;\n\tmov.b32 {pl, ph}, %2;\n\tmov.b32 {vl, vh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, pl, vl, %0;\n\tfma.rn.f32.f16 %1, pl, vh, %1;\n\t}"
+        : "+f"(c0), "+f"(c1) : "r"(pp), "r"(v));
+  }
+  static __device__ __forceinline__ uint32_t pack(float p) {
+    return (uint32_t)__half_as_ushort(__float2half_rn(p));
+  }
+  static __device__ __forceinline__ float unpack(uint32_t pp) {
+    return __half2float(__ushort_as_half((unsigned short)(pp & 0xffffu)));
+  }
+};
+
+// Online softmax over rows staged in shared memory, 16-bit K/V. Lane layout as WarpAttn (LPR lanes per row, 8
+// elements = one 16-byte chunk per lane, RPW rows per warp pass). A call processes G row groups (G*RPW rows):
+//  * QK: each lane dots its chunk for the G groups (mixed FMAs, no widening), then ONE reduce-scatter across the
+//    LPR lanes of a row leaves lane c holding the full score of group c / (LPR/G) (log2(LPR) shuffle rounds,
+//    G-1 + log2(LPR/G) shuffles in total instead of G*log2(LPR));
+//  * one max / rescale per call; p = exp2(s - m) is rounded to the K/V type and used both in the numerator
+//    (mixed FMA with V) and in the running sum l, so the weights stay a convex combination.
+template <typename T, int DH>
+struct PackedAttn {
+  static constexpr int VEC = 8;
+  static constexpr int LPR = DH / VEC;
+  static constexpr int RPW = 32 / LPR;
+  static constexpr int G = LPR >= 4 ? 4 : LPR;
+  static constexpr int SPAN = LPR / G;  // lanes holding the same group after the reduce-scatter
+
+  uint32_t q2[4];  // this lane's query chunk, packed pairs (unscaled)
+  float acc[VEC];
+  float m, l;
+  float qscale;    // softmax scale * log2(e)
+  int sub, c;
+
+  __device__ __forceinline__ void init(const T* qrow, float scale_log2, int lane) {
+    sub = lane / LPR;
+    c = lane - sub * LPR;
+    const uint4 v = *reinterpret_cast<const uint4*>(qrow + c * VEC);
+    q2[0] = v.x; q2[1] = v.y; q2[2] = v.z; q2[3] = v.w;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+    m = -INFINITY;
+    l = 0.f;
+    qscale = scale_log2;
+  }
+
+  // Staged rows of the current call (registers), so the shared-memory stage can be released before the math.
+  uint4 kk[G], vv[G];
+  bool ok[G];
+
+  // Load rows r = (g0 + g) * RPW + sub for g < G (valid when r < n); K rows at kst, V rows at vst (stride DH).
+  __device__ __forceinline__ void load(const T* kst, const T* vst, int g0, int n) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int r = (g0 + g) * RPW + sub;
+      ok[g] = r < n;
+      kk[g] = vv[g] = make_uint4(0u, 0u, 0u, 0u);
+      if (ok[g]) {
+        kk[g] = *reinterpret_cast<const uint4*>(kst + (size_t)r * DH + c * VEC);
+        vv[g] = *reinterpret_cast<const uint4*>(vst + (size_t)r * DH + c * VEC);
+      }
+    }
+  }
+
+  // Online-softmax update with the loaded rows.
+  __device__ __forceinline__ void compute() {
+    float part[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float a = Mixed<T>::dot2(q2[0], kk[g].x, 0.f);
+      a = Mixed<T>::dot2(q2[1], kk[g].y, a);
+      a = Mixed<T>::dot2(q2[2], kk[g].z, a);
+      part[g] = Mixed<T>::dot2(q2[3], kk[g].w, a);
+    }
+    // reduce-scatter over the LPR lanes of a row: halve the value list while it has more than one entry
+    int nv = G;
+#pragma unroll
+    for (int o = LPR / 2; o >= 1; o >>= 1) {
+      if (nv > 1) {
+        const int h = nv / 2;
+        const bool up = (c & o) != 0;
+#pragma unroll
+        for (int j = 0; j < G / 2; ++j) {
+          if (j < h) {
+            const float keep = up ? part[j + h] : part[j];
+            const float send = up ? part[j] : part[j + h];
+            part[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        }
+        nv = h;
+      } else {
+        part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+      }
+    }
+    const int myg = c / SPAN;
+    bool myok = false;
+#pragma unroll
+    for (int g = 0; g < G; ++g) myok |= (g == myg) && ok[g];
+    const float s = myok ? part[0] * qscale : -INFINITY;
+    float mx = s;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float m_new = fmaxf(m, mx);
+    if (m_new == -INFINITY) return;  // nothing valid yet (warp-uniform)
+    const float alpha = exp2f(m - m_new);
+    const uint32_t pp = myok ? Mixed<T>::pack(exp2f(s - m_new)) : 0u;
+    l *= alpha;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] *= alpha;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint32_t pg = __shfl_sync(0xffffffffu, pp, sub * LPR + g * SPAN);
+      if (ok[g]) {
+        l += Mixed<T>::unpack(pg);
+        Mixed<T>::axpy2(pg, vv[g].x, acc[0], acc[1]);
+        Mixed<T>::axpy2(pg, vv[g].y, acc[2], acc[3]);
+        Mixed<T>::axpy2(pg, vv[g].z, acc[4], acc[5]);
+        Mixed<T>::axpy2(pg, vv[g].w, acc[6], acc[7]);
+      }
+    }
+    m = m_new;
+  }
+
+  __device__ __forceinline__ void groups(const T* kst, const T* vst, int g0, int n) {
+    load(kst, vst, g0, n);
+    compute();
+  }
+
+  __device__ __forceinline__ void reduce_rows() {
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1) {
+      l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    }
+  }
+
+  __device__ __forceinline__ void stage(const T* kst, const T* vst, int n, int warp, int nw) {
+    const int ngroups = ceil_div(n, RPW);
+    for (int gb = warp * G; gb < ngroups; gb += nw * G) groups(kst, vst, gb, n);
+  }
+
+  __device__ __forceinline__ void one_row(const T* k, const T* v) { groups(k, v, 0, 1); }
+};
+
+// Attention math used on staged rows: widening fp32 math for fp32 caches, packed mixed-precision math for 16-bit.
+template <typename T, int DH> struct StageAttn { using type = WarpAttn<T, DH>; };
+template <typename WA> struct EarlyRelease { static constexpr bool value = false; };
+template <typename T, int DH> struct EarlyRelease<PackedAttn<T, DH>> { static constexpr bool value = true; };
+// Rows one register-staged call of a warp covers (PackedAttn only).
+template <typename WA> struct RowsPerCall { static constexpr int value = 0; };
+template <typename T, int DH> struct RowsPerCall<PackedAttn<T, DH>> {
+  static constexpr int value = PackedAttn<T, DH>::G * PackedAttn<T, DH>::RPW;
+};
+template <int DH> struct StageAttn<__nv_bfloat16, DH> { using type = PackedAttn<__nv_bfloat16, DH>; };
+template <int DH> struct StageAttn<__half, DH> { using type = PackedAttn<__half, DH>; };
 
 // Merge partial softmax state b into a (both in the log2 domain).
 __device__ __forceinline__ void merge_state(float& ma, float& la, float* acca, float mb, float lb, const float* accb,

@@ -66,7 +66,7 @@ template <typename T, int DH, int CH, int NST, int NCW>
 __host__ __device__ inline size_t decode_smem_bytes(int wmax) {
   size_t off = (sizeof(DecodeShared) + 127) & ~(size_t)127;
   off += DecodeCfg<T, DH, CH, NST, NCW>::RING_BYTES;
-  off += (size_t)(2 * wmax + 1) * DH * sizeof(float);
+  off += (size_t)(2 * wmax + 1) * stage_row_floats<DH>() * sizeof(float);
   off += (size_t)NCW * DH * sizeof(float);
   off += (size_t)DH * sizeof(float);
   return off;
@@ -128,8 +128,8 @@ __device__ void tree_update_block(const T* __restrict__ kbase, int64_t c_st, con
 template <typename T, int DH, int CH, int NST, int NCW>
 __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) {
   using Cfg = DecodeCfg<T, DH, CH, NST, NCW>;
-  using WA = WarpAttn<T, DH>;
-  constexpr int VEC = WA::VEC, RPW = WA::RPW;
+  using WA = typename StageAttn<T, DH>::type;
+  constexpr int VEC = WA::VEC;
   constexpr int ROWB = DH * (int)sizeof(T);
   static_assert(NST <= 8 && NCW <= 8, "ring too deep");
 
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
   T* ring = reinterpret_cast<T*>(smem_raw + off);
   off += Cfg::RING_BYTES;
   float* dstage = reinterpret_cast<float*>(smem_raw + off);
-  off += (size_t)(2 * p.wmax + 1) * DH * sizeof(float);
+  off += (size_t)(2 * p.wmax + 1) * stage_row_floats<DH>() * sizeof(float);
   float* part_acc = reinterpret_cast<float*>(smem_raw + off);
   off += (size_t)NCW * DH * sizeof(float);
   float* cta_acc = reinterpret_cast<float*>(smem_raw + off);
@@ -272,11 +272,10 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
     if (warp == 0) {
       int nk = 0;
       if (active) {
-        float qv[4];
-        load_q4<T, DH>(qkv_row + h * DH, lane, qv);
+        load_qf<T, DH>(qkv_row + h * DH, sh.ds, lane);
         const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
         const int keep = min(p.n_tree, p.wmax);
-        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, 2 * p.wmax + 1, lane);
+        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, sh.ds, dstage, 2 * p.wmax + 1, lane);
         build_ranges(
             sh.rl, nk, [&](int i) -> int64_t { return sh.ds.kid[i]; }, leaf, t, p.Lw, w0, lane);
       } else if (lane == 0) {
@@ -288,9 +287,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
       named_bar_arrive(1, 64);
       if (rank == 0 && active) {
         // the new token (position t) from this step's k/v rows
-        const T* kr[1] = {wa.sub == 0 ? qkv_row + p.k_ofs + h * DH : nullptr};
-        const T* vr[1] = {wa.sub == 0 ? qkv_row + p.v_ofs + h * DH : nullptr};
-        wa.template rows_global<1>(kr, vr);
+        wa.one_row(qkv_row + p.k_ofs + h * DH, qkv_row + p.v_ofs + h * DH);
       }
     }
     // stream the ring
@@ -305,28 +302,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
       const int n = sh.nrows[s];
       if (n < 0) break;
       const T* kst = ring + (size_t)s * Cfg::STAGE_ELEMS;
-      const T* vst = kst + CH * DH;
-      const int ngroups = ceil_div(n, RPW);
-      for (int g0 = warp; g0 < ngroups; g0 += 2 * NCW) {
-        float kf[2][VEC], vf[2][VEC];
-        float sc[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int g = g0 + u * NCW;
-          const int r = g * RPW + wa.sub;
-          const bool valid = (g < ngroups) && (r < n);
-          if (valid) {
-            load_vec_f32<T>(kst + (size_t)r * DH + wa.c * VEC, kf[u]);
-            load_vec_f32<T>(vst + (size_t)r * DH + wa.c * VEC, vf[u]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) kf[u][i] = vf[u][i] = 0.f;
-          }
-          const float x = wa.row_score(kf[u]);
-          sc[u] = valid ? x : -INFINITY;
-        }
-        wa.template update<2>(sc, vf);
-      }
+      wa.stage(kst, kst + CH * DH, n, warp, NCW);
       if (warp == 0) rows_mine += n;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.empty[s]);
@@ -470,14 +446,17 @@ __global__ void __launch_bounds__(APPEND_THREADS) append_kernel(AppendParams p) 
 // ================================================================================================ persistent
 // Persistent, warp-specialized decode for large batches (B*H >= #SMs). CTA c owns the (b, h) items
 // c, c + G, c + 2G, ... (G = gridDim.x) and pipelines them:
-//   selector warp  : copies item k+1's q/k/v rows into a descriptor slot and runs its tree descent while item k
-//                    streams (descriptor ready -> mbarrier ifull[slot])
-//   producer warp  : 1-D bulk copies (no multicast) of item k's K/V rows into a ring of NST shared-memory stages -
-//                    the window rows first (they need no descent), then the used leaf blocks and the sink - and
-//                    an end-of-item marker stage
-//   consumer warps : online softmax over the ring; at the marker, warps 1.. hand their partial state to warp 0,
-//                    which merges it, writes the output, appends the new k/v rows and, when the new token completes
-//                    a leaf block, forms that leaf node and its right-spine ancestors (fp32, adjacent-pair order)
+//   selector warp    : copies item k+1's q/k/v rows into a descriptor slot and runs its tree descent while item k
+//                      streams (descriptor ready -> mbarrier ifull[slot])
+//   producer warp    : 1-D bulk copies (no multicast) of item k's K/V rows into a ring of NST shared-memory
+//                      stages - the window rows first (they need no descent), then the used leaf blocks and the
+//                      sink - and one end-of-item marker stage per consumer group
+//   consumer groups  : NCG groups of WPG warps take the stages in turn (stage i -> group i % NCG), so several
+//                      groups' math overlaps; a warp moves its rows of a stage into registers, frees the stage,
+//                      then runs the online softmax. At the end of an item every warp hands its partial state to
+//                      warp 0, which merges, writes the output, appends the new k/v rows and, when the new token
+//                      completes a leaf block, forms that leaf node and its right-spine ancestors (fp32,
+//                      adjacent-pair order)
 // Every wait between warps is a bounded mbarrier wait, so a protocol error ends in a recorded error, not a hang.
 constexpr int PSLOTS = 2;
 constexpr int STAGE_FIRST = 1, STAGE_LAST = 2;
@@ -490,27 +469,30 @@ struct __align__(16) PItem {
   int t, bh, nsel, active;
 };
 
-template <typename T, int DH, int NST, int NCW>
+template <typename T, int DH, int NST, int NCW, int NCG>
 struct __align__(16) PShared {
   PItem<T, DH> item[PSLOTS];
   DescentScratch ds;
   uint64_t full[NST], empty[NST], ifull[PSLOTS], iempty[PSLOTS], pready[2], pfree[2];
   int nrows[NST], slot[NST], flags[NST];
   float part_m[2][NCW], part_l[2][NCW];
-  int part_rows[2];
-  int consumed;
+  int part_rows[2][NCW];
+  int consumed[NCG];
   int abort_flag;
 };
 
-template <typename T, int DH, int CH, int NST, int NCW>
+template <typename T, int DH, int CH, int NST, int NCG, int WPG>
 struct PCfg {
+  static constexpr int NCW = NCG * WPG;
   static constexpr int NTHREADS = (NCW + 2) * 32;
   static constexpr int STAGE_ELEMS = 2 * CH * DH;
   static constexpr size_t RING_BYTES = (size_t)NST * STAGE_ELEMS * sizeof(T);
   static constexpr int TU_FLOATS = 2048;
+  using Sh = PShared<T, DH, NST, NCW, NCG>;
   static size_t smem_bytes(int stage_rows) {
-    size_t off = (sizeof(PShared<T, DH, NST, NCW>) + 127) & ~(size_t)127;
-    return off + RING_BYTES + (size_t)stage_rows * DH * 4 + (size_t)2 * NCW * DH * 4 + (size_t)TU_FLOATS * 4;
+    size_t off = (sizeof(Sh) + 127) & ~(size_t)127;
+    return off + RING_BYTES + (size_t)stage_rows * stage_row_floats<DH>() * 4 + (size_t)2 * NCW * DH * 4 +
+           (size_t)TU_FLOATS * 4;
   }
 };
 
@@ -561,14 +543,17 @@ __device__ void tree_update_warp(const T* __restrict__ kbase, int64_t c_st, cons
   }
 }
 
-template <typename T, int DH, int CH, int NST, int NCW>
-__global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
-  using Cfg = PCfg<T, DH, CH, NST, NCW>;
-  using Sh = PShared<T, DH, NST, NCW>;
-  using WA = WarpAttn<T, DH>;
-  constexpr int VEC = WA::VEC, RPW = WA::RPW;
+template <typename T, int DH, int CH, int NST, int NCG, int WPG>
+__global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
+  using Cfg = PCfg<T, DH, CH, NST, NCG, WPG>;
+  constexpr int NCW = Cfg::NCW;
+  using Sh = typename Cfg::Sh;
+  using WA = typename StageAttn<T, DH>::type;
+  constexpr int VEC = WA::VEC;
   constexpr int ROWB = DH * (int)sizeof(T);
-  static_assert(NCW >= 2 && NST <= 16, "pipeline shape");
+  // a warp's rows of a stage fit one register-staged call when early release is possible
+  constexpr bool EARLY = EarlyRelease<WA>::value && (CH <= WPG * RowsPerCall<WA>::value);
+  static_assert(NCW >= 2 && NST <= 16 && NST % NCG == 0, "pipeline shape");
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
@@ -576,7 +561,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
   T* ring = reinterpret_cast<T*>(smem_raw + off);
   off += Cfg::RING_BYTES;
   float* dstage = reinterpret_cast<float*>(smem_raw + off);
-  off += (size_t)stage_rows * DH * sizeof(float);
+  off += (size_t)stage_rows * stage_row_floats<DH>() * sizeof(float);
   float* part_acc = reinterpret_cast<float*>(smem_raw + off);  // [2][NCW][DH]
   off += (size_t)2 * NCW * DH * sizeof(float);
   float* tu = reinterpret_cast<float*>(smem_raw + off);
@@ -590,7 +575,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       mbar_init(&sh.full[s], 1);
-      mbar_init(&sh.empty[s], NCW);
+      mbar_init(&sh.empty[s], WPG);
     }
     for (int s = 0; s < PSLOTS; ++s) {
       mbar_init(&sh.ifull[s], 1);
@@ -600,7 +585,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
       mbar_init(&sh.pready[s], NCW - 1);
       mbar_init(&sh.pfree[s], 1);
     }
-    sh.consumed = 0;
+    for (int g = 0; g < NCG; ++g) sh.consumed[g] = g;
     sh.abort_flag = 0;
     fence_mbar_init();
   }
@@ -635,10 +620,9 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
       __syncwarp();
       int nk = 0;
       if (active) {
-        float qv[4];
-        load_q4<T, DH>(it.q, lane, qv);
+        load_qf<T, DH>(it.q, sh.ds, lane);
         const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
-        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, qv, sh.ds, dstage, stage_rows, lane);
+        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, sh.ds, dstage, stage_rows, lane);
         build_ranges(
             it.rl, nk, [&](int i) -> int64_t { return sh.ds.kid[i]; }, leaf, t, p.Lw, max(t - p.Lw + 1, 0), lane);
         for (int i = lane; i < nk; i += 32) it.sel[i] = sh.ds.kid[i];
@@ -676,15 +660,20 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
         const int w0 = max(t - p.Lw + 1, 0);
         const T* kbase = reinterpret_cast<const T*>(p.kc) + b * p.c_sb + h * p.c_sh;
         const T* vbase = reinterpret_cast<const T*>(p.vc) + b * p.c_sb + h * p.c_sh;
-        int first = STAGE_FIRST;
+        unsigned started = 0;  // consumer groups that saw a stage of item k
+        auto flag_first = [&]() -> int {
+          const int g = it % NCG;
+          const int f = (started >> g) & 1 ? 0 : STAGE_FIRST;
+          started |= 1u << g;
+          return f;
+        };
         for (int r0 = w0; active && r0 < t; r0 += CH) {  // window rows [w0, t)
           int s;
           if (!(ok = acquire(s))) break;
           const int n = min(CH, t - r0);
           sh.nrows[s] = n;
-          sh.flags[s] = first;
+          sh.flags[s] = flag_first();
           sh.slot[s] = slot;
-          first = 0;
           T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
           mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
           bulk_g2s_hint(kd, kbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
@@ -710,9 +699,8 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
             }
           }
           sh.nrows[s] = n;
-          sh.flags[s] = first;
+          sh.flags[s] = flag_first();
           sh.slot[s] = slot;
-          first = 0;
           T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
           mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
           int put = 0;
@@ -729,20 +717,22 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
           }
           ++it;
         }
-        if (!ok) break;
-        int s;  // end-of-item marker
-        if (!(ok = acquire(s))) break;
-        sh.nrows[s] = 0;
-        sh.flags[s] = first | STAGE_LAST;
-        sh.slot[s] = slot;
-        mbar_arrive(&sh.full[s]);
-        ++it;
+        for (int g = 0; g < NCG && ok; ++g) {  // one end-of-item marker per consumer group
+          int s;
+          if (!(ok = acquire(s))) break;
+          sh.nrows[s] = 0;
+          sh.flags[s] = flag_first() | STAGE_LAST;
+          sh.slot[s] = slot;
+          mbar_arrive(&sh.full[s]);
+          ++it;
+        }
       }
-      if (ok) {
+      for (int g = 0; g < NCG && ok; ++g) {  // one sentinel per consumer group
         int s;
         if ((ok = acquire(s))) {
           sh.nrows[s] = -1;
           mbar_arrive(&sh.full[s]);
+          ++it;
         }
       }
       if (!ok) atomicExch(&sh.abort_flag, 1);
@@ -750,12 +740,14 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
     __syncwarp();
     named_bar_sync(2, (NCW + 1) * 32);
     if (lane == 0) {  // no bulk copy of this CTA may still be in flight when it exits
-      for (int i = sh.consumed; i < it; ++i) mbar_wait_bounded(&sh.full[i % NST], (i / NST) & 1, K_DECODE, 2);
+      for (int i = 0; i < it; ++i)
+        if (i >= sh.consumed[i % NCG]) mbar_wait_bounded(&sh.full[i % NST], (i / NST) & 1, K_DECODE, 2);
     }
   } else {
     // ------------------------------------------------------------------ consumer warps
+    const int cg = warp / WPG, wig = warp - cg * WPG;
     WA wa;
-    int it = 0, k = 0, rows = 0;
+    int it = cg, k = 0, rows = 0;
     bool ok = true;
     while (true) {
       const int s = it % NST;
@@ -764,7 +756,10 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
         break;
       }
       const int n = sh.nrows[s];
-      if (n < 0) break;
+      if (n < 0) {
+        it += NCG;  // the sentinel counts as consumed
+        break;
+      }
       const int fl = sh.flags[s], slot = sh.slot[s];
       PItem<T, DH>& item = sh.item[slot];
       if (fl & STAGE_FIRST) {
@@ -775,43 +770,23 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
         wa.init(item.q, p.scale * LOG2E, lane);
         rows = 0;
         if (warp == 0 && item.active) {  // the new token, from this step's rows
-          float kf[1][VEC], vf[1][VEC], sc[1];
-          load_vec_f32<T>(item.k + wa.c * VEC, kf[0]);
-          load_vec_f32<T>(item.v + wa.c * VEC, vf[0]);
-          const float x = wa.row_score(kf[0]);
-          sc[0] = wa.sub == 0 ? x : -INFINITY;
-          wa.template update<1>(sc, vf);
+          wa.one_row(item.k, item.v);
           rows = 1;
         }
       }
-      if (n > 0) {
-        const T* kst = ring + (size_t)s * Cfg::STAGE_ELEMS;
-        const T* vst = kst + CH * DH;
-        const int ngroups = ceil_div(n, RPW);
-        for (int g0 = warp; g0 < ngroups; g0 += 2 * NCW) {
-          float kf[2][VEC], vf[2][VEC], sc[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int g = g0 + u * NCW;
-            const int r = g * RPW + wa.sub;
-            const bool valid = (g < ngroups) && (r < n);
-            if (valid) {
-              load_vec_f32<T>(kst + (size_t)r * DH + wa.c * VEC, kf[u]);
-              load_vec_f32<T>(vst + (size_t)r * DH + wa.c * VEC, vf[u]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < VEC; ++i) kf[u][i] = vf[u][i] = 0.f;
-            }
-            const float x = wa.row_score(kf[u]);
-            sc[u] = valid ? x : -INFINITY;
-          }
-          wa.template update<2>(sc, vf);
-        }
-        if (warp == 0) rows += n;
+      const T* kst = ring + (size_t)s * Cfg::STAGE_ELEMS;
+      if constexpr (EARLY) {
+        if (n > 0) wa.load(kst, kst + CH * DH, wig * WA::G, n);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.empty[s]);
+        if (n > 0) wa.compute();
+      } else {
+        if (n > 0) wa.stage(kst, kst + CH * DH, n, wig, WPG);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.empty[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.empty[s]);
-      ++it;
+      if (wig == 0) rows += n;
+      it += NCG;
       if (!(fl & STAGE_LAST)) continue;
       // ---------------------------------------------------------------- end of item k: merge + finalize
       const int par = k & 1;
@@ -825,6 +800,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
         if (lane == 0) {
           sh.part_m[par][warp] = wa.m;
           sh.part_l[par][warp] = wa.l;
+          sh.part_rows[par][warp] = wig == 0 ? rows : 0;
         }
         if (wa.sub == 0) {
 #pragma unroll
@@ -836,6 +812,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
         if (lane == 0) {
           sh.part_m[par][0] = wa.m;
           sh.part_l[par][0] = wa.l;
+          sh.part_rows[par][0] = rows;
         }
         if (wa.sub == 0) {
 #pragma unroll
@@ -848,8 +825,11 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
           float m = -INFINITY;
           for (int w = 0; w < NCW; ++w) m = fmaxf(m, sh.part_m[par][w]);
           float l = 0.f;
-          for (int w = 0; w < NCW; ++w)
+          int keys = 0;
+          for (int w = 0; w < NCW; ++w) {
             if (sh.part_m[par][w] != -INFINITY) l += sh.part_l[par][w] * exp2f(sh.part_m[par][w] - m);
+            keys += sh.part_rows[par][w];
+          }
           const float inv = l > 0.f ? 1.f / l : 0.f;
           T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
           for (int d = lane; d < DH; d += 32) {
@@ -861,7 +841,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
           const int bhi = item.bh;
           if (lane == 0) {
             if (p.lse) p.lse[bhi] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
-            if (p.nkeys) p.nkeys[bhi] = rows;
+            if (p.nkeys) p.nkeys[bhi] = keys;
             if (p.sel) {
               int32_t* so = p.sel + (int64_t)bhi * (p.wmax + 1);
               so[0] = item.nsel;
@@ -890,7 +870,7 @@ __global__ void __launch_bounds__((NCW + 2) * 32) decode_persistent_kernel(Decod
       ++k;
     }
     if (!ok) atomicExch(&sh.abort_flag, 1);
-    if (warp == 0 && lane == 0) sh.consumed = it;
+    if (wig == 0 && lane == 0) sh.consumed[cg] = it;
     named_bar_sync(2, (NCW + 1) * 32);
   }
 }

@@ -24,12 +24,17 @@ constexpr int CAND_LIMIT = 2 * WMAX_LIMIT + 1;  // largest candidate list of one
 
 // Per-warp shared scratch of one descent (the staged node rows live in a separate, host-sized buffer of
 // (2*wmax+1) * DH floats).
-struct DescentScratch {
+struct __align__(16) DescentScratch {
+  float qf[128];  // the query in fp32 (first DH entries), written by the caller before a descent
   int cid[CAND_LIMIT];
   float csc[CAND_LIMIT];
   int kid[WMAX_LIMIT];
   float ksc[WMAX_LIMIT];
 };
+
+// Staged node rows are padded to DH + 4 floats so that 8 lanes reading 8 different rows at the same column hit
+// 8 different bank groups (conflict-free lane-per-candidate scoring).
+template <int DH> __host__ __device__ constexpr int stage_row_floats() { return DH + 4; }
 
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
@@ -43,15 +48,17 @@ __device__ __forceinline__ float pow2_neg(int l) { return __int_as_float((127 - 
 
 template <int DH>
 struct Descent {
-  static constexpr int G = DH / 4;    // lanes per node row (float4 each)
-  static constexpr int NPP = 32 / G;  // node rows per warp pass
+  static constexpr int G = DH / 4;                      // 16-byte chunks per node row
+  static constexpr int SROW = stage_row_floats<DH>();  // staged row stride (floats)
 
   // Async-copy the contiguous node rows [a, a+n) of one level into stage rows [r0, r0+n).
   static __device__ __forceinline__ void stage_range(const float* __restrict__ lvl, int a, int n, float* stage,
                                                      int r0, int lane) {
     const float* src = lvl + (int64_t)a * DH;
-    float* dst = stage + (size_t)r0 * DH;
-    for (int x = lane; x < n * G; x += 32) cp_async16(dst + x * 4, src + x * 4);
+    for (int x = lane; x < n * G; x += 32) {
+      const int r = x / G, cc = x - (x / G) * G;
+      cp_async16(stage + (size_t)(r0 + r) * SROW + cc * 4, src + (size_t)x * 4);
+    }
   }
 
   // Async-copy the rows of candidates sc.cid[0..n) into stage rows [0, n).
@@ -59,27 +66,32 @@ struct Descent {
                                                       float* stage, int lane) {
     for (int x = lane; x < n * G; x += 32) {
       const int j = x / G, cc = x - (x / G) * G;
-      cp_async16(stage + j * DH + cc * 4, lvl + (int64_t)sc.cid[j] * DH + cc * 4);
+      cp_async16(stage + (size_t)j * SROW + cc * 4, lvl + (int64_t)sc.cid[j] * DH + cc * 4);
     }
   }
 
-  // Score candidates 0..n-1 (candidate j's row = stage + row_of(j) * DH) into sc.csc.
+  // Score candidates 0..n-1 (candidate j's row = stage + row_of(j) * SROW) into sc.csc: one lane per candidate,
+  // the query read from sc.qf by broadcast.
   template <typename RowFn>
-  static __device__ __forceinline__ void score(int n, float scale, const float (&qv)[4], DescentScratch& sc,
-                                               const float* stage, RowFn row_of, int lane) {
-    const int sub = lane / G, c = lane - (lane / G) * G;
-    for (int base = 0; base < n; base += NPP) {
-      const int j = base + sub;
-      float s = 0.f;
+  static __device__ __forceinline__ void score(int n, float scale, DescentScratch& sc, const float* stage,
+                                               RowFn row_of, int lane) {
+    for (int base = 0; base < n; base += 32) {
+      const int j = base + lane;
       if (j < n) {
-        const float4 v = *reinterpret_cast<const float4*>(stage + (size_t)row_of(j) * DH + c * 4);
-        s = qv[0] * v.x;
-        s = fmaf(qv[1], v.y, s);
-        s = fmaf(qv[2], v.z, s);
-        s = fmaf(qv[3], v.w, s);
+        const float* row = stage + (size_t)row_of(j) * SROW;
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < G; ++cc) {
+          const float4 qv = *reinterpret_cast<const float4*>(sc.qf + cc * 4);
+          const float4 v = *reinterpret_cast<const float4*>(row + cc * 4);
+          if (cc & 1) {
+            a1 = fmaf(qv.x, v.x, a1); a1 = fmaf(qv.y, v.y, a1); a1 = fmaf(qv.z, v.z, a1); a1 = fmaf(qv.w, v.w, a1);
+          } else {
+            a0 = fmaf(qv.x, v.x, a0); a0 = fmaf(qv.y, v.y, a0); a0 = fmaf(qv.z, v.z, a0); a0 = fmaf(qv.w, v.w, a0);
+          }
+        }
+        sc.csc[j] = (a0 + a1) * scale;
       }
-      s = warp_sum_sub(s, G);
-      if (c == 0 && j < n) sc.csc[j] = s * scale;
     }
     __syncwarp();
   }
@@ -107,9 +119,9 @@ struct Descent {
   // `stage` holds stage_rows node rows (>= 2*wmax+1). From l* downwards, the whole reachable range of as many
   // levels as fit is fetched in ONE round of async copies (levels below l* only ever hold candidates inside
   // [a_l* << (l*-l), t >> l)); deeper levels are fetched level by level (children of the kept nodes only).
+  // The query must be in sc.qf (fp32) before the call.
   static __device__ int run(const float* __restrict__ nodes_bh, const LevelView& lv, int t, int wmax, int keep_last,
-                            bool sorted_out, const float (&qv)[4], DescentScratch& sc, float* stage, int stage_rows,
-                            int lane) {
+                            bool sorted_out, DescentScratch& sc, float* stage, int stage_rows, int lane) {
     const int Lm = lv.Lm, L0 = lv.L0;
     const int eLm = t >> Lm;
     const int aLm = eLm - (eLm & 1);
@@ -130,7 +142,7 @@ struct Descent {
         stage_range(nodes_bh + (int64_t)lv.off[L0] * DH, a, n, stage, 0, lane);
         cp_async_wait_all();
         __syncwarp();
-        score(n, pow2_neg(L0), qv, sc, stage, [](int j) { return j; }, lane);
+        score(n, pow2_neg(L0), sc, stage, [](int j) { return j; }, lane);
         return topk(n, keep_last, sc, lane);
       }
       for (int j = lane; j < n; j += 32) sc.kid[j] = a + j;
@@ -156,7 +168,7 @@ struct Descent {
       const int n = (t >> lstar) - astar;
       for (int j = lane; j < n; j += 32) sc.cid[j] = astar + j;
       __syncwarp();
-      score(n, pow2_neg(lstar), qv, sc, stage, [](int j) { return j; }, lane);
+      score(n, pow2_neg(lstar), sc, stage, [](int j) { return j; }, lane);
       nk = topk(n, lstar == L0 ? keep_last : wmax, sc, lane);
       seg = n;
     }
@@ -173,13 +185,13 @@ struct Descent {
       const float* lvl = nodes_bh + (int64_t)lv.off[l] * DH;
       if (l >= lp) {
         const int base = seg - (astar << (lstar - l));  // row of node m = base + m
-        score(n, pow2_neg(l), qv, sc, stage, [&](int j) { return base + sc.cid[j]; }, lane);
+        score(n, pow2_neg(l), sc, stage, [&](int j) { return base + sc.cid[j]; }, lane);
         seg += (t >> l) - (astar << (lstar - l));
       } else {
         stage_gather(lvl, n, sc, stage, lane);
         cp_async_wait_all();
         __syncwarp();
-        score(n, pow2_neg(l), qv, sc, stage, [](int j) { return j; }, lane);
+        score(n, pow2_neg(l), sc, stage, [](int j) { return j; }, lane);
       }
       nk = topk(n, l == L0 ? keep_last : wmax, sc, lane);
     }
@@ -187,13 +199,11 @@ struct Descent {
   }
 };
 
-// Load this lane's 4 query dims (c*4 .. c*4+3, c = lane % (DH/4)) as fp32.
+// Widen a query row into the descent scratch (sc.qf) with a warp.
 template <typename QT, int DH>
-__device__ __forceinline__ void load_q4(const QT* __restrict__ q, int lane, float (&qv)[4]) {
-  constexpr int G = DH / 4;
-  const int c = lane % G;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) qv[i] = to_f32(q[c * 4 + i]);
+__device__ __forceinline__ void load_qf(const QT* __restrict__ q, DescentScratch& sc, int lane) {
+  for (int d = lane; d < DH; d += 32) sc.qf[d] = to_f32(q[d]);
+  __syncwarp();
 }
 
 // ------------------------------------------------------------------------------------------------ select kernel
@@ -215,7 +225,7 @@ __global__ void __launch_bounds__(128) select_kernel(SelectParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
-  const int stage_floats = (2 * p.wmax + 1) * DH;
+  const int stage_floats = (2 * p.wmax + 1) * stage_row_floats<DH>();
   DescentScratch* scr = reinterpret_cast<DescentScratch*>(smem_raw);
   float* stage_base = reinterpret_cast<float*>(smem_raw + sizeof(DescentScratch) * nwarps);
   DescentScratch& sc = scr[warp];
@@ -239,10 +249,9 @@ __global__ void __launch_bounds__(128) select_kernel(SelectParams p) {
     return;
   }
   const int t = (int)tt;
-  float qv[4];
-  load_q4<QT, DH>(reinterpret_cast<const QT*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st, lane, qv);
+  load_qf<QT, DH>(reinterpret_cast<const QT*>(p.q) + b * p.q_sb + h * p.q_sh + n * p.q_st, sc, lane);
   const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
-  const int nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, p.wmax, true, qv, sc, stage, 2 * p.wmax + 1, lane);
+  const int nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, p.wmax, true, sc, stage, 2 * p.wmax + 1, lane);
   for (int i = lane; i < p.wl; i += 32) {
     const bool ok = i < nk;
     p.ids[obase + i] = ok ? sc.kid[i] : 0;

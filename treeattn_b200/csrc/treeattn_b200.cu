@@ -120,7 +120,7 @@ struct Select {
     // 4 warps (queries) per CTA unless their staging rows would not fit in shared memory
     int warps = 4;
     auto smem_for = [&](int w) {
-      return sizeof(ta::DescentScratch) * w + (size_t)w * (2 * p.wmax + 1) * DH * sizeof(float);
+      return sizeof(ta::DescentScratch) * w + (size_t)w * (2 * p.wmax + 1) * ta::stage_row_floats<DH>() * sizeof(float);
     };
     while (warps > 1 && smem_for(warps) > 200 * 1024) warps >>= 1;
     const size_t smem = smem_for(warps);
@@ -271,10 +271,10 @@ struct Decode {
   static int persistent(ta::DecodeParams p, cudaStream_t st) {
     constexpr int ROWB = DH * (int)sizeof(T);
     constexpr int CH = ROWB <= 128 ? 64 : 32;
-    constexpr int NST = 4, NCW = 4;
-    using Cfg = ta::PCfg<T, DH, CH, NST, NCW>;
-    auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCW>;
-    const int stage_rows = std::max(2 * p.wmax + 1, 32768 / (DH * 4));
+    constexpr int NST = 4, NCG = 2, WPG = 4;
+    using Cfg = ta::PCfg<T, DH, CH, NST, NCG, WPG>;
+    auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG>;
+    const int stage_rows = std::max(2 * p.wmax + 1, 32768 / (ta::stage_row_floats<DH>() * 4));
     const size_t smem = Cfg::smem_bytes(stage_rows);
     if (smem > 220 * 1024) return fail(TA_ERR_ARG, "ta_decode_step: %zu B of shared memory needed", smem);
     if ((1 << p.lv.L0) > Cfg::TU_FLOATS) return fail(TA_ERR_ARG, "ta_decode_step: leaf block too large");
