@@ -484,7 +484,7 @@ struct __align__(16) PShared {
 template <typename T, int DH, int CH, int NST, int NCG, int WPG>
 struct PCfg {
   static constexpr int NCW = NCG * WPG;
-  static constexpr int NTHREADS = (NCW + 2) * 32;
+  static constexpr int NTHREADS = (NCW + 3) * 32;  // consumers, producer, selector, finalizer
   static constexpr int STAGE_ELEMS = 2 * CH * DH;
   static constexpr size_t RING_BYTES = (size_t)NST * STAGE_ELEMS * sizeof(T);
   static constexpr int TU_FLOATS = 2048;
@@ -544,7 +544,7 @@ __device__ void tree_update_warp(const T* __restrict__ kbase, int64_t c_st, cons
 }
 
 template <typename T, int DH, int CH, int NST, int NCG, int WPG>
-__global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
+__global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
   using Cfg = PCfg<T, DH, CH, NST, NCG, WPG>;
   constexpr int NCW = Cfg::NCW;
   using Sh = typename Cfg::Sh;
@@ -554,6 +554,7 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
   // a warp's rows of a stage fit one register-staged call when early release is possible
   constexpr bool EARLY = EarlyRelease<WA>::value && (CH <= WPG * RowsPerCall<WA>::value);
   static_assert(NCW >= 2 && NST <= 16 && NST % NCG == 0, "pipeline shape");
+  constexpr int W_PROD = NCW, W_SEL = NCW + 1, W_FIN = NCW + 2;
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
@@ -582,7 +583,7 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
       mbar_init(&sh.iempty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sh.pready[s], NCW - 1);
+      mbar_init(&sh.pready[s], NCW);
       mbar_init(&sh.pfree[s], 1);
     }
     for (int g = 0; g < NCG; ++g) sh.consumed[g] = g;
@@ -591,7 +592,7 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
   }
   __syncthreads();
 
-  if (warp == NCW + 1) {
+  if (warp == W_SEL) {
     // ------------------------------------------------------------------ selector warp
     const int keep = min(p.n_tree, p.wmax);
     for (int k = 0; k < K; ++k) {
@@ -639,7 +640,7 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.ifull[slot]);
     }
-  } else if (warp == NCW) {
+  } else if (warp == W_PROD) {
     // ------------------------------------------------------------------ producer warp (lane 0 issues)
     int it = 0;
     bool ok = true;
@@ -660,19 +661,24 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
         const int w0 = max(t - p.Lw + 1, 0);
         const T* kbase = reinterpret_cast<const T*>(p.kc) + b * p.c_sb + h * p.c_sh;
         const T* vbase = reinterpret_cast<const T*>(p.vc) + b * p.c_sb + h * p.c_sh;
-        unsigned started = 0;  // consumer groups that saw a stage of item k
-        auto flag_first = [&]() -> int {
+        unsigned started = 0, lasted = 0;  // consumer groups that got a FIRST / LAST stage of item k
+        // flags of the stage about to be issued (index it -> group it % NCG)
+        auto flags_for = [&](bool last) -> int {
           const int g = it % NCG;
-          const int f = (started >> g) & 1 ? 0 : STAGE_FIRST;
+          int f = ((started >> g) & 1) ? 0 : STAGE_FIRST;
           started |= 1u << g;
+          if (last && !((lasted >> g) & 1)) {
+            f |= STAGE_LAST;
+            lasted |= 1u << g;
+          }
           return f;
         };
-        for (int r0 = w0; active && r0 < t; r0 += CH) {  // window rows [w0, t)
+        for (int r0 = w0; active && r0 < t; r0 += CH) {  // window rows [w0, t) (their LAST is not known yet)
           int s;
           if (!(ok = acquire(s))) break;
           const int n = min(CH, t - r0);
           sh.nrows[s] = n;
-          sh.flags[s] = flag_first();
+          sh.flags[s] = flags_for(false);
           sh.slot[s] = slot;
           T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
           mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
@@ -683,8 +689,9 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
         if (!ok) break;
         if (!(ok = mbar_wait_bounded(&sh.ifull[slot], (k / PSLOTS) & 1, K_DECODE, 11))) break;
         const RangeList& rl = sh.item[slot].rl;
+        const int n_leaf_stages = ceil_div(rl.pref[rl.n], CH);
         int ri = 0, roff = 0;
-        while (ri < rl.n) {  // leaf blocks + sink, packed CH rows per stage
+        for (int j = 0; j < n_leaf_stages; ++j) {  // leaf blocks + sink, packed CH rows per stage
           int s;
           if (!(ok = acquire(s))) break;
           int n = 0;
@@ -699,7 +706,7 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
             }
           }
           sh.nrows[s] = n;
-          sh.flags[s] = flag_first();
+          sh.flags[s] = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
           sh.slot[s] = slot;
           T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
           mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
@@ -717,11 +724,11 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
           }
           ++it;
         }
-        for (int g = 0; g < NCG && ok; ++g) {  // one end-of-item marker per consumer group
+        while (ok && lasted != (1u << NCG) - 1u) {  // groups still without a LAST: empty end-of-item stages
           int s;
           if (!(ok = acquire(s))) break;
           sh.nrows[s] = 0;
-          sh.flags[s] = flag_first() | STAGE_LAST;
+          sh.flags[s] = flags_for(true);
           sh.slot[s] = slot;
           mbar_arrive(&sh.full[s]);
           ++it;
@@ -743,6 +750,60 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
       for (int i = 0; i < it; ++i)
         if (i >= sh.consumed[i % NCG]) mbar_wait_bounded(&sh.full[i % NST], (i / NST) & 1, K_DECODE, 2);
     }
+  } else if (warp == W_FIN) {
+    // ------------------------------------------------------------------ finalizer warp
+    for (int k = 0; k < K; ++k) {
+      const int slot = k % PSLOTS, par = k & 1;
+      if (!mbar_wait_bounded(&sh.pready[par], (k >> 1) & 1, K_DECODE, 6)) {
+        if (lane == 0) atomicExch(&sh.abort_flag, 1);
+        break;
+      }
+      PItem<T, DH>& item = sh.item[slot];
+      const float* pacc = part_acc + (size_t)par * NCW * DH;
+      if (item.active) {
+        const int b = item.bh / p.H, h = item.bh % p.H, t = item.t;
+        float m = -INFINITY;
+        for (int w = 0; w < NCW; ++w) m = fmaxf(m, sh.part_m[par][w]);
+        float l = 0.f;
+        int keys = 0;
+        for (int w = 0; w < NCW; ++w) {
+          if (sh.part_m[par][w] != -INFINITY) l += sh.part_l[par][w] * exp2f(sh.part_m[par][w] - m);
+          keys += sh.part_rows[par][w];
+        }
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
+        for (int d = lane; d < DH; d += 32) {
+          float a = 0.f;
+          for (int w = 0; w < NCW; ++w)
+            if (sh.part_m[par][w] != -INFINITY) a += pacc[w * DH + d] * exp2f(sh.part_m[par][w] - m);
+          orow[d] = from_f32<T>(a * inv);
+        }
+        if (lane == 0) {
+          if (p.lse) p.lse[item.bh] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
+          if (p.nkeys) p.nkeys[item.bh] = keys;
+          if (p.sel) {
+            int32_t* so = p.sel + (int64_t)item.bh * (p.wmax + 1);
+            so[0] = item.nsel;
+            for (int i = 0; i < p.wmax; ++i) so[1 + i] = i < item.nsel ? item.sel[i] : -1;
+          }
+        }
+        // append this step's k / v rows at position t
+        T* kc = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh;
+        T* vc = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh;
+        for (int c = lane; c < DH / VEC; c += 32) {
+          *reinterpret_cast<uint4*>(kc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.k + c * VEC);
+          *reinterpret_cast<uint4*>(vc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.v + c * VEC);
+        }
+        if (((t + 1) & (leaf - 1)) == 0)
+          tree_update_warp<T, DH>(kc, p.c_st, item.k, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, tu,
+                                  Cfg::TU_FLOATS, lane);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sh.pfree[par]);
+        mbar_arrive(&sh.iempty[slot]);
+      }
+    }
   } else {
     // ------------------------------------------------------------------ consumer warps
     const int cg = warp / WPG, wig = warp - cg * WPG;
@@ -761,12 +822,12 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
         break;
       }
       const int fl = sh.flags[s], slot = sh.slot[s];
-      PItem<T, DH>& item = sh.item[slot];
       if (fl & STAGE_FIRST) {
         if (!mbar_wait_bounded(&sh.ifull[slot], (k / PSLOTS) & 1, K_DECODE, 4)) {
           ok = false;
           break;
         }
+        PItem<T, DH>& item = sh.item[slot];
         wa.init(item.q, p.scale * LOG2E, lane);
         rows = 0;
         if (warp == 0 && item.active) {  // the new token, from this step's rows
@@ -788,85 +849,25 @@ __global__ void __launch_bounds__((NCG * WPG + 2) * 32) decode_persistent_kernel
       if (wig == 0) rows += n;
       it += NCG;
       if (!(fl & STAGE_LAST)) continue;
-      // ---------------------------------------------------------------- end of item k: merge + finalize
+      // ---------------------------------------------------------------- end of item k: hand the partial over
       const int par = k & 1;
       wa.reduce_rows();
       float* pacc = part_acc + (size_t)par * NCW * DH;
-      if (warp > 0) {
-        if (k >= 2 && !mbar_wait_bounded(&sh.pfree[par], ((k >> 1) - 1) & 1, K_DECODE, 5)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          sh.part_m[par][warp] = wa.m;
-          sh.part_l[par][warp] = wa.l;
-          sh.part_rows[par][warp] = wig == 0 ? rows : 0;
-        }
-        if (wa.sub == 0) {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) pacc[warp * DH + wa.c * VEC + i] = wa.acc[i];
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.pready[par]);
-      } else {
-        if (lane == 0) {
-          sh.part_m[par][0] = wa.m;
-          sh.part_l[par][0] = wa.l;
-          sh.part_rows[par][0] = rows;
-        }
-        if (wa.sub == 0) {
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) pacc[wa.c * VEC + i] = wa.acc[i];
-        }
-        __syncwarp();
-        const bool got = mbar_wait_bounded(&sh.pready[par], (k >> 1) & 1, K_DECODE, 6);
-        if (got && item.active) {
-          const int b = item.bh / p.H, h = item.bh % p.H, t = item.t;
-          float m = -INFINITY;
-          for (int w = 0; w < NCW; ++w) m = fmaxf(m, sh.part_m[par][w]);
-          float l = 0.f;
-          int keys = 0;
-          for (int w = 0; w < NCW; ++w) {
-            if (sh.part_m[par][w] != -INFINITY) l += sh.part_l[par][w] * exp2f(sh.part_m[par][w] - m);
-            keys += sh.part_rows[par][w];
-          }
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
-          for (int d = lane; d < DH; d += 32) {
-            float a = 0.f;
-            for (int w = 0; w < NCW; ++w)
-              if (sh.part_m[par][w] != -INFINITY) a += pacc[w * DH + d] * exp2f(sh.part_m[par][w] - m);
-            orow[d] = from_f32<T>(a * inv);
-          }
-          const int bhi = item.bh;
-          if (lane == 0) {
-            if (p.lse) p.lse[bhi] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
-            if (p.nkeys) p.nkeys[bhi] = keys;
-            if (p.sel) {
-              int32_t* so = p.sel + (int64_t)bhi * (p.wmax + 1);
-              so[0] = item.nsel;
-              for (int i = 0; i < p.wmax; ++i) so[1 + i] = i < item.nsel ? item.sel[i] : -1;
-            }
-          }
-          // append this step's k / v rows at position t
-          T* kc = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh;
-          T* vc = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh;
-          for (int c = lane; c < DH / VEC; c += 32) {
-            *reinterpret_cast<uint4*>(kc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.k + c * VEC);
-            *reinterpret_cast<uint4*>(vc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.v + c * VEC);
-          }
-          if (((t + 1) & (leaf - 1)) == 0)
-            tree_update_warp<T, DH>(kc, p.c_st, item.k, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, tu,
-                                    Cfg::TU_FLOATS, lane);
-        }
-        if (!got) ok = false;
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sh.pfree[par]);
-          mbar_arrive(&sh.iempty[slot]);
-        }
-        if (!got) break;
+      if (k >= 2 && !mbar_wait_bounded(&sh.pfree[par], ((k >> 1) - 1) & 1, K_DECODE, 5)) {
+        ok = false;
+        break;
       }
+      if (lane == 0) {
+        sh.part_m[par][warp] = wa.m;
+        sh.part_l[par][warp] = wa.l;
+        sh.part_rows[par][warp] = wig == 0 ? rows : 0;
+      }
+      if (wa.sub == 0) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) pacc[warp * DH + wa.c * VEC + i] = wa.acc[i];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.pready[par]);
       ++k;
     }
     if (!ok) atomicExch(&sh.abort_flag, 1);
