@@ -162,14 +162,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread is parked by the hardware until the phase completes (or
+// the hint, in ns, runs out) instead of spinning and taking issue slots from the warps doing the work.
+constexpr uint32_t TA_SUSPEND_HINT_NS = 0x989680u;  // 10 ms
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(TA_SUSPEND_HINT_NS)
       : "memory");
   return ok != 0;
 }
@@ -181,7 +185,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0 && global_timer_ns() - t0 > TA_WAIT_LIMIT_NS) {
+    if ((++spins & 3u) == 0 && global_timer_ns() - t0 > TA_WAIT_LIMIT_NS) {
       record_error(DEV_WAIT_TIMEOUT, kernel, where, (int)parity);
       return false;
     }

@@ -610,20 +610,25 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         if (lane == 0) record_error(DEV_POS_RANGE, K_DECODE, t, p.lv.cap);
         t = 0;
       }
+      // this step's q/k/v rows and the node rows of the descent (they depend on t only) in one round of async
+      // copies
       const T* row = reinterpret_cast<const T*>(p.qkv) + b * p.qkv_sb;
       constexpr int CPR = DH / VEC;  // 16-byte chunks per row
       for (int x = lane; x < 3 * CPR; x += 32) {
         const int part = x / CPR, c = x - (x / CPR) * CPR;
         const int64_t src = (part == 0 ? 0 : (part == 1 ? p.k_ofs : p.v_ofs)) + h * DH + c * VEC;
         T* dst = (part == 0 ? it.q : (part == 1 ? it.k : it.v)) + c * VEC;
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(row + src);
+        cp_async16(dst, row + src);
       }
+      const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
+      const typename Descent<DH>::Plan pl = Descent<DH>::plan(p.lv, t, p.wmax, stage_rows);
+      if (active) Descent<DH>::prefetch(nodes_bh, p.lv, t, pl, keep < (t >> p.lv.L0), dstage, lane);
+      cp_async_wait_all();
       __syncwarp();
       int nk = 0;
       if (active) {
         load_qf<T, DH>(it.q, sh.ds, lane);
-        const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
-        nk = Descent<DH>::run(nodes_bh, p.lv, t, p.wmax, keep, false, sh.ds, dstage, stage_rows, lane);
+        nk = Descent<DH>::select(nodes_bh, p.lv, t, pl, p.wmax, keep, false, sh.ds, dstage, lane);
         build_ranges(
             it.rl, nk, [&](int i) -> int64_t { return sh.ds.kid[i]; }, leaf, t, p.Lw, max(t - p.Lw + 1, 0), lane);
         for (int i = lane; i < nk; i += 32) it.sel[i] = sh.ds.kid[i];

@@ -26,11 +26,20 @@ constexpr int CAND_LIMIT = 2 * WMAX_LIMIT + 1;  // largest candidate list of one
 // (2*wmax+1) * DH floats).
 struct __align__(16) DescentScratch {
   float qf[128];  // the query in fp32 (first DH entries), written by the caller before a descent
+  unsigned long long ckey[CAND_LIMIT];  // order key of each scored candidate (see order_key)
   int cid[CAND_LIMIT];
   float csc[CAND_LIMIT];
   int kid[WMAX_LIMIT];
   float ksc[WMAX_LIMIT];
 };
+
+// One unsigned 64-bit key per candidate whose order is the library's total order on (score, id): higher score
+// first (scores mapped monotonically to unsigned, NaN as -inf), then the smaller node id.
+__device__ __forceinline__ unsigned long long order_key(float s, int id) {
+  uint32_t u = __float_as_uint(rank_key(s));
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (uint32_t)(0x7fffffff - id);
+}
 
 // Staged node rows are padded to DH + 4 floats so that 8 lanes reading 8 different rows at the same column hit
 // 8 different bank groups (conflict-free lane-per-candidate scoring).
@@ -90,58 +99,120 @@ struct Descent {
             a0 = fmaf(qv.x, v.x, a0); a0 = fmaf(qv.y, v.y, a0); a0 = fmaf(qv.z, v.z, a0); a0 = fmaf(qv.w, v.w, a0);
           }
         }
-        sc.csc[j] = (a0 + a1) * scale;
+        const float v = (a0 + a1) * scale;
+        sc.csc[j] = v;
+        sc.ckey[j] = order_key(v, sc.cid[j]);
       }
     }
     __syncwarp();
   }
 
   // Keep the best `keep` of the n scored candidates, best first, into sc.kid / sc.ksc. Returns the count.
-  static __device__ __forceinline__ int topk(int n, int keep, DescentScratch& sc, int lane) {
-    for (int j = lane; j < n; j += 32) {
-      const float sj = rank_key(sc.csc[j]);
-      const int ij = sc.cid[j];
-      int r = 0;
-      for (int i = 0; i < n; ++i) r += better(rank_key(sc.csc[i]), sc.cid[i], sj, ij) ? 1 : 0;
-      if (r < keep) {
-        sc.kid[r] = ij;
-        sc.ksc[r] = sc.csc[j];
+  // Lane j owns candidates j, j+32, ... (R per lane); a candidate's rank = how many keys beat it, counted over
+  // broadcast shared-memory reads of all n keys.
+  template <int R>
+  static __device__ __forceinline__ void topk_r(int n, int keep, DescentScratch& sc, int lane) {
+    unsigned long long mine[R];
+    int rank[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int j = r * 32 + lane;
+      mine[r] = j < n ? sc.ckey[j] : 0ull;
+      rank[r] = 0;
+    }
+#pragma unroll 8
+    for (int i = 0; i < n; ++i) {
+      const unsigned long long ki = sc.ckey[i];
+#pragma unroll
+      for (int r = 0; r < R; ++r) rank[r] += ki > mine[r] ? 1 : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int j = r * 32 + lane;
+      if (j < n && rank[r] < keep) {
+        sc.kid[rank[r]] = sc.cid[j];
+        sc.ksc[rank[r]] = sc.csc[j];
       }
+    }
+  }
+
+  static __device__ __forceinline__ int topk(int n, int keep, DescentScratch& sc, int lane) {
+    switch ((n + 31) >> 5) {
+      case 0: break;
+      case 1: topk_r<1>(n, keep, sc, lane); break;
+      case 2: topk_r<2>(n, keep, sc, lane); break;
+      case 3: topk_r<3>(n, keep, sc, lane); break;
+      case 4: topk_r<4>(n, keep, sc, lane); break;
+      default: topk_r<5>(n, keep, sc, lane); break;
     }
     __syncwarp();
     return n < keep ? n : keep;
   }
 
-  // Full descent for query position t. Returns the number of kept leaves; sc.kid[0..nk) holds the leaf ids.
-  // If `sorted_out` or if more leaves are reachable than `keep_last`, the leaf level is scored and the ids are
-  // best first with scores in sc.ksc; otherwise (everything reachable is kept) they are in ascending order
-  // and sc.ksc is not written.
-  // `stage` holds stage_rows node rows (>= 2*wmax+1). From l* downwards, the whole reachable range of as many
-  // levels as fit is fetched in ONE round of async copies (levels below l* only ever hold candidates inside
-  // [a_l* << (l*-l), t >> l)); deeper levels are fetched level by level (children of the kept nodes only).
-  // The query must be in sc.qf (fp32) before the call.
-  static __device__ int run(const float* __restrict__ nodes_bh, const LevelView& lv, int t, int wmax, int keep_last,
-                            bool sorted_out, DescentScratch& sc, float* stage, int stage_rows, int lane) {
+  // Where the descent starts (see run()): l* = -1 when every reachable leaf is kept without scoring.
+  struct Plan {
+    int lstar;  // first level that needs a real top-k, -1 if none
+    int astar;  // first reachable node of level l* (or of L0 when lstar < 0)
+    int lp;     // lowest level whose whole reachable range is prefetched
+  };
+
+  static __device__ __forceinline__ Plan plan(const LevelView& lv, int t, int wmax, int stage_rows) {
     const int Lm = lv.Lm, L0 = lv.L0;
     const int eLm = t >> Lm;
     const int aLm = eLm - (eLm & 1);
-    int lstar = -1;
+    Plan pl{-1, aLm << (Lm - L0), L0};
     for (int l = Lm; l >= L0; --l) {
       const int e = t >> l, a = aLm << (Lm - l);
       if (e - a > wmax) {
-        lstar = l;
+        pl.lstar = l;
+        pl.astar = a;
         break;
       }
     }
-    if (lstar < 0) {
-      const int a = aLm << (Lm - L0), e = t >> L0;
+    if (pl.lstar >= 0) {
+      int rows = 0;
+      pl.lp = pl.lstar;
+      for (int l = pl.lstar; l >= L0; --l) {
+        const int n_l = (t >> l) - (pl.astar << (pl.lstar - l));
+        if (rows + n_l > stage_rows) break;
+        rows += n_l;
+        pl.lp = l;
+      }
+    }
+    return pl;
+  }
+
+  // Issue (do not wait for) the async copies of the prefetched levels: [a_l, t >> l) for l in [lp, l*], packed
+  // from stage row 0. With lstar < 0 the leaf level's reachable range is staged when `need_l0` (it is scored).
+  static __device__ __forceinline__ void prefetch(const float* __restrict__ nodes_bh, const LevelView& lv, int t,
+                                                  const Plan& pl, bool need_l0, float* stage, int lane) {
+    if (pl.lstar < 0) {
+      const int n = (t >> lv.L0) - pl.astar;
+      if (need_l0 && n > 0) stage_range(nodes_bh + (int64_t)lv.off[lv.L0] * DH, pl.astar, n, stage, 0, lane);
+      return;
+    }
+    int rows = 0;
+    for (int l = pl.lstar; l >= pl.lp; --l) {
+      const int a_l = pl.astar << (pl.lstar - l);
+      const int n_l = (t >> l) - a_l;
+      stage_range(nodes_bh + (int64_t)lv.off[l] * DH, a_l, n_l, stage, rows, lane);
+      rows += n_l;
+    }
+  }
+
+  // The descent proper, after prefetch() completed (cp_async_wait_all + __syncwarp) and sc.qf holds the query.
+  // Returns the number of kept leaves; sc.kid[0..nk) holds the leaf ids. If `sorted_out` or if more leaves are
+  // reachable than `keep_last`, the leaf level is scored and the ids are best first with scores in sc.ksc;
+  // otherwise (everything reachable is kept) they are in ascending order and sc.ksc is not written.
+  static __device__ int select(const float* __restrict__ nodes_bh, const LevelView& lv, int t, const Plan& pl,
+                               int wmax, int keep_last, bool sorted_out, DescentScratch& sc, float* stage, int lane) {
+    const int L0 = lv.L0;
+    if (pl.lstar < 0) {
+      const int a = pl.astar, e = t >> L0;
       const int n = e - a;
       for (int j = lane; j < n; j += 32) sc.cid[j] = a + j;
       __syncwarp();
       if (n > 0 && (sorted_out || n > keep_last)) {
-        stage_range(nodes_bh + (int64_t)lv.off[L0] * DH, a, n, stage, 0, lane);
-        cp_async_wait_all();
-        __syncwarp();
         score(n, pow2_neg(L0), sc, stage, [](int j) { return j; }, lane);
         return topk(n, keep_last, sc, lane);
       }
@@ -149,19 +220,7 @@ struct Descent {
       __syncwarp();
       return n;
     }
-    // prefetch plan: levels l*, l*-1, ..., lp (reachable ranges [a_l, e_l)), packed from stage row 0
-    const int astar = aLm << (Lm - lstar);
-    int lp = lstar, rows = 0;
-    for (int l = lstar; l >= L0; --l) {
-      const int n_l = (t >> l) - (astar << (lstar - l));
-      if (rows + n_l > stage_rows) break;
-      stage_range(nodes_bh + (int64_t)lv.off[l] * DH, astar << (lstar - l), n_l, stage, rows, lane);
-      rows += n_l;
-      lp = l;
-    }
-    cp_async_wait_all();
-    __syncwarp();
-    // first real selection: the whole reachable range of level l* (stage rows 0..n-1)
+    const int lstar = pl.lstar, astar = pl.astar;
     int nk;
     int seg = 0;  // stage row of the first node of the current prefetched level
     {
@@ -182,13 +241,12 @@ struct Descent {
       if (bit && lane == 0) sc.cid[2 * nk] = (t >> l) - 1;
       __syncwarp();
       const int n = 2 * nk + bit;
-      const float* lvl = nodes_bh + (int64_t)lv.off[l] * DH;
-      if (l >= lp) {
+      if (l >= pl.lp) {
         const int base = seg - (astar << (lstar - l));  // row of node m = base + m
         score(n, pow2_neg(l), sc, stage, [&](int j) { return base + sc.cid[j]; }, lane);
         seg += (t >> l) - (astar << (lstar - l));
       } else {
-        stage_gather(lvl, n, sc, stage, lane);
+        stage_gather(nodes_bh + (int64_t)lv.off[l] * DH, n, sc, stage, lane);
         cp_async_wait_all();
         __syncwarp();
         score(n, pow2_neg(l), sc, stage, [](int j) { return j; }, lane);
@@ -196,6 +254,16 @@ struct Descent {
       nk = topk(n, l == L0 ? keep_last : wmax, sc, lane);
     }
     return nk;
+  }
+
+  // plan + prefetch + wait + select. The query must be in sc.qf (fp32) before the call.
+  static __device__ int run(const float* __restrict__ nodes_bh, const LevelView& lv, int t, int wmax, int keep_last,
+                            bool sorted_out, DescentScratch& sc, float* stage, int stage_rows, int lane) {
+    const Plan pl = plan(lv, t, wmax, stage_rows);
+    prefetch(nodes_bh, lv, t, pl, true, stage, lane);
+    cp_async_wait_all();
+    __syncwarp();
+    return select(nodes_bh, lv, t, pl, wmax, keep_last, sorted_out, sc, stage, lane);
   }
 };
 

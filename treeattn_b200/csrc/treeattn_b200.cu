@@ -274,7 +274,12 @@ struct Decode {
     constexpr int NST = 4, NCG = 2, WPG = 4;
     using Cfg = ta::PCfg<T, DH, CH, NST, NCG, WPG>;
     auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG>;
-    const int stage_rows = std::max(2 * p.wmax + 1, 32768 / (ta::stage_row_floats<DH>() * 4));
+    // descent staging rows: whatever keeps two CTAs per SM (111 KiB each), at least one full level (2*wmax+1)
+    const size_t row_bytes = (size_t)ta::stage_row_floats<DH>() * 4;
+    const size_t base = Cfg::smem_bytes(0);
+    const size_t budget = 111 * 1024;
+    const int fit = budget > base ? (int)((budget - base) / row_bytes) : 0;
+    const int stage_rows = std::max(2 * p.wmax + 1, std::min(fit, 256));
     const size_t smem = Cfg::smem_bytes(stage_rows);
     if (smem > 220 * 1024) return fail(TA_ERR_ARG, "ta_decode_step: %zu B of shared memory needed", smem);
     if ((1 << p.lv.L0) > Cfg::TU_FLOATS) return fail(TA_ERR_ARG, "ta_decode_step: leaf block too large");
