@@ -48,6 +48,9 @@ def parse():
     p.add_argument('--kernel-only', action='store_true',
                    help='time only the fused decode kernel on the config-4 shape (random caches of 4 layers, '
                         'rotated so that no launch finds its KV in L2) and print one JSON line')
+    p.add_argument('--gather-dot', action='store_true',
+                   help='configuration 2 instead: the block gather-dot kernel alone (B=8, H=12, dh=64, T=4096 bf16, '
+                        '16 sorted unique 64-token blocks per (b, h)); prints one JSON line')
     p.add_argument('--profile-steps', type=int, default=0,
                    help='profiling mode: after prefill and warm-up run this many eager decode steps between '
                         'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
@@ -130,6 +133,17 @@ class Clocks:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == 'Active'})
         return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=max(smax) if smax else None,
                     reasons=reasons, samples=len(rows))
+
+
+def profiled_traffic():
+    """DRAM bytes (read + write) per launch of the decode kernel from the committed ncu summary, or None."""
+    try:
+        for line in open(os.path.join(ROOT, 'profiles', 'decode_kernel_config4.md')):
+            if line.startswith('traffic_bytes_per_launch:'):
+                return float(line.split(':')[1])
+    except OSError:
+        pass
+    return None
 
 
 def measured_peaks():
@@ -244,6 +258,53 @@ def run_kernel_only(a, dev):
                           keys_per_head=float(nk.float().mean()))), flush=True)
 
 
+def run_gather_dot(a, dev):
+    """Configuration 2: per (b, h), scores of q against the 1024 keys of 16 selected 64-token blocks (fp32 out).
+    The 13 MB working set fits in L2, so ROT independent copies of K (> L2 in total) are cycled through."""
+    from treeattn_b200 import _ops
+    B, H, T, dh, blk, nblk = 8, 12, 4096, 64, 64, 16
+    ROT = 16
+    g = torch.Generator(device=dev).manual_seed(3)
+    Ks = [torch.randn(B, H, T, dh, device=dev, generator=g).to(torch.bfloat16) for _ in range(ROT)]
+    q = torch.randn(B, H, dh, device=dev, generator=g).to(torch.bfloat16)
+    blocks = torch.stack([torch.randperm(T // blk, device=dev, generator=g)[:nblk].sort().values
+                          for _ in range(B * H)]).view(B, H, nblk).int()
+    out = torch.empty(B, H, nblk * blk, device=dev, dtype=torch.float32)
+    for K in Ks:
+        _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=2, out=out)
+    torch.cuda.synchronize()
+    if a.profile_steps:
+        torch.cuda.cudart().cudaProfilerStart()
+        for K in Ks[:a.profile_steps]:
+            _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=2, out=out)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        return
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(gr, stream=s):
+        for K in Ks:
+            _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=2, out=out)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    gr.replay()
+    torch.cuda.synchronize()
+    reps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * ROT)
+    byts = B * H * nblk * blk * dh * 2 + B * H * dh * 2 + B * H * nblk * 4 + B * H * nblk * blk * 4
+    peaks = measured_peaks()
+    peak = peaks['hbm_gbs'] if peaks else 6650.0
+    print(json.dumps(dict(gather_dot=True, config='B=8 H=12 dh=64 T=4096 bf16, 16 blocks of 64 per (b,h)',
+                          kernel_us=us, bytes_per_call=byts, achieved_gbs=byts / us / 1e3, frac=byts / us / 1e3 / peak,
+                          rotated_copies=ROT)), flush=True)
+
+
 def run_reference(a, rank, world):
     if rank != 0:
         return
@@ -270,15 +331,18 @@ def main():
         run_reference(a, rank, world)
         return
     import torch.distributed as dist
+    from treeattn_b200 import dist as tdist
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group('nccl', timeout=timedelta(seconds=600), device_id=dev)
+        tdist.init('nccl', timeout_s=600, device=dev)
     from treeattn_b200 import _ops
     from treeattn_b200.engine import Decoder
     if a.kernel_only:
         run_kernel_only(a, dev)
+        return
+    if a.gather_dot:
+        run_gather_dot(a, dev)
         return
 
     B, T0, K, Wm = a.batch, a.prompt, a.steps, max(a.warmup, 3)
@@ -375,13 +439,9 @@ def main():
     del kg
 
     # ---------------------------------------------------------------- reduce over ranks
-    t = torch.tensor([ms, ms_e2e, kern_ms], device=dev, dtype=torch.float64)
+    ms, ms_e2e, kern_ms = tdist.max_over_ranks([ms, ms_e2e, kern_ms], dev)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        toks = dec.tokens.clone()
-        allt = [torch.empty_like(toks) for _ in range(world)]
-        dist.all_gather(allt, toks)  # generated tokens gathered off the hot path
-    ms, ms_e2e, kern_ms = t.tolist()
+        tdist.gather_rows(dec.tokens.view(-1, 1))  # generated tokens gathered off the hot path
     if rank == 0:
         peaks = measured_peaks()
         peak = peaks['hbm_gbs'] if peaks else 6650.0
@@ -401,7 +461,9 @@ def main():
                              d2h_bytes_per_step=B * 8),
                     gpu_launches=NL * K,
                     roofline=dict(bound='hbm', achieved=achieved, peak=peak, unit='GB/s', frac=achieved / peak,
-                                  traffic=None, kernel='ta_decode_step (decode_kernel<bf16,64>)',
+                                  traffic=profiled_traffic(), traffic_source='profiles/decode_kernel_config4.md (ncu, '
+                                  'same kernel and shape, t=4096)',
+                                  kernel='ta_decode_step (decode_persistent_kernel<bf16,64>)',
                                   kernel_us=kern_ms * 1e3, bytes_per_launch=sel_bytes,
                                   peak_source='MEASURED_PEAKS.json hbm_gbs (burst copy)' if peaks else 'fallback'),
                     clocks=ck)

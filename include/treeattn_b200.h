@@ -129,6 +129,19 @@ int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv
 /* The `splits` value ta_decode_step chooses for B*H (b, h) pairs on the current device (-1 = persistent). */
 int ta_decode_default_splits(int B, int H);
 
+/* Row kernels of the batched decode step around the attention (callers of the hot path):
+ * ta_embed_ln: x[b] = wte[tok[b]] + wpe[pos[b]] (fp32, (B, C)) and h[b] = LayerNorm(x[b]) * w in `dtype`
+ *   (reference model.py:75-77 and engine.py:165 embedding, model.py:12-18 LayerNorm without bias).
+ * ta_add_ln: x[b] += y[b] (y in `dtype`, NULL = no add), h[b] = LayerNorm(x[b]) * w (engine.py:175-176 residual
+ *   adds followed by ln2 / the next layer's ln1).
+ * ta_gelu: in-place exact (erf) GELU of n elements (model.py:31 F.gelu), n a multiple of 8.
+ * ta_argmax_advance: tok[b] = argmax(logits[b]) (first maximum), pos[b] += 1 (greedy step, phase2.py:61-62). */
+int ta_embed_ln(const void* wte, const void* wpe, int dtype, const int64_t* tok, const int32_t* pos, int B, int V,
+                int P, int C, const float* w, float eps, float* x, void* h, void* stream);
+int ta_add_ln(float* x, const void* y, int dtype, int B, int C, const float* w, float eps, void* h, void* stream);
+int ta_gelu(void* x, int dtype, int64_t n, void* stream);
+int ta_argmax_advance(const void* logits, int dtype, int B, int V, int64_t* tok, int32_t* pos, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,10 @@ SIGNATURES = {
     'ta_decode_step': [P, I, I, I, I, L, L, L, P, P, L, L, L, P, L, L, I, I, I, P, I, I, I, F, P, L, P, P, P, I,
                        P],
     'ta_decode_default_splits': [I, I],
+    'ta_embed_ln': [P, P, I, P, P, I, I, I, I, P, F, P, P, P],
+    'ta_add_ln': [P, P, I, I, I, P, F, P, P],
+    'ta_gelu': [P, I, L, P],
+    'ta_argmax_advance': [P, I, I, I, P, P, P],
 }
 _RESTYPES = {'ta_last_error': ctypes.c_char_p, 'ta_level_nodes': c_int64}
 

@@ -288,6 +288,31 @@ def decode_step(qkv, kc, vc, levels, pos, H, wmax, n_tree, Lw, scale, out, lse=N
               _p(sel), int(splits), _stream(qkv))
 
 
+def embed_ln(wte, wpe, tok, pos, w, x_out, h_out, eps=1e-5):
+    """x_out = wte[tok] + wpe[pos] (fp32), h_out = LayerNorm(x_out) * w (h_out's dtype, same as the tables)."""
+    B, C = x_out.shape
+    _lib.call('ta_embed_ln', _p(wte), _p(wpe), _code(wte), _p(tok), _p(pos), B, wte.shape[0], wpe.shape[0], C, _p(w),
+              float(eps), _p(x_out), _p(h_out), _stream(x_out))
+
+
+def add_ln(x, y, w, h_out, eps=1e-5):
+    """x += y (if y is not None), h_out = LayerNorm(x) * w in h_out's dtype. x: (B, C) fp32 contiguous."""
+    B, C = x.shape
+    _lib.call('ta_add_ln', _p(x), _p(y), _code(h_out), B, C, _p(w), float(eps), _p(h_out), _stream(x))
+
+
+def gelu_(x):
+    """In-place exact GELU (contiguous tensor, numel a multiple of 8)."""
+    _lib.call('ta_gelu', _p(x), _code(x), x.numel(), _stream(x))
+    return x
+
+
+def argmax_advance(logits, tok, pos):
+    """tok = logits.argmax(-1), pos += 1 (one fused launch)."""
+    B, V = logits.shape
+    _lib.call('ta_argmax_advance', _p(logits), _code(logits), B, V, _p(tok), _p(pos), _stream(logits))
+
+
 def default_splits(B, H):
     return _lib.load().ta_decode_default_splits(B, H)
 

@@ -48,6 +48,7 @@ enum KernelId : int {
   K_APPEND = 8,
   K_DECODE = 9,
   K_FINISH = 10,
+  K_ROWS = 11,
 };
 
 // ------------------------------------------------------------------------------------------------ types

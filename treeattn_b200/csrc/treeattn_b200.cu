@@ -9,6 +9,7 @@
 
 #include "../../include/treeattn_b200.h"
 #include "decode.cuh"
+#include "model_ops.cuh"
 
 namespace {
 
@@ -300,6 +301,59 @@ struct Decode {
   }
 };
 
+template <typename T, int MAXV>
+int launch_embed(const void* wte, const void* wpe, const int64_t* tok, const int32_t* pos, int B, int V, int P, int C,
+                 const float* w, float eps, float* x, void* h, cudaStream_t st) {
+  ta::embed_ln_kernel<T, MAXV><<<B, ta::ROW_THREADS, 0, st>>>(reinterpret_cast<const T*>(wte),
+                                                                reinterpret_cast<const T*>(wpe), tok, pos, V, P, C, w,
+                                                                eps, x, reinterpret_cast<T*>(h));
+  return check_launch("ta_embed_ln");
+}
+
+template <typename T>
+int embed_by_c(const void* wte, const void* wpe, const int64_t* tok, const int32_t* pos, int B, int V, int P, int C,
+               const float* w, float eps, float* x, void* h, cudaStream_t st) {
+  const int need = (C + ta::ROW_THREADS - 1) / ta::ROW_THREADS;
+  if (need <= 1) return launch_embed<T, 1>(wte, wpe, tok, pos, B, V, P, C, w, eps, x, h, st);
+  if (need <= 2) return launch_embed<T, 2>(wte, wpe, tok, pos, B, V, P, C, w, eps, x, h, st);
+  if (need <= 4) return launch_embed<T, 4>(wte, wpe, tok, pos, B, V, P, C, w, eps, x, h, st);
+  if (need <= 8) return launch_embed<T, 8>(wte, wpe, tok, pos, B, V, P, C, w, eps, x, h, st);
+  if (need <= 16) return launch_embed<T, 16>(wte, wpe, tok, pos, B, V, P, C, w, eps, x, h, st);
+  return fail(TA_ERR_ARG, "row width %d above 4096", C);
+}
+
+template <typename T>
+int add_ln_by_c(float* x, const void* y, int B, int C, const float* w, float eps, void* h, cudaStream_t st) {
+  const int need = (C + 255) / 256;  // 16-byte chunks per lane
+  const int blocks = (B + 3) / 4;
+  const T* yy = reinterpret_cast<const T*>(y);
+  T* hh = reinterpret_cast<T*>(h);
+  if (need <= 1) ta::add_ln_warp_kernel<T, 1><<<blocks, 128, 0, st>>>(x, yy, B, C, w, eps, hh);
+  else if (need <= 2) ta::add_ln_warp_kernel<T, 2><<<blocks, 128, 0, st>>>(x, yy, B, C, w, eps, hh);
+  else if (need <= 4) ta::add_ln_warp_kernel<T, 4><<<blocks, 128, 0, st>>>(x, yy, B, C, w, eps, hh);
+  else if (need <= 8) ta::add_ln_warp_kernel<T, 8><<<blocks, 128, 0, st>>>(x, yy, B, C, w, eps, hh);
+  else return fail(TA_ERR_ARG, "ta_add_ln: row width %d above 2048", C);
+  return check_launch("ta_add_ln");
+}
+
+int rows_dispatch(int dtype, int kind, const void* a0, const void* a1, const int64_t* tok, const int32_t* pos, int B,
+                  int V, int P, int C, const float* w, float eps, float* x, void* h, cudaStream_t st) {
+  if (kind == 1 && (C % 8 != 0 || !aligned16(x) || !aligned16(h) || (a1 && !aligned16(a1))))
+    return fail(TA_ERR_ARG, "ta_add_ln: rows must be multiples of 8 elements and 16-byte aligned");
+  switch (dtype) {
+    case TA_F32:
+      return kind == 0 ? embed_by_c<float>(a0, a1, tok, pos, B, V, P, C, w, eps, x, h, st)
+                       : add_ln_by_c<float>(x, a1, B, C, w, eps, h, st);
+    case TA_BF16:
+      return kind == 0 ? embed_by_c<__nv_bfloat16>(a0, a1, tok, pos, B, V, P, C, w, eps, x, h, st)
+                       : add_ln_by_c<__nv_bfloat16>(x, a1, B, C, w, eps, h, st);
+    case TA_F16:
+      return kind == 0 ? embed_by_c<__half>(a0, a1, tok, pos, B, V, P, C, w, eps, x, h, st)
+                       : add_ln_by_c<__half>(x, a1, B, C, w, eps, h, st);
+    default: return fail(TA_ERR_ARG, "bad dtype %d", dtype);
+  }
+}
+
 }  // namespace
 
 // ================================================================================================== C ABI
@@ -508,6 +562,51 @@ int ta_append(const void* k, const void* v, int dtype, int B, int H, int dh, int
 }
 
 int ta_decode_default_splits(int B, int H) { return default_splits(B, H); }
+
+int ta_embed_ln(const void* wte, const void* wpe, int dtype, const int64_t* tok, const int32_t* pos, int B, int V,
+                int P, int C, const float* w, float eps, float* x, void* h, void* stream) {
+  g_err.clear();
+  if (!wte || !wpe || !tok || !pos || !w || !x || !h) return fail(TA_ERR_ARG, "ta_embed_ln: null pointer");
+  if (B < 0 || V < 1 || P < 1 || C < 1) return fail(TA_ERR_ARG, "ta_embed_ln: bad sizes");
+  if (B == 0) return TA_OK;
+  return rows_dispatch(dtype, 0, wte, wpe, tok, pos, B, V, P, C, w, eps, x, h, S(stream));
+}
+
+int ta_add_ln(float* x, const void* y, int dtype, int B, int C, const float* w, float eps, void* h, void* stream) {
+  g_err.clear();
+  if (!x || !w || !h) return fail(TA_ERR_ARG, "ta_add_ln: null pointer");
+  if (B < 0 || C < 1) return fail(TA_ERR_ARG, "ta_add_ln: bad sizes");
+  if (B == 0) return TA_OK;
+  return rows_dispatch(dtype, 1, nullptr, y, nullptr, nullptr, B, 0, 0, C, w, eps, x, h, S(stream));
+}
+
+int ta_gelu(void* x, int dtype, int64_t n, void* stream) {
+  g_err.clear();
+  if (!x || n < 0 || n % 8 != 0 || !aligned16(x)) return fail(TA_ERR_ARG, "ta_gelu: bad arguments");
+  if (n == 0) return TA_OK;
+  const unsigned blocks = (unsigned)((n / 8 + 255) / 256);
+  switch (dtype) {
+    case TA_F32: ta::gelu_kernel<float><<<blocks, 256, 0, S(stream)>>>(reinterpret_cast<float*>(x), n); break;
+    case TA_BF16: ta::gelu_kernel<__nv_bfloat16><<<blocks, 256, 0, S(stream)>>>(reinterpret_cast<__nv_bfloat16*>(x), n); break;
+    case TA_F16: ta::gelu_kernel<__half><<<blocks, 256, 0, S(stream)>>>(reinterpret_cast<__half*>(x), n); break;
+    default: return fail(TA_ERR_ARG, "ta_gelu: bad dtype %d", dtype);
+  }
+  return check_launch("ta_gelu");
+}
+
+int ta_argmax_advance(const void* logits, int dtype, int B, int V, int64_t* tok, int32_t* pos, void* stream) {
+  g_err.clear();
+  if (!logits || !tok || !pos) return fail(TA_ERR_ARG, "ta_argmax_advance: null pointer");
+  if (B < 0 || V < 1) return fail(TA_ERR_ARG, "ta_argmax_advance: bad sizes");
+  if (B == 0) return TA_OK;
+  switch (dtype) {
+    case TA_F32: ta::argmax_advance_kernel<float><<<B, ta::ARG_THREADS, 0, S(stream)>>>(reinterpret_cast<const float*>(logits), V, tok, pos); break;
+    case TA_BF16: ta::argmax_advance_kernel<__nv_bfloat16><<<B, ta::ARG_THREADS, 0, S(stream)>>>(reinterpret_cast<const __nv_bfloat16*>(logits), V, tok, pos); break;
+    case TA_F16: ta::argmax_advance_kernel<__half><<<B, ta::ARG_THREADS, 0, S(stream)>>>(reinterpret_cast<const __half*>(logits), V, tok, pos); break;
+    default: return fail(TA_ERR_ARG, "ta_argmax_advance: bad dtype %d", dtype);
+  }
+  return check_launch("ta_argmax_advance");
+}
 
 int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,
                    void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st, float* nodes, int64_t n_sb,

@@ -164,30 +164,44 @@ class Decoder:
                        for _ in range(self.nl)]
         self._tok = torch.zeros(B, device=dev, dtype=torch.int64)
         self._pos = torch.zeros(B, device=dev, dtype=torch.int32)
-        self._qkv = torch.empty(B, 3 * C, device=dev, dtype=self.dtype)
-        self._att = torch.empty(B, C, device=dev, dtype=self.dtype)
+        dt = self.dtype
+        self._x = torch.empty(B, C, device=dev, dtype=torch.float32)   # residual stream (fp32)
+        self._h = torch.empty(B, C, device=dev, dtype=dt)               # layer-norm output
+        self._qkv = torch.empty(B, 3 * C, device=dev, dtype=dt)
+        self._att = torch.empty(B, C, device=dev, dtype=dt)
+        self._proj = torch.empty(B, C, device=dev, dtype=dt)
+        self._fc = torch.empty(B, 4 * C, device=dev, dtype=dt)
+        self._mlp = torch.empty(B, C, device=dev, dtype=dt)
+        self._logits = torch.empty(B, self.W['wte'].shape[0], device=dev, dtype=dt)
         self._nkeys = torch.zeros(self.nl, B, self.H, device=dev, dtype=torch.int32)
-        self._logits = None
         self._graph = None
         self._graph_greedy = None
 
     # -------------------------------------------------------------- one model step on the static buffers
     def _forward_step(self):
-        W, dt = self.W, self.dtype
-        x = W['wte'].index_select(0, self._tok).float() + W['wpe'].index_select(0, self._pos.long()).float()
-        for i, L in enumerate(W['layers']):
+        """Logits (B, V) of the tokens in self._tok at positions self._pos; appends their K/V to every layer.
+        Per layer: [x += mlp; h = ln1(x)] qkv-matmul, fused decode attention, c_proj-matmul, [x += proj;
+        h = ln2(x)], c_fc-matmul, GELU, c_mlp-matmul (the bracketed steps are single launches)."""
+        W = self.W
+        L = W['layers']
+        _ops.embed_ln(W['wte'], W['wpe'], self._tok, self._pos, L[0]['ln1'], self._x, self._h)
+        for i, Li in enumerate(L):
             st = self.states[i]
-            torch.mm(_ln(x, L['ln1']).to(dt), L['c_attn'].t(), out=self._qkv)
+            torch.mm(self._h, Li['c_attn'].t(), out=self._qkv)
             _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree, self.Lw,
                              self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits)
-            x = x + F.linear(self._att, L['c_proj']).float()
-            x = x + F.linear(F.gelu(F.linear(_ln(x, L['ln2']).to(dt), L['c_fc'])), L['c_mlp']).float()
-        return F.linear(_ln(x, W['ln_f']).to(dt), W['wte'])
+            torch.mm(self._att, Li['c_proj'].t(), out=self._proj)
+            _ops.add_ln(self._x, self._proj, Li['ln2'], self._h)
+            torch.mm(self._h, Li['c_fc'].t(), out=self._fc)
+            torch.mm(_ops.gelu_(self._fc), Li['c_mlp'].t(), out=self._mlp)
+            nxt = L[i + 1]['ln1'] if i + 1 < len(L) else W['ln_f']
+            _ops.add_ln(self._x, self._mlp, nxt, self._h)
+        torch.mm(self._h, W['wte'].t(), out=self._logits)
+        return self._logits
 
     def _greedy_step(self):
         logits = self._forward_step()
-        self._tok.copy_(logits.argmax(-1))
-        self._pos.add_(1)
+        _ops.argmax_advance(logits, self._tok, self._pos)
         return logits
 
     def _capture(self, fn):
@@ -220,7 +234,7 @@ class Decoder:
         snap = self._snapshot()
         self._forward_step()  # warm-up outside capture (library attribute setup, cuBLAS handles)
         self._restore(snap)
-        self._graph, self._logits = self._capture(self._forward_step)
+        self._graph, _ = self._capture(self._forward_step)
         self._restore(snap)
         self._graph_greedy, _ = self._capture(self._greedy_step)
         self._restore(snap)
