@@ -45,6 +45,9 @@ def parse():
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
     p.add_argument('--splits', type=int, default=0, help='CTAs per (b, h) in the decode kernel (0 = auto)')
+    p.add_argument('--config5', action='store_true',
+                   help='with --kernel-only: the configuration-5 shape (dh 128, 128-token leaves, top-32, window 256, '
+                        '32768-token context, Tcap 65536, 16 heads); --batch is per GPU (32 = 256 over 8 GPUs)')
     p.add_argument('--kernel-only', action='store_true',
                    help='time only the fused decode kernel on the config-4 shape (random caches of 4 layers, '
                         'rotated so that no launch finds its KV in L2) and print one JSON line')
@@ -202,27 +205,34 @@ def run_kernel_only(a, dev):
     launches are bracketed by cudaProfilerStart/Stop for ncu."""
     from treeattn_b200 import _ops
     from treeattn_b200._ops import Levels
-    B, T0, dh = a.batch, a.prompt, C // H
-    L0, Lm = int(math.log2(LEAF)), int(math.log2(TCAP)) - 1
+    if a.config5:
+        Hh, dh, leaf, topk, window, tcap = 16, 128, 128, 32, 256, 65536
+        B, T0 = a.batch if a.batch != 64 else 32, 32768
+    else:
+        Hh, dh, leaf, topk, window, tcap = H, C // H, LEAF, TOPK, WINDOW, TCAP
+        B, T0 = a.batch, a.prompt
+    Cm = Hh * dh
+    L0, Lm = int(math.log2(leaf)), int(math.log2(tcap)) - 1
     cap = T0 + 64
     nlay = 4
     g = torch.Generator(device=dev).manual_seed(7)
     layers = []
     for _ in range(nlay):
-        K = (torch.randn(B, H, cap, dh, device=dev, generator=g) * 0.5).to(torch.bfloat16)
-        Vv = torch.randn(B, H, cap, dh, device=dev, generator=g).to(torch.bfloat16)
-        lv = Levels.empty(B, H, dh, cap, L0, Lm, dev)
+        K = (torch.randn(B, Hh, cap, dh, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        Vv = torch.randn(B, Hh, cap, dh, device=dev, generator=g).to(torch.bfloat16)
+        lv = Levels.empty(B, Hh, dh, cap, L0, Lm, dev)
         _ops.build_levels(K[:, :, :T0], cap, L0, Lm, zero_sink=True, out=lv)
         layers.append((K, Vv, lv))
-    qkv = torch.randn(B, 3 * C, device=dev, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(B, 3 * Cm, device=dev, generator=g).to(torch.bfloat16)
     pos = torch.full((B,), T0, device=dev, dtype=torch.int32)
-    att = torch.empty(B, C, device=dev, dtype=torch.bfloat16)
-    nk = torch.empty(B, H, device=dev, dtype=torch.int32)
-    splits = a.splits or _ops.default_splits(B, H)
+    att = torch.empty(B, Cm, device=dev, dtype=torch.bfloat16)
+    nk = torch.empty(B, Hh, device=dev, dtype=torch.int32)
+    splits = a.splits or _ops.default_splits(B, Hh)
 
     def run_all():
         for K, Vv, lv in layers:
-            _ops.decode_step(qkv, K, Vv, lv, pos, H, TOPK, TOPK, WINDOW, 1 / 8.0, att, nkeys=nk, splits=splits)
+            _ops.decode_step(qkv, K, Vv, lv, pos, Hh, topk, topk, window, 1 / math.sqrt(dh), att, nkeys=nk,
+                             splits=splits)
 
     run_all()
     torch.cuda.synchronize()
@@ -253,7 +263,8 @@ def run_kernel_only(a, dev):
     byts = float(nk.sum()) * dh * 2 * 2
     peaks = measured_peaks()
     peak = peaks['hbm_gbs'] if peaks else 6650.0
-    print(json.dumps(dict(kernel_only=True, batch=B, prompt=T0, splits=splits, kernel_us=us, bytes_per_launch=byts,
+    print(json.dumps(dict(kernel_only=True, config='5' if a.config5 else '4', batch=B, heads=Hh, dh=dh, prompt=T0,
+                          splits=splits, kernel_us=us, bytes_per_launch=byts,
                           achieved_gbs=byts / us / 1e3, frac=byts / us / 1e3 / peak,
                           keys_per_head=float(nk.float().mean()))), flush=True)
 

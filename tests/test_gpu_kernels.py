@@ -427,6 +427,68 @@ def test_decode_persistent_many_items(dt, dh, L0):
     _no_device_error()
 
 
+@pytest.mark.parametrize('splits', [-1, 1])
+def test_decode_long_context_wide_heads(splits):
+    """dh=128 with 128-token leaf blocks and long prompts: the descent gathers several levels below the prefetched
+    ones on demand, each item streams ~130 stages through the ring (every slot reused many times by both consumer
+    groups), and the window alone spans 8 stages. Selected sets, outputs and key counts vs the oracle."""
+    ops = _ops()
+    from treeattn_b200._ops import Levels
+    dt, dh, L0, wmax, beam, local = torch.bfloat16, 128, 7, 32, 32, 256
+    rng = np.random.default_rng(5)
+    B, H = 6, 4
+    C = H * dh
+    leaf = 1 << L0
+    T0 = rng.integers(7000, 12000, B).tolist()
+    steps = 3
+    cap = max(T0) + steps + 1
+    Tcap = 1 << int(math.ceil(math.log2(cap)))
+    Lm = int(round(math.log2(Tcap))) - 1
+    rnd = lambda a: torch.as_tensor(a).to(dt).float().numpy()
+    kc = torch.zeros(B, H, cap, dh, device=DEV, dtype=dt)
+    vc = torch.zeros_like(kc)
+    lv = Levels.empty(B, H, dh, cap, L0, Lm, DEV)
+    states = []
+    for b in range(B):
+        K0 = rnd(rng.standard_normal((H, T0[b], dh)).astype(np.float32))
+        V0 = rnd(rng.standard_normal((H, T0[b], dh)).astype(np.float32))
+        kc[b, :, :T0[b]] = torch.as_tensor(K0).to(DEV, dt)
+        vc[b, :, :T0[b]] = torch.as_tensor(V0).to(DEV, dt)
+        st = oracle.SegStateNP(H, dh, cap, L0, Lm)
+        st.fill(K0, V0)
+        states.append(st)
+    ops.build_levels(kc, cap, L0, Lm, zero_sink=True, out=lv)
+    for b in range(B):
+        for l in range(L0, Lm + 1):
+            lv.level(l)[b, :, T0[b] >> l:] = 0
+    out = torch.empty(B, C, device=DEV, dtype=dt)
+    nkeys = torch.empty(B, H, device=DEV, dtype=torch.int32)
+    sel = torch.empty(B, H, wmax + 1, device=DEV, dtype=torch.int32)
+    ntree = oracle.n_tree_fixed(beam, wmax)
+    worst, n_cmp = 0.0, 0
+    for s_i in range(steps):
+        pos = torch.tensor([T0[b] + s_i for b in range(B)], device=DEV, dtype=torch.int32)
+        qkv_np = rnd(rng.standard_normal((B, 3 * C)).astype(np.float32))
+        ops.decode_step(torch.as_tensor(qkv_np).to(DEV, dt), kc, vc, lv, pos, H, wmax, ntree, local,
+                        1 / math.sqrt(dh), out, nkeys=nkeys, sel=sel, splits=splits)
+        o_n, nk_n, sel_n = out.float().cpu().numpy(), nkeys.cpu().numpy(), sel.cpu().numpy()
+        for b in range(B):
+            q, k, v = [qkv_np[b, j * C:(j + 1) * C].reshape(H, dh) for j in range(3)]
+            ro, _, (rids, rused, margin) = oracle.seg_attend(states[b], q, k, v, T0[b] + s_i, wmax, beam, local,
+                                                             with_sel=True)
+            for h in range(H):
+                if margin[h] <= 1e-6:
+                    continue
+                n_cmp += 1
+                assert sorted(sel_n[b, h, 1:1 + sel_n[b, h, 0]].tolist()) == sorted(rids[h][rused[h]].tolist())
+                worst = max(worst, float(np.abs(o_n[b, h * dh:(h + 1) * dh] - ro[h]).max()))
+                assert nk_n[b, h] == len(set(
+                    [p for p in oracle.leaves_to_pos(rids[h], rused[h], leaf).tolist() if p >= 0] +
+                    [0] + list(range(T0[b] + s_i - local + 1, T0[b] + s_i + 1)))), (b, h, s_i)
+    assert worst < 2e-2 and n_cmp > 0.9 * steps * B * H, (worst, n_cmp)
+    _no_device_error()
+
+
 def test_decode_bad_position_records_error():
     """A position outside the capacity is rejected inside the kernel (no memory access, error recorded)."""
     ops = _ops()

@@ -553,6 +553,9 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
   constexpr int ROWB = DH * (int)sizeof(T);
   // a warp's rows of a stage fit one register-staged call when early release is possible
   constexpr bool EARLY = EarlyRelease<WA>::value && (CH <= WPG * RowsPerCall<WA>::value);
+  // NST % NCG == 0: every ring slot is always consumed by the same group. If two groups shared a slot, a group
+  // could reach a slot whose previous phase (the other group's stage) is still in flight, and a parity wait would
+  // take the older completed phase of the same parity for the new one.
   static_assert(NCW >= 2 && NST <= 16 && NST % NCG == 0, "pipeline shape");
   constexpr int W_PROD = NCW, W_SEL = NCW + 1, W_FIN = NCW + 2;
 

@@ -271,14 +271,16 @@ struct Decode {
 
   static int persistent(ta::DecodeParams p, cudaStream_t st) {
     constexpr int ROWB = DH * (int)sizeof(T);
-    constexpr int CH = ROWB <= 128 ? 64 : 32;
-    constexpr int NST = 4, NCG = 2, WPG = 4;
+    constexpr int CH = ROWB <= 128 ? 64 : 32;          // 16 KB stages (K + V) up to 256-byte rows
+    constexpr int NST = ROWB == 256 ? 6 : 4;           // 256-byte rows: one CTA per SM with a deeper ring
+    constexpr int NCG = 2, WPG = 4;
     using Cfg = ta::PCfg<T, DH, CH, NST, NCG, WPG>;
     auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG>;
-    // descent staging rows: whatever keeps two CTAs per SM (111 KiB each), at least one full level (2*wmax+1)
+    // descent staging rows: whatever keeps two CTAs per SM (111 KiB each) when at least one full level
+    // (2*wmax+1 rows) fits that way, else what one CTA per SM allows
     const size_t row_bytes = (size_t)ta::stage_row_floats<DH>() * 4;
     const size_t base = Cfg::smem_bytes(0);
-    const size_t budget = 111 * 1024;
+    const size_t budget = base + (size_t)(2 * p.wmax + 1) * row_bytes <= 111 * 1024 ? 111 * 1024 : 218 * 1024;
     const int fit = budget > base ? (int)((budget - base) / row_bytes) : 0;
     const int stage_rows = std::max(2 * p.wmax + 1, std::min(fit, 256));
     const size_t smem = Cfg::smem_bytes(stage_rows);
