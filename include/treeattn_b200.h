@@ -126,8 +126,9 @@ int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv
                    float scale, void* out, int64_t o_sb, float* lse, int32_t* nkeys, int32_t* sel, int splits,
                    void* stream);
 
-/* The `splits` value ta_decode_step chooses for B*H (b, h) pairs on the current device (-1 = persistent). */
-int ta_decode_default_splits(int B, int H);
+/* The `splits` value ta_decode_step chooses for B*H (b, h) pairs of head dim dh and element type dtype on the
+ * current device (-1 = persistent). */
+int ta_decode_default_splits(int B, int H, int dh, int dtype);
 
 /* Row kernels of the batched decode step around the attention (callers of the hot path):
  * ta_embed_ln: x[b] = wte[tok[b]] + wpe[pos[b]] (fp32, (B, C)) and h[b] = LayerNorm(x[b]) * w in `dtype`

@@ -36,7 +36,7 @@ SIGNATURES = {
     'ta_append': [P, P, I, I, I, I, L, L, L, L, P, P, L, L, L, P, L, L, I, I, I, P, P],
     'ta_decode_step': [P, I, I, I, I, L, L, L, P, P, L, L, L, P, L, L, I, I, I, P, I, I, I, F, P, L, P, P, P, I,
                        P],
-    'ta_decode_default_splits': [I, I],
+    'ta_decode_default_splits': [I, I, I, I],
     'ta_embed_ln': [P, P, I, P, P, I, I, I, I, P, F, P, P, P],
     'ta_add_ln': [P, P, I, I, I, P, F, P, P],
     'ta_gelu': [P, I, L, P],

@@ -313,8 +313,9 @@ def argmax_advance(logits, tok, pos):
     _lib.call('ta_argmax_advance', _p(logits), _code(logits), B, V, _p(tok), _p(pos), _stream(logits))
 
 
-def default_splits(B, H):
-    return _lib.load().ta_decode_default_splits(B, H)
+def default_splits(B, H, dh, dtype):
+    """The decode mode ta_decode_step picks for B*H (b, h) pairs of head dim dh and element type dtype."""
+    return _lib.load().ta_decode_default_splits(B, H, dh, _DT[dtype])
 
 
 def device_error():

@@ -194,7 +194,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (bytes multiple of 16,
-// both addresses 16-byte aligned). No multicast.
+// both addresses 16-byte aligned), one destination CTA.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

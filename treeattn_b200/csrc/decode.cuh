@@ -5,7 +5,7 @@
 // the node rows come from L2 after the first CTA), while a producer warp already streams the local-window
 // rows. The key set - used leaf blocks cut at the window, the sink, the window, and the new token - is cut
 // into stages of <= CH rows; stage c belongs to CTA c % S. A producer warp fills a ring of NST shared-memory
-// stages with 1-D bulk copies (cp.async.bulk, no multicast) and mbarriers; NCW consumer warps run the online
+// stages with 1-D bulk copies (cp.async.bulk, one destination CTA each) and mbarriers; NCW consumer warps run the online
 // softmax from shared memory. Partial (max, sum, acc) states are merged across the cluster through
 // distributed shared memory, rank 0 writes the output, appends the new K/V rows and, when the new token
 // completes a leaf block, forms that leaf node and its right-spine ancestors (fp32, adjacent-pair order).
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(APPEND_THREADS) append_kernel(AppendParams p) 
 // c, c + G, c + 2G, ... (G = gridDim.x) and pipelines them:
 //   selector warp    : copies item k+1's q/k/v rows into a descriptor slot and runs its tree descent while item k
 //                      streams (descriptor ready -> mbarrier ifull[slot])
-//   producer warp    : 1-D bulk copies (no multicast) of item k's K/V rows into a ring of NST shared-memory
+//   producer warp    : 1-D bulk copies (one destination CTA) of item k's K/V rows into a ring of NST shared-memory
 //                      stages - the window rows first (they need no descent), then the used leaf blocks and the
 //                      sink - and one end-of-item marker stage per consumer group
 //   consumer groups  : NCG groups of WPG warps take the stages in turn (stage i -> group i % NCG), so several

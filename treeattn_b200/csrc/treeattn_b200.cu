@@ -224,12 +224,14 @@ int num_sms() {
   return g_num_sms;
 }
 
-// Decode mode for B*H (b, h) pairs: -1 = persistent pipelined kernel (enough pairs for every SM), otherwise the
-// number of CTAs per (b, h) of the cluster kernel (~4 resident CTAs per SM).
-int default_splits(int B, int H) {
+// Decode mode for B*H (b, h) pairs of row_bytes-wide K/V rows: -1 = persistent pipelined kernel (enough pairs
+// for every SM, rows of at most 128 bytes so that two CTAs share an SM), otherwise the number of CTAs per (b, h)
+// of the cluster kernel (~4 resident CTAs per SM). With wider rows the persistent kernel runs one CTA per SM and
+// its consumer warps cannot hide their latency, so the cluster kernel (several CTAs per SM) streams faster.
+int default_splits(int B, int H, int row_bytes) {
   const int pairs = B * H;
   if (pairs <= 0) return 1;
-  if (pairs >= num_sms()) return -1;
+  if (pairs >= num_sms()) return row_bytes <= 128 ? -1 : 1;
   const int target = 4 * num_sms();
   int s = 1;
   while (s < 8 && pairs * s < target) s <<= 1;
@@ -269,11 +271,22 @@ struct Decode {
     return check_launch("ta_decode_step");
   }
 
+  // Pipeline shape of the persistent kernel for 256-byte rows (bf16/f16 dh=128, f32 dh=64), which run one CTA
+  // per SM: rows per stage, ring stages and consumer groups (compile-time; NST must be a multiple of NCG).
+#ifndef TA_WIDE_CH
+#define TA_WIDE_CH 32
+#endif
+#ifndef TA_WIDE_NST
+#define TA_WIDE_NST 6
+#endif
+#ifndef TA_WIDE_NCG
+#define TA_WIDE_NCG 2
+#endif
   static int persistent(ta::DecodeParams p, cudaStream_t st) {
     constexpr int ROWB = DH * (int)sizeof(T);
-    constexpr int CH = ROWB <= 128 ? 64 : 32;          // 16 KB stages (K + V) up to 256-byte rows
-    constexpr int NST = ROWB == 256 ? 6 : 4;           // 256-byte rows: one CTA per SM with a deeper ring
-    constexpr int NCG = 2, WPG = 4;
+    constexpr int CH = ROWB <= 128 ? 64 : (ROWB == 256 ? TA_WIDE_CH : 32);  // rows per stage
+    constexpr int NST = ROWB == 256 ? TA_WIDE_NST : 4;                        // ring stages
+    constexpr int NCG = ROWB == 256 ? TA_WIDE_NCG : 2, WPG = 4;               // consumer groups x warps
     using Cfg = ta::PCfg<T, DH, CH, NST, NCG, WPG>;
     auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG>;
     // descent staging rows: whatever keeps two CTAs per SM (111 KiB each) when at least one full level
@@ -563,7 +576,10 @@ int ta_append(const void* k, const void* v, int dtype, int B, int H, int dh, int
   return by_type_dh<Append>(dtype, dh, p, S(stream));
 }
 
-int ta_decode_default_splits(int B, int H) { return default_splits(B, H); }
+int ta_decode_default_splits(int B, int H, int dh, int dtype) {
+  if (!valid_dtype(dtype) || dh < 1) return 1;
+  return default_splits(B, H, dh * esize_of(dtype));
+}
 
 int ta_embed_ln(const void* wte, const void* wpe, int dtype, const int64_t* tok, const int32_t* pos, int B, int V,
                 int P, int C, const float* w, float eps, float* x, void* h, void* stream) {
@@ -622,7 +638,7 @@ int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv
   if (wmax < 1 || wmax > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_decode_step: wmax=%d outside [1, 64]", wmax);
   if (n_tree < 0) return fail(TA_ERR_ARG, "ta_decode_step: n_tree < 0");
   if (Lw < 1) return fail(TA_ERR_ARG, "ta_decode_step: window %d < 1", Lw);
-  if (splits == 0) splits = default_splits(B, H);
+  if (splits == 0) splits = default_splits(B, H, dh * esize_of(dtype));
   if (splits < -1 || splits > 8) return fail(TA_ERR_ARG, "ta_decode_step: splits=%d outside [-1, 8]", splits);
   if (!qkv || !kc || !vc || !nodes || !pos || !out) return fail(TA_ERR_ARG, "ta_decode_step: null pointer");
   const int es = esize_of(dtype);

@@ -154,7 +154,7 @@ class Decoder:
         self.Lw = max(cfg.local, 3)
         self.scale = 1.0 / math.sqrt(self.dh)
         self.use_graphs = graphs
-        self.splits = splits or _ops.default_splits(batch, n_head)
+        self.splits = splits or _ops.default_splits(batch, n_head, self.dh, self.dtype)
         self.reset()
 
     # -------------------------------------------------------------- state
