@@ -82,6 +82,18 @@ int ta_seg_attn(const void* q, const void* k, const void* v, int dtype, int B, i
                 int ntree_const, int leaf, int Lw, float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st,
                 float* lse, int32_t* nkeys, void* stream);
 
+/* Same computation and arguments as ta_seg_attn (fastseg.py:367-383: static keys, dedupe_fast, _attn_fwd), on
+ * the tensor cores for whole sequences (prefill): 128 queries of one (b, h) per CTA stream the union of their
+ * key sets in 64-key tiles (tcgen05.mma into tensor memory, TMA loads), each query masked to its own
+ * deduplicated keys. bf16 / f16, dh 64 or 128, leaf >= 2, at most 1024 leaf blocks per sequence (T_kv / leaf); queries of
+ * a 128-tile should be close in position (the window union is streamed). */
+int ta_prefill_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int Nq, int dh,
+                    int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                    int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const int64_t* tq, int64_t tq_sb,
+                    int64_t tq_st, const int64_t* ids, const uint8_t* vld, int wl, const int64_t* n_tree,
+                    int ntree_const, int leaf, int Lw, float scale, void* o, int64_t o_sb, int64_t o_sh,
+                    int64_t o_st, float* lse, int32_t* nkeys, void* stream);
+
 /* Replaces fastseg.sparse_attn forward (fastseg.py:173-177, _attn_fwd 49-78): cand (B, H, T, Kc) key
  * positions (int32 if cand64 == 0, else int64), -1 = unused. o (B, H, T, dh) in q's dtype, lse may be NULL. */
 int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int T, int dh,

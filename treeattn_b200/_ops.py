@@ -165,11 +165,19 @@ def finish(ids, vld, lhat, wmax, leaf, nid=None, match=None, nL=None, positions=
     return dict(tree_pos=tree_pos, leaf_ok=vld, nb_pos=nb_pos, n_tree=n_tree, nb_leaves=nb_leaves)
 
 
-def seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_lse=False, want_nkeys=True):
+def prefill_supported(dtype, dh, T_kv, leaf):
+    """Whether ta_prefill_attn (tensor-core tiles) takes this shape: 16-bit, dh 64 / 128, <= 1024 leaves."""
+    return dtype in (torch.bfloat16, torch.float16) and dh in (64, 128) and leaf >= 2 and -(-T_kv // leaf) <= 1024
+
+
+def seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_lse=False, want_nkeys=True,
+             entry='ta_seg_attn'):
     """Attention of each query over its used leaves (first n_tree valid of ids/vld), sink and window.
 
     q (B, H, Nq, dh), k / v (B, H, T_kv, dh): any strides with a contiguous head dim. n_tree: int or (B, H, Nq).
-    `out` (B, H, Nq, dh) may be a strided view (e.g. of a (B, Nq, H, dh) buffer). Returns (out, lse, nkeys)."""
+    `out` (B, H, Nq, dh) may be a strided view (e.g. of a (B, Nq, H, dh) buffer). Returns (out, lse, nkeys).
+    entry: 'ta_seg_attn' (a warp per query) or 'ta_prefill_attn' (tensor-core tiles of 128 queries; 16-bit,
+    dh 64 / 128)."""
     _need_cuda('seg_attn', q, k, v, tq, ids, vld)
     _unit_inner('seg_attn', q, k, v)
     B, H, Nq, dh = q.shape
@@ -190,11 +198,16 @@ def seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_lse=
         ntp, ntc = None, int(n_tree)
     lse = torch.empty(B, H, Nq, device=q.device, dtype=torch.float32) if want_lse else None
     nkeys = torch.empty(B, H, Nq, device=q.device, dtype=torch.int32) if want_nkeys else None
-    _lib.call('ta_seg_attn', _p(q), _p(k), _p(v), _code(q), B, H, Nq, dh, q.stride(0), q.stride(1), q.stride(2),
+    _lib.call(entry, _p(q), _p(k), _p(v), _code(q), B, H, Nq, dh, q.stride(0), q.stride(1), q.stride(2),
               k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), T_kv, _p(tq), sb, st,
               _p(ids), _p(vld), wl, _p(ntp), ntc, leaf, Lw, float(scale), _p(out), out.stride(0), out.stride(1),
               out.stride(2), _p(lse), _p(nkeys), _stream(q))
     return out, lse, nkeys
+
+
+def prefill_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_lse=False, want_nkeys=True):
+    """seg_attn on the tensor-core tile kernel (ta_prefill_attn)."""
+    return seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out, want_lse, want_nkeys, 'ta_prefill_attn')
 
 
 def sparse_attn_fwd(q, k, v, cand, scale):

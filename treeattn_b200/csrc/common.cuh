@@ -49,6 +49,7 @@ enum KernelId : int {
   K_DECODE = 9,
   K_FINISH = 10,
   K_ROWS = 11,
+  K_PREFILL = 12,
 };
 
 // ------------------------------------------------------------------------------------------------ types

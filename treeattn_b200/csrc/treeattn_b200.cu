@@ -8,8 +8,11 @@
 #include <string>
 
 #include "../../include/treeattn_b200.h"
+#include <cudaTypedefs.h>
+
 #include "decode.cuh"
 #include "model_ops.cuh"
+#include "prefill.cuh"
 
 namespace {
 
@@ -145,6 +148,59 @@ struct SegAttn {
     if (nq == 0) return TA_OK;
     ta::seg_attn_kernel<T, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
     return check_launch("ta_seg_attn");
+  }
+};
+
+// ---------------------------------------------------------------------------------------------- prefill tiles
+// cuTensorMapEncodeTiled from the driver, looked up once (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+
+int get_encode_tiled() {
+  if (g_encode_tiled) return TA_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult qr = cudaDriverEntryPointSymbolNotFound;
+  const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr);
+  if (e != cudaSuccess || qr != cudaDriverEntryPointSuccess || !fn)
+    return fail(TA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
+  g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return TA_OK;
+}
+
+// 4-D tensor map over a (B, H, rows, dh) 16-bit tensor with element strides (sb, sh, st) and a contiguous head
+// dim: dims (dh, rows, H, B), box 64 x box_rows x 1 x 1, 128-byte swizzle, zero fill outside the tensor. The
+// stride of a size-1 dim is replaced by a valid one (it is never stepped).
+int make_rows_map(CUtensorMap* m, const void* ptr, int dtype, int dh, int rows, int H, int B, int64_t st, int64_t sh,
+                  int64_t sb, int box_rows, const char* what) {
+  if (H == 1) sh = st * rows;
+  if (B == 1) sb = sh * H;
+  const cuuint64_t dims[4] = {(cuuint64_t)dh, (cuuint64_t)rows, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = g_encode_tiled(
+      m, dtype == TA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+      const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TA_ERR_ARG, "ta_prefill_attn: tensor map for %s rejected (CUresult %d)", what, (int)r);
+  return TA_OK;
+}
+
+template <typename T, int DH>
+struct Prefill {
+  static constexpr int NS = DH == 64 ? 2 : 3;  // K/V ring stages (dh 64: two CTAs per SM)
+  static int run(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const ta::PrefillParams& p,
+                 cudaStream_t st) {
+    auto kern = ta::prefill_tile_kernel<T, DH, NS>;
+    const size_t smem = ta::prefill_smem_bytes<DH, NS>(p.leaf_words, p.tile_words);
+    static size_t smem_set = 0;
+    if (smem > smem_set) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return check_launch("ta_prefill_attn (shared memory attribute)");
+      smem_set = smem;
+    }
+    const int64_t grid = (int64_t)p.B * p.H * p.n_qtiles;
+    kern<<<(unsigned)grid, ta::PF_THREADS, smem, st>>>(mq, mk, mv, p);
+    return check_launch("ta_prefill_attn");
   }
 };
 
@@ -484,6 +540,52 @@ int ta_seg_attn(const void* q, const void* k, const void* v, int dtype, int B, i
   p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
   p.lse = lse; p.nkeys = nkeys;
   return by_type_dh<SegAttn>(dtype, dh, p, S(stream));
+}
+
+int ta_prefill_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int Nq, int dh,
+                    int64_t q_sb, int64_t q_sh, int64_t q_st, int64_t k_sb, int64_t k_sh, int64_t k_st,
+                    int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const int64_t* tq, int64_t tq_sb,
+                    int64_t tq_st, const int64_t* ids, const uint8_t* vld, int wl, const int64_t* n_tree,
+                    int ntree_const, int leaf, int Lw, float scale, void* o, int64_t o_sb, int64_t o_sh,
+                    int64_t o_st, float* lse, int32_t* nkeys, void* stream) {
+  g_err.clear();
+  if (dtype != TA_BF16 && dtype != TA_F16) return fail(TA_ERR_ARG, "ta_prefill_attn: dtype must be bf16 or f16");
+  if (dh != 64 && dh != 128) return fail(TA_ERR_ARG, "ta_prefill_attn: head dim %d not 64 or 128", dh);
+  if (wl < 0 || wl > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_prefill_attn: wl=%d outside [0, 64]", wl);
+  if (leaf < 2 || (leaf & (leaf - 1))) return fail(TA_ERR_ARG, "ta_prefill_attn: leaf %d not a power of two >= 2", leaf);
+  if (Lw < 1) return fail(TA_ERR_ARG, "ta_prefill_attn: window %d < 1", Lw);
+  if (B < 0 || H < 0 || Nq < 0 || T_kv < 1) return fail(TA_ERR_ARG, "ta_prefill_attn: bad sizes");
+  if (!q || !k || !v || !tq || (wl > 0 && (!ids || !vld)) || !o) return fail(TA_ERR_ARG, "ta_prefill_attn: null pointer");
+  const int64_t nleaves = ((int64_t)T_kv + leaf - 1) / leaf, ntiles = ((int64_t)T_kv + ta::PF_KT - 1) / ta::PF_KT;
+  if (nleaves > 32 * ta::PF_MAX_LEAF_WORDS)
+    return fail(TA_ERR_ARG, "ta_prefill_attn: %lld leaf blocks per sequence (at most %d; use ta_seg_attn)",
+                (long long)nleaves, 32 * ta::PF_MAX_LEAF_WORDS);
+  if (ntiles > 32 * ta::PF_MAX_TILE_WORDS) return fail(TA_ERR_ARG, "ta_prefill_attn: T_kv %d too long", T_kv);
+  if (!rows_aligned(q, 2, {q_sb, q_sh, q_st}) || !rows_aligned(k, 2, {k_sb, k_sh, k_st}) ||
+      !rows_aligned(v, 2, {v_sb, v_sh, v_st}) || !rows_aligned(o, 2, {o_sb, o_sh, o_st}))
+    return fail(TA_ERR_ARG, "ta_prefill_attn: q/k/v/o rows must be 16-byte aligned");
+  if ((int64_t)B * H * Nq == 0) return TA_OK;
+  if (int r = get_encode_tiled()) return r;
+  CUtensorMap mq, mk, mv;
+  if (int r = make_rows_map(&mq, q, dtype, dh, Nq, H, B, q_st, q_sh, q_sb, ta::PF_QT, "q")) return r;
+  if (int r = make_rows_map(&mk, k, dtype, dh, T_kv, H, B, k_st, k_sh, k_sb, ta::PF_KT, "k")) return r;
+  if (int r = make_rows_map(&mv, v, dtype, dh, T_kv, H, B, v_st, v_sh, v_sb, ta::PF_KT, "v")) return r;
+  ta::PrefillParams p{};
+  p.tq = tq; p.tq_sb = tq_sb; p.tq_st = tq_st;
+  p.ids = ids; p.vld = vld; p.n_tree = n_tree; p.ntree_const = ntree_const;
+  p.B = B; p.H = H; p.Nq = Nq; p.wl = wl; p.Lw = Lw; p.T_kv = T_kv;
+  p.L0 = 0;
+  while ((1 << p.L0) < leaf) ++p.L0;
+  p.n_qtiles = (Nq + ta::PF_QT - 1) / ta::PF_QT;
+  p.leaf_words = (int)((nleaves + 31) / 32);
+  p.tile_words = (int)((ntiles + 31) / 32);
+  p.scale_log2 = scale * ta::LOG2E;
+  p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
+  p.lse = lse; p.nkeys = nkeys;
+  cudaStream_t st = S(stream);
+  if (dtype == TA_BF16)
+    return dh == 64 ? Prefill<__nv_bfloat16, 64>::run(mq, mk, mv, p, st) : Prefill<__nv_bfloat16, 128>::run(mq, mk, mv, p, st);
+  return dh == 64 ? Prefill<__half, 64>::run(mq, mk, mv, p, st) : Prefill<__half, 128>::run(mq, mk, mv, p, st);
 }
 
 int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B, int H, int T, int dh,
