@@ -54,6 +54,10 @@ def parse():
     p.add_argument('--gather-dot', action='store_true',
                    help='configuration 2 instead: the block gather-dot kernel alone (B=8, H=12, dh=64, T=4096 bf16, '
                         '16 sorted unique 64-token blocks per (b, h)); prints one JSON line')
+    p.add_argument('--prefill-attn', action='store_true',
+                   help='configuration 3 instead: one layer of prefill sparse attention (B=4, H=12, T=8192, dh=64 '
+                        'bf16, leaf 64, top-16, window 128; selection from the tree kernels on random q/k), timing the '
+                        'tensor-core tile kernel and the warp-per-query kernel; prints one JSON line')
     p.add_argument('--profile-steps', type=int, default=0,
                    help='profiling mode: after prefill and warm-up run this many eager decode steps between '
                         'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
@@ -316,6 +320,95 @@ def run_gather_dot(a, dev):
                           rotated_copies=ROT)), flush=True)
 
 
+def union_tile_pairs(ids, vld, n_tree, leaf, Lw, T, qt=128, kt=64):
+    """(query tile, key tile) pairs the prefill tile kernel streams: per (b, h, 128-query tile) the union of the
+    used leaves' key tiles (parts before each query's window), the window tiles and tile 0."""
+    B, H, N, wl = ids.shape
+    dev = ids.device
+    t = torch.arange(N, device=dev)
+    w0 = (t - Lw + 1).clamp(min=0)
+    slot = torch.arange(wl, device=dev)
+    used = vld.bool() & (slot < n_tree) & (ids >= 0) & (ids * leaf < w0.view(1, 1, N, 1))
+    ntq, ntk = -(-N // qt), -(-T // kt)
+    occ = torch.zeros(B, H, ntq, ntk, dtype=torch.bool, device=dev)
+    per = max(leaf // kt, 1)
+    for j in range(per):  # key tiles a leaf spans (leaf >= kt) or the tile holding it (leaf < kt)
+        tile = (ids.clamp(min=0) * leaf // kt + j).clamp(max=ntk - 1)
+        qi = (t // qt).view(1, 1, N, 1).expand_as(tile)
+        bi = torch.arange(B, device=dev).view(B, 1, 1, 1).expand_as(tile)
+        hi = torch.arange(H, device=dev).view(1, H, 1, 1).expand_as(tile)
+        occ[bi[used], hi[used], qi[used], tile[used]] = True
+    for q0 in range(ntq):
+        lo, hi_ = int(w0[q0 * qt]) // kt, min(q0 * qt + qt - 1, N - 1) // kt
+        occ[:, :, q0, lo:hi_ + 1] = True
+        if int(w0[min(q0 * qt + qt - 1, N - 1)]) > 0:
+            occ[:, :, q0, 0] = True
+    return int(occ.sum())
+
+
+def run_prefill_attn(a, dev):
+    """Configuration 3, one layer of prefill sparse attention: B=4, H=12, T=8192, dh=64 bf16, 64-token leaves,
+    top-16, 128-token window. q / k / v random, the selection from build_levels + select (the model's own
+    kernels). Each launch is timed alone with CUDA events after a 256 MB L2 flush."""
+    from treeattn_b200 import _ops
+    from treeattn_b200._ops import Levels
+    B = a.batch if a.batch != 64 else 4
+    Hh, T, dh, leaf, topk, window = 12, 8192, 64, 64, 16, 128
+    L0, Lm = 6, _ops.lm_of(T)
+    g = torch.Generator(device=dev).manual_seed(11)
+    q = torch.randn(B, Hh, T, dh, device=dev, generator=g).to(torch.bfloat16)
+    k = (torch.randn(B, Hh, T, dh, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    v = torch.randn(B, Hh, T, dh, device=dev, generator=g).to(torch.bfloat16)
+    tq = torch.arange(T, device=dev)
+    lv = Levels.empty(B, Hh, dh, T, L0, Lm, dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps):
+        ts = []
+        for r in range(reps + 1):
+            flush.fill_(r & 0xff)
+            e0, e1 = ev(), ev()
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if r:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    sel_us = timed(lambda: (_ops.build_levels(k, T, L0, Lm, zero_sink=True, out=lv),
+                            _ops.select(q, lv, tq, topk)), 3)
+    ids, vld, _ = _ops.select(q, lv, tq, topk)
+    ntree = 16
+    out = torch.empty_like(q)
+    if a.profile_steps:
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(a.profile_steps):
+            _ops.prefill_attn(q, k, v, tq, ids, vld, ntree, leaf, window, dh ** -0.5, out=out, want_nkeys=False)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        return
+    _, _, nk = _ops.prefill_attn(q, k, v, tq, ids, vld, ntree, leaf, window, dh ** -0.5, out=out)
+    tile_us = timed(lambda: _ops.prefill_attn(q, k, v, tq, ids, vld, ntree, leaf, window, dh ** -0.5, out=out,
+                                              want_nkeys=False), 10)
+    warp_us = timed(lambda: _ops.seg_attn(q, k, v, tq, ids, vld, ntree, leaf, window, dh ** -0.5, out=out,
+                                          want_nkeys=False), 3)
+    keys = float(nk.sum())
+    flops = 4.0 * dh * keys
+    pairs = union_tile_pairs(ids, vld, ntree, leaf, window, T)
+    uflops = 4.0 * dh * 128 * 64 * pairs
+    peaks = measured_peaks()
+    peak = peaks['bf16_tflops'] if peaks else 1590.0
+    print(json.dumps(dict(prefill_attn=True, config='3: B=%d H=12 T=8192 dh=64 bf16 leaf 64 top-16 window 128' % B,
+                          tile_kernel_us=tile_us, warp_kernel_us=warp_us, selection_us=sel_us,
+                          keys_per_query=keys / (B * Hh * T), algorithmic_flops=flops,
+                          achieved_tflops=flops / tile_us / 1e6, frac=flops / tile_us / 1e6 / peak,
+                          union_tile_pairs=pairs, union_flops=uflops, union_tflops=uflops / tile_us / 1e6,
+                          union_frac=uflops / tile_us / 1e6 / peak, warp_achieved_tflops=flops / warp_us / 1e6,
+                          peak_tflops=peak)), flush=True)
+
+
 def run_reference(a, rank, world):
     if rank != 0:
         return
@@ -354,6 +447,9 @@ def main():
         return
     if a.gather_dot:
         run_gather_dot(a, dev)
+        return
+    if a.prefill_attn:
+        run_prefill_attn(a, dev)
         return
 
     B, T0, K, Wm = a.batch, a.prompt, a.steps, max(a.warmup, 3)

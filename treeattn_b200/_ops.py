@@ -210,6 +210,15 @@ def prefill_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_
     return seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out, want_lse, want_nkeys, 'ta_prefill_attn')
 
 
+def attend_leaves(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=None, want_lse=False, want_nkeys=True):
+    """seg_attn on the kernel that suits the call: tensor-core tiles (ta_prefill_attn) for runs of at least 64
+    queries of a supported shape (prefill: consecutive positions), otherwise a warp per query (ta_seg_attn)."""
+    Nq, dh = q.shape[2], q.shape[3]
+    tiles = Nq >= 64 and prefill_supported(q.dtype, dh, k.shape[2], leaf)
+    return seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out, want_lse, want_nkeys,
+                    'ta_prefill_attn' if tiles else 'ta_seg_attn')
+
+
 def sparse_attn_fwd(q, k, v, cand, scale):
     """fastseg sparse_attn forward: cand (B, H, T, Kc) positions, -1 unused. Returns (o, lse)."""
     _need_cuda('sparse_attn', q, k, v, cand)

@@ -327,8 +327,8 @@ class Decoder:
                 _ops.build_levels(Kc, st.cap, st.L0, st.Lm, zero_sink=True, out=lv)
                 ids, vld, _ = _ops.select(q, lv, tq, self.wmax)
                 o = torch.empty(nb, T0, H, dh, device=self.dev, dtype=dt)
-                _ops.seg_attn(q, Kc, Vc, tq, ids, vld, self.n_tree, 1 << st.L0, self.Lw, self.scale,
-                              out=o.transpose(1, 2), want_nkeys=False)
+                _ops.attend_leaves(q, Kc, Vc, tq, ids, vld, self.n_tree, 1 << st.L0, self.Lw, self.scale,
+                                   out=o.transpose(1, 2), want_nkeys=False)
                 del ids, vld
                 x = x + F.linear(o.view(nb, T0, C), L['c_proj']).float()
                 x = x + F.linear(F.gelu(F.linear(_ln(x, L['ln2']).to(dt), L['c_fc'])), L['c_mlp']).float()

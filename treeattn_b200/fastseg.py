@@ -156,7 +156,7 @@ class SegAttention(nn.Module):
                 used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
             Lw = max(cfg.local, 3)
             tq = torch.arange(T, device=q.device)
-            out, _, nkeys = _ops.seg_attn(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=out)
+            out, _, nkeys = _ops.attend_leaves(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=out)
             n_used = used.sum(-1).float()
             self.aux['keys_total'] = nkeys.float().mean()
             self.aux['keys_tree'] = (n_used * leaf).mean()
