@@ -31,6 +31,9 @@ sys.path.insert(0, ROOT)
 
 V, C, H, NL = 50304, 768, 12, 12
 LEAF, TOPK, WINDOW, TCAP = 64, 16, 128, 8192
+# own kernels per greedy step: embed+LN; per layer the fused decode attention, 2 x add+LN and GELU; argmax+advance
+# (the projections are cuBLAS)
+OWN_LAUNCHES_PER_STEP = 1 + NL * 4 + 1
 METRIC = 'decode tok/s (config 4: 12x768 bf16 GPT, batch 64/GPU, 4096-token prompts, leaf 64, top-16, window 128)'
 
 
@@ -195,12 +198,53 @@ def cpu_decode_sample(seconds, W_dev=None, seed=0):
         if time.perf_counter() - t0 > seconds or steps >= 512:
             break
     dt = time.perf_counter() - t0
+    return steps / dt, steps, _cpu_threads()
+
+
+def _cpu_threads():
     try:
         from threadpoolctl import threadpool_info
-        threads = max([i.get('num_threads', 1) for i in threadpool_info()] + [1])
+        return max([i.get('num_threads', 1) for i in threadpool_info()] + [1])
     except Exception:
-        threads = 1
-    return steps / dt, steps, threads
+        return 1
+
+
+def cpu_gather_dot_sample(q, K, blocks, blk, byts, seconds=4.0):
+    """Configuration 2 on the host: the CPU oracle's gather_dot (the reference's torch fallback form,
+    fastseg.py:121-122) on the same q, K and block ids, repeated for a bounded time; GB/s on the same
+    algorithmic bytes as the kernel."""
+    import numpy as np
+
+    import oracle
+    qn = q.float().cpu().numpy()[:, :, None]
+    Kn = K.float().cpu().numpy()
+    bl = blocks.long().cpu().numpy()
+    cand = (bl[..., None] * blk + np.arange(blk)).reshape(bl.shape[0], bl.shape[1], 1, -1)
+    oracle.gather_dot(qn, Kn, cand, 0.125)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        oracle.gather_dot(qn, Kn, cand, 0.125)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return dict(value=byts / dt / 1e9, unit='GB/s', cores=_cpu_threads(), kind='port',
+                sample='%d calls of the full configuration-2 gather-dot (numpy fp32 oracle), %.2f ms each' % (n, dt * 1e3))
+
+
+def cpu_prefill_sample(q, k, v, leaf, topk, window):
+    """Configuration 3 on the host: the CPU oracle's SegAttention.sparse_attend (fastseg.py:345-389: levels,
+    descent, static keys, dedupe, exact attention) for ONE (b, h) of the whole 8192-token sequence, fp32 numpy;
+    TFLOP/s on that head's algorithmic FLOPs (4 dh per kept key per query)."""
+    import numpy as np
+
+    import oracle
+    qh, kh, vh = [t[:1, :1].float().cpu().numpy() for t in (q, k, v)]
+    t0 = time.perf_counter()
+    _, stats = oracle.seg_attention(qh, kh, vh, topk, topk, window, L0=int(math.log2(leaf)))
+    dt = time.perf_counter() - t0
+    flops = 4.0 * qh.shape[-1] * stats['keys_total'] * qh.shape[2]
+    return dict(value=flops / dt / 1e12, unit='TFLOP/s', cores=_cpu_threads(), kind='port',
+                sample='one (b, h) of 8192 queries (selection + attention, numpy fp32 oracle) in %.2f s; the GPU '
+                       'figure covers 48 (b, h)' % dt)
 
 
 def run_kernel_only(a, dev):
@@ -315,9 +359,12 @@ def run_gather_dot(a, dev):
     byts = B * H * nblk * blk * dh * 2 + B * H * dh * 2 + B * H * nblk * 4 + B * H * nblk * blk * 4
     peaks = measured_peaks()
     peak = peaks['hbm_gbs'] if peaks else 6650.0
-    print(json.dumps(dict(gather_dot=True, config='B=8 H=12 dh=64 T=4096 bf16, 16 blocks of 64 per (b,h)',
-                          kernel_us=us, bytes_per_call=byts, achieved_gbs=byts / us / 1e3, frac=byts / us / 1e3 / peak,
-                          rotated_copies=ROT)), flush=True)
+    line = dict(gather_dot=True, config='B=8 H=12 dh=64 T=4096 bf16, 16 blocks of 64 per (b,h)',
+                kernel_us=us, bytes_per_call=byts, achieved_gbs=byts / us / 1e3, frac=byts / us / 1e3 / peak,
+                rotated_copies=ROT)
+    if not a.no_cpu_baseline:
+        line['cpu_baseline'] = cpu_gather_dot_sample(q, Ks[0], blocks, blk, byts, seconds=min(a.cpu_seconds, 4.0))
+    print(json.dumps(line), flush=True)
 
 
 def union_tile_pairs(ids, vld, n_tree, leaf, Lw, T, qt=128, kt=64):
@@ -400,13 +447,16 @@ def run_prefill_attn(a, dev):
     uflops = 4.0 * dh * 128 * 64 * pairs
     peaks = measured_peaks()
     peak = peaks['bf16_tflops'] if peaks else 1590.0
-    print(json.dumps(dict(prefill_attn=True, config='3: B=%d H=12 T=8192 dh=64 bf16 leaf 64 top-16 window 128' % B,
-                          tile_kernel_us=tile_us, warp_kernel_us=warp_us, selection_us=sel_us,
-                          keys_per_query=keys / (B * Hh * T), algorithmic_flops=flops,
-                          achieved_tflops=flops / tile_us / 1e6, frac=flops / tile_us / 1e6 / peak,
-                          union_tile_pairs=pairs, union_flops=uflops, union_tflops=uflops / tile_us / 1e6,
-                          union_frac=uflops / tile_us / 1e6 / peak, warp_achieved_tflops=flops / warp_us / 1e6,
-                          peak_tflops=peak)), flush=True)
+    line = dict(prefill_attn=True, config='3: B=%d H=12 T=8192 dh=64 bf16 leaf 64 top-16 window 128' % B,
+                tile_kernel_us=tile_us, warp_kernel_us=warp_us, selection_us=sel_us,
+                keys_per_query=keys / (B * Hh * T), algorithmic_flops=flops,
+                achieved_tflops=flops / tile_us / 1e6, frac=flops / tile_us / 1e6 / peak,
+                union_tile_pairs=pairs, union_flops=uflops, union_tflops=uflops / tile_us / 1e6,
+                union_frac=uflops / tile_us / 1e6 / peak, warp_achieved_tflops=flops / warp_us / 1e6,
+                peak_tflops=peak)
+    if not a.no_cpu_baseline:
+        line['cpu_baseline'] = cpu_prefill_sample(q, k, v, leaf, topk, window)
+    print(json.dumps(line), flush=True)
 
 
 def run_reference(a, rank, world):
@@ -566,7 +616,7 @@ def main():
                                 splits=dec.splits),
                     e2e=dict(value=tokens / (ms_e2e * 1e-3), unit='tokens/s', h2d_bytes_per_step=B * 8,
                              d2h_bytes_per_step=B * 8),
-                    gpu_launches=NL * K,
+                    gpu_launches=OWN_LAUNCHES_PER_STEP * K,
                     roofline=dict(bound='hbm', achieved=achieved, peak=peak, unit='GB/s', frac=achieved / peak,
                                   traffic=profiled_traffic(), traffic_source='profiles/decode_kernel_config4.md (ncu, '
                                   'same kernel and shape, t=4096)',
