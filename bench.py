@@ -29,12 +29,31 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-V, C, H, NL = 50304, 768, 12, 12
-LEAF, TOPK, WINDOW, TCAP = 64, 16, 128, 8192
+
+class Spec:
+    """A decode-engine configuration of BASELINE.json (model, tree and run)."""
+
+    def __init__(self, name, V, C, H, NL, leaf, topk, window, tcap, batch, prompt, fill):
+        self.name, self.V, self.C, self.H, self.NL = name, V, C, H, NL
+        self.leaf, self.topk, self.window, self.tcap = leaf, topk, window, tcap
+        self.batch, self.prompt, self.fill = batch, prompt, fill
+        self.dh = C // H
+
+
+# configuration 4: prompts run through the model (prefill), then greedy decoding
+CFG4 = Spec('4', V=50304, C=768, H=12, NL=12, leaf=64, topk=16, window=128, tcap=8192, batch=64, prompt=4096,
+            fill='prefill')
+# configuration 5: 32768-token contexts; the caches are filled with random keys/values (the decode cost does not
+# depend on their values) and the trees built from them, since a 24-layer prefill of the contexts is not the
+# measured step; batch per GPU is what fits in HBM (256 sequences need 1.65 TB of KV: more than 8 GPUs hold)
+CFG5 = Spec('5', V=32000, C=2048, H=16, NL=24, leaf=128, topk=32, window=256, tcap=65536, batch=20, prompt=32768,
+            fill='random')
+V, C, H, NL = CFG4.V, CFG4.C, CFG4.H, CFG4.NL
+LEAF, TOPK, WINDOW, TCAP = CFG4.leaf, CFG4.topk, CFG4.window, CFG4.tcap
 # own kernels per greedy step: embed+LN; per layer the fused decode attention, 2 x add+LN and GELU; argmax+advance
 # (the projections are cuBLAS)
-OWN_LAUNCHES_PER_STEP = 1 + NL * 4 + 1
 METRIC = 'decode tok/s (config 4: 12x768 bf16 GPT, batch 64/GPU, 4096-token prompts, leaf 64, top-16, window 128)'
+METRIC5 = 'decode tok/s (config 5: 24x2048 bf16 GPT, 32768-token contexts, leaf 128, top-32, window 256)'
 
 
 def parse():
@@ -49,8 +68,10 @@ def parse():
     p.add_argument('--cpu-seconds', type=float, default=12.0)
     p.add_argument('--splits', type=int, default=0, help='CTAs per (b, h) in the decode kernel (0 = auto)')
     p.add_argument('--config5', action='store_true',
-                   help='with --kernel-only: the configuration-5 shape (dh 128, 128-token leaves, top-32, window 256, '
-                        '32768-token context, Tcap 65536, 16 heads); --batch is per GPU (32 = 256 over 8 GPUs)')
+                   help='configuration 5 instead of 4: 24 layers x 2048 (16 heads, dh 128, vocab 32000), 128-token '
+                        'leaves, top-32, window 256, 32768-token contexts (random-filled caches), 128 steps, 20 '
+                        'sequences per GPU (what fits in HBM); with --kernel-only the decode kernel alone at '
+                        'batch 32')
     p.add_argument('--kernel-only', action='store_true',
                    help='time only the fused decode kernel on the config-4 shape (random caches of 4 layers, '
                         'rotated so that no launch finds its KV in L2) and print one JSON line')
@@ -61,25 +82,29 @@ def parse():
                    help='configuration 3 instead: one layer of prefill sparse attention (B=4, H=12, T=8192, dh=64 '
                         'bf16, leaf 64, top-16, window 128; selection from the tree kernels on random q/k), timing the '
                         'tensor-core tile kernel and the warp-per-query kernel; prints one JSON line')
+    p.add_argument('--config1', action='store_true',
+                   help='configuration 1 instead: the full forward of the 4-layer d=256 fp32 GPT (B=2, T=512, leaf 32, '
+                        'top-4, window 64) on the GPU and on the CPU oracle, logits compared; prints one JSON line')
     p.add_argument('--profile-steps', type=int, default=0,
                    help='profiling mode: after prefill and warm-up run this many eager decode steps between '
                         'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
     return p.parse_args()
 
 
-def make_cfg(prompt, steps):
+def make_cfg(M):
     from treeattn_b200.config import Config
-    return Config(vocab_size=V, seq_len=TCAP, n_layer=NL, n_head=H, n_embd=C, attn='seg', wmax=TOPK, beam=TOPK,
-                  local=WINDOW, neighbors=False, beam_mode='fixed', leaf=LEAF)
+    return Config(vocab_size=M.V, seq_len=M.tcap, n_layer=M.NL, n_head=M.H, n_embd=M.C, attn='seg', wmax=M.topk,
+                  beam=M.topk, local=M.window, neighbors=False, beam_mode='fixed', leaf=M.leaf)
 
 
-def make_weights(device, seed, dtype):
-    """Random-init weights of the configuration-4 architecture (GPT._init: N(0, 0.02), c_proj 0.02/sqrt(2L))."""
+def make_weights(device, seed, dtype, M=CFG4):
+    """Random-init weights of the architecture (GPT._init: N(0, 0.02), c_proj 0.02/sqrt(2L))."""
     g = torch.Generator(device=device).manual_seed(seed)
     n = lambda *s, std=0.02: (torch.randn(*s, generator=g, device=device) * std).to(dtype)
-    sp = 0.02 / math.sqrt(2 * NL)
-    W = dict(wte=n(V, C), wpe=n(TCAP, C), ln_f=torch.ones(C, device=device), layers=[])
-    for _ in range(NL):
+    sp = 0.02 / math.sqrt(2 * M.NL)
+    C = M.C
+    W = dict(wte=n(M.V, C), wpe=n(M.tcap, C), ln_f=torch.ones(C, device=device), layers=[])
+    for _ in range(M.NL):
         W['layers'].append(dict(ln1=torch.ones(C, device=device), c_attn=n(3 * C, C), c_proj=n(C, C, std=sp),
                                 ln2=torch.ones(C, device=device), c_fc=n(4 * C, C), c_mlp=n(C, 4 * C, std=sp)))
     return W
@@ -163,31 +188,21 @@ def measured_peaks():
         return None
 
 
-def cpu_decode_sample(seconds, W_dev=None, seed=0):
-    """Time the CPU oracle's decode (numpy, fp32, the reference engine's algorithm: engine.py:149-177 Decoder,
-    batch 1) on the configuration-4 model for a bounded number of steps. The prompt cache (4096 positions per
-    layer) is filled with random keys/values instead of a CPU prefill (the time of a decode step does not depend
-    on the values). Returns (tokens/s, steps, threads)."""
+def _cpu_decoder_rate(M, seconds, W, n_layers, seed):
+    """Steps per second of the CPU oracle's decoder (batch 1) with n_layers layers, prompt cache of M.prompt
+    random positions per layer."""
     import numpy as np
 
     import oracle
     rng = np.random.default_rng(seed)
-    if W_dev is not None:
-        f = lambda t: t.float().cpu().numpy()
-        W = dict(wte=f(W_dev['wte']), wpe=f(W_dev['wpe']), ln_f=f(W_dev['ln_f']),
-                 layers=[{k: f(v) for k, v in L.items()} for L in W_dev['layers']])
-    else:
-        n = lambda *s, std=0.02: (rng.standard_normal(s, dtype=np.float32) * std)
-        W = dict(wte=n(V, C), wpe=n(TCAP, C), ln_f=np.ones(C, np.float32),
-                 layers=[dict(ln1=np.ones(C, np.float32), c_attn=n(3 * C, C), c_proj=n(C, C), ln2=np.ones(C, np.float32),
-                              c_fc=n(4 * C, C), c_mlp=n(C, 4 * C)) for _ in range(NL)])
-    T0 = 4096
-    dec = oracle.DecoderNP(W, H, TCAP, TOPK, TOPK, WINDOW, L0=int(math.log2(LEAF)), cap=T0 + 512)
+    W = dict(W, layers=W['layers'][:n_layers])
+    T0 = M.prompt
+    dec = oracle.DecoderNP(W, M.H, M.tcap, M.topk, M.topk, M.window, L0=int(math.log2(M.leaf)), cap=T0 + 512)
     dec.reset(1)
     for st in dec.states[0]:
-        st.fill(rng.standard_normal((H, T0, C // H), dtype=np.float32),
-                rng.standard_normal((H, T0, C // H), dtype=np.float32))
-    tok = rng.integers(0, V, 1)
+        st.fill(rng.standard_normal((M.H, T0, M.dh), dtype=np.float32),
+                rng.standard_normal((M.H, T0, M.dh), dtype=np.float32))
+    tok = rng.integers(0, M.V, 1)
     dec.step(tok, T0)  # warm-up
     t0 = time.perf_counter()
     steps = 0
@@ -197,8 +212,38 @@ def cpu_decode_sample(seconds, W_dev=None, seed=0):
         steps += 1
         if time.perf_counter() - t0 > seconds or steps >= 512:
             break
-    dt = time.perf_counter() - t0
-    return steps / dt, steps, _cpu_threads()
+    return steps / (time.perf_counter() - t0), steps
+
+
+def cpu_decode_sample(seconds, W_dev=None, seed=0, M=CFG4):
+    """Time the CPU oracle's decode (numpy, fp32, the reference engine's algorithm: engine.py:149-177 Decoder,
+    batch 1) for a bounded number of steps. The prompt caches are filled with random keys/values instead of a CPU
+    prefill (the time of a decode step does not depend on the values). Configuration 4 runs the whole model;
+    for larger models (configuration 5: 24 layers, 32768-token caches) one- and two-layer decoders are timed and
+    the step is extrapolated to all layers (t1 + (NL - 1) (t2 - t1)). Returns (tokens/s, steps, threads, how)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    if W_dev is not None:
+        f = lambda t: t.float().cpu().numpy()
+        W = dict(wte=f(W_dev['wte']), wpe=f(W_dev['wpe']), ln_f=f(W_dev['ln_f']),
+                 layers=[{k: f(v) for k, v in L.items()} for L in W_dev['layers']])
+    else:
+        n = lambda *s, std=0.02: (rng.standard_normal(s, dtype=np.float32) * std)
+        C = M.C
+        nl = M.NL if M is CFG4 else 2
+        W = dict(wte=n(M.V, C), wpe=n(M.tcap, C), ln_f=np.ones(C, np.float32),
+                 layers=[dict(ln1=np.ones(C, np.float32), c_attn=n(3 * C, C), c_proj=n(C, C),
+                              ln2=np.ones(C, np.float32), c_fc=n(4 * C, C), c_mlp=n(C, 4 * C)) for _ in range(nl)])
+    if M is CFG4:
+        rate, steps = _cpu_decoder_rate(M, seconds, W, M.NL, seed)
+        return rate, steps, _cpu_threads(), '%d greedy decode steps of 1 sequence at t~%d' % (steps, M.prompt)
+    r1, s1 = _cpu_decoder_rate(M, seconds / 2, W, 1, seed)
+    r2, s2 = _cpu_decoder_rate(M, seconds / 2, W, 2, seed)
+    t1, t2 = 1.0 / r1, 1.0 / r2
+    t_step = t1 + (M.NL - 1) * max(t2 - t1, 0.0)
+    return 1.0 / t_step, s1 + s2, _cpu_threads(), (
+        '%d + %d greedy steps of 1 sequence at t~%d with 1- and 2-layer decoders (%.1f / %.1f ms), extrapolated to '
+        '%d layers' % (s1, s2, M.prompt, t1 * 1e3, t2 * 1e3, M.NL))
 
 
 def _cpu_threads():
@@ -459,6 +504,52 @@ def run_prefill_attn(a, dev):
     print(json.dumps(line), flush=True)
 
 
+def run_config1(a, dev):
+    """Configuration 1: GPT 4 layers, d=256, 4 heads, vocab 4096, T=512, leaf 32, top-4, window 64, fp32, batch 2,
+    weights from torch.manual_seed(0) + GPT._init, tokens uniform from a seeded generator. The whole forward (our
+    SegAttention path on the GPU) against the CPU oracle's forward (numpy fp32 restatement of model.py +
+    fastseg.SegAttention) on the same weights and tokens: times and the max-abs logit difference (bound 1e-4 plus
+    the reference's own fp32 noise at near-tied selections, which the parity tests pin separately)."""
+    import numpy as np
+
+    import oracle
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    cfg = Config(vocab_size=4096, seq_len=512, n_layer=4, n_head=4, n_embd=256, attn='seg', wmax=4, beam=4, local=64,
+                 neighbors=False, beam_mode='fixed', leaf=32)
+    torch.manual_seed(0)
+    m = GPT(cfg).eval()
+    idx = torch.randint(0, 4096, (2, 512), generator=torch.Generator().manual_seed(1))
+    W = oracle.weights_from_state_dict({k: v.float() for k, v in m.state_dict().items()}, cfg.n_layer)
+    m = m.to(dev)
+    idx_d = idx.to(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        for _ in range(3):
+            logits, _, stats = m(idx_d)
+        torch.cuda.synchronize()
+        e0, e1 = ev(), ev()
+        reps = 10
+        e0.record()
+        for _ in range(reps):
+            logits, _, stats = m(idx_d)
+        e1.record()
+        torch.cuda.synchronize()
+    gpu_ms = e0.elapsed_time(e1) / reps
+    t0 = time.perf_counter()
+    ref, rstats = oracle.gpt_forward(W, idx.numpy(), cfg.n_head, cfg.wmax, cfg.beam, cfg.local, L0=5)
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    diff = float(np.abs(logits.float().cpu().numpy() - ref).max())
+    toks = 2 * 512
+    print(json.dumps(dict(config1=True, config='1: GPT 4x256 fp32, B=2, T=512, leaf 32, top-4, window 64',
+                          gpu_forward_ms=gpu_ms, gpu_tokens_per_s=toks / (gpu_ms * 1e-3),
+                          max_abs_logit_diff=diff, keys_total=stats['keys_total'],
+                          ref_keys_total=rstats['keys_total'],
+                          cpu_baseline=dict(value=toks / (cpu_ms * 1e-3), unit='tokens/s', cores=_cpu_threads(),
+                                            kind='port', sample='one full forward (2 x 512 tokens) of the CPU oracle '
+                                            'in %.0f ms' % cpu_ms))), flush=True)
+
+
 def run_reference(a, rank, world):
     if rank != 0:
         return
@@ -501,17 +592,51 @@ def main():
     if a.prefill_attn:
         run_prefill_attn(a, dev)
         return
+    if a.config1:
+        run_config1(a, dev)
+        return
 
-    B, T0, K, Wm = a.batch, a.prompt, a.steps, max(a.warmup, 3)
-    cap = ((T0 + Wm + 2 * K + 8 + LEAF - 1) // LEAF) * LEAF
-    cfg = make_cfg(T0, K)
-    W = make_weights(dev, 1234, torch.bfloat16)
-    dec = Decoder(W, NL, H, C, TCAP, 'seg', cfg, dev, batch=B, dtype=torch.bfloat16, cap=cap, splits=a.splits)
-    g = torch.Generator(device=dev).manual_seed(100 + rank)
-    prompts = torch.randint(0, V, (B, T0), device=dev, generator=g)
+    run_engine(a, CFG5 if a.config5 else CFG4, dev, rank, world, local)
+
+
+def fill_random(dec, M, T0, seed):
+    """Caches of every layer: positions [0, T0) from N(0, 0.25) keys and N(0, 1) values (bf16), trees built from
+    them; every sequence at position T0 with a random token (configuration 5: a 32768-token prefill of 24 layers is
+    not the measured step and the decode cost does not depend on the values)."""
+    from treeattn_b200 import _ops
+    g = torch.Generator(device=dec.dev).manual_seed(seed)
+    for st in dec.states:
+        for b in range(dec.batch):  # one sequence at a time: no full-size temporaries
+            st.K[b, :, :T0].normal_(generator=g).mul_(0.5)
+            st.V[b, :, :T0].normal_(generator=g)
+        _ops.build_levels(st.K[:, :, :T0], st.cap, st.L0, st.Lm, zero_sink=True, out=st.levels)
+    dec._tok.copy_(torch.randint(0, M.V, (dec.batch,), device=dec.dev, generator=g))
+    dec._pos.fill_(T0)
+
+
+def run_engine(a, M, dev, rank, world, local):
+    """Greedy batched decoding of configuration 4 (default) or 5: timed device-resident loop, end-to-end serving
+    loop, decode-kernel roofline, CPU-oracle baseline; one JSON line from rank 0."""
+    import torch.distributed as dist
+    from treeattn_b200 import _ops
+    from treeattn_b200 import dist as tdist
+    from treeattn_b200.engine import Decoder
+    C, H, NL, dh = M.C, M.H, M.NL, M.dh
+    B = a.batch if (a.batch != 64 or M is CFG4) else M.batch
+    T0 = a.prompt if (a.prompt != 4096 or M is CFG4) else M.prompt
+    K, Wm = a.steps if (a.steps != 256 or M is CFG4) else 128, max(a.warmup, 3)
+    cap = ((T0 + Wm + 2 * K + 8 + M.leaf - 1) // M.leaf) * M.leaf
+    cfg = make_cfg(M)
+    W = make_weights(dev, 1234, torch.bfloat16, M)
+    dec = Decoder(W, NL, H, C, M.tcap, 'seg', cfg, dev, batch=B, dtype=torch.bfloat16, cap=cap, splits=a.splits)
     torch.cuda.synchronize()
     t_pf = time.time()
-    dec.prefill(prompts)
+    if M.fill == 'prefill':
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        prompts = torch.randint(0, M.V, (B, T0), device=dev, generator=g)
+        dec.prefill(prompts)
+    else:
+        fill_random(dec, M, T0, 100 + rank)
     torch.cuda.synchronize()
     t_pf = time.time() - t_pf
     if a.profile_steps:
@@ -566,7 +691,7 @@ def main():
     ms_e2e = f0.elapsed_time(f1)
 
     # ---------------------------------------------------------------- roofline: the fused decode kernel alone
-    # The 12 per-layer launches (one per layer cache, so consecutive launches read different KV and nothing stays
+    # The per-layer launches (one per layer cache, so consecutive launches read different KV and nothing stays
     # in L2) are captured in a CUDA graph and replayed, so the events see kernel time, not Python launch time.
     # Relaunching at the same position is idempotent (same appended row, same tree node).
     pos = dec.positions.clone()
@@ -576,8 +701,8 @@ def main():
 
     def layer_launches():
         for st in dec.states:
-            _ops.decode_step(qkv, st.K, st.V, st.levels, pos, H, TOPK, TOPK, WINDOW, 1 / 8.0, att, nkeys=nk,
-                             splits=dec.splits)
+            _ops.decode_step(qkv, st.K, st.V, st.levels, pos, H, M.topk, M.topk, M.window, 1 / math.sqrt(dh), att,
+                             nkeys=nk, splits=dec.splits)
 
     layer_launches()
     torch.cuda.synchronize()
@@ -592,7 +717,7 @@ def main():
     r1.record()
     torch.cuda.synchronize()
     kern_ms = r0.elapsed_time(r1) / (reps * NL)
-    sel_bytes = float(nk.sum()) * (C // H) * 2 * 2  # K and V rows of the selected keys, bf16
+    sel_bytes = float(nk.sum()) * dh * 2 * 2  # K and V rows of the selected keys, bf16
     del kg
 
     # ---------------------------------------------------------------- reduce over ranks
@@ -604,32 +729,39 @@ def main():
         peak = peaks['hbm_gbs'] if peaks else 6650.0
         achieved = sel_bytes / (kern_ms * 1e-3) / 1e9
         tokens = B * K * world
-        line = dict(metric=METRIC, value=tokens / (ms * 1e-3), unit='tokens/s', n_gpus=world, steps=K, warmup=Wm,
-                    ms_per_step=ms / K, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
-                    data='synthetic (uniform random tokens, N(0,0.02) random-init weights)',
-                    config=dict(workload='config 4: KV-cache decode, 12x768 GPT bf16, batch %d/GPU, prompt %d, '
-                                         'leaf %d, top-%d, window %d' % (B, T0, LEAF, TOPK, WINDOW),
+        kname = ('decode_persistent_kernel<bf16,%d>' % dh) if dec.splits < 0 else (
+            'decode_kernel<bf16,%d> (%d CTA per (b, h))' % (dh, dec.splits))
+        traffic = profiled_traffic() if M is CFG4 else None
+        line = dict(metric=METRIC if M is CFG4 else METRIC5, value=tokens / (ms * 1e-3), unit='tokens/s',
+                    n_gpus=world, steps=K, warmup=Wm, ms_per_step=ms / K, higher_is_better=True, scaling='weak',
+                    vs_baseline=None, dtype='bf16',
+                    data='synthetic (uniform random tokens, N(0,0.02) random-init weights%s)' % (
+                        '' if M.fill == 'prefill' else '; caches filled with random keys/values'),
+                    config=dict(workload='config %s: KV-cache decode, %dx%d GPT bf16 (%d heads, vocab %d), batch '
+                                         '%d/GPU, context %d, leaf %d, top-%d, window %d' % (
+                                             M.name, NL, C, H, M.V, B, T0, M.leaf, M.topk, M.window),
                                 global_batch=B * world, seq_len=T0, parallelism='dp%d (batch sharded, no collective)'
                                 % world, l2='inputs larger than L2 (KV cache %.1f GB/GPU)' % (
-                                    2 * NL * B * H * cap * (C // H) * 2 / 1e9),
+                                    2 * NL * B * H * cap * dh * 2 / 1e9),
                                 prefill_s=round(t_pf, 2), keys_per_head=round(keys_mean, 1),
                                 splits=dec.splits),
                     e2e=dict(value=tokens / (ms_e2e * 1e-3), unit='tokens/s', h2d_bytes_per_step=B * 8,
                              d2h_bytes_per_step=B * 8),
-                    gpu_launches=OWN_LAUNCHES_PER_STEP * K,
+                    gpu_launches=(1 + NL * 4 + 1) * K,
                     roofline=dict(bound='hbm', achieved=achieved, peak=peak, unit='GB/s', frac=achieved / peak,
-                                  traffic=profiled_traffic(), traffic_source='profiles/decode_kernel_config4.md (ncu, '
-                                  'same kernel and shape, t=4096)',
-                                  kernel='ta_decode_step (decode_persistent_kernel<bf16,64>)',
+                                  traffic=traffic, traffic_source=(
+                                      'profiles/decode_kernel_config4.md (ncu, same kernel and shape, t=4096)'
+                                      if traffic else None),
+                                  kernel='ta_decode_step (%s)' % kname,
                                   kernel_us=kern_ms * 1e3, bytes_per_launch=sel_bytes,
                                   peak_source='MEASURED_PEAKS.json hbm_gbs (burst copy)' if peaks else 'fallback'),
                     clocks=ck)
         if world == 1 and not a.no_cpu_baseline:
-            v, steps, threads = cpu_decode_sample(a.cpu_seconds, W_dev=W)
+            v, steps, threads, how = cpu_decode_sample(a.cpu_seconds, W_dev=W if M is CFG4 else None, M=M)
             line['cpu_baseline'] = dict(value=v, unit='tokens/s', cores=threads, kind='port',
-                                        sample='%d greedy decode steps of 1 sequence at t~4096 on the CPU oracle '
-                                               '(numpy fp32 restatement of the reference engine), same weights, '
-                                               'cache filled with random K/V' % steps)
+                                        sample=how + ' on the CPU oracle (numpy fp32 restatement of the reference '
+                                        'engine), %s weights, cache filled with random K/V' % (
+                                            'same' if M is CFG4 else 'random'))
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -214,31 +214,18 @@ class Decoder:
         torch.cuda.current_stream(self.dev).wait_stream(s)
         return g, out
 
-    def _snapshot(self):
-        return [(st.K.clone(), st.V.clone(), st.levels.nodes.clone()) for st in self.states], \
-            self._tok.clone(), self._pos.clone()
-
-    def _restore(self, snap):
-        sts, tok, pos = snap
-        for st, (K, V, N) in zip(self.states, sts):
-            st.K.copy_(K)
-            st.V.copy_(V)
-            st.levels.nodes.copy_(N)
-        self._tok.copy_(tok)
-        self._pos.copy_(pos)
-
     def _ensure_graphs(self):
-        """Capture the step graphs once (a capture runs the kernels, so the state is saved and restored)."""
+        """Capture the step graphs once. Capturing records the launches without running them; the one eager
+        warm-up step before it (library attribute set-up, cuBLAS handles) feeds the current tokens at the current
+        positions, which the next real step repeats exactly: it writes the same k/v rows at the same positions and
+        forms the same tree nodes, and it advances no token or position, so no state needs to be saved around it
+        (a copy of every cache would double the memory of a long-context decoder)."""
         if self._graph is not None or not self.use_graphs:
             return
-        snap = self._snapshot()
-        self._forward_step()  # warm-up outside capture (library attribute setup, cuBLAS handles)
-        self._restore(snap)
+        self._forward_step()
+        torch.cuda.current_stream(self.dev).synchronize()
         self._graph, _ = self._capture(self._forward_step)
-        self._restore(snap)
         self._graph_greedy, _ = self._capture(self._greedy_step)
-        self._restore(snap)
-        del snap
 
     # -------------------------------------------------------------- public API
     @torch.no_grad()
