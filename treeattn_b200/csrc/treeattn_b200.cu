@@ -283,11 +283,13 @@ int num_sms() {
 // Decode mode for B*H (b, h) pairs of row_bytes-wide K/V rows: -1 = persistent pipelined kernel (enough pairs
 // for every SM, rows of at most 128 bytes so that two CTAs share an SM), otherwise the number of CTAs per (b, h)
 // of the cluster kernel (~4 resident CTAs per SM). With wider rows the persistent kernel runs one CTA per SM and
-// its consumer warps cannot hide their latency, so the cluster kernel (several CTAs per SM) streams faster.
+// its consumer warps cannot hide their latency, so the cluster kernel (several CTAs per SM) streams faster once
+// there are about three pairs per SM; below that (e.g. 320 pairs of 32768-token contexts, dh 128: 0.54 vs 0.47
+// of HBM bandwidth measured; 512 pairs: 0.66 vs 0.72) the persistent kernel's one-item-ahead descent wins.
 int default_splits(int B, int H, int row_bytes) {
   const int pairs = B * H;
   if (pairs <= 0) return 1;
-  if (pairs >= num_sms()) return row_bytes <= 128 ? -1 : 1;
+  if (pairs >= num_sms()) return (row_bytes <= 128 || pairs < 3 * num_sms()) ? -1 : 1;
   const int target = 4 * num_sms();
   int s = 1;
   while (s < 8 && pairs * s < target) s <<= 1;
