@@ -136,6 +136,34 @@ def test_select_random(T, L0, wmax, dh, dt):
     _check_select(q, k, L0, wmax, qdtype=dt, kdtype=dt)
 
 
+@pytest.mark.parametrize('T,L0,wmax,dh,dt,perm', [(8192, 6, 16, 64, torch.bfloat16, False),
+                                                  (512, 5, 4, 64, torch.float32, False),
+                                                  (1024, 3, 8, 128, torch.float16, True),
+                                                  (4096, 5, 16, 32, torch.bfloat16, True),
+                                                  (1000, 3, 16, 64, torch.float32, False),
+                                                  (2048, 4, 12, 64, torch.bfloat16, False)])
+def test_select_tile_matches_warp_kernel(T, L0, wmax, dh, dt, perm):
+    """Whole sequences go through the tile kernel (dense per-level scores in shared memory, one thread per query);
+    fewer than 32 queries per call through the warp-per-query kernel. Same scores in the same order, so ids,
+    validity and scores are bit-identical (shuffled positions, a ragged last tile, a capacity that is not a power
+    of two)."""
+    ops = _ops()
+    g = np.random.default_rng(T + L0 + dh)
+    B, H = 2, 3
+    q = torch.as_tensor(g.standard_normal((B, H, T, dh)).astype(np.float32)).to(DEV, dt)
+    k = torch.as_tensor(g.standard_normal((B, H, T, dh)).astype(np.float32)).to(DEV, dt)
+    Lm = int(math.ceil(math.log2(T))) - 1
+    lv = ops.build_levels(k, T, L0, Lm)
+    tq = torch.randperm(T, device=DEV) if perm else torch.arange(T, device=DEV)
+    ids, vld, sct = ops.select(q, lv, tq, wmax)
+    for s0 in range(0, T, 16):
+        i2, v2, s2 = ops.select(q[:, :, s0:s0 + 16], lv, tq[s0:s0 + 16], wmax)
+        assert torch.equal(i2, ids[:, :, s0:s0 + 16]), s0
+        assert torch.equal(v2, vld[:, :, s0:s0 + 16]), s0
+        assert torch.equal(s2, sct[:, :, s0:s0 + 16]), s0
+    _no_device_error()
+
+
 def test_select_per_batch_positions_and_small_lm():
     """Per-sequence positions (decode form) and a top level below the highest position bit (the reference then
     never injects the older subtrees: seg.py:54-57 with Lm < log2 t)."""

@@ -328,6 +328,211 @@ __global__ void __launch_bounds__(128) select_kernel(SelectParams p) {
   }
 }
 
+// ------------------------------------------------------------------------------------------------ tile select
+// Whole-sequence descent for 128 queries of one (b, h) per CTA (prefill / select_seg on long sequences). The
+// warp-per-query kernel above reads every candidate's node row from L2 and spends most of its instructions on
+// per-level scoring and ranking; here the CTA scores each level DENSELY once for all its queries - every node of
+// the level in the past of the tile's last query, against all 128 queries - as a small fp32 FMA GEMM on
+// shared-memory tiles, and then each thread (one query) descends on its candidates' scores read from shared
+// memory, keeping its beam in registers.
+//  * The dot products accumulate in exactly the order of Descent::score (even 4-element chunks into one sum, odd
+//    chunks into another, in element order, then (a0 + a1) * 2^-l), so scores are bit-identical to the warp
+//    kernel's, and so is the selection (same (score, smaller id) order through the same 64-bit keys).
+//  * A level whose candidates all fit the beam (every query of the warp) keeps them without ranking; otherwise the
+//    best w of the 2*nk + 1 candidate keys are found by a fully unrolled insertion network into a sorted register
+//    list (compare-exchange on 64-bit keys: the order is a total order, so the network's result is exact).
+constexpr int TS_QT = 128;       // queries per CTA = threads
+constexpr int TS_THREADS = 128;  // GEMM: thread = 4 node rows x 8 queries of a 32-row block
+constexpr int TS_RB = 32;        // node rows per staged block
+constexpr int TS_RMAX = 128;     // largest level (nodes: cap >> L0) the score table may hold
+constexpr int TS_WMAX = 16;      // largest beam the register list holds
+
+// rmax = nodes of the leaf level (cap >> L0), the largest level
+template <int DH>
+__host__ __device__ inline size_t select_tile_smem_bytes(int rmax) {
+  return (size_t)DH * TS_QT * 4                  // qT[d][q]
+         + (size_t)DH * (TS_RB + 4) * 4          // nodeT[d][r] of one block (padded rows)
+         + (size_t)rmax * TS_QT * 4;             // S[r][q] of one level
+}
+
+__device__ __forceinline__ int key_id(unsigned long long k) { return 0x7fffffff - (int)(uint32_t)k; }
+__device__ __forceinline__ float key_score(unsigned long long k) {
+  uint32_t u = (uint32_t)(k >> 32);
+  u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+  return __uint_as_float(u);
+}
+
+template <typename QT, int DH, int W>
+__global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* qT = reinterpret_cast<float*>(smem_raw);
+  constexpr int NP = TS_RB + 4;  // nodeT row pitch (floats)
+  float* nodeT = qT + DH * TS_QT;
+  float* S = nodeT + DH * NP;
+  __shared__ int s_tmax;
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int n0 = blockIdx.x * TS_QT;
+  const LevelView& lv = p.lv;
+  const float* nodes_bh = lv.nodes + b * lv.s_b + h * lv.s_h;
+
+  // ---------------------------------------------------------------- the tile's queries (fp32, transposed)
+  const int q = tid;
+  int t = -1;
+  if (tid == 0) s_tmax = -1;
+  __syncthreads();
+  if (n0 + q < p.Nq) {
+    const int64_t tt = p.tq[b * p.tq_sb + (int64_t)(n0 + q) * p.tq_st];
+    if (tt < 0 || tt >= lv.cap) {
+      record_error(DEV_POS_RANGE, K_SELECT, (int)tt, lv.cap);
+    } else {
+      t = (int)tt;
+      atomicMax(&s_tmax, t);
+    }
+  }
+  constexpr int QV = TypeInfo<QT>::VEC;  // elements per 16-byte load (rows 16-byte aligned: checked by the host)
+  for (int x = tid; x < TS_QT * (DH / QV); x += TS_THREADS) {
+    const int qq = x % TS_QT, c = x / TS_QT;  // consecutive threads: consecutive queries (conflict-free writes)
+    float v[QV];
+    if (n0 + qq < p.Nq) {
+      load_vec_f32<QT>(reinterpret_cast<const QT*>(p.q) + b * p.q_sb + h * p.q_sh + (int64_t)(n0 + qq) * p.q_st +
+                           c * QV, v);
+    } else {
+#pragma unroll
+      for (int e = 0; e < QV; ++e) v[e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < QV; ++e) qT[(c * QV + e) * TS_QT + qq] = v[e];
+  }
+  __syncthreads();
+  const int tmax = s_tmax;
+  const int w = p.wmax;  // <= W
+  unsigned long long kept[W];  // this query's beam, best first (0 = empty slot: below every real key)
+#pragma unroll
+  for (int i = 0; i < W; ++i) kept[i] = 0ull;
+  int nk = 0;
+
+  const int tr = tid >> 4, tq8 = (tid & 15) * 8;  // GEMM: rows tr*4..+3 of the block, queries tq8..tq8+7
+  for (int l = lv.Lm; l >= lv.L0; --l) {
+    const int rows = tmax < 0 ? 0 : min(tmax >> l, lv.cap >> l);  // nodes fully in the past of the last query
+    const float scale = pow2_neg(l);
+    const float* lvl = nodes_bh + (int64_t)lv.off[l] * DH;
+    // ---------------------------------------------------------------- dense scores of this level
+    for (int r0 = 0; r0 < rows; r0 += TS_RB) {
+      const int nr = min(TS_RB, rows - r0);
+      __syncthreads();  // previous block's readers of nodeT are done
+      for (int x = tid; x < TS_RB * (DH / 4); x += TS_THREADS) {
+        const int r = x % TS_RB, c4 = x / TS_RB;  // consecutive threads: consecutive rows (conflict-free writes)
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nr) v = __ldg(reinterpret_cast<const float4*>(lvl + (int64_t)(r0 + r) * DH + c4 * 4));
+        nodeT[(c4 * 4 + 0) * NP + r] = v.x;
+        nodeT[(c4 * 4 + 1) * NP + r] = v.y;
+        nodeT[(c4 * 4 + 2) * NP + r] = v.z;
+        nodeT[(c4 * 4 + 3) * NP + r] = v.w;
+      }
+      __syncthreads();
+      float a0[4][8], a1[4][8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a0[i][j] = a1[i][j] = 0.f;
+#pragma unroll 2
+      for (int cc = 0; cc < DH / 4; ++cc) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = cc * 4 + e;
+          const float4 nv = *reinterpret_cast<const float4*>(nodeT + d * NP + tr * 4);
+          const float4 q0 = *reinterpret_cast<const float4*>(qT + d * TS_QT + tq8);
+          const float4 q1 = *reinterpret_cast<const float4*>(qT + d * TS_QT + tq8 + 4);
+          const float nr4[4] = {nv.x, nv.y, nv.z, nv.w};
+          const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (cc & 1) a1[i][j] = fmaf(qv[j], nr4[i], a1[i][j]);
+              else a0[i][j] = fmaf(qv[j], nr4[i], a0[i][j]);
+            }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = r0 + tr * 4 + i;
+        if (tr * 4 + i < nr) {
+          float4 o0, o1;
+          o0.x = (a0[i][0] + a1[i][0]) * scale; o0.y = (a0[i][1] + a1[i][1]) * scale;
+          o0.z = (a0[i][2] + a1[i][2]) * scale; o0.w = (a0[i][3] + a1[i][3]) * scale;
+          o1.x = (a0[i][4] + a1[i][4]) * scale; o1.y = (a0[i][5] + a1[i][5]) * scale;
+          o1.z = (a0[i][6] + a1[i][6]) * scale; o1.w = (a0[i][7] + a1[i][7]) * scale;
+          *reinterpret_cast<float4*>(S + r * TS_QT + tq8) = o0;
+          *reinterpret_cast<float4*>(S + r * TS_QT + tq8 + 4) = o1;
+        }
+      }
+    }
+    __syncthreads();
+    // ---------------------------------------------------------------- one level of this thread's descent
+    // candidates: the children of the kept nodes (all in the past), then the newly available past-only subtree
+    const int bit = (t >= 0) ? (t >> l) & 1 : 0;
+    unsigned long long c[2 * W + 1];
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      if (i < nk) {
+        const int m = key_id(kept[i]);
+        c[2 * i] = order_key(S[(2 * m) * TS_QT + q], 2 * m);
+        c[2 * i + 1] = order_key(S[(2 * m + 1) * TS_QT + q], 2 * m + 1);
+      } else {
+        c[2 * i] = c[2 * i + 1] = 0ull;
+      }
+    }
+    {
+      const int inj = (t >> l) - 1;
+      c[2 * W] = bit ? order_key(S[inj * TS_QT + q], inj) : 0ull;
+    }
+    const int n = 2 * nk + bit;
+    const bool rank = (l == lv.L0) || n > w;  // the order matters (the leaf level) or some candidate is dropped
+    if (__any_sync(0xffffffffu, rank)) {
+      // the best w keys, best first: insertion network into a sorted list (empty slots hold 0)
+#pragma unroll
+      for (int i = 0; i < W; ++i) kept[i] = 0ull;
+#pragma unroll
+      for (int j = 0; j < 2 * W + 1; ++j) {
+        unsigned long long key = c[j];
+#pragma unroll
+        for (int i = 0; i < W; ++i) {
+          const unsigned long long hi = kept[i] > key ? kept[i] : key;
+          key = kept[i] > key ? key : kept[i];
+          kept[i] = hi;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < W; ++i)
+        if (i >= w) kept[i] = 0ull;
+    } else {
+      // every candidate is kept (order irrelevant above the leaf level): children in place, the injected one after
+#pragma unroll
+      for (int i = 0; i < W; ++i) kept[i] = i < 2 * nk ? c[i] : (i == 2 * nk ? c[2 * W] : 0ull);
+    }
+    nk = min(n, w);
+    __syncthreads();  // S is rewritten by the next level
+  }
+  (void)lane;
+  // ---------------------------------------------------------------- outputs (best first)
+  if (n0 + q < p.Nq) {
+    const size_t obase = ((size_t)bh * p.Nq + n0 + q) * p.wl;
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      if (i < p.wl) {
+        const bool ok = t >= 0 && i < nk;
+        p.ids[obase + i] = ok ? key_id(kept[i]) : 0;
+        p.vld[obase + i] = ok ? 1 : 0;
+        if (p.sct) p.sct[obase + i] = ok ? key_score(kept[i]) : -INFINITY;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ finish
 // seg.py:106-119 (leaves_to_pos, finish), one thread per query. Leaf m expands to positions
 // [m*leaf, (m+1)*leaf) stored as tree_pos[j*wl + i] = ids[i]*leaf + j (the reference's cat([2*ids, 2*ids+1])

@@ -121,6 +121,14 @@ struct BuildLevels {
 template <typename QT, int DH>
 struct Select {
   static int run(ta::SelectParams p, cudaStream_t st) {
+    // whole sequences (many queries per (b, h)) on trees whose leaf level fits the score table: the tile kernel
+    const int rmax = p.lv.cap >> p.lv.L0;
+    const int64_t qs = (int64_t)sizeof(QT);
+    const bool q_aligned = (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0 && (p.q_sb * qs) % 16 == 0 &&
+                           (p.q_sh * qs) % 16 == 0 && (p.q_st * qs) % 16 == 0;
+    if (DH >= 32 && p.Nq >= ta::TS_QT / 4 && rmax <= ta::TS_RMAX && p.wmax <= ta::TS_WMAX && p.wl <= p.wmax &&
+        q_aligned)
+      return p.wmax <= 4 ? tile<4>(p, st, rmax) : (p.wmax <= 8 ? tile<8>(p, st, rmax) : tile<16>(p, st, rmax));
     // 4 warps (queries) per CTA unless their staging rows would not fit in shared memory
     int warps = 4;
     auto smem_for = [&](int w) {
@@ -138,6 +146,22 @@ struct Select {
     if (nq == 0) return TA_OK;
     ta::select_kernel<QT, DH><<<(unsigned)((nq + warps - 1) / warps), warps * 32, smem, st>>>(p);
     return check_launch("ta_select");
+  }
+
+  template <int W>
+  static int tile(ta::SelectParams p, cudaStream_t st, int rmax) {
+    auto kern = ta::select_tile_kernel<QT, DH, W>;
+    const size_t smem = ta::select_tile_smem_bytes<DH>(rmax);
+    static size_t smem_set = 0;
+    if (smem > smem_set) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return check_launch("ta_select (shared memory attribute)");
+      smem_set = smem;
+    }
+    if ((int64_t)p.B * p.H == 0 || p.Nq == 0) return TA_OK;
+    const dim3 grid((unsigned)((p.Nq + ta::TS_QT - 1) / ta::TS_QT), (unsigned)(p.B * p.H), 1);
+    kern<<<grid, ta::TS_THREADS, smem, st>>>(p);
+    return check_launch("ta_select(tile)");
   }
 };
 
