@@ -65,13 +65,55 @@ __global__ void build_leaf_level_kernel(const T* __restrict__ k, int64_t k_sb, i
   const T* kp = k + b * k_sb + h * k_sh + d;
   PairwiseAcc acc;
   const int p0 = m * leaf;
-  for (int i = 0; i < leaf; ++i) {
-    const int p = p0 + i;
-    float v = 0.f;
-    if ((p != 0 || !zero_sink) && p < T_len) v = to_f32(kp[(int64_t)p * k_st]);
-    acc.push(i, v);
+  auto key_at = [&](int p) -> float {
+    return ((p != 0 || !zero_sink) && p < T_len) ? to_f32(kp[(int64_t)p * k_st]) : 0.f;
+  };
+  if (leaf >= 8) {
+    for (int i0 = 0; i0 < leaf; i0 += 8) {  // 8 independent loads in flight, then the ordered pairwise adds
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = key_at(p0 + i0 + j);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc.push(i0 + j, v[j]);
+    }
+  } else {
+    for (int i = 0; i < leaf; ++i) acc.push(i, key_at(p0 + i));
   }
   nodes[b * n_sb + h * n_sh + (int64_t)m * dh + d] = acc.stk[L0];
+}
+
+// Upper levels of one (b, h) per CTA in shared memory: the complete leaf-level nodes are staged, then every level
+// L0+1..Lm is formed in parallel over (node, dim) as parent = left + right (the same fp32 adds, in the same
+// order, as the reference's repeated pairwise sums) and written out. Only nodes complete within the first T_len
+// positions are formed (m < T_len >> l).
+__global__ void __launch_bounds__(256) build_upper_levels_smem_kernel(float* __restrict__ nodes, int64_t n_sb,
+                                                                      int64_t n_sh, int H, int dh, LevelView lv,
+                                                                      int T_len) {
+  extern __shared__ __align__(16) float lvl_smem[];
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  float* base = nodes + b * n_sb + h * n_sh;
+  const int n_leaf = T_len >> lv.L0;
+  // stage the leaf level; level l (> L0) is then built in place at offset 0 of the buffer's second half
+  float* cur = lvl_smem;
+  float* nxt = lvl_smem + (size_t)n_leaf * dh;
+  const float* src0 = base + (int64_t)lv.off[lv.L0] * dh;
+  for (int x = threadIdx.x; x < n_leaf * dh / 4; x += blockDim.x)
+    reinterpret_cast<float4*>(cur)[x] = reinterpret_cast<const float4*>(src0)[x];
+  __syncthreads();
+  for (int l = lv.L0 + 1; l <= lv.Lm; ++l) {
+    const int n = T_len >> l;
+    if (n == 0) break;
+    float* dst = base + (int64_t)lv.off[l] * dh;
+    for (int x = threadIdx.x; x < n * dh; x += blockDim.x) {
+      const int m = x / dh, d = x - (x / dh) * dh;
+      const float v = cur[(2 * m) * dh + d] + cur[(2 * m + 1) * dh + d];
+      nxt[x] = v;
+      dst[x] = v;
+    }
+    __syncthreads();
+    float* tmp = cur; cur = nxt; nxt = tmp;
+  }
 }
 
 // Upper levels: one thread per (bh, dim) walks levels L0+1..Lm, parent = left + right.

@@ -110,8 +110,24 @@ struct BuildLevels {
       if (int r = check_launch("ta_build_levels(leaf)")) return r;
     }
     if (Lm > L0 && n_leaf > 1) {
-      const int n = B * H * DH;
-      ta::build_upper_levels_kernel<<<(n + 127) / 128, 128, 0, st>>>(nodes, n_sb, n_sh, H, DH, lv, B * H, T_len);
+      // one CTA per (b, h) in shared memory (the leaf level and the level being formed) when it fits and the node
+      // rows are 16-byte aligned, else one thread per (b, h, dim) walking the levels
+      const size_t smem = (size_t)2 * n_leaf * DH * sizeof(float);
+      const bool aligned = (reinterpret_cast<uintptr_t>(nodes) & 15u) == 0 && (n_sb * 4) % 16 == 0 &&
+                           (n_sh * 4) % 16 == 0;
+      if (aligned && smem <= 200 * 1024 && (int64_t)B * H <= 0x7fffffff) {
+        static size_t smem_set = 0;
+        if (smem > 48 * 1024 && smem > smem_set) {
+          cudaFuncSetAttribute(ta::build_upper_levels_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               200 * 1024);
+          smem_set = 200 * 1024;
+        }
+        if (B * H > 0)
+          ta::build_upper_levels_smem_kernel<<<(unsigned)(B * H), 256, smem, st>>>(nodes, n_sb, n_sh, H, DH, lv, T_len);
+      } else {
+        const int n = B * H * DH;
+        ta::build_upper_levels_kernel<<<(n + 127) / 128, 128, 0, st>>>(nodes, n_sb, n_sh, H, DH, lv, B * H, T_len);
+      }
       if (int r = check_launch("ta_build_levels(upper)")) return r;
     }
     return TA_OK;
