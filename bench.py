@@ -477,6 +477,8 @@ def run_prefill_attn(a, dev):
     if a.profile_steps:
         torch.cuda.cudart().cudaProfilerStart()
         for _ in range(a.profile_steps):
+            _ops.build_levels(k, T, L0, Lm, zero_sink=True, out=lv)
+            _ops.select(q, lv, tq, topk)
             _ops.prefill_attn(q, k, v, tq, ids, vld, ntree, leaf, window, dh ** -0.5, out=out, want_nkeys=False)
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()

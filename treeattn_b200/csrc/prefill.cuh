@@ -111,6 +111,14 @@ __device__ __forceinline__ uint64_t range_mask64(int lo, int hi) {
   return upto & ~((1ull << lo) - 1ull);
 }
 
+// 2^x by the hardware's approximate base-2 exponential (ex2.approx.ftz: 2^-inf = 0, relative error ~2^-22,
+// below the 16-bit rounding of P that follows).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -185,7 +193,7 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
   }
   for (int i = tid; i < p.tile_words; i += PF_THREADS) tbits[i] = 0u;
   if (warp < 4)
-    for (int i = 0; i < p.leaf_words; ++i) qbits[tid * p.leaf_words + i] = 0u;
+    for (int i = 0; i < p.leaf_words; ++i) qbits[i * PF_QT + tid] = 0u;
   if (warp == 4 && lane == 0) {
     tma_prefetch_map(&tm_q);
     tma_prefetch_map(&tm_k);
@@ -213,12 +221,12 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       const int ntree = p.n_tree ? (int)p.n_tree[qid] : p.ntree_const;
       const int64_t sb = qid * p.wl;
       const int64_t leaf = 1ll << L0;
-      uint32_t* qb = qbits + tid * p.leaf_words;
+      uint32_t* qb = qbits + tid;  // word i of this query's leaf bitmap at qb[i * PF_QT] (conflict-free)
       for (int i = 0; i < p.wl && i < ntree; ++i) {
         if (!p.vld[sb + i]) continue;
         const int64_t m = p.ids[sb + i];
         if (m < 0 || m * leaf >= (int64_t)w0) continue;  // only the part before the window counts
-        qb[m >> 5] |= 1u << (m & 31);
+        qb[(m >> 5) * PF_QT] |= 1u << (m & 31);
         const int a = (int)(m * leaf), c = (int)min(m * leaf + leaf, (int64_t)w0) - 1;
         bitmap_set_range(tbits, a >> 6, c >> 6);
       }
@@ -319,7 +327,7 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
     int keys = 0;
     bool ok = true;
     unsigned char* prow_base = sP + (tid >> 3) * 1024 + (tid & 7) * 128;
-    const uint32_t* qb = qbits + tid * p.leaf_words;
+    const uint32_t* qb = qbits + tid;
 
     auto consume = [&](int j) -> bool {
       // warp-uniform outcome: the tcgen05.ld below is executed by the whole warp
@@ -327,7 +335,7 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       tc_fence_after();
       const float mj = (j & 1) ? m_h1 : m_h0;
       const bool live = mj != -INFINITY;
-      const float f = live ? exp2f(m_acc - mj) : 1.f;
+      const float f = live ? ex2_approx(m_acc - mj) : 1.f;
 #pragma unroll
       for (int c = 0; c < DH / 32; ++c) {
         float v[32];
@@ -373,10 +381,10 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
           uint64_t lm;
           if (L0 >= 6) {
             const int m = P0 >> L0;
-            lm = ((qb[m >> 5] >> (m & 31)) & 1u) ? ~0ull : 0ull;
+            lm = ((qb[(m >> 5) * PF_QT] >> (m & 31)) & 1u) ? ~0ull : 0ull;
           } else {
             const int m0 = P0 >> L0, nb = 64 >> L0;  // leaves of this tile (L0 >= 1: nb <= 32, in one word)
-            const uint32_t field = (qb[m0 >> 5] >> (m0 & 31)) & (nb == 32 ? 0xffffffffu : ((1u << nb) - 1u));
+            const uint32_t field = (qb[(m0 >> 5) * PF_QT] >> (m0 & 31)) & (nb == 32 ? 0xffffffffu : ((1u << nb) - 1u));
             lm = 0ull;
             for (int i = 0; i < nb; ++i)
               if ((field >> i) & 1u) lm |= range_mask64(i << L0, ((i + 1) << L0) - 1);
@@ -387,28 +395,40 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
         }
       }
       keys += __popcll(vm);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        s[i] = ((vm >> i) & 1ull) ? s[i] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[i]);
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float mu = m_new == -INFINITY ? 0.f : m_new;
-      l_run *= exp2f(m_run - mu);
-      // P row (16-bit, rounded; the same rounded weights enter l) into the swizzled K-major P buffer
+      // warp-uniform shortcut: a tile masked for all 32 queries of the warp contributes nothing (its P rows are
+      // zero and the running max is unchanged)
+      const bool none = __all_sync(0xffffffffu, vm == 0ull);
       unsigned char* prow = prow_base + (n & 1) * C::P_BYTES;
+      float m_new = m_run;
+      if (none) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        // max over the raw scores (scaling by a positive constant is monotone under rounding: max commutes)
+        float mx = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t pk = pack2<T>(exp2f(s[c * 8 + 2 * e] - mu), exp2f(s[c * 8 + 2 * e + 1] - mu));
-          const float2 back = unpack2<T>(pk);
-          l_run += back.x + back.y;
-          w[e] = pk;
+        for (int i = 0; i < 64; ++i) {
+          s[i] = ((vm >> i) & 1ull) ? s[i] : -INFINITY;
+          mx = fmaxf(mx, s[i]);
         }
-        *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        m_new = fmaxf(m_run, mx * p.scale_log2);
+        const float mu = m_new == -INFINITY ? 0.f : m_new;
+        l_run *= ex2_approx(m_run - mu);
+        // P row (16-bit, rounded; the same rounded weights enter l) into the swizzled K-major P buffer;
+        // p = 2^(s * scale_log2 - mu) with the scaling fused into one FMA
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t pk = pack2<T>(ex2_approx(fmaf(s[c * 8 + 2 * e], p.scale_log2, -mu)),
+                                         ex2_approx(fmaf(s[c * 8 + 2 * e + 1], p.scale_log2, -mu)));
+            const float2 back = unpack2<T>(pk);
+            l_run += back.x + back.y;
+            w[e] = pk;
+          }
+          *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();

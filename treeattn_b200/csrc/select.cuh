@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(128) select_kernel(SelectParams p) {
 //    chunks into another, in element order, then (a0 + a1) * 2^-l), so scores are bit-identical to the warp
 //    kernel's, and so is the selection (same (score, smaller id) order through the same 64-bit keys).
 //  * A level whose candidates all fit the beam (every query of the warp) keeps them without ranking; otherwise the
-//    best w of the 2*nk + 1 candidate keys are found by a fully unrolled insertion network into a sorted register
-//    list (compare-exchange on 64-bit keys: the order is a total order, so the network's result is exact).
+//    best w of the 2*nk + 1 candidate keys are found by fully unrolled bitonic networks on register arrays
+//    (compare-exchange on 64-bit keys: the order is a total order, so the networks' result is exact).
 constexpr int TS_QT = 128;       // queries per CTA = threads
 constexpr int TS_THREADS = 128;  // GEMM: thread = 4 node rows x 8 queries of a 32-row block
 constexpr int TS_RB = 32;        // node rows per staged block
@@ -360,6 +360,36 @@ __device__ __forceinline__ float key_score(unsigned long long k) {
   uint32_t u = (uint32_t)(k >> 32);
   u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
   return __uint_as_float(u);
+}
+
+// Compare-exchange networks on register arrays of 64-bit keys (indices are compile-time after unrolling).
+__device__ __forceinline__ void cswap(unsigned long long& a, unsigned long long& b, bool desc) {
+  const bool sw = desc ? (a < b) : (a > b);
+  const unsigned long long x = sw ? b : a, y = sw ? a : b;
+  a = x;
+  b = y;
+}
+
+// Sort a bitonic sequence of N keys (descending if desc).
+template <int N>
+__device__ __forceinline__ void bitonic_merge(unsigned long long* v, bool desc) {
+#pragma unroll
+  for (int j = N / 2; j > 0; j >>= 1)
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if ((i & j) == 0) cswap(v[i], v[i + j], desc);
+}
+
+// Sort N keys (N a power of two; descending if desc).
+template <int N>
+__device__ __forceinline__ void bitonic_sort(unsigned long long* v, bool desc) {
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1)
+#pragma unroll
+    for (int j = k / 2; j > 0; j >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if ((i & j) == 0) cswap(v[i], v[i + j], (((i & k) == 0) == desc));
 }
 
 template <typename QT, int DH, int W>
@@ -414,7 +444,9 @@ __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p)
   for (int i = 0; i < W; ++i) kept[i] = 0ull;
   int nk = 0;
 
-  const int tr = tid >> 4, tq8 = (tid & 15) * 8;  // GEMM: rows tr*4..+3 of the block, queries tq8..tq8+7
+  // GEMM: rows tr*4..+3 of the block, queries tq4..tq4+3 and 64+tq4..64+tq4+3 (16 threads read 256 contiguous
+  // bytes of a query row: conflict-free)
+  const int tr = tid >> 4, tq4 = (tid & 15) * 4;
   for (int l = lv.Lm; l >= lv.L0; --l) {
     const int rows = tmax < 0 ? 0 : min(tmax >> l, lv.cap >> l);  // nodes fully in the past of the last query
     const float scale = pow2_neg(l);
@@ -444,8 +476,8 @@ __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p)
         for (int e = 0; e < 4; ++e) {
           const int d = cc * 4 + e;
           const float4 nv = *reinterpret_cast<const float4*>(nodeT + d * NP + tr * 4);
-          const float4 q0 = *reinterpret_cast<const float4*>(qT + d * TS_QT + tq8);
-          const float4 q1 = *reinterpret_cast<const float4*>(qT + d * TS_QT + tq8 + 4);
+          const float4 q0 = *reinterpret_cast<const float4*>(qT + d * TS_QT + tq4);
+          const float4 q1 = *reinterpret_cast<const float4*>(qT + d * TS_QT + 64 + tq4);
           const float nr4[4] = {nv.x, nv.y, nv.z, nv.w};
           const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
@@ -466,8 +498,8 @@ __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p)
           o0.z = (a0[i][2] + a1[i][2]) * scale; o0.w = (a0[i][3] + a1[i][3]) * scale;
           o1.x = (a0[i][4] + a1[i][4]) * scale; o1.y = (a0[i][5] + a1[i][5]) * scale;
           o1.z = (a0[i][6] + a1[i][6]) * scale; o1.w = (a0[i][7] + a1[i][7]) * scale;
-          *reinterpret_cast<float4*>(S + r * TS_QT + tq8) = o0;
-          *reinterpret_cast<float4*>(S + r * TS_QT + tq8 + 4) = o1;
+          *reinterpret_cast<float4*>(S + r * TS_QT + tq4) = o0;
+          *reinterpret_cast<float4*>(S + r * TS_QT + 64 + tq4) = o1;
         }
       }
     }
@@ -493,12 +525,16 @@ __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p)
     const int n = 2 * nk + bit;
     const bool rank = (l == lv.L0) || n > w;  // the order matters (the leaf level) or some candidate is dropped
     if (__any_sync(0xffffffffu, rank)) {
-      // the best w keys, best first: insertion network into a sorted list (empty slots hold 0)
+      // the best w keys, best first (empty slots hold 0, below every real key): sort the first W children
+      // descending and the other W ascending, keep the elementwise larger halves (the W best of the 2W, a
+      // bitonic sequence), sort it, then let the injected candidate bubble in
+      bitonic_sort<W>(c, true);
+      bitonic_sort<W>(c + W, false);
 #pragma unroll
-      for (int i = 0; i < W; ++i) kept[i] = 0ull;
-#pragma unroll
-      for (int j = 0; j < 2 * W + 1; ++j) {
-        unsigned long long key = c[j];
+      for (int i = 0; i < W; ++i) kept[i] = c[i] > c[W + i] ? c[i] : c[W + i];
+      bitonic_merge<W>(kept, true);
+      {
+        unsigned long long key = c[2 * W];
 #pragma unroll
         for (int i = 0; i < W; ++i) {
           const unsigned long long hi = kept[i] > key ? kept[i] : key;
