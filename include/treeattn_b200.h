@@ -101,6 +101,14 @@ int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B
                    int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const void* cand, int cand64, int Kc,
                    float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st, float* lse, void* stream);
 
+/* Replaces the backward of fastseg.sparse_attn (fastseg.py:80-110 _attn_bwd, 158-170 _SparseAttnFn.backward):
+ * from the forward's o and lse (natural log) and the output gradient dout, dq (q's dtype) and the fp32 key / value
+ * gradients dk, dv, which are ACCUMULATED (vector atomics, as the reference does; zero them first). All tensors
+ * dense: q, o, dout, dq (B, H, T, dh); k, v, dk, dv (B, H, T_kv, dh); cand (B, H, T, Kc), -1 = unused. */
+int ta_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                       const float* lse, int dtype, int B, int H, int T, int T_kv, int dh, const void* cand,
+                       int cand64, int Kc, float scale, void* dq, float* dk, float* dv, void* stream);
+
 /* Replaces fastseg.gather_dot (fastseg.py:118-130, _gather_dot_kernel 34-47): out (B, H, N, C) fp32 =
  * scale * q[b,h,n] . S[b,h,cand[b,h,n,c]] with ids clamped to [0, M-1]. q and S share `dtype`. */
 int ta_gather_dot(const void* q, const void* S, int dtype, int B, int H, int N, int M, int C, int dh,

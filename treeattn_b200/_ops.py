@@ -239,6 +239,25 @@ def sparse_attn_fwd(q, k, v, cand, scale):
     return o, lse
 
 
+def sparse_attn_bwd(q, k, v, cand, o, lse, do, scale):
+    """Gradients of sparse_attn (fastseg _attn_bwd): returns dq (q's dtype), dk, dv (k's / v's dtype; accumulated
+    in fp32 by the kernel)."""
+    _need_cuda('sparse_attn_bwd', q, k, v, cand, o, lse, do)
+    q, k, v, o, do = [t.contiguous() for t in (q, k, v, o, do)]
+    if cand.dtype not in (torch.int32, torch.int64):
+        cand = cand.to(torch.int64)
+    cand = cand.contiguous()
+    B, H, T, dh = q.shape
+    T_kv = k.shape[2]
+    dq = torch.empty_like(q)
+    dk = torch.zeros(B, H, T_kv, dh, device=q.device, dtype=torch.float32)
+    dv = torch.zeros(B, H, T_kv, dh, device=q.device, dtype=torch.float32)
+    _lib.call('ta_sparse_attn_bwd', _p(q), _p(k), _p(v), _p(o), _p(do), _p(lse.contiguous()), _code(q), B, H, T,
+              T_kv, dh, _p(cand), 1 if cand.dtype == torch.int64 else 0, cand.shape[-1], float(scale), _p(dq),
+              _p(dk), _p(dv), _stream(q))
+    return dq, dk.to(k.dtype), dv.to(v.dtype)
+
+
 def gather_dot(q, S, cand, scale):
     """fastseg.gather_dot: (B, H, N, C) fp32 = scale * q . S[cand] (ids clamped to [0, M-1])."""
     _need_cuda('gather_dot', q, S, cand)

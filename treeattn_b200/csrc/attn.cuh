@@ -555,6 +555,110 @@ __global__ void __launch_bounds__(128) sparse_attn_kernel(SparseAttnParams p) {
   if (lane == 0 && p.lse) p.lse[qid] = wa.l > 0.f ? (wa.m + log2f(wa.l)) * LN2 : -INFINITY;
 }
 
+// ------------------------------------------------------------------------------------------------ sparse_attn bwd
+// fastseg.py:80-110 _attn_bwd / 158-170 _SparseAttnFn.backward: with p = exp(scale q.k - lse) over the query's
+// candidate keys (-1 unused), di = o . do, dp = do . v and ds = p (dp - di):
+//   dq = sum_keys ds scale k          (fp32, stored in q's dtype)
+//   dk[key] += ds scale q, dv[key] += p do   (fp32 accumulators shared by all queries: vector atomics, as the
+//                                             reference accumulates them; the caller zeroes them)
+// One warp per query, LPR lanes per key row (16-byte chunks), RPW keys per warp step; dot products reduced within
+// the row's lanes, dq across the rows at the end. All tensors dense: q, o, do, dq (B, H, T, dh); k, v, dk, dv
+// (B, H, T_kv, dh).
+struct SparseAttnBwdParams {
+  const void *q, *k, *v, *o, *dout;
+  const float* lse;       // (B,H,T) natural log
+  const void* cand;       // (B,H,T,Kc) contiguous, int32 or int64
+  int cand64;
+  int B, H, T, Kc, T_kv;
+  float scale;
+  void* dq;
+  float* dk;
+  float* dv;
+};
+
+__device__ __forceinline__ void atomic_add_vec(float* dst, const float* v, int n) {
+  // n = 4 or 8, dst 16-byte aligned (sm_90+: one vector atomic per 16 bytes)
+  for (int i = 0; i < n; i += 4) atomicAdd(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+}
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(128) sparse_attn_bwd_kernel(SparseAttnBwdParams p) {
+  constexpr int VEC = TypeInfo<T>::VEC;
+  constexpr int LPR = DH / VEC;  // lanes per key row
+  constexpr int RPW = 32 / LPR;  // key rows per warp step
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qid = (int64_t)blockIdx.x * 4 + warp;
+  if (qid >= (int64_t)p.B * p.H * p.T) return;
+  const int64_t bh = qid / p.T;
+  const int c = lane % LPR, sub = lane / LPR;
+  const int64_t row = qid * DH + c * VEC;
+  float q[VEC], dov[VEC], ov[VEC], dq[VEC];
+  load_vec_f32<T>(reinterpret_cast<const T*>(p.q) + row, q);
+  load_vec_f32<T>(reinterpret_cast<const T*>(p.dout) + row, dov);
+  load_vec_f32<T>(reinterpret_cast<const T*>(p.o) + row, ov);
+  float di = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    di = fmaf(ov[i], dov[i], di);
+    dq[i] = 0.f;
+  }
+  di = warp_sum_sub(di, LPR);
+  const float lse = p.lse[qid];
+  const T* kb = reinterpret_cast<const T*>(p.k) + bh * (int64_t)p.T_kv * DH + c * VEC;
+  const T* vb = reinterpret_cast<const T*>(p.v) + bh * (int64_t)p.T_kv * DH + c * VEC;
+  float* dkb = p.dk + bh * (int64_t)p.T_kv * DH + c * VEC;
+  float* dvb = p.dv + bh * (int64_t)p.T_kv * DH + c * VEC;
+  const int64_t cbase = qid * p.Kc;
+  for (int base = 0; base < p.Kc; base += RPW) {
+    const int g = base + sub;
+    int64_t pos = -1;
+    if (g < p.Kc) {
+      pos = p.cand64 ? reinterpret_cast<const int64_t*>(p.cand)[cbase + g]
+                     : (int64_t)reinterpret_cast<const int32_t*>(p.cand)[cbase + g];
+      if (pos >= p.T_kv) {
+        if (c == 0) record_error(DEV_INDEX_RANGE, K_SPARSE_ATTN, (int)pos, p.T_kv);
+        pos = -1;
+      }
+    }
+    const bool valid = pos >= 0;
+    float kv[VEC], vv[VEC];
+    if (valid) {
+      load_vec_f32<T>(kb + pos * DH, kv);
+      load_vec_f32<T>(vb + pos * DH, vv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) kv[i] = vv[i] = 0.f;
+    }
+    float sdot = 0.f, pdot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      sdot = fmaf(q[i], kv[i], sdot);
+      pdot = fmaf(dov[i], vv[i], pdot);
+    }
+    sdot = warp_sum_sub(sdot, LPR);
+    pdot = warp_sum_sub(pdot, LPR);
+    const float pr = valid ? expf(sdot * p.scale - lse) : 0.f;
+    const float ds = pr * (pdot - di);
+    const float dss = ds * p.scale;
+    if (valid) {
+      float gk[VEC], gv[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        dq[i] = fmaf(dss, kv[i], dq[i]);
+        gk[i] = dss * q[i];
+        gv[i] = pr * dov[i];
+      }
+      atomic_add_vec(dkb + pos * DH, gk, VEC);
+      atomic_add_vec(dvb + pos * DH, gv, VEC);
+    }
+  }
+  // dq: sum over the RPW row slots (lanes with the same chunk c)
+#pragma unroll
+  for (int i = 0; i < VEC; ++i)
+    for (int o = LPR; o < 32; o <<= 1) dq[i] += __shfl_xor_sync(0xffffffffu, dq[i], o);
+  if (sub == 0) store_vec_from_f32<T>(reinterpret_cast<T*>(p.dq) + row, dq);
+}
+
 // ------------------------------------------------------------------------------------------------ gather_dot
 // fastseg.py:118-130: out[b,h,n,c] = scale * q[b,h,n] . S[b,h,cand[b,h,n,c]] in fp32; ids clamped to [0, M-1]
 // as the reference does. One warp per query row.

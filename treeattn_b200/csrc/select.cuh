@@ -394,8 +394,8 @@ __device__ __forceinline__ void bitonic_sort(unsigned long long* v, bool desc) {
 
 template <typename QT, int DH, int W>
 __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* qT = reinterpret_cast<float*>(smem_raw);
+  extern __shared__ __align__(16) unsigned char ts_smem_raw[];
+  float* qT = reinterpret_cast<float*>(ts_smem_raw);
   constexpr int NP = TS_RB + 4;  // nodeT row pitch (floats)
   float* nodeT = qT + DH * TS_QT;
   float* S = nodeT + DH * NP;

@@ -255,6 +255,16 @@ struct SparseAttn {
 };
 
 template <typename T, int DH>
+struct SparseAttnBwd {
+  static int run(ta::SparseAttnBwdParams p, cudaStream_t st) {
+    const int64_t nq = (int64_t)p.B * p.H * p.T;
+    if (nq == 0) return TA_OK;
+    ta::sparse_attn_bwd_kernel<T, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_sparse_attn_bwd");
+  }
+};
+
+template <typename T, int DH>
 struct GatherDot {
   static int run(ta::GatherDotParams p, cudaStream_t st) {
     const int64_t nq = (int64_t)p.B * p.H * p.N;
@@ -654,6 +664,26 @@ int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B
   p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
   p.lse = lse;
   return by_type_dh<SparseAttn>(dtype, dh, p, S(stream));
+}
+
+int ta_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                       const float* lse, int dtype, int B, int H, int T, int T_kv, int dh, const void* cand,
+                       int cand64, int Kc, float scale, void* dq, float* dk, float* dv, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_sparse_attn_bwd: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_sparse_attn_bwd: unsupported head dim %d", dh);
+  if (B < 0 || H < 0 || T < 0 || T_kv < 0 || Kc < 0) return fail(TA_ERR_ARG, "ta_sparse_attn_bwd: bad sizes");
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv || (Kc > 0 && !cand))
+    return fail(TA_ERR_ARG, "ta_sparse_attn_bwd: null pointer");
+  for (const void* ptr : {q, k, v, o, dout, (const void*)dq, (const void*)dk, (const void*)dv})
+    if (!aligned16(ptr)) return fail(TA_ERR_ARG, "ta_sparse_attn_bwd: tensors must be 16-byte aligned");
+  ta::SparseAttnBwdParams p{};
+  p.q = q; p.k = k; p.v = v; p.o = o; p.dout = dout; p.lse = lse;
+  p.cand = cand; p.cand64 = cand64;
+  p.B = B; p.H = H; p.T = T; p.Kc = Kc; p.T_kv = T_kv;
+  p.scale = scale;
+  p.dq = dq; p.dk = dk; p.dv = dv;
+  return by_type_dh<SparseAttnBwd>(dtype, dh, p, S(stream));
 }
 
 int ta_gather_dot(const void* q, const void* Sn, int dtype, int B, int H, int N, int M, int C, int dh,

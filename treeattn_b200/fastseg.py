@@ -32,18 +32,27 @@ def gather_dot(q, S, cand, scale):
 
 # ------------------------------------------------------------------ attention over the selected keys
 class _SparseAttnFn(torch.autograd.Function):
+    """fastseg.py:143-170: forward saves q, k, v, cand, o and the log-sum-exp; backward recomputes the softmax
+    weights from them (ta_sparse_attn_bwd)."""
+
     @staticmethod
     def forward(ctx, q, k, v, cand, scale):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         o, lse = _ops.sparse_attn_fwd(q, k, v, cand, scale)
+        ctx.save_for_backward(q, k, v, cand, o, lse)
+        ctx.scale = scale
         return o
 
     @staticmethod
     def backward(ctx, do):
-        raise NotImplementedError('sparse_attn backward is not implemented in treeattn_b200 (inference path)')
+        q, k, v, cand, o, lse = ctx.saved_tensors
+        dq, dk, dv = _ops.sparse_attn_bwd(q, k, v, cand, o, lse, do, ctx.scale)
+        return dq, dk, dv, None, None
 
 
 def sparse_attn(q, k, v, cand, scale):
-    """cand: (b,H,T,K) int, -1 = unused slot. Exact softmax attention over the used keys."""
+    """cand: (b,H,T,K) int, -1 = unused slot. Exact softmax attention over the used keys; differentiable in q, k
+    and v (fastseg.py:173-177)."""
     return _SparseAttnFn.apply(q, k, v, cand, scale)
 
 
@@ -111,15 +120,22 @@ class SegAttention(nn.Module):
         b, T, C = x.shape
         q, k, v = self.c_attn(x).split(C, dim=2)
         q, k, v = [t.view(b, T, self.H, self.dh).transpose(1, 2) for t in (q, k, v)]
+        if self._needs_grad(q, k, v):
+            out = self.sparse_attend(q, k, v)
+            return self.c_proj(out.transpose(1, 2).reshape(b, T, C))
         out = torch.empty(b, T, self.H, self.dh, device=x.device, dtype=q.dtype)
         self.sparse_attend(q, k, v, out=out.transpose(1, 2))
         return self.c_proj(out.view(b, T, C))
 
-    def _lhat(self, q, k):
+    @staticmethod
+    def _needs_grad(q, k, v):
+        return torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v))
+
+    def _lhat(self, q, k, with_logits=False):
         cfg = self.cfg
         b, H, T, dh = q.shape
         if cfg.beam_mode != 'pred':
-            return None
+            return (None, None) if with_logits else None
         t = torch.arange(T, device=q.device)
         qd = q.detach()
         feats = [qd, torch.log(qd.float().norm(dim=-1, keepdim=True) + 1e-6).to(qd.dtype),
@@ -129,7 +145,8 @@ class SegAttention(nn.Module):
             prefix_mean = (kd.cumsum(2) - kd) / t.clamp(min=1).view(1, 1, T, 1).float()
             feats.append(prefix_mean.to(qd.dtype))
         plog = self.pred(torch.cat(feats, -1))
-        return self.classes[plog.argmax(-1).detach()]
+        lhat = self.classes[plog.argmax(-1).detach()]
+        return (lhat, plog) if with_logits else lhat
 
     def sparse_attend(self, q, k, v, out=None):
         cfg = self.cfg
@@ -137,9 +154,12 @@ class SegAttention(nn.Module):
             gate_apply(None, None, None, cfg.gate_q)
         if cfg.neighbors:
             raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
-        if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
-            raise NotImplementedError('SegAttention backward is not implemented in treeattn_b200 (inference path); '
-                                      'run under torch.no_grad()')
+        if self._needs_grad(q, k, v):
+            o = self._sparse_attend_autograd(q, k, v)
+            if out is not None:
+                out.copy_(o)
+                return out
+            return o
         b, H, T, dh = q.shape
         scale = 1.0 / math.sqrt(dh)
         self.aux = {}
@@ -163,4 +183,56 @@ class SegAttention(nn.Module):
             self.aux['keys_nb'] = torch.zeros((), device=q.device)
             self.aux['nb_leaves'] = torch.zeros((), device=q.device)
             self.aux['leaves_used'] = n_used.mean()
+        return out
+
+    def _sparse_attend_autograd(self, q, k, v):
+        """The training form (fastseg.py:345-405 as the reference runs it): selection without gradients, the
+        explicit candidate list [tree positions, neighbour positions, static keys] deduplicated, then the
+        differentiable sparse_attn (ta_sparse_attn / ta_sparse_attn_bwd); in training mode with the learned budget
+        head also its classification loss in aux['pred']."""
+        cfg = self.cfg
+        b, H, T, dh = q.shape
+        dev = q.device
+        scale = 1.0 / math.sqrt(dh)
+        t = torch.arange(T, device=dev)
+        self.aux = {}
+        lhat, plog = self._lhat(q, k, with_logits=True)
+        if lhat is None:
+            lhat = torch.full((b, H, T), cfg.beam, dtype=torch.long, device=dev)
+        with torch.no_grad():
+            sel = select_seg(q.detach(), k.detach(), lhat, cfg)
+            tree_pos, nb_pos, leaf_ok = sel['tree_pos'], sel['nb_pos'], sel['leaf_ok']
+            wl = leaf_ok.shape[-1]
+            leaf = tree_pos.shape[-1] // max(wl, 1)
+            NBK = nb_pos.shape[-1]
+            Lw = max(cfg.local, 3)
+            st = torch.cat([torch.zeros(T, 1, dtype=torch.long, device=dev),
+                            t.unsqueeze(1) - torch.arange(Lw, device=dev).unsqueeze(0)], 1)
+            st = st.masked_fill(st < 0, -1).view(1, 1, T, 1 + Lw).expand(b, H, T, 1 + Lw)
+            cand = torch.cat([tree_pos, nb_pos, st], -1)
+            used = leaf_ok & (torch.arange(wl, device=dev) < sel['n_tree'].unsqueeze(-1))
+            tv_used = torch.cat([used] * leaf, -1) & (tree_pos >= 0)
+            rest = torch.cat([nb_pos >= 0, st >= 0], -1)
+            keep = dedupe_fast(cand, torch.cat([tv_used, rest], -1))
+            cand_k = torch.where(keep, cand, torch.full_like(cand, -1)).to(torch.int32)
+        out = sparse_attn(q, k, v, cand_k, scale)
+        self.aux['keys_total'] = keep.sum(-1).float().mean()
+        self.aux['keys_tree'] = keep[..., :leaf * wl].sum(-1).float().mean()
+        self.aux['keys_nb'] = keep[..., leaf * wl:leaf * wl + NBK].sum(-1).float().mean()
+        self.aux['nb_leaves'] = sel['nb_leaves'].float().mean()
+        self.aux['leaves_used'] = used.sum(-1).float().mean()
+        if self.training and plog is not None:
+            with torch.no_grad():
+                tv_full = torch.cat([leaf_ok] * leaf, -1) & (tree_pos >= 0)
+                keep_f = dedupe_fast(cand, torch.cat([tv_full, rest], -1))
+                Sf = gather_dot(q.detach(), k.detach(), cand, scale)
+                wf = torch.softmax(Sf.masked_fill(~keep_f, float('-inf')), -1)
+                wt = wf[..., :leaf * wl]
+                leaf_mass = sum(wt[..., j * wl:(j + 1) * wl] for j in range(leaf))
+                total = leaf_mass.sum(-1, keepdim=True)
+                need = (leaf_mass.cumsum(-1) < 0.9 * total).sum(-1) + 1
+                label = (need.unsqueeze(-1) > self.classes).sum(-1).clamp(max=len(self.classes) - 1)
+                rows = total.squeeze(-1) > 0
+            if bool(rows.any()):
+                self.aux['pred'] = F.cross_entropy(plog.float()[rows], label[rows])
         return out
