@@ -101,6 +101,15 @@ int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B
                    int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const void* cand, int cand64, int Kc,
                    float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st, float* lse, void* stream);
 
+/* Replaces dyntree.LaneTree.search (dyntree.py:108-127): beam descent for one query per lane over a dynamic
+ * content tree whose nodes hold key sums and counts. q (P, dh) fp32; sums (P, 2^(D+1) - 1, dh) fp32 and cnt
+ * (P, 2^(D+1) - 1) int32 packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2, l = 0..D). A child is valid
+ * when its parent is and its count is positive and scores q . sum / count; per level the best min(wmax, 2 * width)
+ * are kept. Outputs (P, wl) best first: node ids of level D (0 when invalid), validity, scores (-inf when invalid;
+ * sct may be NULL). */
+int ta_lane_search(const float* q, const float* sums, const int32_t* cnt, int P, int D, int dh, int wmax, int wl,
+                   int64_t* ids, uint8_t* vld, float* sct, void* stream);
+
 /* Replaces the backward of fastseg.sparse_attn (fastseg.py:80-110 _attn_bwd, 158-170 _SparseAttnFn.backward):
  * from the forward's o and lse (natural log) and the output gradient dout, dq (q's dtype) and the fp32 key / value
  * gradients dk, dv, which are ACCUMULATED (vector atomics, as the reference does; zero them first). All tensors

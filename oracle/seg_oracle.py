@@ -13,7 +13,7 @@ import numpy as np
 
 F32 = np.float32
 
-__all__ = ['level_sums', 'tree_pass', 'leaves_to_pos', 'finish', 'n_tree_fixed', 'static_keys', 'dedupe',
+__all__ = ['level_sums', 'tree_pass', 'lane_search', 'leaves_to_pos', 'finish', 'n_tree_fixed', 'static_keys', 'dedupe',
            'sparse_attn', 'gather_dot', 'select_seg', 'seg_attention', 'layer_norm', 'gelu', 'gpt_forward',
            'weights_from_state_dict', 'SegStateNP', 'seg_attend', 'DecoderNP', 'bf16_round', 'Lw_of']
 
@@ -234,6 +234,52 @@ def seg_attention(q, k, v, wmax, beam, local, L0=1, chunk=64):
     stats = dict(keys_total=float(keep.sum(-1).mean()), keys_tree=float(keep[..., :leaf * wl].sum(-1).mean()),
                  keys_nb=0.0, nb_leaves=0.0, leaves_used=float(used.sum(-1).mean()))
     return out, stats
+
+
+# ------------------------------------------------------------------------------------------------ dynamic tree
+def lane_search(q, sums, cnt, D, wmax, with_margin=False):
+    """dyntree.py:108-127 LaneTree.search: beam descent from the root (level 0) to level D over a tree whose
+    nodes hold key SUMS and counts, packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2). A node is
+    valid when its parent is and its count is positive; its score is q . sum / count. At each level the children
+    [2*cur, 2*cur + 1] of the kept nodes are ranked and the best min(wmax, 2 * width) are kept, best first.
+    q (P, dh); sums (P, 2^(D+1) - 1, dh); cnt (P, 2^(D+1) - 1). Returns ids, vld, sct (P, wl) (+ the tie margin:
+    smallest gap between the last kept and the best dropped valid candidate, relative to |q| |mean|)."""
+    q = np.asarray(q, F32)
+    sums = np.asarray(sums, F32)
+    cnt = np.asarray(cnt, np.int64)
+    P, dh = q.shape
+    cur = np.zeros((P, 1), np.int64)
+    cvld = cnt[:, :1] > 0
+    sct = None
+    margin = np.full(P, np.inf)
+    qn = np.linalg.norm(q.astype(np.float64), axis=-1)
+    for l in range(1, D + 1):
+        off = (1 << l) - 1
+        ch = np.concatenate([2 * cur, 2 * cur + 1], -1)
+        cv = np.concatenate([cvld, cvld], -1)
+        cc = np.take_along_axis(cnt[:, off:off + (1 << l)], ch, 1)
+        cv = cv & (cc > 0)
+        sm = sums[np.arange(P)[:, None], off + ch]
+        sc = (np.einsum('pd,pcd->pc', q, sm).astype(F32) / np.maximum(cc, 1).astype(F32)).astype(F32)
+        sc = np.where(cv, sc, F32(-np.inf))
+        w = min(wmax, ch.shape[-1])
+        order = np.argsort(-sc, axis=-1, kind='stable')
+        if with_margin:
+            srt = np.take_along_axis(sc, order, -1).astype(np.float64)
+            nrm = np.linalg.norm(sm.astype(np.float64), axis=-1) / np.maximum(cc, 1)
+            nrm = np.take_along_axis(nrm, order, -1) * qn[:, None]
+            cut = cv.sum(-1) > w
+            if w < sc.shape[-1]:
+                with np.errstate(invalid='ignore', divide='ignore'):
+                    gap = (srt[:, w - 1] - srt[:, w]) / np.maximum(np.maximum(nrm[:, w - 1], nrm[:, w]), 1e-30)
+                margin = np.minimum(margin, np.where(cut, gap, np.inf))
+        order = order[:, :w]
+        cur = np.take_along_axis(ch, order, -1)
+        cvld = np.take_along_axis(cv, order, -1)
+        sct = np.take_along_axis(sc, order, -1)
+    if with_margin:
+        return cur, cvld, sct, margin
+    return cur, cvld, sct
 
 
 # ------------------------------------------------------------------------------------------------ model

@@ -4,7 +4,7 @@ The reference (Dex8123/treeattn, pure Python/PyTorch) is importable only in the 
 mounted read-only; it is made importable as the package `treeattn` through a symlink in a temp directory.
 The GPU box never runs this script: the tests read the committed .npz files.
 
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [--only=lanetree]
 
 Leaf blocks of 2^L0 tokens (the benchmark configs use 32, 64 and 128) are produced with the reference's own
 functions on the level-shifted tree ("adapter"): seg.level_sums, then seg.tree_pass with
@@ -28,9 +28,31 @@ def import_reference(path):
     os.symlink(os.path.abspath(path), os.path.join(d, 'treeattn'))
     sys.path.insert(0, d)
     import treeattn  # noqa: F401
-    from treeattn import config, engine, fastseg, forest, model, seg, attention_dyn
+    from treeattn import config, engine, fastseg, forest, model, seg, attention_dyn, dyntree
     return dict(config=config, engine=engine, fastseg=fastseg, forest=forest, model=model, seg=seg,
-                attention_dyn=attention_dyn)
+                attention_dyn=attention_dyn, dyntree=dyntree)
+
+
+def lanetree_golden(R):
+    """dyntree.LaneTree.search (dyntree.py:108-127) on a tree the reference builds (2-means splits) and grows
+    (insertions), lanes with different prefix lengths; the node sums / counts are stored packed level by level
+    (level l at rows 2^l - 1 .. 2^(l+1) - 2), the way the B200 kernel reads them."""
+    dyn = R['dyntree']
+    torch.manual_seed(5)
+    P, C, dh = 6, 256, 32
+    kfull = torch.randn(P, C, dh)
+    n = torch.tensor([0, 17, 64, 100, 150, 200])
+    tree = dyn.LaneTree(kfull, n, iters=3)
+    ar = torch.arange(P)
+    for i in range(20):
+        kpos = n + i
+        tree.insert(kfull[ar, kpos], kpos, kpos >= 1)
+    qt = torch.randn(P, dh)
+    d = dict(q=np_(qt), sums=np_(torch.cat(tree.sums, 1)), cnt=np_(torch.cat(tree.cnt, 1)), D=tree.D)
+    for wmax in (4, 8, 3):
+        cur, cvld, sct = tree.search(qt, wmax)
+        d['ids_%d' % wmax], d['vld_%d' % wmax], d['sct_%d' % wmax] = np_(cur), np_(cvld), np_(sct)
+    return d
 
 
 def np_(t):
@@ -54,8 +76,13 @@ def adapter_tree_pass(R, q, k, L0, wmax):
     return seg.tree_pass(q.float(), getU, tq, Lm - sh, wmax)
 
 
-def main(ref_path):
+def main(ref_path, only=None):
     R = import_reference(ref_path)
+    if only == 'lanetree':  # regenerate this fixture alone (the others are left untouched)
+        d = lanetree_golden(R)
+        np.savez_compressed(os.path.join(HERE, 'lanetree.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
+        print('wrote lanetree')
+        return
     Config = R['config'].Config
     seg, fastseg, engine, ad = R['seg'], R['fastseg'], R['engine'], R['attention_dyn']
     out = {}
@@ -187,10 +214,14 @@ def main(ref_path):
                                                                          for p in m.state_dict().values()]),
                           L0=L0, **{'stat_' + kk: vv for kk, vv in stats.items()})
 
+    out['lanetree'] = lanetree_golden(R)
+
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
         print('wrote', name, sum(np.asarray(vv).nbytes for vv in d.values()) // 1024, 'KiB')
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('TREEATTN_REFERENCE', '/root/reference'))
+    args = [x for x in sys.argv[1:] if not x.startswith('--only=')]
+    only = next((x.split('=', 1)[1] for x in sys.argv[1:] if x.startswith('--only=')), None)
+    main(args[0] if args else os.environ.get('TREEATTN_REFERENCE', '/root/reference'), only)

@@ -549,3 +549,49 @@ def test_bad_arguments_raise():
         ops.select(q, lv, torch.arange(16, device=DEV), 0)  # wmax 0
     with pytest.raises(ValueError):
         ops.build_levels(q.cpu(), 16, 1, 3)  # CPU tensors: no CPU path
+
+
+# ------------------------------------------------------------------------------------------------ lane tree
+@pytest.mark.parametrize('wmax', [4, 8, 3])
+def test_lane_search_golden(wmax):
+    """LaneTree.search on the tree the reference built and grew (golden): same valid leaves, scores within 1e-6."""
+    from treeattn_b200.dyntree import LaneTree
+    g = load('lanetree')
+    tree = LaneTree.from_levels(to_dev(g['sums']), torch.as_tensor(g['cnt']).to(DEV))
+    assert tree.D == int(g['D'])
+    ids, vld, sct = tree.search(to_dev(g['q']), wmax)
+    _, _, _, margin = oracle.lane_search(g['q'], g['sums'], g['cnt'], int(g['D']), wmax, with_margin=True)
+    bad, n, _ = compare_sets(ids.cpu().numpy(), vld.cpu().numpy(), g['ids_%d' % wmax], g['vld_%d' % wmax],
+                             tied(margin))
+    assert bad == 0 and n == g['q'].shape[0]
+    v = vld.cpu().numpy()
+    np.testing.assert_allclose(np.where(v, sct.cpu().numpy(), 0), np.where(g['vld_%d' % wmax], g['sct_%d' % wmax], 0),
+                               atol=1e-6)
+    _no_device_error()
+
+
+@pytest.mark.parametrize('P,D,dh,wmax', [(300, 9, 64, 16), (64, 6, 128, 8), (100, 10, 16, 64), (7, 3, 32, 2)])
+def test_lane_search_random(P, D, dh, wmax):
+    """Random trees with empty subtrees (count 0 prunes a node and everything below it): kernel vs oracle."""
+    from treeattn_b200.dyntree import LaneTree
+    rng = np.random.default_rng(P + D)
+    NN = (2 << D) - 1
+    leaf_cnt = rng.integers(0, 3, (P, 1 << D))
+    leaf_cnt[rng.random((P, 1 << D)) < 0.3] = 0
+    leaf_sum = (rng.standard_normal((P, 1 << D, dh)) * leaf_cnt[..., None]).astype(np.float32)
+    sums, cnt = [leaf_sum], [leaf_cnt]
+    for _ in range(D):
+        s_, c_ = sums[0], cnt[0]
+        sums.insert(0, s_.reshape(P, -1, 2, dh).sum(2))
+        cnt.insert(0, c_.reshape(P, -1, 2).sum(2))
+    S = np.concatenate(sums, 1).astype(np.float32)
+    Cn = np.concatenate(cnt, 1).astype(np.int32)
+    assert S.shape[1] == NN
+    q = rng.standard_normal((P, dh)).astype(np.float32)
+    tree = LaneTree.from_levels(to_dev(S), torch.as_tensor(Cn).to(DEV))
+    ids, vld, sct = tree.search(to_dev(q), wmax)
+    rids, rvld, rsct, margin = oracle.lane_search(q, S, Cn, D, wmax, with_margin=True)
+    bad, n, _ = compare_sets(ids.cpu().numpy(), vld.cpu().numpy(), rids, rvld, tied(margin))
+    assert bad == 0 and n >= 0.98 * P, (bad, n)
+    assert (vld.cpu().numpy().sum(-1) == rvld.sum(-1)).all()
+    _no_device_error()

@@ -153,3 +153,14 @@ def test_engine_matches_forward_leaf_blocks():
     dec.reset(2)
     got = np.stack([dec.step(idx[:, t], t)[0] for t in range(128)], 1)
     np.testing.assert_allclose(got, ref, atol=1e-5)
+
+
+@pytest.mark.parametrize('wmax', [4, 8, 3])
+def test_lane_search_golden(wmax):
+    """LaneTree.search (dyntree.py:108-127) on a tree the reference built and grew: the oracle's descent keeps
+    the same valid leaves (no query is near a tie here) with scores within 1e-6."""
+    g = load('lanetree')
+    ids, vld, sct, margin = oracle.lane_search(g['q'], g['sums'], g['cnt'], int(g['D']), wmax, with_margin=True)
+    bad, n, _ = compare_sets(ids, vld, g['ids_%d' % wmax], g['vld_%d' % wmax], tied(margin))
+    assert bad == 0 and n == g['q'].shape[0]
+    np.testing.assert_allclose(np.where(vld, sct, 0), np.where(g['vld_%d' % wmax], g['sct_%d' % wmax], 0), atol=1e-6)

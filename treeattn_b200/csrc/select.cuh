@@ -569,6 +569,89 @@ __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p)
   }
 }
 
+// ------------------------------------------------------------------------------------------------ lane tree
+// Beam descent over the dynamic content tree (dyntree.py:108-127 LaneTree.search): one query per lane (tree),
+// nodes holding key SUMS and counts, packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2, l = 0..D).
+// From the root, at every level the children of the kept nodes are candidates; a child is valid when its count is
+// positive (its parent being valid), scored by q . sum / count; the best min(wmax, 2 * previous width) valid
+// ones are kept, best first, ties by the smaller node id. One warp per query: lane-per-candidate scoring from L2,
+// rank-counting top-k on the (score, id) order keys (Descent::topk).
+struct LaneSearchParams {
+  const float* q;      // (P, dh) fp32
+  const float* sums;   // (P, NN, dh) fp32, NN = 2^(D+1) - 1
+  const int32_t* cnt;  // (P, NN)
+  int P, D, wmax, wl;
+  int64_t* ids;        // (P, wl) node ids of level D, best first (0 in invalid slots)
+  uint8_t* vld;        // (P, wl)
+  float* sct;          // (P, wl) scores (-inf invalid), may be null
+};
+
+template <int DH>
+__global__ void __launch_bounds__(128) lane_search_kernel(LaneSearchParams p) {
+  __shared__ DescentScratch scr[4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qi = (int64_t)blockIdx.x * 4 + warp;
+  if (qi >= p.P) return;
+  DescentScratch& sc = scr[warp];
+  const int NN = (2 << p.D) - 1;
+  const float* sums = p.sums + qi * (int64_t)NN * DH;
+  const int32_t* cnt = p.cnt + qi * (int64_t)NN;
+  for (int d = lane; d < DH; d += 32) sc.qf[d] = p.q[qi * DH + d];
+  if (lane == 0) sc.kid[0] = 0;
+  __syncwarp();
+  int nk = cnt[0] > 0 ? 1 : 0;
+  int w = 1;
+  for (int l = 1; l <= p.D; ++l) {
+    const int off = (1 << l) - 1;
+    // valid children of the kept nodes, compacted (kept node i -> children 2m, 2m+1)
+    int n = 0;
+    for (int base = 0; base < 2 * nk; base += 32) {
+      const int j = base + lane;
+      int c = -1;
+      if (j < 2 * nk) {
+        const int m = sc.kid[j >> 1];
+        c = 2 * m + (j & 1);
+        if (cnt[off + c] <= 0) c = -1;
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, c >= 0);
+      if (c >= 0) sc.cid[n + __popc(mask & ((1u << lane) - 1u))] = c;
+      n += __popc(mask);
+    }
+    __syncwarp();
+    // lane-per-candidate scores: (q . sum) / count in fp32
+    for (int base = 0; base < n; base += 32) {
+      const int j = base + lane;
+      if (j < n) {
+        const int c = sc.cid[j];
+        const float* row = sums + (int64_t)(off + c) * DH;
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < DH / 4; ++cc) {
+          const float4 qv = *reinterpret_cast<const float4*>(sc.qf + cc * 4);
+          const float4 v = __ldg(reinterpret_cast<const float4*>(row + cc * 4));
+          if (cc & 1) {
+            a1 = fmaf(qv.x, v.x, a1); a1 = fmaf(qv.y, v.y, a1); a1 = fmaf(qv.z, v.z, a1); a1 = fmaf(qv.w, v.w, a1);
+          } else {
+            a0 = fmaf(qv.x, v.x, a0); a0 = fmaf(qv.y, v.y, a0); a0 = fmaf(qv.z, v.z, a0); a0 = fmaf(qv.w, v.w, a0);
+          }
+        }
+        const float s = (a0 + a1) / (float)cnt[off + c];
+        sc.csc[j] = s;
+        sc.ckey[j] = order_key(s, c);
+      }
+    }
+    __syncwarp();
+    w = min(p.wmax, 2 * w);
+    nk = Descent<DH>::topk(n, w, sc, lane);
+  }
+  for (int i = lane; i < p.wl; i += 32) {
+    const bool ok = i < nk;
+    p.ids[qi * p.wl + i] = ok ? sc.kid[i] : 0;
+    p.vld[qi * p.wl + i] = ok ? 1 : 0;
+    if (p.sct) p.sct[qi * p.wl + i] = ok ? sc.ksc[i] : -INFINITY;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ finish
 // seg.py:106-119 (leaves_to_pos, finish), one thread per query. Leaf m expands to positions
 // [m*leaf, (m+1)*leaf) stored as tree_pos[j*wl + i] = ids[i]*leaf + j (the reference's cat([2*ids, 2*ids+1])

@@ -265,6 +265,15 @@ struct SparseAttnBwd {
 };
 
 template <typename T, int DH>
+struct LaneSearch {
+  static int run(ta::LaneSearchParams p, cudaStream_t st) {
+    if (p.P == 0) return TA_OK;
+    ta::lane_search_kernel<DH><<<(unsigned)((p.P + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_lane_search");
+  }
+};
+
+template <typename T, int DH>
 struct GatherDot {
   static int run(ta::GatherDotParams p, cudaStream_t st) {
     const int64_t nq = (int64_t)p.B * p.H * p.N;
@@ -664,6 +673,19 @@ int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B
   p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
   p.lse = lse;
   return by_type_dh<SparseAttn>(dtype, dh, p, S(stream));
+}
+
+int ta_lane_search(const float* q, const float* sums, const int32_t* cnt, int P, int D, int dh, int wmax, int wl,
+                   int64_t* ids, uint8_t* vld, float* sct, void* stream) {
+  g_err.clear();
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_lane_search: unsupported head dim %d", dh);
+  if (P < 0 || D < 1 || D > 24) return fail(TA_ERR_ARG, "ta_lane_search: bad sizes P=%d D=%d", P, D);
+  if (wmax < 1 || wmax > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_lane_search: wmax=%d outside [1, 64]", wmax);
+  if (wl < 1 || wl > wmax) return fail(TA_ERR_ARG, "ta_lane_search: wl=%d outside [1, wmax]", wl);
+  if (!q || !sums || !cnt || !ids || !vld) return fail(TA_ERR_ARG, "ta_lane_search: null pointer");
+  if (!aligned16(q) || !aligned16(sums)) return fail(TA_ERR_ARG, "ta_lane_search: q / sums must be 16-byte aligned");
+  ta::LaneSearchParams p{q, sums, cnt, P, D, wmax, wl, ids, vld, sct};
+  return by_dh<LaneSearch, float>(dh, p, S(stream));
 }
 
 int ta_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
