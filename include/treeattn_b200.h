@@ -101,6 +101,20 @@ int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B
                    int64_t v_sb, int64_t v_sh, int64_t v_st, int T_kv, const void* cand, int cand64, int Kc,
                    float scale, void* o, int64_t o_sb, int64_t o_sh, int64_t o_st, float* lse, void* stream);
 
+/* Replaces seg.neighbor_pass (seg.py:73-103) / fastseg.neighbor_pass_fast (fastseg.py:274-299) on leaf blocks of
+ * 2^L0 tokens: query (b, h, n) at position tq[b*tq_sb + n*tq_st] re-scores the nb_store best leaves stored by each
+ * of the nb_window previous positions (st_leaf / st_score / st_ok (B, H, T_st, nb_store) contiguous, indexed by
+ * position) against the level-L0 node rows leaf_nodes (row m of (b, h) at + b*n_sb + h*n_sh + m*dh, n_leaf rows)
+ * and matches those it scores at least base - nb_rho |base|, scanning no deeper than nb_cap_min +
+ * round((nb_window - nb_cap_min) * match rate over the first nb_probe positions). neighbors == 0 reproduces
+ * cfg.neighbors=False (no matches). Outputs (B, H, Nq, nb_window*nb_store) contiguous: nid (the stored ids), match;
+ * nL (B, H, Nq) = distinct matched leaves. nb_window * nb_store <= 32. */
+int ta_neighbor_pass(const void* q, int q_dtype, int B, int H, int Nq, int dh, int64_t q_sb, int64_t q_sh,
+                     int64_t q_st, const int64_t* tq, int64_t tq_sb, int64_t tq_st, const float* leaf_nodes,
+                     int64_t n_sb, int64_t n_sh, int n_leaf, int L0, const int64_t* st_leaf, const float* st_score,
+                     const uint8_t* st_ok, int T_st, int nb_window, int nb_store, float nb_rho, int nb_probe,
+                     int nb_cap_min, int neighbors, int64_t* nid, uint8_t* match, int64_t* nL, void* stream);
+
 /* Replaces dyntree.LaneTree.search (dyntree.py:108-127): beam descent for one query per lane over a dynamic
  * content tree whose nodes hold key sums and counts. q (P, dh) fp32; sums (P, 2^(D+1) - 1, dh) fp32 and cnt
  * (P, 2^(D+1) - 1) int32 packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2, l = 0..D). A child is valid

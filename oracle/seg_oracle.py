@@ -13,7 +13,7 @@ import numpy as np
 
 F32 = np.float32
 
-__all__ = ['level_sums', 'tree_pass', 'lane_search', 'leaves_to_pos', 'finish', 'n_tree_fixed', 'static_keys', 'dedupe',
+__all__ = ['level_sums', 'tree_pass', 'lane_search', 'neighbor_pass', 'leaves_to_pos', 'finish', 'n_tree_fixed', 'static_keys', 'dedupe',
            'sparse_attn', 'gather_dot', 'select_seg', 'seg_attention', 'layer_norm', 'gelu', 'gpt_forward',
            'weights_from_state_dict', 'SegStateNP', 'seg_attend', 'DecoderNP', 'bf16_round', 'Lw_of']
 
@@ -194,9 +194,51 @@ def gather_dot(q, S, cand, scale):
 
 
 # ------------------------------------------------------------------------------------------------ selection
-def select_seg(q, k, lhat, wmax, L0=1, nb_width=0, with_margin=False):
-    """seg.py:122-140 select_seg with neighbour borrowing switched off (cfg.neighbors=False makes
-    neighbor_pass return no matches, seg.py:97-98): fp32 copies, sink zeroed, levels, descent, finish."""
+def neighbor_pass(q, S_leaf, st_leaf, st_score, st_ok, tq, L0, nb_window, nb_store, nb_rho, nb_probe, nb_cap_min,
+                  neighbors=True, with_margin=False):
+    """seg.py:73-103 neighbor_pass: every query looks at the nb_store best leaves stored by each of the
+    nb_window previous positions (st_* (B, H, T_st, NS) indexed by position), scores them itself
+    (q . S_L0[leaf] / 2^L0) and matches those it scores at least base - rho |base| (base = the stored score); the
+    scan depth is capped by the match rate over the first nb_probe positions: cap = cap_min + round((Wn - cap_min)
+    * rate) (round half to even). Returns ids (B, H, Nq, Wn*NS), match, nL = distinct matched leaves (and, with
+    with_margin, the smallest |score - threshold| relative to |q| |S| / 2^L0: near 0 the match is an fp32 tie)."""
+    q = np.asarray(q, F32)
+    B, H, Nq, dh = q.shape
+    Wn, NS = nb_window, nb_store
+    tq = np.asarray(tq, np.int64)
+    jpos = tq[:, None] - np.arange(1, Wn + 1)[None, :]
+    jval = jpos >= 0
+    jc = np.maximum(jpos, 0)
+    ids = np.asarray(st_leaf)[:, :, jc].reshape(B, H, Nq, Wn * NS)
+    base = np.asarray(st_score, F32)[:, :, jc].reshape(B, H, Nq, Wn * NS)
+    ok0 = (np.asarray(st_ok, bool)[:, :, jc] & jval[None, None, :, :, None]).reshape(B, H, Nq, Wn * NS)
+    U = _gather_rows(np.asarray(S_leaf, F32), np.clip(ids, 0, S_leaf.shape[2] - 1))
+    sc_t = (np.einsum('bhnd,bhncd->bhnc', q, U).astype(F32) * F32(2.0 ** -L0)).astype(F32)
+    thr = (base - (F32(nb_rho) * np.abs(base)).astype(F32)).astype(F32)
+    match = ok0 & (sc_t >= thr)
+    probe = nb_probe * NS
+    rate = (match[..., :probe].sum(-1).astype(F32) / np.maximum(ok0[..., :probe].sum(-1), 1).astype(F32)).astype(F32)
+    cap = nb_cap_min + np.rint(F32(Wn - nb_cap_min) * rate).astype(np.int64)
+    didx = np.arange(Wn * NS) // NS + 1
+    match = match & (didx <= cap[..., None])
+    if not neighbors:
+        match = np.zeros_like(match)
+    idm = np.where(match, ids, -1)
+    ss = np.sort(idm, -1)
+    vs = ss >= 0
+    nL = vs.sum(-1) - ((ss[..., 1:] == ss[..., :-1]) & vs[..., 1:]).sum(-1)
+    if with_margin:
+        nrm = np.linalg.norm(U.astype(np.float64), axis=-1) * np.linalg.norm(q.astype(np.float64), axis=-1)[..., None]
+        gap = np.where(ok0, np.abs(sc_t.astype(np.float64) - thr) / np.maximum(nrm * 2.0 ** -L0, 1e-30), np.inf)
+        return ids, match, nL, gap.min(-1)
+    return ids, match, nL
+
+
+def select_seg(q, k, lhat, wmax, L0=1, nb_width=0, with_margin=False, nb=None):
+    """seg.py:122-140 select_seg: fp32 copies, sink zeroed, levels, descent, neighbour pass, finish. nb = None
+    stands for cfg.neighbors=False (neighbor_pass returns no matches, seg.py:97-98; nb_width slots of empty
+    matches); otherwise nb = dict(nb_window, nb_store, nb_rho, nb_probe, nb_cap_min) runs the neighbour pass on
+    the descent's own results (the nb_store best leaves and scores of every position)."""
     q = np.asarray(q, F32)
     B, H, T, dh = q.shape
     Lm = int(round(math.log2(T))) - 1
@@ -204,10 +246,19 @@ def select_seg(q, k, lhat, wmax, L0=1, nb_width=0, with_margin=False):
     tq = np.arange(T)
     r = tree_pass(q, S, tq, L0, Lm, wmax, with_margin=with_margin)
     ids, vld, sct = r[:3]
-    nid = np.zeros((B, H, T, nb_width), np.int64)
-    match = np.zeros((B, H, T, nb_width), bool)
-    nL = np.zeros((B, H, T), np.int64)
+    nb_margin = None
+    if nb is None:
+        nid = np.zeros((B, H, T, nb_width), np.int64)
+        match = np.zeros((B, H, T, nb_width), bool)
+        nL = np.zeros((B, H, T), np.int64)
+    else:
+        NS = nb['nb_store']
+        nid, match, nL, nb_margin = neighbor_pass(q, S[L0], ids[..., :NS], sct[..., :NS], vld[..., :NS], tq, L0,
+                                                  nb['nb_window'], NS, nb['nb_rho'], nb['nb_probe'],
+                                                  nb['nb_cap_min'], with_margin=True)
     sel = finish(ids, vld, nid, match, nL, lhat, wmax, leaf=1 << L0)
+    if nb_margin is not None:
+        sel['nb_margin'] = nb_margin
     sel['ids'], sel['sct'] = ids, sct
     if with_margin:
         sel['margin'] = r[3]

@@ -4,7 +4,7 @@ The reference (Dex8123/treeattn, pure Python/PyTorch) is importable only in the 
 mounted read-only; it is made importable as the package `treeattn` through a symlink in a temp directory.
 The GPU box never runs this script: the tests read the committed .npz files.
 
-    python tests/golden/make_golden.py /path/to/reference [--only=lanetree]
+    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb]
 
 Leaf blocks of 2^L0 tokens (the benchmark configs use 32, 64 and 128) are produced with the reference's own
 functions on the level-shifted tree ("adapter"): seg.level_sums, then seg.tree_pass with
@@ -76,12 +76,32 @@ def adapter_tree_pass(R, q, k, L0, wmax):
     return seg.tree_pass(q.float(), getU, tq, Lm - sh, wmax)
 
 
+def tiny_gpt_nb_golden(R):
+    """A tiny GPT with neighbour borrowing on (the reference's default cfg.neighbors=True), leaf 2: the forward
+    logits and statistics, and the reference engine's token-by-token logits on the same weights (its decode step
+    stores every position's best leaves and borrows from the previous nb_window positions)."""
+    Config, engine = R['config'].Config, R['engine']
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=3,
+                 neighbors=True, beam_mode='fixed')
+    torch.manual_seed(6)
+    m = R['model'].GPT(cfg).eval()
+    idx = torch.randint(0, 64, (1, 128), generator=torch.Generator().manual_seed(7))
+    with torch.no_grad():
+        logits, _, stats = m(idx)
+        dec = engine.Decoder(engine.weights_from_ours(m.state_dict(), cfg), cfg.n_layer, cfg.n_head, cfg.n_embd,
+                             128, 'seg', cfg, 'cpu')
+        steps = [dec.step(int(idx[0, t]), t) for t in range(128)]
+    return dict(idx=np_(idx), logits=np_(logits), dec_logits=np.stack([np_(st[0]) for st in steps]),
+                dec_keys=np.array([st[1] for st in steps]), **{'stat_' + kk: vv for kk, vv in stats.items()})
+
+
 def main(ref_path, only=None):
     R = import_reference(ref_path)
-    if only == 'lanetree':  # regenerate this fixture alone (the others are left untouched)
-        d = lanetree_golden(R)
-        np.savez_compressed(os.path.join(HERE, 'lanetree.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
-        print('wrote lanetree')
+    single = dict(lanetree=lanetree_golden, tiny_gpt_nb=tiny_gpt_nb_golden)
+    if only in single:  # regenerate this fixture alone (the others are left untouched)
+        d = single[only](R)
+        np.savez_compressed(os.path.join(HERE, only + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
+        print('wrote', only)
         return
     Config = R['config'].Config
     seg, fastseg, engine, ad = R['seg'], R['fastseg'], R['engine'], R['attention_dyn']
@@ -215,6 +235,7 @@ def main(ref_path, only=None):
                           L0=L0, **{'stat_' + kk: vv for kk, vv in stats.items()})
 
     out['lanetree'] = lanetree_golden(R)
+    out['tiny_gpt_nb'] = tiny_gpt_nb_golden(R)
 
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})

@@ -232,3 +232,94 @@ def test_bf16_model_vs_oracle():
     W = oracle.weights_from_state_dict({k: v.float() for k, v in m.state_dict().items()}, cfg.n_layer)
     ref, _ = oracle.gpt_forward(W, idx.numpy(), cfg.n_head, cfg.wmax, cfg.beam, cfg.local, L0=4, bf16=True)
     assert np.abs(logits.float().cpu().numpy() - ref).max() < 2e-2
+
+
+# ------------------------------------------------------------------------------------------------ neighbours
+def test_select_seg_neighbours_golden():
+    """seg.select_seg with neighbour borrowing (ta_neighbor_pass + ta_finish) on the reference's fixture, leaf 2:
+    tree positions, neighbour positions, budgets and nb_leaves equal the reference's on every query."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.seg import select_seg
+    g = load('sel_nb')
+    cfg = Config(attn='seg', seq_len=128, wmax=int(g['wmax']), beam=4, beam_mode='fixed')
+    assert cfg.neighbors and cfg.nb_window == int(g['nb_window']) and cfg.nb_store == int(g['nb_store'])
+    sel = select_seg(torch.as_tensor(g['q']).to(DEV), torch.as_tensor(g['k']).to(DEV),
+                     torch.as_tensor(g['lhat']).to(DEV), cfg)
+    srt = lambda a: np.sort(a, -1)
+    assert (srt(sel['tree_pos'].cpu().numpy()) == srt(g['tree_pos'])).all()
+    assert (srt(sel['nb_pos'].cpu().numpy()) == srt(g['nb_pos'])).all()
+    assert (sel['n_tree'].cpu().numpy() == g['n_tree']).all()
+    assert (sel['nb_leaves'].cpu().numpy() == g['nb_leaves']).all()
+    _no_device_error()
+
+
+def test_gpt_neighbours_golden():
+    """The reference's tiny GPT with neighbour borrowing on (leaf 2): logits within 1e-4 and the aux statistics
+    (keys_total / keys_tree / keys_nb / nb_leaves / leaves_used) equal."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    g = load('tiny_gpt_nb')
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=3,
+                 neighbors=True, beam_mode='fixed')
+    torch.manual_seed(6)
+    m = GPT(cfg).eval().to(DEV)
+    with torch.no_grad():
+        logits, _, stats = m(torch.as_tensor(g['idx']).to(DEV))
+    np.testing.assert_allclose(logits.cpu().numpy(), g['logits'], atol=1e-4)
+    for k in ('keys_total', 'keys_tree', 'keys_nb', 'nb_leaves', 'leaves_used'):
+        assert abs(stats[k] - float(g['stat_' + k])) < 1e-4, (k, stats[k], float(g['stat_' + k]))
+    _no_device_error()
+
+
+@pytest.mark.parametrize('dt', [torch.float32, torch.bfloat16])
+def test_neighbours_leaf_blocks_vs_oracle(dt):
+    """Neighbour borrowing on 8-token leaf blocks, longer sequences: kernel selection vs the oracle's, queries
+    near an fp32 tie (their own descent, a stored leaf of the nb_window positions before them, or a match
+    threshold) excluded."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.seg import select_seg
+    rng = np.random.default_rng(11)
+    B, H, T, dh = 2, 3, 1024, 64
+    q = torch.as_tensor(rng.standard_normal((B, H, T, dh)).astype(np.float32)).to(dt)
+    k = torch.as_tensor(rng.standard_normal((B, H, T, dh)).astype(np.float32)).to(dt)
+    lhat = torch.as_tensor(rng.integers(2, 9, (B, H, T)))
+    cfg = Config(attn='seg', seq_len=T, wmax=8, beam=4, beam_mode='fixed', leaf=8)
+    sel = select_seg(q.to(DEV), k.to(DEV), lhat.to(DEV), cfg)
+    nb = dict(nb_window=cfg.nb_window, nb_store=cfg.nb_store, nb_rho=cfg.nb_rho, nb_probe=cfg.nb_probe,
+              nb_cap_min=cfg.nb_cap_min)
+    ref = oracle.select_seg(q.float().numpy(), k.float().numpy(), lhat.numpy(), 8, L0=3, with_margin=True, nb=nb)
+    tie = ref['margin'] <= 1e-6
+    near = np.zeros_like(tie)
+    for d in range(0, cfg.nb_window + 1):  # a tie at any of the positions a query borrows from
+        near[..., d:] |= tie[..., :T - d]
+    excl = near | (ref['nb_margin'] <= 1e-6)
+    srt = lambda a: np.sort(a, -1)
+    ok = ~excl
+    for key in ('tree_pos', 'nb_pos'):
+        eq = (srt(sel[key].cpu().numpy()) == srt(ref[key])).all(-1)
+        assert eq[ok].all(), (key, int((~eq & ok).sum()))
+    assert (sel['nb_leaves'].cpu().numpy() == ref['nb_leaves'])[ok].all()
+    assert (sel['n_tree'].cpu().numpy() == ref['n_tree'])[ok].all()
+    assert ok.mean() > 0.95 and (ref['nb_pos'] >= 0).sum() > 1000
+    _no_device_error()
+
+
+def test_seg_attention_neighbours_autograd_matches_inference():
+    """With neighbours on, the fused inference path (tree + borrowed leaves deduplicated, one attention kernel)
+    and the training form (explicit candidate list + sparse_attn) give the same output."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.fastseg import SegAttention
+    cfg = Config(vocab_size=64, seq_len=256, n_layer=1, n_head=2, n_embd=64, attn='seg', wmax=4, beam=3, local=16,
+                 neighbors=True, beam_mode='fixed', leaf=4)
+    torch.manual_seed(3)
+    m = SegAttention(cfg).to(DEV)
+    x = torch.randn(2, 256, 64, device=DEV)
+    with torch.no_grad():
+        y_fast = m(x)
+        aux_fast = {k: float(v) for k, v in m.aux.items()}
+    y = m(x.clone().requires_grad_(True))
+    aux_train = {k: float(v) for k, v in m.aux.items()}
+    assert float((y.detach() - y_fast).abs().max()) < 1e-5
+    for k in ('keys_total', 'keys_tree', 'keys_nb', 'nb_leaves', 'leaves_used'):
+        assert abs(aux_fast[k] - aux_train[k]) < 1e-4, (k, aux_fast[k], aux_train[k])
+    assert aux_fast['keys_nb'] > 0

@@ -164,3 +164,21 @@ def test_lane_search_golden(wmax):
     bad, n, _ = compare_sets(ids, vld, g['ids_%d' % wmax], g['vld_%d' % wmax], tied(margin))
     assert bad == 0 and n == g['q'].shape[0]
     np.testing.assert_allclose(np.where(vld, sct, 0), np.where(g['vld_%d' % wmax], g['sct_%d' % wmax], 0), atol=1e-6)
+
+
+def _nb_cfg(g):
+    return dict(nb_window=int(g['nb_window']), nb_store=int(g['nb_store']), nb_rho=float(g['nb_rho']),
+                nb_probe=int(g['nb_probe']), nb_cap_min=int(g['nb_cap_min']))
+
+
+def test_select_seg_with_neighbours_golden():
+    """seg.select_seg with neighbour borrowing on (cfg.neighbors=True, the reference's default), leaf 2: tree
+    positions, neighbour positions (1232 matched), budgets and nb_leaves equal the reference's on every query."""
+    g = load('sel_nb')
+    sel = oracle.select_seg(g['q'], g['k'], g['lhat'], int(g['wmax']), L0=1, with_margin=True, nb=_nb_cfg(g))
+    assert (sel['margin'] > 1e-6).all() and (sel['nb_margin'] > 1e-6).all()  # no near-tie in this fixture
+    srt = lambda a: np.sort(a, -1)
+    assert (srt(sel['tree_pos']) == srt(g['tree_pos'])).all()
+    assert (srt(sel['nb_pos']) == srt(g['nb_pos'])).all() and (g['nb_pos'] >= 0).sum() > 1000
+    assert (sel['leaf_ok'] == g['leaf_ok']).all()
+    assert (sel['n_tree'] == g['n_tree']).all() and (sel['nb_leaves'] == g['nb_leaves']).all()

@@ -32,6 +32,8 @@ SIGNATURES = {
     'ta_prefill_attn': [P, P, P, I, I, I, I, I, L, L, L, L, L, L, L, L, L, I, P, L, L, P, P, I, P, I, I, I, F,
                         P, L, L, L, P, P, P],
     'ta_sparse_attn': [P, P, P, I, I, I, I, I, L, L, L, L, L, L, L, L, L, I, P, I, I, F, P, L, L, L, P, P],
+    'ta_neighbor_pass': [P, I, I, I, I, I, L, L, L, P, L, L, P, L, L, I, I, P, P, P, I, I, I, F, I, I, I, P, P, P,
+                         P],
     'ta_lane_search': [P, P, P, I, I, I, I, I, P, P, P, P],
     'ta_sparse_attn_bwd': [P, P, P, P, P, P, I, I, I, I, I, I, P, I, I, F, P, P, P, P],
     'ta_gather_dot': [P, P, I, I, I, I, I, I, I, L, L, L, L, L, L, P, I, F, P, P],

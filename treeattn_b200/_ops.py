@@ -140,6 +140,32 @@ def select(q, levels, tq, wmax, wl=None):
     return ids, vld, sct
 
 
+def neighbor_pass(q, levels, st_leaf, st_score, st_ok, tq, nb_window, nb_store, nb_rho, nb_probe, nb_cap_min,
+                  neighbors=True):
+    """seg.neighbor_pass on leaf blocks: q (B, H, Nq, dh), the tree (its leaf level is read), stored best leaves
+    st_* (B, H, T_st, NS) indexed by position, tq positions. Returns nid (int64), match (bool) (B, H, Nq, Wn*NS)
+    and nL (B, H, Nq) int64."""
+    _need_cuda('neighbor_pass', q, tq, levels.nodes, st_leaf)
+    _unit_inner('neighbor_pass', q)
+    B, H, Nq, dh = q.shape
+    st_leaf = st_leaf.to(torch.int64).contiguous()
+    st_score = st_score.to(torch.float32).contiguous()
+    st_ok = st_ok.to(torch.bool).contiguous()
+    T_st = st_leaf.shape[2]
+    tq = tq.to(torch.int64)
+    sb, stq = _tq_strides(tq, B, Nq)
+    leaf = levels.level(levels.L0)
+    W = nb_window * nb_store
+    nid = torch.empty(B, H, Nq, W, device=q.device, dtype=torch.int64)
+    match = torch.empty(B, H, Nq, W, device=q.device, dtype=torch.bool)
+    nL = torch.empty(B, H, Nq, device=q.device, dtype=torch.int64)
+    _lib.call('ta_neighbor_pass', _p(q), _code(q), B, H, Nq, dh, q.stride(0), q.stride(1), q.stride(2), _p(tq), sb,
+              stq, _p(leaf), leaf.stride(0), leaf.stride(1), leaf.shape[2], levels.L0, _p(st_leaf), _p(st_score),
+              _p(st_ok), T_st, int(nb_window), int(nb_store), float(nb_rho), int(nb_probe), int(nb_cap_min),
+              1 if neighbors else 0, _p(nid), _p(match), _p(nL), _stream(q))
+    return nid, match, nL
+
+
 def finish(ids, vld, lhat, wmax, leaf, nid=None, match=None, nL=None, positions=True):
     """seg.finish: returns dict(tree_pos, leaf_ok, nb_pos, n_tree, nb_leaves) (positions=False: n_tree only)."""
     _need_cuda('finish', ids, vld, lhat)

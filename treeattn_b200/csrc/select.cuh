@@ -569,6 +569,99 @@ __global__ void __launch_bounds__(TS_THREADS) select_tile_kernel(SelectParams p)
   }
 }
 
+// ------------------------------------------------------------------------------------------------ neighbours
+// seg.py:73-103 neighbor_pass: query n at position t looks at the NS best leaves stored by each of the Wn previous
+// positions (st_* (B, H, T_st, NS), indexed by position), scores each itself (q . S_L0[leaf] * 2^-L0) and matches
+// those it scores at least base - rho |base| (base = the stored score); the scan depth is capped by the match rate
+// over the first nb_probe positions: cap = cap_min + round_half_even((Wn - cap_min) * rate). One warp per query,
+// one lane per stored leaf (Wn * NS <= 32). The threshold, rate and cap are formed with the same fp32 roundings
+// as the reference (no fused multiply-add).
+struct NeighborParams {
+  const void* q;
+  int64_t q_sb, q_sh, q_st;
+  const int64_t* tq;
+  int64_t tq_sb, tq_st;
+  const float* leaf_nodes;  // level-L0 node rows of (b=0, h=0); row m of (b, h) at + b*n_sb + h*n_sh + m*dh
+  int64_t n_sb, n_sh;
+  int n_leaf;
+  float scale;              // 2^-L0
+  const int64_t* st_leaf;   // (B, H, T_st, NS) contiguous
+  const float* st_score;
+  const uint8_t* st_ok;
+  int T_st;
+  int B, H, Nq, Wn, NS, probe, cap_min, neighbors;
+  float rho;
+  int64_t* nid;             // (B, H, Nq, Wn*NS)
+  uint8_t* match;           // (B, H, Nq, Wn*NS)
+  int64_t* nL;              // (B, H, Nq)
+};
+
+template <typename QT, int DH>
+__global__ void __launch_bounds__(128) neighbor_pass_kernel(NeighborParams p) {
+  __shared__ __align__(16) float qs[4][DH];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qid = (int64_t)blockIdx.x * 4 + warp;
+  if (qid >= (int64_t)p.B * p.H * p.Nq) return;
+  const int n = (int)(qid % p.Nq);
+  const int64_t bh = qid / p.Nq;
+  const int b = (int)(bh / p.H), h = (int)(bh % p.H);
+  const int64_t t = p.tq[b * p.tq_sb + (int64_t)n * p.tq_st];
+  const QT* qrow = reinterpret_cast<const QT*>(p.q) + b * p.q_sb + h * p.q_sh + (int64_t)n * p.q_st;
+  for (int d = lane; d < DH; d += 32) qs[warp][d] = to_f32(qrow[d]);
+  __syncwarp();
+  const int W = p.Wn * p.NS;
+  const int j = lane;
+  const int dist = j / p.NS + 1, slot = j - (j / p.NS) * p.NS;
+  const int64_t jpos = t - dist;
+  const bool jval = j < W && jpos >= 0 && jpos < p.T_st;
+  const int64_t jc = jpos < 0 ? 0 : (jpos >= p.T_st ? p.T_st - 1 : jpos);
+  const int64_t sidx = (bh * p.T_st + jc) * p.NS + slot;
+  int64_t id = 0;
+  float base = 0.f;
+  bool ok0 = false;
+  if (j < W) {
+    id = p.st_leaf[sidx];
+    base = p.st_score[sidx];
+    ok0 = jval && p.st_ok[sidx] != 0;
+  }
+  // this query's own score of the stored leaf
+  float sc = 0.f;
+  if (ok0) {
+    const int64_t m = id < 0 ? 0 : (id >= p.n_leaf ? p.n_leaf - 1 : id);
+    const float* row = p.leaf_nodes + b * p.n_sb + h * p.n_sh + m * DH;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < DH / 4; ++cc) {
+      const float4 qv = *reinterpret_cast<const float4*>(&qs[warp][cc * 4]);
+      const float4 v = __ldg(reinterpret_cast<const float4*>(row + cc * 4));
+      if (cc & 1) {
+        a1 = fmaf(qv.x, v.x, a1); a1 = fmaf(qv.y, v.y, a1); a1 = fmaf(qv.z, v.z, a1); a1 = fmaf(qv.w, v.w, a1);
+      } else {
+        a0 = fmaf(qv.x, v.x, a0); a0 = fmaf(qv.y, v.y, a0); a0 = fmaf(qv.z, v.z, a0); a0 = fmaf(qv.w, v.w, a0);
+      }
+    }
+    sc = __fmul_rn(__fadd_rn(a0, a1), p.scale);
+  }
+  const float thr = __fsub_rn(base, __fmul_rn(p.rho, fabsf(base)));
+  bool m = ok0 && sc >= thr;
+  const unsigned pm = p.probe >= 32 ? 0xffffffffu : ((1u << p.probe) - 1u);
+  const unsigned bm = __ballot_sync(0xffffffffu, m), bo = __ballot_sync(0xffffffffu, ok0);
+  const int nm = __popc(bm & pm), no = __popc(bo & pm);
+  const float rate = __fdiv_rn((float)nm, (float)(no > 1 ? no : 1));
+  const int cap = p.cap_min + (int)rintf(__fmul_rn((float)(p.Wn - p.cap_min), rate));
+  m = m && dist <= cap && p.neighbors != 0;
+  // distinct matched leaves: a matched lane counts when no lower matched lane holds the same id
+  const unsigned long long key = m ? (unsigned long long)id : (0xffffffff00000000ull | (unsigned)lane);
+  const unsigned same = __match_any_sync(0xffffffffu, key);
+  const bool first = m && (__ffs(same) - 1) == lane;
+  const int nl = __popc(__ballot_sync(0xffffffffu, first));
+  if (j < W) {
+    p.nid[qid * W + j] = id;
+    p.match[qid * W + j] = m ? 1 : 0;
+  }
+  if (lane == 0) p.nL[qid] = nl;
+}
+
 // ------------------------------------------------------------------------------------------------ lane tree
 // Beam descent over the dynamic content tree (dyntree.py:108-127 LaneTree.search): one query per lane (tree),
 // nodes holding key SUMS and counts, packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2, l = 0..D).

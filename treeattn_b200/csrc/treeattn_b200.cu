@@ -264,6 +264,16 @@ struct SparseAttnBwd {
   }
 };
 
+template <typename QT, int DH>
+struct NeighborPass {
+  static int run(ta::NeighborParams p, cudaStream_t st) {
+    const int64_t nq = (int64_t)p.B * p.H * p.Nq;
+    if (nq == 0) return TA_OK;
+    ta::neighbor_pass_kernel<QT, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_neighbor_pass");
+  }
+};
+
 template <typename T, int DH>
 struct LaneSearch {
   static int run(ta::LaneSearchParams p, cudaStream_t st) {
@@ -673,6 +683,36 @@ int ta_sparse_attn(const void* q, const void* k, const void* v, int dtype, int B
   p.o = o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_st = o_st;
   p.lse = lse;
   return by_type_dh<SparseAttn>(dtype, dh, p, S(stream));
+}
+
+int ta_neighbor_pass(const void* q, int q_dtype, int B, int H, int Nq, int dh, int64_t q_sb, int64_t q_sh,
+                     int64_t q_st, const int64_t* tq, int64_t tq_sb, int64_t tq_st, const float* leaf_nodes,
+                     int64_t n_sb, int64_t n_sh, int n_leaf, int L0, const int64_t* st_leaf, const float* st_score,
+                     const uint8_t* st_ok, int T_st, int nb_window, int nb_store, float nb_rho, int nb_probe,
+                     int nb_cap_min, int neighbors, int64_t* nid, uint8_t* match, int64_t* nL, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(q_dtype)) return fail(TA_ERR_ARG, "ta_neighbor_pass: bad dtype %d", q_dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_neighbor_pass: unsupported head dim %d", dh);
+  if (B < 0 || H < 0 || Nq < 0 || n_leaf < 1 || T_st < 1 || L0 < 0 || L0 > 30)
+    return fail(TA_ERR_ARG, "ta_neighbor_pass: bad sizes");
+  if (nb_window < 1 || nb_store < 1 || nb_window * nb_store > 32)
+    return fail(TA_ERR_ARG, "ta_neighbor_pass: nb_window * nb_store = %d outside [1, 32]", nb_window * nb_store);
+  if (nb_probe < 0 || nb_cap_min < 0) return fail(TA_ERR_ARG, "ta_neighbor_pass: bad probe / cap");
+  if (!q || !tq || !leaf_nodes || !st_leaf || !st_score || !st_ok || !nid || !match || !nL)
+    return fail(TA_ERR_ARG, "ta_neighbor_pass: null pointer");
+  if (!aligned16(leaf_nodes) || (n_sb * 4) % 16 || (n_sh * 4) % 16)
+    return fail(TA_ERR_ARG, "ta_neighbor_pass: node rows must be 16-byte aligned");
+  ta::NeighborParams p{};
+  p.q = q; p.q_sb = q_sb; p.q_sh = q_sh; p.q_st = q_st;
+  p.tq = tq; p.tq_sb = tq_sb; p.tq_st = tq_st;
+  p.leaf_nodes = leaf_nodes; p.n_sb = n_sb; p.n_sh = n_sh; p.n_leaf = n_leaf;
+  p.scale = ldexpf(1.f, -L0);
+  p.st_leaf = st_leaf; p.st_score = st_score; p.st_ok = st_ok; p.T_st = T_st;
+  p.B = B; p.H = H; p.Nq = Nq; p.Wn = nb_window; p.NS = nb_store;
+  p.probe = std::min(nb_probe * nb_store, nb_window * nb_store);
+  p.cap_min = nb_cap_min; p.neighbors = neighbors; p.rho = nb_rho;
+  p.nid = nid; p.match = match; p.nL = nL;
+  return by_type_dh<NeighborPass>(q_dtype, dh, p, S(stream));
 }
 
 int ta_lane_search(const float* q, const float* sums, const int32_t* cnt, int P, int D, int dh, int wmax, int wl,

@@ -152,8 +152,6 @@ class SegAttention(nn.Module):
         cfg = self.cfg
         if cfg.gate:
             gate_apply(None, None, None, cfg.gate_q)
-        if cfg.neighbors:
-            raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
         if self._needs_grad(q, k, v):
             o = self._sparse_attend_autograd(q, k, v)
             if out is not None:
@@ -168,20 +166,40 @@ class SegAttention(nn.Module):
             ids, vld, sct, lv = select_tree(q.detach(), k.detach(), cfg)
             leaf = 1 << lv.L0
             wl = ids.shape[-1]
-            if lhat is None:
-                n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
-                used = vld & (torch.arange(wl, device=q.device) < n_tree)
-            else:
-                n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, positions=False)['n_tree']
-                used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
             Lw = max(cfg.local, 3)
             tq = torch.arange(T, device=q.device)
-            out, _, nkeys = _ops.attend_leaves(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=out)
+            keys_nb = torch.zeros((), device=q.device)
+            nb_leaves = torch.zeros((), device=q.device)
+            if cfg.neighbors:
+                # neighbour borrowing (fastseg.py:359-366): matched leaves of earlier queries join the tree's
+                # first n_tree leaves; a leaf held by both counts once (dedupe over leaf ids)
+                NS = cfg.nb_store
+                nid, match, nL = neighbor_pass(q.detach(), lv, ids[..., :NS], sct[..., :NS], vld[..., :NS], tq,
+                                               cfg)
+                if lhat is None:
+                    lhat = torch.full((b, H, T), cfg.beam, dtype=torch.long, device=q.device)
+                n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, nid=nid, match=match, nL=nL,
+                                     positions=False)['n_tree']
+                used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
+                leaves = torch.cat([ids, nid], -1)
+                keep = _ops.dedupe(leaves, torch.cat([used, match], -1))
+                out, _, nkeys = _ops.attend_leaves(q, k, v, tq, leaves, keep, leaves.shape[-1], leaf, Lw, scale,
+                                                   out=out)
+                keys_nb = (keep[..., wl:].sum(-1).float() * leaf).mean()
+                nb_leaves = nL.float().mean()
+            else:
+                if lhat is None:
+                    n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
+                    used = vld & (torch.arange(wl, device=q.device) < n_tree)
+                else:
+                    n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, positions=False)['n_tree']
+                    used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
+                out, _, nkeys = _ops.attend_leaves(q, k, v, tq, ids, vld, n_tree, leaf, Lw, scale, out=out)
             n_used = used.sum(-1).float()
             self.aux['keys_total'] = nkeys.float().mean()
             self.aux['keys_tree'] = (n_used * leaf).mean()
-            self.aux['keys_nb'] = torch.zeros((), device=q.device)
-            self.aux['nb_leaves'] = torch.zeros((), device=q.device)
+            self.aux['keys_nb'] = keys_nb
+            self.aux['nb_leaves'] = nb_leaves
             self.aux['leaves_used'] = n_used.mean()
         return out
 

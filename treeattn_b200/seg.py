@@ -5,8 +5,7 @@ Same names, arguments and results as the reference module. Differences, all expl
     its bound getU) instead of an arbitrary getU callable: the descent runs inside one CUDA kernel.
   * Leaf blocks of cfg.leaf tokens (default 2 = the reference) are supported; positions of a leaf block m are
     [m*leaf, (m+1)*leaf), stored leaf-slot-major as the reference's cat([2*ids, 2*ids+1]) is at leaf 2.
-  * The mean-log gate (cfg.gate) and neighbour borrowing with matches (cfg.neighbors=True) raise
-    NotImplementedError instead of silently changing the result.
+  * The mean-log gate (cfg.gate) raises NotImplementedError instead of silently changing the result.
 """
 import torch
 
@@ -62,18 +61,12 @@ def tree_pass(q, getU, tq, Lm, wmax):
 
 @torch.no_grad()
 def neighbor_pass(q, getU1, st_leaf, st_score, st_ok, tq, cfg):
-    """seg.py:73-103 with cfg.neighbors=False: the stored ids of the nb_window earlier queries, no matches,
-    nL = 0. Neighbour matching itself raises NotImplementedError."""
-    if cfg.neighbors:
-        raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
-    b, H, Nq, dh = q.shape
-    Wn, NS = cfg.nb_window, cfg.nb_store
-    back = torch.arange(1, Wn + 1, device=q.device).view(1, Wn)
-    jc = (tq.view(Nq, 1) - back).clamp(min=0)
-    ids = st_leaf[:, :, jc].reshape(b, H, Nq, Wn * NS)
-    match = torch.zeros(ids.shape, dtype=torch.bool, device=q.device)
-    nL = torch.zeros(b, H, Nq, dtype=torch.long, device=q.device)
-    return ids, match, nL
+    """seg.py:73-103: borrow the best leaves stored by the nb_window previous positions (st_* (b, H, T, NS)) that
+    this query also scores well on (ta_neighbor_pass). getU1 is the tree (its leaf level scores the stored
+    leaves). Returns ids (b, H, Nq, Wn*NS), match and nL; with cfg.neighbors=False no leaf matches."""
+    lv = _as_levels(getU1)
+    return _ops.neighbor_pass(q, lv, st_leaf, st_score, st_ok, tq.to(q.device), cfg.nb_window, cfg.nb_store,
+                              cfg.nb_rho, cfg.nb_probe, cfg.nb_cap_min, neighbors=cfg.neighbors)
 
 
 def leaves_to_pos(ids, ok, leaf=2):
@@ -109,5 +102,5 @@ def select_seg(q, k, lhat, cfg):
     ids, vld, sct, lv = select_tree(q, k, cfg)
     NS = cfg.nb_store
     tq = torch.arange(T, device=q.device)
-    nid, match, nL = neighbor_pass(q, None, ids[..., :NS], sct[..., :NS], vld[..., :NS], tq, cfg)
+    nid, match, nL = neighbor_pass(q, lv, ids[..., :NS], sct[..., :NS], vld[..., :NS], tq, cfg)
     return _ops.finish(ids, vld, lhat, cfg.wmax, 1 << lv.L0, nid=nid, match=match, nL=nL)
