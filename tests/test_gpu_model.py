@@ -323,3 +323,51 @@ def test_seg_attention_neighbours_autograd_matches_inference():
     for k in ('keys_total', 'keys_tree', 'keys_nb', 'nb_leaves', 'leaves_used'):
         assert abs(aux_fast[k] - aux_train[k]) < 1e-4, (k, aux_fast[k], aux_train[k])
     assert aux_fast['keys_nb'] > 0
+
+
+def test_engine_neighbours_golden():
+    """The reference engine's token-by-token decoding with neighbour borrowing (each position stores its best
+    leaves, later positions borrow the matched ones): our Decoder (general-selection step, CUDA graph) gives the
+    reference's logits within 1e-4 and the same keys read per step."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    g = load('tiny_gpt_nb')
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=3,
+                 neighbors=True, beam_mode='fixed')
+    torch.manual_seed(6)
+    m = GPT(cfg).eval()
+    dec = Decoder(weights_from_ours(m.state_dict(), cfg), cfg.n_layer, cfg.n_head, cfg.n_embd, 128, 'seg', cfg, DEV)
+    idx = g['idx'][0]
+    worst, kw = 0.0, 0.0
+    for t in range(128):
+        lg, keys = dec.step(int(idx[t]), t)
+        worst = max(worst, float(np.abs(lg.cpu().numpy() - g['dec_logits'][t]).max()))
+        kw = max(kw, abs(float(keys) - float(g['dec_keys'][t])))
+    assert worst < 1e-4 and kw < 1e-4, (worst, kw)
+    _no_device_error()
+
+
+@pytest.mark.parametrize('global_pool', [False, True])
+def test_engine_pred_neighbours_matches_forward(global_pool):
+    """Learned budget head + neighbour borrowing on 4-token leaf blocks, batch 3: prefill of the first half and
+    token-by-token steps give the whole-sequence forward's logits (the property of the reference's
+    test_seg.test_engine_matches_forward), 1e-4."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=64, attn='seg', wmax=8, beam=4, local=8,
+                 neighbors=True, beam_mode='pred', beam_classes=(2, 4, 8), global_pool=global_pool, leaf=4)
+    torch.manual_seed(12)
+    m = GPT(cfg).eval().to(DEV)
+    idx = torch.randint(0, 64, (3, 128), device=DEV)
+    with torch.no_grad():
+        ref = m(idx)[0]
+    dec = Decoder(weights_from_ours(m.state_dict(), cfg), cfg.n_layer, cfg.n_head, cfg.n_embd, 128, 'seg', cfg, DEV,
+                  batch=3)
+    last = dec.prefill(idx[:, :64])
+    np.testing.assert_allclose(last.float().cpu().numpy(), ref[:, 63].cpu().numpy(), atol=1e-4)
+    for t in range(64, 128):
+        lg, _ = dec.step(idx[:, t], t)
+        np.testing.assert_allclose(lg.float().cpu().numpy(), ref[:, t].cpu().numpy(), atol=1e-4)
+    _no_device_error()

@@ -46,6 +46,12 @@ class SegState:
         self.K = torch.zeros(batch, H, self.cap, dh, device=dev, dtype=dtype)
         self.V = torch.zeros(batch, H, self.cap, dh, device=dev, dtype=dtype)
         self.levels = Levels.empty(batch, H, dh, self.cap, self.L0, self.Lm, dev)
+        if cfg.neighbors:  # the best leaves every position found, for neighbour borrowing (engine.py:28-31)
+            NS = cfg.nb_store
+            self.st_leaf = torch.zeros(batch, H, self.cap, NS, device=dev, dtype=torch.int64)
+            self.st_score = torch.zeros(batch, H, self.cap, NS, device=dev, dtype=torch.float32)
+            self.st_ok = torch.zeros(batch, H, self.cap, NS, device=dev, dtype=torch.bool)
+        self.ksum = torch.zeros(batch, H, dh, device=dev, dtype=torch.float32)  # sum of the keys added so far
 
     @property
     def raw(self):
@@ -61,6 +67,7 @@ class SegState:
             k, v = k[:, :, 0], v[:, :, 0]
         pos = _positions(t, self.batch, self.K.device)
         _ops.append(k.to(self.K.dtype), v.to(self.V.dtype), self.K, self.V, self.levels, pos)
+        self.ksum += k.float()
 
     def fill(self, K, V):
         """Load positions [0, T) at once (K, V: (B, H, T, dh)) and build the levels (reference fill)."""
@@ -70,6 +77,65 @@ class SegState:
         self.K[:, :, :T].copy_(K)
         self.V[:, :, :T].copy_(V)
         _ops.build_levels(self.K[:, :, :T], self.cap, self.L0, self.Lm, zero_sink=True, out=self.levels)
+        self.ksum.copy_(K.float().sum(2))
+
+
+def pred_budget(pw, q, kmean, H):
+    """The learned leaf budget (engine.py:89-94, fastseg.py:352-365): features [q, log |q|, one-hot head] (+ the
+    mean of the earlier keys with cfg.global_pool) through the two-layer head, argmax over the budget classes.
+    q (B, H, N, dh); kmean (B, H, N, dh) or None. Returns (B, H, N) int64 leaf budgets."""
+    qf = q.float()
+    B, _, N, dh = qf.shape
+    feats = [qf, torch.log(qf.norm(dim=-1, keepdim=True) + 1e-6),
+             torch.eye(H, device=q.device).view(1, H, 1, H).expand(B, H, N, H)]
+    if kmean is not None:
+        feats.append(kmean.float())
+    h = F.relu(F.linear(torch.cat(feats, -1), pw['w1'].float(), pw['b1'].float()))
+    lg = F.linear(h, pw['w2'].float(), pw['b2'].float())
+    return pw['classes'][lg.argmax(-1)]
+
+
+def _general_step(state, pw, q, k, v, pos, out=None, update=True):
+    """One decoding step with the general selection (engine.py:84-120): learned budget (beam_mode='pred') and
+    neighbour borrowing (cfg.neighbors) - descent, neighbour pass and budget on the tree before position t,
+    this position's best leaves stored for the following ones, then append and exact attention over the used tree
+    leaves, the matched borrowed ones (deduplicated), the sink and the window. q, k, v (B, H, 1, dh) in the cache
+    dtype, pos (B,) int32. update=False selects and attends without storing or appending (the cache must then
+    already hold position t). Returns (out (B, H, 1, dh), keys (B, H, 1) int32)."""
+    cfg = state.cfg
+    B, H, _, dh = q.shape
+    leaf = 1 << state.L0
+    tq = pos.to(torch.int64)
+    if cfg.beam_mode == 'pred':
+        kmean = (state.ksum / tq.clamp(min=1).view(B, 1, 1).float()).unsqueeze(2) if cfg.global_pool else None
+        lhat = pred_budget(pw, q, kmean, H)
+    else:
+        lhat = torch.full((B, H, 1), cfg.beam, device=q.device, dtype=torch.int64)
+    ids, vld, sct = _ops.select(q, state.levels, tq, cfg.wmax)
+    wl = ids.shape[-1]
+    if cfg.neighbors:
+        NS = cfg.nb_store
+        nid, match, nL = _ops.neighbor_pass(q, state.levels, state.st_leaf, state.st_score, state.st_ok, tq,
+                                            cfg.nb_window, NS, cfg.nb_rho, cfg.nb_probe, cfg.nb_cap_min)
+        n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, nid=nid, match=match, nL=nL, positions=False)['n_tree']
+        if update:
+            bi = torch.arange(B, device=q.device)
+            state.st_leaf[bi, :, tq] = ids[:, :, 0, :NS]
+            state.st_score[bi, :, tq] = sct[:, :, 0, :NS]
+            state.st_ok[bi, :, tq] = vld[:, :, 0, :NS]
+    else:
+        n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, positions=False)['n_tree']
+    if update:
+        state.add(pos, k, v)
+    used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
+    if cfg.neighbors:
+        leaves = torch.cat([ids, nid], -1)
+        keep = _ops.dedupe(leaves, torch.cat([used, match], -1))
+    else:
+        leaves, keep = ids, used
+    o, _, nkeys = _ops.seg_attn(q, state.K, state.V, tq, leaves, keep, leaves.shape[-1], leaf, max(cfg.local, 3),
+                                1.0 / math.sqrt(dh), out=out)
+    return o, nkeys
 
 
 @torch.no_grad()
@@ -77,15 +143,15 @@ def seg_attend(state, pw, q, k, v, t, update=True):
     """One decoding step of segment-tree attention for a batch. q, k, v: (B, H, 1, dh). Returns (out (B, H, 1,
     dh), keys read per head as a 0-d device tensor)."""
     cfg = state.cfg
-    if cfg.beam_mode == 'pred':
-        raise NotImplementedError("beam_mode='pred' decoding is not implemented in treeattn_b200")
-    if cfg.neighbors:
-        raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
     B, H, _, dh = q.shape
     pos = _positions(t, B, q.device)
+    qx = q.to(state.K.dtype)
+    kx, vx = [None if t_ is None else t_.to(state.K.dtype) for t_ in (k, v)]  # k / v unused when update=False
+    if cfg.neighbors or cfg.beam_mode == 'pred':
+        out, nkeys = _general_step(state, pw, qx, kx, vx, pos, update=update)
+        return out, nkeys.float().mean()
     if update:
         state.add(pos, k, v)
-    qx = q.to(state.K.dtype)
     ids, vld, _ = _ops.select(qx, state.levels, pos.to(torch.int64), cfg.wmax)
     n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
     out, _, nkeys = _ops.seg_attn(qx, state.K, state.V, pos.to(torch.int64), ids, vld, n_tree,
@@ -134,10 +200,6 @@ class Decoder:
             raise NotImplementedError("Decoder mode '%s' is not implemented in treeattn_b200 (only 'seg')" % mode)
         if cfg is None:
             raise ValueError("mode 'seg' needs cfg")
-        if cfg.beam_mode == 'pred':
-            raise NotImplementedError("beam_mode='pred' decoding is not implemented in treeattn_b200")
-        if cfg.neighbors:
-            raise NotImplementedError('neighbour borrowing (cfg.neighbors=True) is not implemented in treeattn_b200')
         self.dev = torch.device(dev)
         self.dtype = dtype or W['wte'].dtype
         cast = lambda t: t.to(device=self.dev, dtype=self.dtype).contiguous()
@@ -145,6 +207,12 @@ class Decoder:
                       layers=[dict(ln1=L['ln1'].to(self.dev, torch.float32), c_attn=cast(L['c_attn']),
                                    c_proj=cast(L['c_proj']), ln2=L['ln2'].to(self.dev, torch.float32),
                                    c_fc=cast(L['c_fc']), c_mlp=cast(L['c_mlp'])) for L in W['layers'][:n_layer]])
+        # general selection (learned budget, neighbour borrowing): per layer the separate kernels of
+        # _general_step instead of the single fused decode kernel
+        self.general = cfg.neighbors or cfg.beam_mode == 'pred'
+        if cfg.beam_mode == 'pred':
+            for Ld, L in zip(self.W['layers'], W['layers'][:n_layer]):
+                Ld['pw'] = {k_: (t.to(self.dev) if torch.is_tensor(t) else t) for k_, t in L['pw'].items()}
         self.nl, self.H, self.C, self.Tcap = n_layer, n_head, n_embd, Tcap
         self.dh, self.mode, self.cfg = n_embd // n_head, mode, cfg
         self.batch = batch
@@ -188,8 +256,14 @@ class Decoder:
         for i, Li in enumerate(L):
             st = self.states[i]
             torch.mm(self._h, Li['c_attn'].t(), out=self._qkv)
-            _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree, self.Lw,
-                             self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits)
+            if self.general:
+                B, C, H, dh = self.batch, self.C, self.H, self.dh
+                q, k, v = [self._qkv[:, j * C:(j + 1) * C].view(B, H, 1, dh) for j in range(3)]
+                _, nk = _general_step(st, Li.get('pw'), q, k, v, self._pos, out=self._att.view(B, H, 1, dh))
+                self._nkeys[i].copy_(nk.view(B, H))
+            else:
+                _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree,
+                                 self.Lw, self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits)
             torch.mm(self._att, Li['c_proj'].t(), out=self._proj)
             _ops.add_ln(self._x, self._proj, Li['ln2'], self._h)
             torch.mm(self._h, Li['c_fc'].t(), out=self._fc)
@@ -217,13 +291,17 @@ class Decoder:
     def _ensure_graphs(self):
         """Capture the step graphs once. Capturing records the launches without running them; the one eager
         warm-up step before it (library attribute set-up, cuBLAS handles) feeds the current tokens at the current
-        positions, which the next real step repeats exactly: it writes the same k/v rows at the same positions and
-        forms the same tree nodes, and it advances no token or position, so no state needs to be saved around it
-        (a copy of every cache would double the memory of a long-context decoder)."""
+        positions, which the next real step repeats exactly: it writes the same k/v rows at the same positions, forms
+        the same tree nodes and stores the same best leaves, and it advances no token or position, so the caches
+        need no copy around it (a copy of every cache would double the memory of a long-context decoder); only the
+        running key sums, which it would count twice, are saved and restored."""
         if self._graph is not None or not self.use_graphs:
             return
+        ksums = [st.ksum.clone() for st in self.states]  # the running key sums are not idempotent: restored
         self._forward_step()
         torch.cuda.current_stream(self.dev).synchronize()
+        for st, ks in zip(self.states, ksums):
+            st.ksum.copy_(ks)
         self._graph, _ = self._capture(self._forward_step)
         self._graph_greedy, _ = self._capture(self._greedy_step)
 
@@ -283,6 +361,36 @@ class Decoder:
     def positions(self):
         return self._pos
 
+    def _prefill_selection(self, st, L, q, k, lv, tq, ids, vld, sct, b0, b1):
+        """General selection for a prompt (the whole-sequence form of _general_step): learned budgets, the
+        neighbour pass over the prompt's own descents, whose best leaves are stored for the decode steps that
+        follow. Returns the leaf list and the kept (used, deduplicated) mask."""
+        cfg = self.cfg
+        nb, H, T0, _ = q.shape
+        leaf = 1 << st.L0
+        wl = ids.shape[-1]
+        if cfg.beam_mode == 'pred':
+            km = None
+            if cfg.global_pool:
+                kf = k.float()
+                km = (kf.cumsum(2) - kf) / tq.clamp(min=1).view(1, 1, T0, 1).float()
+            lhat = pred_budget(L['pw'], q, km, H)
+        else:
+            lhat = torch.full((nb, H, T0), cfg.beam, device=q.device, dtype=torch.int64)
+        if not cfg.neighbors:
+            n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, positions=False)['n_tree']
+            return ids, vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
+        NS = cfg.nb_store
+        nid, match, nL = _ops.neighbor_pass(q, lv, ids[..., :NS], sct[..., :NS], vld[..., :NS], tq, cfg.nb_window,
+                                            NS, cfg.nb_rho, cfg.nb_probe, cfg.nb_cap_min)
+        n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, nid=nid, match=match, nL=nL, positions=False)['n_tree']
+        st.st_leaf[b0:b1, :, :T0] = ids[..., :NS]
+        st.st_score[b0:b1, :, :T0] = sct[..., :NS]
+        st.st_ok[b0:b1, :, :T0] = vld[..., :NS]
+        used = vld & (torch.arange(wl, device=q.device) < n_tree.unsqueeze(-1))
+        leaves = torch.cat([ids, nid], -1)
+        return leaves, _ops.dedupe(leaves, torch.cat([used, match], -1))
+
     @torch.no_grad()
     def prefill(self, idx, chunk=16):
         """Run a prompt idx (B, T0) through the model (the training-mode forward semantics, reference
@@ -312,11 +420,19 @@ class Decoder:
                 Vc.copy_(v)
                 lv = Levels(st.levels.nodes[b0:b1], st.cap, st.L0, st.Lm)
                 _ops.build_levels(Kc, st.cap, st.L0, st.Lm, zero_sink=True, out=lv)
-                ids, vld, _ = _ops.select(q, lv, tq, self.wmax)
+                ids, vld, sct = _ops.select(q, lv, tq, self.wmax)
                 o = torch.empty(nb, T0, H, dh, device=self.dev, dtype=dt)
-                _ops.attend_leaves(q, Kc, Vc, tq, ids, vld, self.n_tree, 1 << st.L0, self.Lw, self.scale,
-                                   out=o.transpose(1, 2), want_nkeys=False)
-                del ids, vld
+                if self.general:
+                    leaves, keep = self._prefill_selection(st, L, q, k, lv, tq, ids, vld, sct, b0, b1)
+                    _ops.attend_leaves(q, Kc, Vc, tq, leaves, keep, leaves.shape[-1], 1 << st.L0, self.Lw,
+                                       self.scale, out=o.transpose(1, 2), want_nkeys=False)
+                    del leaves, keep
+                else:
+                    _ops.attend_leaves(q, Kc, Vc, tq, ids, vld, self.n_tree, 1 << st.L0, self.Lw, self.scale,
+                                       out=o.transpose(1, 2), want_nkeys=False)
+                if self.cfg.beam_mode == 'pred' and self.cfg.global_pool:  # running key sums for the budget head
+                    st.ksum[b0:b1] = Kc.float().sum(2)
+                del ids, vld, sct
                 x = x + F.linear(o.view(nb, T0, C), L['c_proj']).float()
                 x = x + F.linear(F.gelu(F.linear(_ln(x, L['ln2']).to(dt), L['c_fc'])), L['c_mlp']).float()
             last[b0:b1] = F.linear(_ln(x[:, -1], W['ln_f']).to(dt), W['wte'])
