@@ -117,3 +117,27 @@ def test_gpt_training_step_with_budget_head():
     assert losses[-1] < losses[0]
     pred_grad = m.blocks[0].attn.pred[0].weight.grad
     assert pred_grad is not None and float(pred_grad.abs().sum()) > 0
+
+
+def test_sparse_attn_queries_without_keys():
+    """A query whose candidates are all unused attends to nothing: output 0 (the reference kernel's l_safe rule),
+    no gradient to q, none from it to any key; the other queries are unaffected."""
+    from treeattn_b200.fastseg import sparse_attn
+    g = torch.Generator().manual_seed(4)
+    B, H, T, dh, K = 1, 2, 16, 64, 6
+    q, k, v = [torch.randn(B, H, T, dh, generator=g) for _ in range(3)]
+    cand = _rand_cand(B, H, T, T, K, g)
+    cand[:, :, 5] = -1
+    qd, kd, vd = [t.to(DEV).requires_grad_(True) for t in (q, k, v)]
+    o = sparse_attn(qd, kd, vd, cand.to(DEV), 0.125)
+    o.sum().backward()
+    assert float(o[:, :, 5].abs().max()) == 0.0
+    assert float(qd.grad[:, :, 5].abs().max()) == 0.0
+    assert torch.isfinite(kd.grad).all() and torch.isfinite(vd.grad).all()
+    qr, kr, vr = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    keep = torch.ones(T, dtype=torch.bool)
+    keep[5] = False
+    orf = sparse_attn_torch(qr[:, :, keep], kr, vr, cand[:, :, keep], 0.125)
+    orf.sum().backward()
+    assert float((o.detach().cpu()[:, :, keep] - orf.detach()).abs().max()) < 1e-4
+    assert float((kd.grad.cpu() - kr.grad).abs().max()) < 1e-4

@@ -65,6 +65,22 @@ def test_argument_validation_without_gpu():
     rc = lib.ta_seg_attn(addr + 2, addr, addr, 1, 1, 1, 1, 64, 0, 0, 64, 0, 0, 64, 0, 0, 64, 16, addr, 0, 1, addr,
                          addr, 1, None, 1, 2, 3, ctypes.c_float(0.125), addr, 0, 0, 64, None, None, None)
     assert rc == _lib.TA_ERR_ARG and 'aligned' in _lib.last_error()
+    # training backward: bad head dim, null pointers
+    rc = lib.ta_sparse_attn_bwd(addr, addr, addr, addr, addr, addr, 1, 1, 1, 4, 4, 48, addr, 0, 2,
+                                ctypes.c_float(0.125), addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'head dim' in _lib.last_error()
+    rc = lib.ta_sparse_attn_bwd(addr, addr, addr, addr, None, addr, 1, 1, 1, 4, 4, 64, addr, 0, 2,
+                                ctypes.c_float(0.125), addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'null' in _lib.last_error()
+    # dynamic-tree search: width above the beam, depth out of range
+    rc = lib.ta_lane_search(addr, addr, addr, 4, 3, 64, 4, 5, addr, addr, None, None)
+    assert rc == _lib.TA_ERR_ARG and 'wl' in _lib.last_error()
+    rc = lib.ta_lane_search(addr, addr, addr, 4, 0, 64, 4, 4, addr, addr, None, None)
+    assert rc == _lib.TA_ERR_ARG and 'D=' in _lib.last_error()
+    # neighbour pass: more than 32 stored leaves per query
+    rc = lib.ta_neighbor_pass(addr, 1, 1, 1, 4, 64, 0, 0, 64, addr, 0, 1, addr, 0, 0, 8, 3, addr, addr, addr, 16,
+                              9, 4, ctypes.c_float(0.35), 3, 2, 1, addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'nb_window' in _lib.last_error()
 
 
 def test_python_layer_rejects_cpu_tensors():

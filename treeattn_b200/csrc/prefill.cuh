@@ -414,18 +414,17 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
         m_new = fmaxf(m_run, mx * p.scale_log2);
         const float mu = m_new == -INFINITY ? 0.f : m_new;
         l_run *= ex2_approx(m_run - mu);
-        // P row (16-bit, rounded; the same rounded weights enter l) into the swizzled K-major P buffer;
-        // p = 2^(s * scale_log2 - mu) with the scaling fused into one FMA
+        // P row (16-bit, rounded for the tensor-core P.V) into the swizzled K-major P buffer; the denominator l sums
+        // the fp32 weights p = 2^(s * scale_log2 - mu) (the scaling fused into one FMA)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const uint32_t pk = pack2<T>(ex2_approx(fmaf(s[c * 8 + 2 * e], p.scale_log2, -mu)),
-                                         ex2_approx(fmaf(s[c * 8 + 2 * e + 1], p.scale_log2, -mu)));
-            const float2 back = unpack2<T>(pk);
-            l_run += back.x + back.y;
-            w[e] = pk;
+            const float p0 = ex2_approx(fmaf(s[c * 8 + 2 * e], p.scale_log2, -mu));
+            const float p1 = ex2_approx(fmaf(s[c * 8 + 2 * e + 1], p.scale_log2, -mu));
+            l_run += p0 + p1;  // the fp32 weights, as the reference's _attn_fwd sums them
+            w[e] = pack2<T>(p0, p1);
           }
           *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
