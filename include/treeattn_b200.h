@@ -54,6 +54,27 @@ int ta_build_levels(const void* k, int dtype, int B, int H, int T_len, int dh, i
                     int64_t k_st, int cap, int L0, int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh,
                     void* stream);
 
+/* The mean-log gate's statistic tree (seg.py:26-41 and fastseg.py:238-251 with cfg.gate, engine.py:47-54):
+ * arguments and layout as ta_build_levels; the leaf-level nodes sum log(|k| + 1e-6) of the (sink-zeroed) keys
+ * instead of the keys, in the same adjacent-pair order. */
+int ta_build_log_levels(const void* k, int dtype, int B, int H, int T_len, int dh, int64_t k_sb, int64_t k_sh,
+                        int64_t k_st, int cap, int L0, int Lm, int zero_sink, float* nodes, int64_t n_sb,
+                        int64_t n_sh, void* stream);
+
+/* Replaces seg.gate_apply (seg.py:16-23) over whole trees (fastseg.level_sums_min, fastseg.py:238-251): for every
+ * complete node (m < T_len >> l) of levels gate_min..Lm, out = raw * [ml >= q-quantile of ml] * dh / kept with
+ * ml = lg / 2^l (torch.quantile's interpolation); levels below gate_min are copied. raw, lg, out share the packed
+ * layout of ta_build_levels (strides n_sb, n_sh). dh 16, 32, 64 or 128. */
+int ta_gate_levels(const float* raw, const float* lg, float* out, int B, int H, int dh, int T_len, int64_t n_sb,
+                   int64_t n_sh, int cap, int L0, int Lm, float gate_q, int gate_min, void* stream);
+
+/* Decoding with the gate (engine.py:33-37 getU, 41-55 add): after ta_append / ta_decode_step appended position
+ * pos[b], forms the log-magnitude nodes completed by pos[b] (leaf block read from the key cache kc, right-spine
+ * ancestors) and the gated copies of every node formed at pos[b]. */
+int ta_gate_append(const void* kc, int dtype, int B, int H, int dh, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                   const float* raw, float* lg, float* out, int64_t n_sb, int64_t n_sh, int cap, int L0, int Lm,
+                   const int32_t* pos, float gate_q, int gate_min, void* stream);
+
 /* Replaces seg.tree_pass (seg.py:44-70) / fastseg.tree_pass_fast (fastseg.py:254-271) on the tree of leaf
  * blocks of 2^L0 tokens: per query (b, h, n) at position tq[b*tq_sb + n*tq_st], the best wmax leaves, best
  * first. Outputs (B, H, Nq, wl) contiguous: ids (int64, invalid slots 0), vld (uint8), sct (fp32 scores

@@ -13,7 +13,8 @@ import numpy as np
 
 F32 = np.float32
 
-__all__ = ['level_sums', 'tree_pass', 'lane_search', 'neighbor_pass', 'leaves_to_pos', 'finish', 'n_tree_fixed', 'static_keys', 'dedupe',
+__all__ = ['level_sums', 'tree_pass', 'lane_search', 'neighbor_pass', 'gate_apply', 'log_sums', 'gated_levels',
+           'torch_quantile', 'leaves_to_pos', 'finish', 'n_tree_fixed', 'static_keys', 'dedupe',
            'sparse_attn', 'gather_dot', 'select_seg', 'seg_attention', 'layer_norm', 'gelu', 'gpt_forward',
            'weights_from_state_dict', 'SegStateNP', 'seg_attend', 'DecoderNP', 'bf16_round', 'Lw_of']
 
@@ -48,6 +49,52 @@ def level_sums(k, L0, Lm, zero_sink=True):
         if l >= L0:
             out[l] = x
     return out
+
+
+def torch_quantile(x, q):
+    """torch.quantile(x, q, dim=-1, keepdim=True) for fp32 x (linear interpolation): ranks = q (n - 1) in fp32, the
+    values a, b at floor and ceil of the rank, weight w = rank - floor, then torch's two-sided lerp with one
+    rounding: w < 0.5 -> a + w (b - a), else b - (1 - w)(b - a) (a fused multiply-add on b - a; evaluated here in
+    float64, where the product is exact)."""
+    x = np.asarray(x, F32)
+    n = x.shape[-1]
+    v = np.sort(x, -1)
+    rank = F32(q) * F32(n - 1)
+    lo = int(np.floor(rank))
+    hi = int(np.ceil(rank))
+    w = F32(rank - F32(lo))
+    a, b = v[..., lo:lo + 1], v[..., hi:hi + 1]
+    d = (b - a).astype(np.float64)
+    if w < 0.5:
+        return (a.astype(np.float64) + np.float64(w) * d).astype(F32)
+    return (b.astype(np.float64) - np.float64(F32(1) - w) * d).astype(F32)
+
+
+def gate_apply(raw, lgsum, size, gate_q):
+    """seg.py:16-23 mean-log dilution gate: keep the dimensions whose mean log-magnitude in the group is at least
+    the gate_q quantile, zero the rest, rescale the kept ones by dh / kept."""
+    raw = np.asarray(raw, F32)
+    ml = (np.asarray(lgsum, F32) / F32(size)).astype(F32)
+    thr = torch_quantile(ml, gate_q)
+    g = (ml >= thr).astype(F32)
+    kept = np.maximum(g.sum(-1, keepdims=True), F32(1)).astype(F32)
+    return ((raw * g).astype(F32) * (F32(raw.shape[-1]) / kept).astype(F32)).astype(F32)
+
+
+def log_sums(k, L0, Lm, zero_sink=True):
+    """The mean-log statistic's tree (seg.py:31-37, fastseg.py:238-251): log(|k| + 1e-6) of the (sink-zeroed)
+    keys summed in the same adjacent-pair order as level_sums."""
+    x = np.array(k, dtype=F32, copy=True)
+    if zero_sink and x.shape[-2] > 0:
+        x[..., 0, :] = 0
+    return level_sums(np.log(np.abs(x) + F32(1e-6)).astype(F32), L0, Lm, zero_sink=False)
+
+
+def gated_levels(k, L0, Lm, gate_q, gate_min=0):
+    """fastseg.py:238-251 level_sums_min with the gate: levels l >= gate_min gated, the others raw."""
+    S = level_sums(k, L0, Lm, zero_sink=True)
+    G = log_sums(k, L0, Lm)
+    return {l: (gate_apply(S[l], G[l], 1 << l, gate_q) if l >= gate_min else S[l]) for l in S}
 
 
 def _gather_rows(S, idx):
@@ -234,15 +281,19 @@ def neighbor_pass(q, S_leaf, st_leaf, st_score, st_ok, tq, L0, nb_window, nb_sto
     return ids, match, nL
 
 
-def select_seg(q, k, lhat, wmax, L0=1, nb_width=0, with_margin=False, nb=None):
+def select_seg(q, k, lhat, wmax, L0=1, nb_width=0, with_margin=False, nb=None, gate=None):
     """seg.py:122-140 select_seg: fp32 copies, sink zeroed, levels, descent, neighbour pass, finish. nb = None
     stands for cfg.neighbors=False (neighbor_pass returns no matches, seg.py:97-98; nb_width slots of empty
     matches); otherwise nb = dict(nb_window, nb_store, nb_rho, nb_probe, nb_cap_min) runs the neighbour pass on
-    the descent's own results (the nb_store best leaves and scores of every position)."""
+    the descent's own results (the nb_store best leaves and scores of every position). gate = (gate_q,
+    gate_min_level) selects on the mean-log gated levels (fastseg.select_seg_fast)."""
     q = np.asarray(q, F32)
     B, H, T, dh = q.shape
     Lm = int(round(math.log2(T))) - 1
-    S = level_sums(k, L0, Lm, zero_sink=True)
+    if gate is None:
+        S = level_sums(k, L0, Lm, zero_sink=True)
+    else:  # gate = (gate_q, gate_min): fastseg.select_seg_fast's gated levels
+        S = gated_levels(k, L0, Lm, gate[0], gate[1])
     tq = np.arange(T)
     r = tree_pass(q, S, tq, L0, Lm, wmax, with_margin=with_margin)
     ids, vld, sct = r[:3]

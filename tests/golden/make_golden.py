@@ -4,7 +4,7 @@ The reference (Dex8123/treeattn, pure Python/PyTorch) is importable only in the 
 mounted read-only; it is made importable as the package `treeattn` through a symlink in a temp directory.
 The GPU box never runs this script: the tests read the committed .npz files.
 
-    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb]
+    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate]
 
 Leaf blocks of 2^L0 tokens (the benchmark configs use 32, 64 and 128) are produced with the reference's own
 functions on the level-shifted tree ("adapter"): seg.level_sums, then seg.tree_pass with
@@ -95,6 +95,35 @@ def tiny_gpt_nb_golden(R):
                 dec_keys=np.array([st[1] for st in steps]), **{'stat_' + kk: vv for kk, vv in stats.items()})
 
 
+def gate_goldens(R):
+    """The mean-log gate (seg.py:16-23, fastseg.py:238-251, engine.py:33-37): fastseg.select_seg_fast on gated
+    levels (gate_min_level 2, neighbours on), and a tiny GPT with the gate - forward logits and the reference
+    engine's token-by-token logits (its SegState keeps the log-magnitude tree and gates gathered nodes)."""
+    Config, fastseg, engine = R['config'].Config, R['fastseg'], R['engine']
+    g = torch.Generator().manual_seed(21)
+    q, k = torch.randn(2, 2, 128, 32, generator=g), torch.randn(2, 2, 128, 32, generator=g)
+    cfg = Config(attn='seg', seq_len=128, wmax=8, beam=4, beam_mode='fixed', gate=True, gate_q=0.25,
+                 gate_min_level=2)
+    lhat = torch.randint(2, 9, (2, 2, 128), generator=g)
+    sel = fastseg.select_seg_fast(q, k, lhat, cfg)
+    out = dict(sel_gate=dict(q=np_(q), k=np_(k), lhat=np_(lhat), wmax=8, gate_q=0.25, gate_min=2,
+                             **{kk: np_(vv) for kk, vv in sel.items()}))
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=3,
+                 neighbors=True, beam_mode='fixed', gate=True, gate_q=0.25, gate_min_level=1)
+    torch.manual_seed(8)
+    m = R['model'].GPT(cfg).eval()
+    idx = torch.randint(0, 64, (1, 128), generator=torch.Generator().manual_seed(9))
+    with torch.no_grad():
+        logits, _, stats = m(idx)
+        dec = engine.Decoder(engine.weights_from_ours(m.state_dict(), cfg), cfg.n_layer, cfg.n_head, cfg.n_embd,
+                             128, 'seg', cfg, 'cpu')
+        steps = [dec.step(int(idx[0, t]), t) for t in range(128)]
+    out['tiny_gpt_gate'] = dict(idx=np_(idx), logits=np_(logits), dec_logits=np.stack([np_(st[0]) for st in steps]),
+                                dec_keys=np.array([st[1] for st in steps]),
+                                **{'stat_' + kk: vv for kk, vv in stats.items()})
+    return out
+
+
 def main(ref_path, only=None):
     R = import_reference(ref_path)
     single = dict(lanetree=lanetree_golden, tiny_gpt_nb=tiny_gpt_nb_golden)
@@ -102,6 +131,11 @@ def main(ref_path, only=None):
         d = single[only](R)
         np.savez_compressed(os.path.join(HERE, only + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
         print('wrote', only)
+        return
+    if only == 'gate':
+        for name, d in gate_goldens(R).items():
+            np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
+            print('wrote', name)
         return
     Config = R['config'].Config
     seg, fastseg, engine, ad = R['seg'], R['fastseg'], R['engine'], R['attention_dyn']
@@ -236,6 +270,7 @@ def main(ref_path, only=None):
 
     out['lanetree'] = lanetree_golden(R)
     out['tiny_gpt_nb'] = tiny_gpt_nb_golden(R)
+    out.update(gate_goldens(R))
 
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})

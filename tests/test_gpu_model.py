@@ -371,3 +371,103 @@ def test_engine_pred_neighbours_matches_forward(global_pool):
         lg, _ = dec.step(idx[:, t], t)
         np.testing.assert_allclose(lg.float().cpu().numpy(), ref[:, t].cpu().numpy(), atol=1e-4)
     _no_device_error()
+
+
+# ------------------------------------------------------------------------------------------------ mean-log gate
+@pytest.mark.parametrize('dt,L0,dh', [(torch.float32, 1, 32), (torch.bfloat16, 3, 64), (torch.float16, 4, 128)])
+def test_gate_levels_vs_oracle(dt, L0, dh):
+    """Log-magnitude tree and gated nodes (ta_build_log_levels, ta_gate_levels) vs the oracle: sums bit-exact,
+    log sums within fp32 rounding of the logarithm, and the gated nodes equal wherever the gate keeps the same
+    dimensions (the q-quantile cut can move only where two dimensions' mean logs tie to an ulp)."""
+    from treeattn_b200 import _ops
+    from treeattn_b200.seg import gated_tree
+    rng = np.random.default_rng(L0 + dh)
+    B, H, T = 2, 3, 512
+    k = torch.as_tensor(rng.standard_normal((B, H, T, dh)).astype(np.float32)).to(dt)
+    Lm = int(math.log2(T)) - 1
+    raw, lg, gated = gated_tree(k.to(DEV), T, L0, Lm, 0.25, L0 + 1)
+    kf = k.float().numpy()
+    S = oracle.level_sums(kf, L0, Lm)
+    G = oracle.log_sums(kf, L0, Lm)
+    R = oracle.gated_levels(kf, L0, Lm, 0.25, L0 + 1)
+    bad = total = 0
+    for l in range(L0, Lm + 1):
+        np.testing.assert_array_equal(raw.level(l).cpu().numpy(), S[l])
+        np.testing.assert_allclose(lg.level(l).cpu().numpy(), G[l], rtol=2e-6, atol=2e-6 * (1 << l))
+        got = gated.level(l).cpu().numpy()
+        same = (got == R[l]).all(-1)
+        bad += int((~same).sum())
+        total += same.size
+    assert bad <= max(1, total // 200), (bad, total)
+    _no_device_error()
+
+
+def test_gate_append_matches_bulk():
+    """Decoding with the gate: the log-magnitude and gated nodes formed step by step (ta_append + ta_gate_append,
+    across several leaf-block boundaries) equal the bulk build of the same cache, bit for bit."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.engine import SegState
+    cfg = Config(attn='seg', seq_len=256, n_head=2, n_embd=128, gate=True, gate_q=0.25, gate_min_level=3, leaf=4,
+                 neighbors=False)
+    rng = np.random.default_rng(5)
+    B, H, dh, T0, steps = 2, 2, 64, 37, 40
+    st = SegState(cfg, 256, H, dh, DEV, batch=B, dtype=torch.bfloat16)
+    K0 = torch.as_tensor(rng.standard_normal((B, H, T0, dh)).astype(np.float32)).to(DEV, torch.bfloat16)
+    st.fill(K0, K0)
+    for s_i in range(steps):
+        kk = torch.as_tensor(rng.standard_normal((B, H, dh)).astype(np.float32)).to(DEV, torch.bfloat16)
+        st.add(T0 + s_i, kk, kk)
+    ref = SegState(cfg, 256, H, dh, DEV, batch=B, dtype=torch.bfloat16)
+    n = T0 + steps
+    ref.fill(st.K[:, :, :n].clone(), st.V[:, :, :n].clone())
+    for l in range(st.L0, st.Lm + 1):
+        m = n >> l
+        for a, b_ in ((st.levels, ref.levels), (st.lg, ref.lg), (st.gated, ref.gated)):
+            assert torch.equal(a.level(l)[:, :, :m], b_.level(l)[:, :, :m]), l
+    _no_device_error()
+
+
+def test_select_seg_fast_gate_golden():
+    """fastseg.select_seg_fast on mean-log gated levels (gate_min_level 2, neighbours on), the reference's fixture:
+    tree and neighbour positions, budgets and nb_leaves equal on every query."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.fastseg import select_seg_fast
+    g = load('sel_gate')
+    cfg = Config(attn='seg', seq_len=128, wmax=int(g['wmax']), beam=4, beam_mode='fixed', gate=True,
+                 gate_q=float(g['gate_q']), gate_min_level=int(g['gate_min']))
+    sel = select_seg_fast(torch.as_tensor(g['q']).to(DEV), torch.as_tensor(g['k']).to(DEV),
+                          torch.as_tensor(g['lhat']).to(DEV), cfg)
+    srt = lambda a: np.sort(a, -1)
+    assert (srt(sel['tree_pos'].cpu().numpy()) == srt(g['tree_pos'])).all()
+    assert (srt(sel['nb_pos'].cpu().numpy()) == srt(g['nb_pos'])).all()
+    assert (sel['n_tree'].cpu().numpy() == g['n_tree']).all()
+    assert (sel['nb_leaves'].cpu().numpy() == g['nb_leaves']).all()
+    _no_device_error()
+
+
+def test_gpt_gate_golden():
+    """The reference's tiny GPT with the gate (gate_min_level 1) and neighbours: forward logits and statistics, and
+    the engine's token-by-token logits, within 1e-4."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    g = load('tiny_gpt_gate')
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=3,
+                 neighbors=True, beam_mode='fixed', gate=True, gate_q=0.25, gate_min_level=1)
+    torch.manual_seed(8)
+    m = GPT(cfg).eval()
+    W = weights_from_ours(m.state_dict(), cfg)
+    m = m.to(DEV)
+    with torch.no_grad():
+        logits, _, stats = m(torch.as_tensor(g['idx']).to(DEV))
+    np.testing.assert_allclose(logits.cpu().numpy(), g['logits'], atol=1e-4)
+    for k in ('keys_total', 'keys_tree', 'keys_nb', 'nb_leaves', 'leaves_used'):
+        assert abs(stats[k] - float(g['stat_' + k])) < 1e-4, (k, stats[k], float(g['stat_' + k]))
+    dec = Decoder(W, cfg.n_layer, cfg.n_head, cfg.n_embd, 128, 'seg', cfg, DEV)
+    worst = 0.0
+    for t in range(128):
+        lg, keys = dec.step(int(g['idx'][0, t]), t)
+        worst = max(worst, float(np.abs(lg.cpu().numpy() - g['dec_logits'][t]).max()))
+        assert abs(float(keys) - float(g['dec_keys'][t])) < 1e-4, t
+    assert worst < 1e-4, worst
+    _no_device_error()

@@ -182,3 +182,25 @@ def test_select_seg_with_neighbours_golden():
     assert (srt(sel['nb_pos']) == srt(g['nb_pos'])).all() and (g['nb_pos'] >= 0).sum() > 1000
     assert (sel['leaf_ok'] == g['leaf_ok']).all()
     assert (sel['n_tree'] == g['n_tree']).all() and (sel['nb_leaves'] == g['nb_leaves']).all()
+
+
+def test_select_seg_gate_golden():
+    """fastseg.select_seg_fast on mean-log gated levels (gate_q 0.25, gate_min_level 2, neighbours on), leaf 2:
+    the oracle's selection equals the reference's on every query."""
+    g = load('sel_gate')
+    nb = dict(nb_window=8, nb_store=2, nb_rho=0.35, nb_probe=3, nb_cap_min=2)
+    sel = oracle.select_seg(g['q'], g['k'], g['lhat'], int(g['wmax']), L0=1, with_margin=True, nb=nb,
+                            gate=(float(g['gate_q']), int(g['gate_min'])))
+    srt = lambda a: np.sort(a, -1)
+    assert (srt(sel['tree_pos']) == srt(g['tree_pos'])).all()
+    assert (srt(sel['nb_pos']) == srt(g['nb_pos'])).all()
+    assert (sel['n_tree'] == g['n_tree']).all() and (sel['nb_leaves'] == g['nb_leaves']).all()
+
+
+def test_quantile_matches_torch():
+    """The gate's threshold: torch.quantile's interpolation with its fused lerp, for several q."""
+    gen = torch.Generator().manual_seed(0)
+    for q in (0.25, 0.1, 0.33, 0.5, 0.9):
+        x = torch.randn(2000, 64, generator=gen)
+        np.testing.assert_array_equal(oracle.torch_quantile(x.numpy(), q), torch.quantile(x, q, dim=-1,
+                                                                                            keepdim=True).numpy())

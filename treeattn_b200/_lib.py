@@ -25,6 +25,9 @@ SIGNATURES = {
     'ta_device_error': [P],
     'ta_level_nodes': [I, I, I],
     'ta_build_levels': [P, I, I, I, I, I, L, L, L, I, I, I, I, P, L, L, P],
+    'ta_build_log_levels': [P, I, I, I, I, I, L, L, L, I, I, I, I, P, L, L, P],
+    'ta_gate_levels': [P, P, P, I, I, I, I, L, L, I, I, I, F, I, P],
+    'ta_gate_append': [P, I, I, I, I, L, L, L, P, P, P, L, L, I, I, I, P, F, I, P],
     'ta_select': [P, I, I, I, I, I, L, L, L, P, L, L, P, L, L, I, I, I, I, I, P, P, P, P],
     'ta_finish': [P, P, P, P, P, P, L, I, I, I, I, P, P, P, P, P],
     'ta_seg_attn': [P, P, P, I, I, I, I, I, L, L, L, L, L, L, L, L, L, I, P, L, L, P, P, I, P, I, I, I, F,

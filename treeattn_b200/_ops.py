@@ -108,6 +108,43 @@ def build_levels(k, cap, L0, Lm, zero_sink=True, out=None):
     return out
 
 
+def build_log_levels(k, cap, L0, Lm, zero_sink=True, out=None):
+    """The gate's log-magnitude tree: levels L0..Lm of pairwise sums of log(|k| + 1e-6). Returns Levels."""
+    _need_cuda('build_log_levels', k)
+    _unit_inner('build_log_levels', k)
+    B, H, T, dh = k.shape
+    if out is None:
+        out = Levels.empty(B, H, dh, cap, L0, Lm, k.device)
+    nd = out.nodes
+    _lib.call('ta_build_log_levels', _p(k), _code(k), B, H, T, dh, k.stride(0), k.stride(1), k.stride(2), out.cap,
+              out.L0, out.Lm, 1 if zero_sink else 0, _p(nd), nd.stride(0), nd.stride(1), _stream(k))
+    return out
+
+
+def gate_levels(raw, lg, gate_q, gate_min, T_len, out=None):
+    """Gated copy of a tree (seg.gate_apply on every complete node of levels >= gate_min). Returns Levels."""
+    _need_cuda('gate_levels', raw.nodes, lg.nodes)
+    B, H, _, dh = raw.nodes.shape
+    if out is None:
+        out = Levels.empty(B, H, dh, raw.cap, raw.L0, raw.Lm, raw.nodes.device)
+    for t_ in (lg.nodes, out.nodes):
+        if t_.stride() != raw.nodes.stride():
+            raise ValueError('gate_levels: raw, lg and out must share one layout')
+    nd = raw.nodes
+    _lib.call('ta_gate_levels', _p(nd), _p(lg.nodes), _p(out.nodes), B, H, dh, int(T_len), nd.stride(0),
+              nd.stride(1), raw.cap, raw.L0, raw.Lm, float(gate_q), int(gate_min), _stream(nd))
+    return out
+
+
+def gate_append(kc, raw, lg, gated, pos, gate_q, gate_min):
+    """After appending position pos[b]: log-magnitude and gated nodes completed by it (decoding with the gate)."""
+    B, H, cap, dh = kc.shape
+    nd = raw.nodes
+    _lib.call('ta_gate_append', _p(kc), _code(kc), B, H, dh, kc.stride(0), kc.stride(1), kc.stride(2), _p(nd),
+              _p(lg.nodes), _p(gated.nodes), nd.stride(0), nd.stride(1), raw.cap, raw.L0, raw.Lm, _p(pos),
+              float(gate_q), int(gate_min), _stream(kc))
+
+
 def _tq_strides(tq, B, Nq):
     if tq.dim() == 1:
         if tq.shape[0] == Nq:

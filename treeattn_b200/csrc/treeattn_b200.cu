@@ -98,13 +98,15 @@ ta::LevelView make_lv(const float* nodes, int64_t n_sb, int64_t n_sh, int cap, i
 template <typename T, int DH>
 struct BuildLevels {
   static int run(const void* k, int B, int H, int T_len, int64_t k_sb, int64_t k_sh, int64_t k_st, int cap, int L0,
-                 int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh, cudaStream_t st) {
+                 int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh, cudaStream_t st,
+                 bool logmag = false) {
     const ta::LevelView lv = make_lv(nodes, n_sb, n_sh, cap, L0, Lm);
     const int n_leaf = T_len >> L0;
     const int64_t total = (int64_t)B * H * n_leaf * DH;
     if (total > 0) {
       const int threads = 256;
-      ta::build_leaf_level_kernel<T><<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
+      auto kern = logmag ? ta::build_leaf_level_kernel<T, true> : ta::build_leaf_level_kernel<T, false>;
+      kern<<<(unsigned)((total + threads - 1) / threads), threads, 0, st>>>(
           reinterpret_cast<const T*>(k), k_sb, k_sh, k_st, H, T_len, DH, L0, nodes + (int64_t)lv.off[L0] * DH, n_sb,
           n_sh, n_leaf, total, zero_sink);
       if (int r = check_launch("ta_build_levels(leaf)")) return r;
@@ -131,6 +133,28 @@ struct BuildLevels {
       if (int r = check_launch("ta_build_levels(upper)")) return r;
     }
     return TA_OK;
+  }
+};
+
+template <typename T, int DH>
+struct BuildLogLevels {
+  static int run(const void* k, int B, int H, int T_len, int64_t k_sb, int64_t k_sh, int64_t k_st, int cap, int L0,
+                 int Lm, int zero_sink, float* nodes, int64_t n_sb, int64_t n_sh, cudaStream_t st) {
+    return BuildLevels<T, DH>::run(k, B, H, T_len, k_sb, k_sh, k_st, cap, L0, Lm, zero_sink, nodes, n_sb, n_sh, st,
+                                   true);
+  }
+};
+
+template <typename T, int DH>
+struct GateAppend {
+  static int run(const void* kc, int B, int H, int64_t c_sb, int64_t c_sh, int64_t c_st, const float* raw, float* lg,
+                 float* out, int64_t n_sb, int64_t n_sh, const ta::LevelView& lv, const int32_t* pos, float gate_q,
+                 int gate_min, cudaStream_t st) {
+    const int64_t threads = (int64_t)B * H * 32;
+    if (threads == 0) return TA_OK;
+    ta::gate_append_kernel<T, DH><<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(
+        reinterpret_cast<const T*>(kc), c_sb, c_sh, c_st, raw, lg, out, n_sb, n_sh, B, H, lv, pos, gate_q, gate_min);
+    return check_launch("ta_gate_append");
   }
 };
 
@@ -535,6 +559,56 @@ int ta_build_levels(const void* k, int dtype, int B, int H, int T_len, int dh, i
   if (!k || !nodes) return fail(TA_ERR_ARG, "ta_build_levels: null pointer");
   return by_type_dh<BuildLevels>(dtype, dh, k, B, H, T_len, k_sb, k_sh, k_st, cap, L0, Lm, zero_sink, nodes, n_sb,
                                  n_sh, S(stream));
+}
+
+int ta_build_log_levels(const void* k, int dtype, int B, int H, int T_len, int dh, int64_t k_sb, int64_t k_sh,
+                        int64_t k_st, int cap, int L0, int Lm, int zero_sink, float* nodes, int64_t n_sb,
+                        int64_t n_sh, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_build_log_levels: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_build_log_levels: unsupported head dim %d", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if (B < 0 || H <= 0 || T_len < 0 || T_len > cap)
+    return fail(TA_ERR_ARG, "ta_build_log_levels: bad sizes B=%d H=%d T=%d cap=%d", B, H, T_len, cap);
+  if (!k || !nodes) return fail(TA_ERR_ARG, "ta_build_log_levels: null pointer");
+  return by_type_dh<BuildLogLevels>(dtype, dh, k, B, H, T_len, k_sb, k_sh, k_st, cap, L0, Lm, zero_sink, nodes, n_sb,
+                                    n_sh, S(stream));
+}
+
+int ta_gate_levels(const float* raw, const float* lg, float* out, int B, int H, int dh, int T_len, int64_t n_sb,
+                   int64_t n_sh, int cap, int L0, int Lm, float gate_q, int gate_min, void* stream) {
+  g_err.clear();
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_gate_levels: head dim %d (16, 32, 64, 128)", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if (B < 0 || H <= 0 || T_len < 0 || T_len > cap) return fail(TA_ERR_ARG, "ta_gate_levels: bad sizes");
+  if (!(gate_q >= 0.f && gate_q <= 1.f)) return fail(TA_ERR_ARG, "ta_gate_levels: gate_q outside [0, 1]");
+  if (!raw || !lg || !out) return fail(TA_ERR_ARG, "ta_gate_levels: null pointer");
+  const ta::LevelView lv = make_lv(raw, n_sb, n_sh, cap, L0, Lm);
+  const int64_t per_bh = ta_level_nodes(cap, L0, Lm);
+  const int64_t threads = (int64_t)B * H * per_bh * 32;
+  if (threads == 0) return TA_OK;
+  const unsigned grid = (unsigned)((threads + 127) / 128);
+  cudaStream_t st = S(stream);
+  auto kern = dh == 16 ? ta::gate_levels_kernel<16>
+              : dh == 32 ? ta::gate_levels_kernel<32> : dh == 64 ? ta::gate_levels_kernel<64> : ta::gate_levels_kernel<128>;
+  kern<<<grid, 128, 0, st>>>(raw, lg, out, n_sb, n_sh, H, lv, T_len, B * H, gate_q, gate_min, per_bh);
+  return check_launch("ta_gate_levels");
+}
+
+int ta_gate_append(const void* kc, int dtype, int B, int H, int dh, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                   const float* raw, float* lg, float* out, int64_t n_sb, int64_t n_sh, int cap, int L0, int Lm,
+                   const int32_t* pos, float gate_q, int gate_min, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_gate_append: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_gate_append: head dim %d (16, 32, 64, 128)", dh);
+  if (int r = check_levels(cap, L0, Lm)) return r;
+  if (L0 > 15) return fail(TA_ERR_ARG, "ta_gate_append: leaf level %d above 15", L0);
+  if (B < 0 || H <= 0) return fail(TA_ERR_ARG, "ta_gate_append: bad sizes");
+  if (!(gate_q >= 0.f && gate_q <= 1.f)) return fail(TA_ERR_ARG, "ta_gate_append: gate_q outside [0, 1]");
+  if (!kc || !raw || !lg || !out || !pos) return fail(TA_ERR_ARG, "ta_gate_append: null pointer");
+  const ta::LevelView lv = make_lv(raw, n_sb, n_sh, cap, L0, Lm);
+  return by_type_dh<GateAppend>(dtype, dh, kc, B, H, c_sb, c_sh, c_st, raw, lg, out, n_sb, n_sh, lv, pos, gate_q,
+                                gate_min, S(stream));
 }
 
 int ta_select(const void* q, int q_dtype, int B, int H, int Nq, int dh, int64_t q_sb, int64_t q_sh, int64_t q_st,

@@ -35,8 +35,6 @@ class SegState:
     of positions actually allocated, so a 4352-token context with Tcap 8192 does not pay for 8192 rows."""
 
     def __init__(self, cfg, Tcap, H, dh, dev, batch=1, dtype=torch.float32, cap=None):
-        if cfg.gate:
-            raise NotImplementedError('the mean-log gate (cfg.gate=True) is not implemented in treeattn_b200')
         self.cfg, self.Tcap, self.H, self.dh = cfg, Tcap, H, dh
         self.Lm = _ops.lm_of(Tcap)
         self.L0 = _ops.log2_exact(getattr(cfg, 'leaf', 2), 'cfg.leaf')
@@ -46,6 +44,9 @@ class SegState:
         self.K = torch.zeros(batch, H, self.cap, dh, device=dev, dtype=dtype)
         self.V = torch.zeros(batch, H, self.cap, dh, device=dev, dtype=dtype)
         self.levels = Levels.empty(batch, H, dh, self.cap, self.L0, self.Lm, dev)
+        if cfg.gate:  # the log-magnitude tree and the gated nodes the descent scores (engine.py:26-27, 33-37)
+            self.lg = Levels.empty(batch, H, dh, self.cap, self.L0, self.Lm, dev)
+            self.gated = Levels.empty(batch, H, dh, self.cap, self.L0, self.Lm, dev)
         if cfg.neighbors:  # the best leaves every position found, for neighbour borrowing (engine.py:28-31)
             NS = cfg.nb_store
             self.st_leaf = torch.zeros(batch, H, self.cap, NS, device=dev, dtype=torch.int64)
@@ -58,8 +59,13 @@ class SegState:
         """{level: (B, H, cap >> l, dh)} views of the stored levels (reference SegState.raw, levels >= L0)."""
         return self.levels.as_dict()
 
+    @property
+    def sel_levels(self):
+        """The tree the descent scores: the gated nodes with cfg.gate, else the sums themselves."""
+        return self.gated if self.cfg.gate else self.levels
+
     def getU(self, l, cand):
-        return gather_nodes(self.levels.level(l), cand)
+        return gather_nodes(self.sel_levels.level(l), cand)
 
     def add(self, t, k, v):
         """k, v: (B, H, dh) (or (B, H, 1, dh)) for position t (int or (B,) tensor)."""
@@ -67,6 +73,9 @@ class SegState:
             k, v = k[:, :, 0], v[:, :, 0]
         pos = _positions(t, self.batch, self.K.device)
         _ops.append(k.to(self.K.dtype), v.to(self.V.dtype), self.K, self.V, self.levels, pos)
+        if self.cfg.gate:
+            _ops.gate_append(self.K, self.levels, self.lg, self.gated, pos, self.cfg.gate_q,
+                             getattr(self.cfg, 'gate_min_level', 0))
         self.ksum += k.float()
 
     def fill(self, K, V):
@@ -77,6 +86,10 @@ class SegState:
         self.K[:, :, :T].copy_(K)
         self.V[:, :, :T].copy_(V)
         _ops.build_levels(self.K[:, :, :T], self.cap, self.L0, self.Lm, zero_sink=True, out=self.levels)
+        if self.cfg.gate:
+            _ops.build_log_levels(self.K[:, :, :T], self.cap, self.L0, self.Lm, zero_sink=True, out=self.lg)
+            _ops.gate_levels(self.levels, self.lg, self.cfg.gate_q, getattr(self.cfg, 'gate_min_level', 0), T,
+                             out=self.gated)
         self.ksum.copy_(K.float().sum(2))
 
 
@@ -111,11 +124,11 @@ def _general_step(state, pw, q, k, v, pos, out=None, update=True):
         lhat = pred_budget(pw, q, kmean, H)
     else:
         lhat = torch.full((B, H, 1), cfg.beam, device=q.device, dtype=torch.int64)
-    ids, vld, sct = _ops.select(q, state.levels, tq, cfg.wmax)
+    ids, vld, sct = _ops.select(q, state.sel_levels, tq, cfg.wmax)
     wl = ids.shape[-1]
     if cfg.neighbors:
         NS = cfg.nb_store
-        nid, match, nL = _ops.neighbor_pass(q, state.levels, state.st_leaf, state.st_score, state.st_ok, tq,
+        nid, match, nL = _ops.neighbor_pass(q, state.sel_levels, state.st_leaf, state.st_score, state.st_ok, tq,
                                             cfg.nb_window, NS, cfg.nb_rho, cfg.nb_probe, cfg.nb_cap_min)
         n_tree = _ops.finish(ids, vld, lhat, cfg.wmax, leaf, nid=nid, match=match, nL=nL, positions=False)['n_tree']
         if update:
@@ -147,7 +160,7 @@ def seg_attend(state, pw, q, k, v, t, update=True):
     pos = _positions(t, B, q.device)
     qx = q.to(state.K.dtype)
     kx, vx = [None if t_ is None else t_.to(state.K.dtype) for t_ in (k, v)]  # k / v unused when update=False
-    if cfg.neighbors or cfg.beam_mode == 'pred':
+    if cfg.neighbors or cfg.beam_mode == 'pred' or cfg.gate:
         out, nkeys = _general_step(state, pw, qx, kx, vx, pos, update=update)
         return out, nkeys.float().mean()
     if update:
@@ -209,7 +222,7 @@ class Decoder:
                                    c_fc=cast(L['c_fc']), c_mlp=cast(L['c_mlp'])) for L in W['layers'][:n_layer]])
         # general selection (learned budget, neighbour borrowing): per layer the separate kernels of
         # _general_step instead of the single fused decode kernel
-        self.general = cfg.neighbors or cfg.beam_mode == 'pred'
+        self.general = cfg.neighbors or cfg.beam_mode == 'pred' or cfg.gate
         if cfg.beam_mode == 'pred':
             for Ld, L in zip(self.W['layers'], W['layers'][:n_layer]):
                 Ld['pw'] = {k_: (t.to(self.dev) if torch.is_tensor(t) else t) for k_, t in L['pw'].items()}
@@ -420,6 +433,11 @@ class Decoder:
                 Vc.copy_(v)
                 lv = Levels(st.levels.nodes[b0:b1], st.cap, st.L0, st.Lm)
                 _ops.build_levels(Kc, st.cap, st.L0, st.Lm, zero_sink=True, out=lv)
+                if self.cfg.gate:  # the descent scores the gated nodes (levels >= gate_min_level)
+                    lg = Levels(st.lg.nodes[b0:b1], st.cap, st.L0, st.Lm)
+                    _ops.build_log_levels(Kc, st.cap, st.L0, st.Lm, zero_sink=True, out=lg)
+                    lv = _ops.gate_levels(lv, lg, self.cfg.gate_q, getattr(self.cfg, 'gate_min_level', 0), T0,
+                                          out=Levels(st.gated.nodes[b0:b1], st.cap, st.L0, st.Lm))
                 ids, vld, sct = _ops.select(q, lv, tq, self.wmax)
                 o = torch.empty(nb, T0, H, dh, device=self.dev, dtype=dt)
                 if self.general:

@@ -10,7 +10,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib, _ops
-from .seg import finish, gate_apply, neighbor_pass, select_seg, select_tree, tree_pass
+from .seg import finish, gate_apply, neighbor_pass, select_seg, select_tree, tree_pass  # noqa: F401
 
 FAST = [True]  # kept for callers that toggle it; this package has only the CUDA path
 
@@ -65,10 +65,12 @@ def dedupe_fast(cand, valid):
 # ------------------------------------------------------------------ key selection (same logic as seg.select_seg)
 @torch.no_grad()
 def level_sums_min(kidx, Lm, gate, gate_q, gate_min):
-    if gate:
-        gate_apply(None, None, None, gate_q)
-    from .seg import level_sums
-    return level_sums(kidx, Lm, False, gate_q)
+    """fastseg.py:238-251: level sums of kidx (sink already zeroed), mean-log gated at levels >= gate_min."""
+    from .seg import gated_tree, level_sums
+    if not gate:
+        return level_sums(kidx, Lm, False, gate_q)
+    T = kidx.shape[2]
+    return gated_tree(kidx, T, 1, Lm, gate_q, gate_min, zero_sink=False)[2].as_dict()
 
 
 @torch.no_grad()
@@ -83,7 +85,13 @@ def neighbor_pass_fast(q, S1, st_leaf, st_score, st_ok, tq, cfg):
 
 @torch.no_grad()
 def select_seg_fast(q, k, lhat, cfg):
-    return select_seg(q, k, lhat, cfg)
+    """fastseg.py:302-314: select_seg with the gate applied from cfg.gate_min_level up."""
+    b, H, T, dh = q.shape
+    ids, vld, sct, lv = select_tree(q, k, cfg)
+    NS = cfg.nb_store
+    tq = torch.arange(T, device=q.device)
+    nid, match, nL = neighbor_pass(q, lv, ids[..., :NS], sct[..., :NS], vld[..., :NS], tq, cfg)
+    return _ops.finish(ids, vld, lhat, cfg.wmax, 1 << lv.L0, nid=nid, match=match, nL=nL)
 
 
 def n_tree_fixed(beam, wmax):
@@ -150,8 +158,6 @@ class SegAttention(nn.Module):
 
     def sparse_attend(self, q, k, v, out=None):
         cfg = self.cfg
-        if cfg.gate:
-            gate_apply(None, None, None, cfg.gate_q)
         if self._needs_grad(q, k, v):
             o = self._sparse_attend_autograd(q, k, v)
             if out is not None:
@@ -218,7 +224,7 @@ class SegAttention(nn.Module):
         if lhat is None:
             lhat = torch.full((b, H, T), cfg.beam, dtype=torch.long, device=dev)
         with torch.no_grad():
-            sel = select_seg(q.detach(), k.detach(), lhat, cfg)
+            sel = select_seg_fast(q.detach(), k.detach(), lhat, cfg)
             tree_pos, nb_pos, leaf_ok = sel['tree_pos'], sel['nb_pos'], sel['leaf_ok']
             wl = leaf_ok.shape[-1]
             leaf = tree_pos.shape[-1] // max(wl, 1)
