@@ -85,6 +85,9 @@ def parse():
     p.add_argument('--config1', action='store_true',
                    help='configuration 1 instead: the full forward of the 4-layer d=256 fp32 GPT (B=2, T=512, leaf 32, '
                         'top-4, window 64) on the GPU and on the CPU oracle, logits compared; prints one JSON line')
+    p.add_argument('--config3', action='store_true',
+                   help='configuration 3 end to end: the 12-layer bf16 GPT forward (prefill) over 4 x 8192 tokens; '
+                        'prints one JSON line')
     p.add_argument('--profile-steps', type=int, default=0,
                    help='profiling mode: after prefill and warm-up run this many eager decode steps between '
                         'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
@@ -438,6 +441,37 @@ def union_tile_pairs(ids, vld, n_tree, leaf, Lw, T, qt=128, kt=64):
     return int(occ.sum())
 
 
+def run_config3(a, dev):
+    """Configuration 3 end to end: the whole 12-layer, 768-wide bf16 GPT forward (SegAttention prefill: levels,
+    tile select, tensor-core tile attention; cuBLAS projections) over B=4 sequences of 8192 uniform-random tokens,
+    leaf 64, top-16, window 128; CUDA events over whole forwards (inputs far above L2). Prints one JSON line."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    B = a.batch if a.batch != 64 else 4
+    T = 8192
+    cfg = Config(vocab_size=50304, seq_len=T, n_layer=12, n_head=12, n_embd=768, attn='seg', wmax=16, beam=16,
+                 local=128, neighbors=False, beam_mode='fixed', leaf=64)
+    torch.manual_seed(0)
+    m = GPT(cfg).eval().to(dev, torch.bfloat16)
+    idx = torch.randint(0, cfg.vocab_size, (B, T), device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        for _ in range(2):
+            logits, _, stats = m(idx)
+        torch.cuda.synchronize()
+        reps = 5
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(reps):
+            logits, _, stats = m(idx)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    print(json.dumps(dict(config3=True, config='3: GPT 12x768 bf16, B=%d x T=%d, leaf 64, top-16, window 128' % (B, T),
+                          forward_ms=ms, tokens_per_s=B * T / (ms * 1e-3), keys_per_query=stats['keys_total'],
+                          data='synthetic (uniform random tokens, N(0,0.02) random-init weights)')), flush=True)
+
+
 def run_prefill_attn(a, dev):
     """Configuration 3, one layer of prefill sparse attention: B=4, H=12, T=8192, dh=64 bf16, 64-token leaves,
     top-16, 128-token window. q / k / v random, the selection from build_levels + select (the model's own
@@ -596,6 +630,9 @@ def main():
         return
     if a.config1:
         run_config1(a, dev)
+        return
+    if a.config3:
+        run_config3(a, dev)
         return
 
     run_engine(a, CFG5 if a.config5 else CFG4, dev, rank, world, local)
