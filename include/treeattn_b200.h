@@ -145,6 +145,42 @@ int ta_neighbor_pass(const void* q, int q_dtype, int B, int H, int Nq, int dh, i
 int ta_lane_search(const float* q, const float* sums, const int32_t* cnt, int P, int D, int dh, int wmax, int wl,
                    int64_t* ids, uint8_t* vld, float* sct, void* stream);
 
+/* Replaces the 2-means splits of the dyntree.LaneTree build (dyntree.py:6-31 masked_two_means_order and 54-73) and,
+ * with all slots valid, forest.build_forest's content sort (forest.py:13-33 two_means_order, 59-67). Lane p orders
+ * C slots (a power of two, 4..16384); slot s holds key row s of the lane's key array, fp32 (C, dh) at
+ * keys + (p / key_lane_div) * key_stride, and is valid when first <= s < n[p]. For every level lvl < `levels` the
+ * valid keys of each group of C >> lvl slots are sorted by their projection on the difference of two 2-means
+ * centres (iters rounds) and dealt to the group's halves, ceil(count / 2) to the left. Output perm (P, C) int32
+ * (the key row in every slot) and valid (P, C) uint8; perm_tmp / valid_tmp are scratch of the same sizes. */
+int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first, int P,
+                  int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, int32_t* perm_tmp,
+                  uint8_t* valid_tmp, void* stream);
+
+/* Completes a dyntree.LaneTree build (dyntree.py:74-80): from the ordered slots of ta_lane_order, the group slots
+ * slot (P, C/2, 2) int32 (key position, -1 = empty) and the node sums (P, C - 1, dh) fp32 / counts (P, C - 1) int32
+ * packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2), formed bottom-up in adjacent pairs. */
+int ta_lane_sums(const float* keys, int64_t key_lane_div, int64_t key_stride, const int32_t* perm,
+                 const uint8_t* valid, int P, int C, int dh, float* sums, int32_t* cnt, int32_t* slot, void* stream);
+
+/* Replaces dyntree.LaneTree.insert (dyntree.py:83-106): key kv[p] (fp32, dh) at position kpos[p] joins lane p's
+ * tree where active[p]: added to the root and, level by level, to the child whose mean scores higher against it
+ * (kv . sum / count; -1e9 when empty, -inf when full; ties left), then to the first free slot of its group. */
+int ta_lane_insert(const float* kv, const int64_t* kpos, const uint8_t* active, int P, int C, int dh, float* sums,
+                   int32_t* cnt, int32_t* slot, void* stream);
+
+/* Replaces dyntree.select_keys (dyntree.py:150-243) after the build: lane p = (b H + h) (T / chunk) + l holds the
+ * tree of the keys [1, l chunk) of (b, h) (ta_lane_order + ta_lane_sums with key_lane_div = T / chunk) and walks
+ * the tokens t = l chunk .. (l + 1) chunk - 1 in order: neighbour rescoring of the nb_store best groups stored by
+ * the previous nb_window tokens of the lane (q . sum / count >= base - rho |base|, scan depth capped by the probe
+ * rate), the beam descent (as ta_lane_search), the tree budget from lhat, and the insertion of the token's key
+ * (t >= 1). q, k (B, H, T, dh) fp32; lhat (B, H, T) int64. Outputs tree_pos (B, H, T, 2 wl), leaf_ok (B, H, T, wl),
+ * nb_pos (B, H, T, 2 nb_window nb_store) int64 positions (-1 = none), n_tree, nb_leaves (B, H, T) int64;
+ * wl = min(wmax, T / 2). The trees are updated in place. */
+int ta_lane_select(const float* q, const float* k, const int64_t* lhat, int B, int H, int T, int dh, int chunk,
+                   int wmax, int nb_window, int nb_store, int nb_probe, int nb_cap_min, float nb_rho, int neighbors,
+                   float* sums, int32_t* cnt, int32_t* slot, int64_t* tree_pos, uint8_t* leaf_ok, int64_t* nb_pos,
+                   int64_t* n_tree, int64_t* nb_leaves, void* stream);
+
 /* Replaces the backward of fastseg.sparse_attn (fastseg.py:80-110 _attn_bwd, 158-170 _SparseAttnFn.backward):
  * from the forward's o and lse (natural log) and the output gradient dout, dq (q's dtype) and the fp32 key / value
  * gradients dk, dv, which are ACCUMULATED (vector atomics, as the reference does; zero them first). All tensors

@@ -1,4 +1,4 @@
-"""CPU oracle of treeattn's segment-tree sparse-attention path (numpy, fp32).
+"""CPU oracle of treeattn's segment-tree sparse-attention path and its dynamic content tree (numpy, fp32).
 
 TEST INFRASTRUCTURE ONLY. The product (treeattn_b200) never imports this package; only tests/,
 __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs use it, and only as the checker or
@@ -6,3 +6,4 @@ as the timed CPU baseline. It is pinned against golden vectors produced by the r
 (tests/golden/make_golden.py, tests/test_oracle_golden.py).
 """
 from .seg_oracle import *  # noqa: F401,F403
+from .dyn_oracle import *  # noqa: F401,F403

@@ -4,7 +4,7 @@ The reference (Dex8123/treeattn, pure Python/PyTorch) is importable only in the 
 mounted read-only; it is made importable as the package `treeattn` through a symlink in a temp directory.
 The GPU box never runs this script: the tests read the committed .npz files.
 
-    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate]
+    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate|dyn]
 
 Leaf blocks of 2^L0 tokens (the benchmark configs use 32, 64 and 128) are produced with the reference's own
 functions on the level-shifted tree ("adapter"): seg.level_sums, then seg.tree_pass with
@@ -124,6 +124,50 @@ def gate_goldens(R):
     return out
 
 
+def dyn_goldens(R):
+    """The dynamic content tree (attn='dyn'): a LaneTree the reference builds (2-means splits, dyntree.py:46-80) and
+    grows (insertions, dyntree.py:83-106), stored as slots, packed node sums and counts after the build and after
+    the insertions; dyntree.select_keys (dyntree.py:150-243) on two configurations (neighbours on, learned-budget
+    style random leaf budgets); and tiny GPTs with DynAttention (attn='dyn', fixed and pred budgets): logits and
+    statistics."""
+    dyn, Config = R['dyntree'], R['config'].Config
+    out = {}
+    g = torch.Generator().manual_seed(31)
+    P, C, dh = 5, 64, 8
+    kfull = torch.randn(P, C, dh, generator=g)
+    n = torch.tensor([0, 8, 20, 33, 40])
+    tree = dyn.LaneTree(kfull, n, iters=3)
+    d = dict(kfull=np_(kfull), n=np_(n), slot0=np_(tree.slot.clone()), sums0=np_(torch.cat(tree.sums, 1)),
+             cnt0=np_(torch.cat(tree.cnt, 1)))
+    ar = torch.arange(P)
+    for i in range(16):
+        kpos = n + i
+        tree.insert(kfull[ar, kpos], kpos, kpos >= 1)
+    d.update(slot1=np_(tree.slot), sums1=np_(torch.cat(tree.sums, 1)), cnt1=np_(torch.cat(tree.cnt, 1)))
+    out['dyn_tree'] = d
+    for name, (B, H, T, hd, kw) in dict(
+            dyn_sel_a=(2, 2, 64, 16, dict(chunk=16, wmax=4, nb_window=4, nb_store=2, nb_probe=2, nb_cap_min=1)),
+            dyn_sel_b=(1, 3, 128, 32, dict(chunk=32, wmax=8))).items():
+        cfg = Config(attn='dyn', seq_len=T, **kw)
+        q, k = torch.randn(B, H, T, hd, generator=g), torch.randn(B, H, T, hd, generator=g)
+        lhat = torch.randint(2, cfg.wmax + 1, (B, H, T), generator=g)
+        sel = dyn.select_keys(q, k, lhat, cfg)
+        out[name] = dict(q=np_(q), k=np_(k), lhat=np_(lhat), chunk=cfg.chunk, wmax=cfg.wmax, nb_window=cfg.nb_window,
+                         nb_store=cfg.nb_store, nb_rho=cfg.nb_rho, nb_probe=cfg.nb_probe, nb_cap_min=cfg.nb_cap_min,
+                         **{kk: np_(vv) for kk, vv in sel.items()})
+    for name, kw in dict(tiny_gpt_dyn=dict(beam_mode='fixed'),
+                         tiny_gpt_dyn_pred=dict(beam_mode='pred', global_pool=True, local=8)).items():
+        cfg = Config(vocab_size=64, seq_len=64, n_layer=2, n_head=2, n_embd=32, attn='dyn', chunk=16, wmax=4, beam=2,
+                     beam_classes=(2, 3, 4), nb_window=4, nb_store=2, nb_probe=2, nb_cap_min=1, **kw)
+        torch.manual_seed(33)
+        m = R['model'].GPT(cfg).eval()
+        idx = torch.randint(0, 64, (2, 64), generator=torch.Generator().manual_seed(34))
+        with torch.no_grad():
+            logits, _, stats = m(idx)
+        out[name] = dict(idx=np_(idx), logits=np_(logits), **{'stat_' + kk: vv for kk, vv in stats.items()})
+    return out
+
+
 def main(ref_path, only=None):
     R = import_reference(ref_path)
     single = dict(lanetree=lanetree_golden, tiny_gpt_nb=tiny_gpt_nb_golden)
@@ -132,8 +176,8 @@ def main(ref_path, only=None):
         np.savez_compressed(os.path.join(HERE, only + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
         print('wrote', only)
         return
-    if only == 'gate':
-        for name, d in gate_goldens(R).items():
+    if only in ('gate', 'dyn'):
+        for name, d in (gate_goldens if only == 'gate' else dyn_goldens)(R).items():
             np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
             print('wrote', name)
         return
@@ -271,6 +315,7 @@ def main(ref_path, only=None):
     out['lanetree'] = lanetree_golden(R)
     out['tiny_gpt_nb'] = tiny_gpt_nb_golden(R)
     out.update(gate_goldens(R))
+    out.update(dyn_goldens(R))
 
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})

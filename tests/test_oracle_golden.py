@@ -204,3 +204,62 @@ def test_quantile_matches_torch():
         x = torch.randn(2000, 64, generator=gen)
         np.testing.assert_array_equal(oracle.torch_quantile(x.numpy(), q), torch.quantile(x, q, dim=-1,
                                                                                             keepdim=True).numpy())
+
+
+# ------------------------------------------------------------------------------------------------ dynamic tree
+def test_dyn_tree_build_and_insert_golden():
+    """dyntree.LaneTree (dyntree.py:46-106): the oracle's 2-means build, then 16 insertions, hold the same keys in the
+    same groups as the reference's tree (children compared in canonical order: a two-key split's orientation is an
+    exact fp32 tie), with the same counts and node sums within fp32 rounding; no decision is near a tie."""
+    g = load('dyn_tree')
+    t = oracle.LaneTreeNP(g['kfull'], g['n'], 3)
+    assert (t.margin > 1e-5).all()
+    a = oracle.canonical_tree(t.slot, t.sums, t.cnt)
+    b = oracle.canonical_tree(g['slot0'], g['sums0'], g['cnt0'])
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[2], b[2])
+    np.testing.assert_allclose(a[1], b[1], atol=1e-5)
+    ar = np.arange(len(g['n']))
+    for i in range(16):
+        kpos = g['n'] + i
+        t.insert(g['kfull'][ar, kpos], kpos, kpos >= 1)
+    assert (t.margin > 1e-5).all()
+    a = oracle.canonical_tree(t.slot, t.sums, t.cnt)
+    b = oracle.canonical_tree(g['slot1'], g['sums1'], g['cnt1'])
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[2], b[2])
+    np.testing.assert_allclose(a[1], b[1], atol=1e-5)
+    assert t.check() < 1e-4
+
+
+def _dyn_sel_args(g):
+    return (int(g['chunk']), int(g['wmax']), int(g['nb_window']), int(g['nb_store']), float(g['nb_rho']),
+            int(g['nb_probe']), int(g['nb_cap_min']))
+
+
+@pytest.mark.parametrize('name', ['dyn_sel_a', 'dyn_sel_b'])
+def test_dyn_select_keys_golden(name):
+    """dyntree.select_keys (dyntree.py:150-243), neighbours on, random leaf budgets: every output equals the
+    reference's on every query (no lane is near a tie)."""
+    g = load(name)
+    sel = oracle.select_keys(g['q'], g['k'], g['lhat'], *_dyn_sel_args(g))
+    assert (sel['margin'] > 1e-6).all()
+    for key in ('tree_pos', 'leaf_ok', 'nb_pos', 'n_tree', 'nb_leaves'):
+        assert np.array_equal(sel[key], g[key]), key
+    assert (g['nb_pos'] >= 0).sum() > 100
+
+
+@pytest.mark.parametrize('name,kw', [('tiny_gpt_dyn', dict(beam_mode='fixed')),
+                                     ('tiny_gpt_dyn_pred', dict(beam_mode='pred', global_pool=True, local=8))])
+def test_tiny_gpt_dyn_golden(name, kw):
+    """A tiny GPT with DynAttention (attn='dyn', attention_dyn.py): the oracle's logits within 1e-6 of the
+    reference's and the same statistics (the model's weights come from the same seeded init)."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    cfg = Config(vocab_size=64, seq_len=64, n_layer=2, n_head=2, n_embd=32, attn='dyn', chunk=16, wmax=4, beam=2,
+                 beam_classes=(2, 3, 4), nb_window=4, nb_store=2, nb_probe=2, nb_cap_min=1, **kw)
+    torch.manual_seed(33)
+    m = GPT(cfg)
+    g = load(name)
+    logits, st = oracle.gpt_forward_dyn(m.state_dict(), cfg.to_dict(), g['idx'])
+    np.testing.assert_allclose(logits, g['logits'], atol=1e-6)
+    for key in ('keys_total', 'keys_tree', 'keys_nb', 'nb_leaves', 'leaves_used'):
+        assert abs(st[key] - float(g['stat_' + key])) < 1e-6, key

@@ -38,6 +38,10 @@ SIGNATURES = {
     'ta_neighbor_pass': [P, I, I, I, I, I, L, L, L, P, L, L, P, L, L, I, I, P, P, P, I, I, I, F, I, I, I, P, P, P,
                          P],
     'ta_lane_search': [P, P, P, I, I, I, I, I, P, P, P, P],
+    'ta_lane_order': [P, L, L, P, I, I, I, I, I, I, P, P, P, P, P],
+    'ta_lane_sums': [P, L, L, P, P, I, I, I, P, P, P, P],
+    'ta_lane_insert': [P, P, P, I, I, I, P, P, P, P],
+    'ta_lane_select': [P, P, P, I, I, I, I, I, I, I, I, I, I, F, I, P, P, P, P, P, P, P, P, P],
     'ta_sparse_attn_bwd': [P, P, P, P, P, P, I, I, I, I, I, I, P, I, I, F, P, P, P, P],
     'ta_gather_dot': [P, P, I, I, I, I, I, I, I, L, L, L, L, L, L, P, I, F, P, P],
     'ta_gather_dot_blocks': [P, P, I, I, I, I, I, L, L, L, L, L, P, I, I, I, F, P, P],

@@ -679,22 +679,16 @@ struct LaneSearchParams {
   float* sct;          // (P, wl) scores (-inf invalid), may be null
 };
 
+// The descent of one query (in sc.qf) over one lane's packed tree; the kept level-D nodes end in sc.kid / sc.ksc,
+// best first. Returns how many are valid.
 template <int DH>
-__global__ void __launch_bounds__(128) lane_search_kernel(LaneSearchParams p) {
-  __shared__ DescentScratch scr[4];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t qi = (int64_t)blockIdx.x * 4 + warp;
-  if (qi >= p.P) return;
-  DescentScratch& sc = scr[warp];
-  const int NN = (2 << p.D) - 1;
-  const float* sums = p.sums + qi * (int64_t)NN * DH;
-  const int32_t* cnt = p.cnt + qi * (int64_t)NN;
-  for (int d = lane; d < DH; d += 32) sc.qf[d] = p.q[qi * DH + d];
+__device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cnt, int D, int wmax,
+                                            DescentScratch& sc, int lane) {
   if (lane == 0) sc.kid[0] = 0;
   __syncwarp();
   int nk = cnt[0] > 0 ? 1 : 0;
   int w = 1;
-  for (int l = 1; l <= p.D; ++l) {
+  for (int l = 1; l <= D; ++l) {
     const int off = (1 << l) - 1;
     // valid children of the kept nodes, compacted (kept node i -> children 2m, 2m+1)
     int n = 0;
@@ -734,9 +728,23 @@ __global__ void __launch_bounds__(128) lane_search_kernel(LaneSearchParams p) {
       }
     }
     __syncwarp();
-    w = min(p.wmax, 2 * w);
+    w = min(wmax, 2 * w);
     nk = Descent<DH>::topk(n, w, sc, lane);
   }
+  __syncwarp();
+  return nk;
+}
+
+template <int DH>
+__global__ void __launch_bounds__(128) lane_search_kernel(LaneSearchParams p) {
+  __shared__ DescentScratch scr[4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qi = (int64_t)blockIdx.x * 4 + warp;
+  if (qi >= p.P) return;
+  DescentScratch& sc = scr[warp];
+  const int NN = (2 << p.D) - 1;
+  for (int d = lane; d < DH; d += 32) sc.qf[d] = p.q[qi * DH + d];
+  const int nk = lane_descend<DH>(p.sums + qi * (int64_t)NN * DH, p.cnt + qi * (int64_t)NN, p.D, p.wmax, sc, lane);
   for (int i = lane; i < p.wl; i += 32) {
     const bool ok = i < nk;
     p.ids[qi * p.wl + i] = ok ? sc.kid[i] : 0;

@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include "decode.cuh"
+#include "dyn.cuh"
 #include "model_ops.cuh"
 #include "prefill.cuh"
 
@@ -304,6 +305,52 @@ struct LaneSearch {
     if (p.P == 0) return TA_OK;
     ta::lane_search_kernel<DH><<<(unsigned)((p.P + 3) / 4), 128, 0, st>>>(p);
     return check_launch("ta_lane_search");
+  }
+};
+
+// One level of the 2-means build: groups of > 256 slots one per CTA, smaller groups one per warp.
+__global__ void lane_init_kernel(const int64_t* n, int first, int P, int C, int32_t* perm, uint8_t* valid) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)P * C) return;
+  const int s = (int)(i % C);
+  perm[i] = s;
+  valid[i] = (s >= first && s < n[i / C]) ? 1 : 0;
+}
+
+template <typename T, int DH>
+struct LaneSplit {
+  static int run(ta::LaneSplitParams p, cudaStream_t st) {
+    const int S = p.C >> p.lvl;
+    const int64_t groups = (int64_t)p.P << p.lvl;
+    if (groups == 0) return TA_OK;
+    if (S > 256) {
+      const size_t smem = ta::SplitSmem<8, DH>::bytes(S);
+      cudaFuncSetAttribute(ta::lane_split_cta_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      ta::lane_split_cta_kernel<DH><<<(unsigned)groups, 256, smem, st>>>(p);
+    } else {
+      const size_t per = (ta::SplitSmem<1, DH>::bytes(S) + 15) & ~(size_t)15;
+      ta::lane_split_warp_kernel<DH><<<(unsigned)((groups + 7) / 8), 256, 8 * per, st>>>(p, groups, S);
+    }
+    return check_launch("ta_lane_order");
+  }
+};
+
+template <typename T, int DH>
+struct LaneInsert {
+  static int run(ta::LaneInsertParams p, cudaStream_t st) {
+    if (p.P == 0) return TA_OK;
+    ta::lane_insert_kernel<DH><<<(unsigned)((p.P + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_lane_insert");
+  }
+};
+
+template <typename T, int DH>
+struct LaneSelect {
+  static int run(ta::LaneSelectParams p, cudaStream_t st) {
+    const int64_t P = (int64_t)p.B * p.H * p.nl;
+    if (P == 0) return TA_OK;
+    ta::lane_select_kernel<DH><<<(unsigned)((P + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_lane_select");
   }
 };
 
@@ -800,6 +847,95 @@ int ta_lane_search(const float* q, const float* sums, const int32_t* cnt, int P,
   if (!aligned16(q) || !aligned16(sums)) return fail(TA_ERR_ARG, "ta_lane_search: q / sums must be 16-byte aligned");
   ta::LaneSearchParams p{q, sums, cnt, P, D, wmax, wl, ids, vld, sct};
   return by_dh<LaneSearch, float>(dh, p, S(stream));
+}
+
+static int log2_exact(int64_t x) {
+  int l = 0;
+  while ((int64_t(1) << l) < x) ++l;
+  return (int64_t(1) << l) == x ? l : -1;
+}
+
+int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first, int P,
+                  int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, int32_t* perm_tmp,
+                  uint8_t* valid_tmp, void* stream) {
+  g_err.clear();
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_lane_order: unsupported head dim %d", dh);
+  const int lc = log2_exact(C);
+  if (P < 0 || lc < 2 || C > 16384) return fail(TA_ERR_ARG, "ta_lane_order: C=%d is not a power of two in [4, 16384]", C);
+  if (levels < 0 || levels > lc - 1) return fail(TA_ERR_ARG, "ta_lane_order: levels=%d outside [0, %d]", levels, lc - 1);
+  if (iters < 0 || first < 0 || key_lane_div < 1) return fail(TA_ERR_ARG, "ta_lane_order: bad iters / first / lane divisor");
+  if (!keys || !n || !perm || !valid || !perm_tmp || !valid_tmp) return fail(TA_ERR_ARG, "ta_lane_order: null pointer");
+  if (P == 0) return TA_OK;
+  cudaStream_t st = S(stream);
+  const int64_t total = (int64_t)P * C;
+  lane_init_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(n, first, P, C, perm, valid);
+  if (int e = check_launch("ta_lane_order")) return e;
+  int32_t* pa = perm; uint8_t* va = valid;
+  int32_t* pb = perm_tmp; uint8_t* vb = valid_tmp;
+  for (int lvl = 0; lvl < levels; ++lvl) {
+    ta::LaneSplitParams p{keys, key_lane_div, key_stride, pa, va, pb, vb, P, C, lvl, iters};
+    if (int e = by_dh<LaneSplit, float>(dh, p, st)) return e;
+    std::swap(pa, pb);
+    std::swap(va, vb);
+  }
+  if (pa != perm) {
+    cudaMemcpyAsync(perm, pa, total * sizeof(int32_t), cudaMemcpyDeviceToDevice, st);
+    cudaMemcpyAsync(valid, va, total, cudaMemcpyDeviceToDevice, st);
+    return check_launch("ta_lane_order");
+  }
+  return TA_OK;
+}
+
+int ta_lane_sums(const float* keys, int64_t key_lane_div, int64_t key_stride, const int32_t* perm,
+                 const uint8_t* valid, int P, int C, int dh, float* sums, int32_t* cnt, int32_t* slot, void* stream) {
+  g_err.clear();
+  const int lc = log2_exact(C);
+  if (dh < 1 || dh > 128 || P < 0 || lc < 1) return fail(TA_ERR_ARG, "ta_lane_sums: bad sizes P=%d C=%d dh=%d", P, C, dh);
+  if (key_lane_div < 1) return fail(TA_ERR_ARG, "ta_lane_sums: bad lane divisor");
+  if (!keys || !perm || !valid || !sums || !cnt || !slot) return fail(TA_ERR_ARG, "ta_lane_sums: null pointer");
+  if (P == 0) return TA_OK;
+  ta::LaneSumsParams p{keys, key_lane_div, key_stride, perm, valid, P, C, lc - 1, dh, sums, cnt, slot};
+  ta::lane_sums_kernel<<<(unsigned)P, 512, 0, S(stream)>>>(p);
+  return check_launch("ta_lane_sums");
+}
+
+int ta_lane_insert(const float* kv, const int64_t* kpos, const uint8_t* active, int P, int C, int dh, float* sums,
+                   int32_t* cnt, int32_t* slot, void* stream) {
+  g_err.clear();
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_lane_insert: unsupported head dim %d", dh);
+  const int lc = log2_exact(C);
+  if (P < 0 || lc < 2) return fail(TA_ERR_ARG, "ta_lane_insert: C=%d is not a power of two >= 4", C);
+  if (!kv || !kpos || !active || !sums || !cnt || !slot) return fail(TA_ERR_ARG, "ta_lane_insert: null pointer");
+  ta::LaneInsertParams p{kv, kpos, active, P, lc - 1, C, sums, cnt, slot};
+  return by_dh<LaneInsert, float>(dh, p, S(stream));
+}
+
+int ta_lane_select(const float* q, const float* k, const int64_t* lhat, int B, int H, int T, int dh, int chunk,
+                   int wmax, int nb_window, int nb_store, int nb_probe, int nb_cap_min, float nb_rho, int neighbors,
+                   float* sums, int32_t* cnt, int32_t* slot, int64_t* tree_pos, uint8_t* leaf_ok, int64_t* nb_pos,
+                   int64_t* n_tree, int64_t* nb_leaves, void* stream) {
+  g_err.clear();
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_lane_select: unsupported head dim %d", dh);
+  const int lt = log2_exact(T);
+  if (B < 0 || H < 0 || lt < 2 || chunk < 1 || T % chunk != 0)
+    return fail(TA_ERR_ARG, "ta_lane_select: T=%d must be a power of two >= 4 and a multiple of chunk=%d", T, chunk);
+  const int D = lt - 1;
+  if (wmax < 1 || wmax > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_lane_select: wmax=%d outside [1, 64]", wmax);
+  const int wl = std::min(wmax, 1 << D);
+  if (nb_window < 1 || nb_store < 1 || nb_window * nb_store > 32 || nb_store > wl)
+    return fail(TA_ERR_ARG, "ta_lane_select: nb_window * nb_store must be <= 32 and nb_store <= %d", wl);
+  if (nb_probe < 0 || nb_cap_min < 0) return fail(TA_ERR_ARG, "ta_lane_select: bad neighbour probe / cap");
+  if (!q || !k || !lhat || !sums || !cnt || !slot || !tree_pos || !leaf_ok || !nb_pos || !n_tree || !nb_leaves)
+    return fail(TA_ERR_ARG, "ta_lane_select: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(sums))
+    return fail(TA_ERR_ARG, "ta_lane_select: q / k / sums must be 16-byte aligned");
+  ta::LaneSelectParams p{};
+  p.q = q; p.k = k; p.lhat = lhat; p.sums = sums; p.cnt = cnt; p.slot = slot;
+  p.B = B; p.H = H; p.T = T; p.Y = chunk; p.nl = T / chunk; p.D = D; p.wmax = wmax; p.wl = wl;
+  p.Wn = nb_window; p.NS = nb_store; p.probe = std::min(nb_probe * nb_store, 32); p.cap_min = nb_cap_min;
+  p.neighbors = neighbors; p.rho = nb_rho;
+  p.tree_pos = tree_pos; p.leaf_ok = leaf_ok; p.nb_pos = nb_pos; p.n_tree = n_tree; p.nb_leaves = nb_leaves;
+  return by_dh<LaneSelect, float>(dh, p, S(stream));
 }
 
 int ta_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,

@@ -209,6 +209,10 @@ class SegAttention(nn.Module):
             self.aux['leaves_used'] = n_used.mean()
         return out
 
+    def _select(self, q, k, lhat):
+        """The non-differentiable key selection of the training form (the segment tree's)."""
+        return select_seg_fast(q, k, lhat, self.cfg)
+
     def _sparse_attend_autograd(self, q, k, v):
         """The training form (fastseg.py:345-405 as the reference runs it): selection without gradients, the
         explicit candidate list [tree positions, neighbour positions, static keys] deduplicated, then the
@@ -224,7 +228,7 @@ class SegAttention(nn.Module):
         if lhat is None:
             lhat = torch.full((b, H, T), cfg.beam, dtype=torch.long, device=dev)
         with torch.no_grad():
-            sel = select_seg_fast(q.detach(), k.detach(), lhat, cfg)
+            sel = self._select(q.detach(), k.detach(), lhat)
             tree_pos, nb_pos, leaf_ok = sel['tree_pos'], sel['nb_pos'], sel['leaf_ok']
             wl = leaf_ok.shape[-1]
             leaf = tree_pos.shape[-1] // max(wl, 1)
