@@ -85,6 +85,9 @@ def parse():
     p.add_argument('--config1', action='store_true',
                    help='configuration 1 instead: the full forward of the 4-layer d=256 fp32 GPT (B=2, T=512, leaf 32, '
                         'top-4, window 64) on the GPU and on the CPU oracle, logits compared; prints one JSON line')
+    p.add_argument('--dyn', action='store_true',
+                   help="the dynamic content tree's select_keys (attn='dyn') at train.py's and a 4096-token "
+                        'configuration; prints one JSON line each')
     p.add_argument('--config3', action='store_true',
                    help='configuration 3 end to end: the 12-layer bf16 GPT forward (prefill) over 4 x 8192 tokens; '
                         'prints one JSON line')
@@ -441,6 +444,67 @@ def union_tile_pairs(ids, vld, n_tree, leaf, Lw, T, qt=128, kt=64):
     return int(occ.sum())
 
 
+def run_dyn(a, dev):
+    """The dynamic content tree's key selection (attn='dyn', dyntree.select_keys) at the reference's training
+    configurations: train.py's defaults (B=8, 6 heads, 512 tokens, dh 64, lanes of 64, wmax 8, neighbours on) and a
+    4096-token window (long_train.py's length) at B=2. q, k ~ N(0, 1) fp32, leaf budgets uniform in [2, wmax].
+    CUDA events around whole select_keys calls (build: ta_lane_order + ta_lane_sums; loop: ta_lane_select) after
+    warm-up; the CPU oracle (numpy) on one (b, h) as the baseline. Prints one JSON line per configuration."""
+    from treeattn_b200 import dyntree
+    from treeattn_b200.config import Config
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    for name, (B, H, T, dh, Y, wmax) in dict(train=(8, 6, 512, 64, 64, 8), long=(2, 6, 4096, 64, 64, 8)).items():
+        cfg = Config(attn='dyn', seq_len=T, chunk=Y, wmax=wmax)
+        g = torch.Generator(device=dev).manual_seed(11)
+        q = torch.randn(B, H, T, dh, device=dev, generator=g)
+        k = torch.randn(B, H, T, dh, device=dev, generator=g)
+        lhat = torch.randint(2, wmax + 1, (B, H, T), device=dev, generator=g)
+        nl = T // Y
+        P = B * H * nl
+        D = T.bit_length() - 2
+        for _ in range(3):
+            dyntree.select_keys(q, k, lhat, cfg)
+        torch.cuda.synchronize()
+        if a.profile_steps:
+            if name != 'long':
+                continue
+            torch.cuda.cudart().cudaProfilerStart()
+            for _ in range(a.profile_steps):
+                dyntree.select_keys(q, k, lhat, cfg)
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+            return
+        reps = 5
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(reps):
+            dyntree.select_keys(q, k, lhat, cfg)
+        e1.record()
+        torch.cuda.synchronize()
+        total_ms = e0.elapsed_time(e1) / reps
+        # the build alone
+        n0 = (torch.arange(nl, device=dev, dtype=torch.int64) * Y).repeat(B * H)
+        e0.record()
+        for _ in range(reps):
+            dyntree._order(k, nl, n0, 1, P, T, dh, cfg.kmeans_iters, D)
+        e1.record()
+        torch.cuda.synchronize()
+        order_ms = e0.elapsed_time(e1) / reps
+        line = dict(dyn_select=True, config='%s: B=%d H=%d T=%d dh=%d lanes of %d, wmax %d, neighbours on' % (
+            name, B, H, T, dh, Y, wmax), lanes=P, select_keys_ms=total_ms, order_ms=order_ms,
+            queries_per_s=B * H * T / (total_ms * 1e-3))
+        if not a.no_cpu_baseline:
+            import oracle
+            qn, kn, ln = q[:1, :1].cpu().numpy(), k[:1, :1].cpu().numpy(), lhat[:1, :1].cpu().numpy()
+            t0 = time.perf_counter()
+            oracle.select_keys(qn, kn, ln, Y, wmax, cfg.nb_window, cfg.nb_store, cfg.nb_rho, cfg.nb_probe,
+                               cfg.nb_cap_min)
+            dt = time.perf_counter() - t0
+            line['cpu_baseline'] = dict(value=T / dt, unit='queries/s', cores=1, kind='port',
+                                        sample='oracle.select_keys on one (b, h) of %d queries' % T)
+        print(json.dumps(line), flush=True)
+
+
 def run_config3(a, dev):
     """Configuration 3 end to end: the whole 12-layer, 768-wide bf16 GPT forward (SegAttention prefill: levels,
     tile select, tensor-core tile attention; cuBLAS projections) over B=4 sequences of 8192 uniform-random tokens,
@@ -633,6 +697,9 @@ def main():
         return
     if a.config3:
         run_config3(a, dev)
+        return
+    if a.dyn:
+        run_dyn(a, dev)
         return
 
     run_engine(a, CFG5 if a.config5 else CFG4, dev, rank, world, local)

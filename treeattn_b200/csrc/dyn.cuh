@@ -8,9 +8,10 @@
 // Kernels:
 //  * lane_split_kernel: one level of the build (dyntree.py:54-73): inside every group of S = C >> lvl slots the
 //    valid keys are ordered by a 2-means projection (dyntree.py:6-31) and dealt to the two halves, ceil(n/2) left.
-//    A "team" (a warp, or the 8 warps of a CTA for large groups) owns one group: one warp per key row with the
-//    lanes over the head dim (coalesced 128-byte row reads, shuffle-reduced dots), per-warp partial centre sums
-//    in registers reduced across the team in shared memory, and a bitonic sort of 64-bit (projection, slot) keys.
+//    A "team" (a warp, or the 8 warps of a CTA for large groups) owns one group: dh/8 lanes per key row, 8 head
+//    dims each (two 16-byte loads), so a warp holds 32 / (dh/8) rows at once, two such steps in flight; per-row
+//    dots reduce over the row's lanes, partial centre sums stay in registers until the end of a pass and are
+//    reduced across the team in shared memory; then a bitonic sort of 64-bit (projection, slot) keys.
 //  * lane_sums_kernel: the slots of the built tree and its node sums / counts bottom-up in adjacent pairs.
 //  * lane_insert_kernel: dyntree.py:83-106, one warp per lane.
 //  * lane_select_kernel: dyntree.py:150-243 select_keys, one warp per lane walking the lane's tokens in order:
@@ -39,9 +40,16 @@ struct LaneSplitParams {
   int P, C, lvl, iters;
 };
 
+// Barrier of a team of NW warps: the warp itself, the whole CTA (bid 0), or named barrier bid of NW warps.
 template <int NW>
-__device__ __forceinline__ void team_sync() {
-  if (NW == 1) __syncwarp(); else __syncthreads();
+__device__ __forceinline__ void team_sync(int bid) {
+  if (NW == 1) {
+    __syncwarp();
+  } else if (bid == 0) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"r"(bid), "r"(NW * 32) : "memory");
+  }
 }
 
 // Shared memory of one team: sort keys (S) | mean, c0, c1, diff (4 DH floats) | per-warp partials (2 NW DH) |
@@ -55,80 +63,114 @@ struct SplitSmem {
 
 template <int NW, int DH>
 struct TwoMeans {
-  static constexpr int NJ = (DH + 31) / 32;  // head dims per lane
+  // Each key row is read by LPR lanes holding 8 consecutive head dims each (two 16-byte loads), so a warp holds
+  // RPW rows at once and U such steps are in flight per iteration; per-row dots reduce over the LPR lanes only.
+  static constexpr int LPR = DH / 8;
+  static constexpr int RPW = 32 / LPR;
+  static constexpr int U = 2;
+  static constexpr int STEP = NW * RPW * U;  // rows per team iteration
   static constexpr int TEAM = NW * 32;
 
-  // Team-sum of per-warp vectors acc[NJ] (lane owns dims lane + 32 j) into out[DH].
-  static __device__ __forceinline__ void reduce_vec(const float (&acc)[NJ], float* red, float* out, int w, int lane,
-                                                    int tid) {
-    if (NW == 1) {
+  static __device__ __forceinline__ float row_sum(float v) {
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        const int d = lane + 32 * j;
-        if (d < DH) out[d] = acc[j];
-      }
-      __syncwarp();
-      return;
-    }
+    for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+  }
+
+  // Sum a per-lane 8-dim vector over the RPW row slots of the warp (lanes with the same dim chunk).
+  static __device__ __forceinline__ void slots_sum(float (&a)[8]) {
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const int d = lane + 32 * j;
-      if (d < DH) red[w * DH + d] = acc[j];
-    }
-    __syncthreads();
-    for (int d = tid; d < DH; d += TEAM) {
-      float s = 0.f;
-      for (int i = 0; i < NW; ++i) s += red[i * DH + d];
-      out[d] = s;
-    }
-    __syncthreads();
+    for (int o = LPR; o < 32; o <<= 1)
+#pragma unroll
+      for (int d = 0; d < 8; ++d) a[d] += __shfl_xor_sync(0xffffffffu, a[d], o);
   }
 
-  static __device__ __forceinline__ int reduce_int(int v, int* redi, int w, int lane) {
-    if (NW == 1) return v;
-    if (lane == 0) redi[w] = v;
-    __syncthreads();
-    int s = 0;
-    for (int i = 0; i < NW; ++i) s += redi[i];
-    __syncthreads();
-    return s;
-  }
-
-  static __device__ __forceinline__ unsigned long long reduce_max(unsigned long long v, unsigned long long* redk,
-                                                                  int w, int lane) {
-    if (NW == 1) return v;
-    if (lane == 0) redk[w] = v;
-    __syncthreads();
-    unsigned long long m = 0;
-    for (int i = 0; i < NW; ++i) m = redk[i] > m ? redk[i] : m;
-    __syncthreads();
-    return m;
-  }
-
-  static __device__ __forceinline__ float warp_sum(float v) {
+  static __device__ __forceinline__ int warp_isum(int v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
   }
 
-  static __device__ __forceinline__ void load_row(const float* row, float (&x)[NJ], int lane) {
+  static __device__ __forceinline__ unsigned long long warp_kmax(unsigned long long v) {
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const int d = lane + 32 * j;
-      x[j] = d < DH ? __ldg(row + d) : 0.f;
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long u = __shfl_xor_sync(0xffffffffu, v, o);
+      v = u > v ? u : v;
+    }
+    return v;
+  }
+
+  // Team sum of the warps' 8-dim chunks (already summed over the warp's row slots) into out[DH].
+  static __device__ __forceinline__ void team_vec(const float (&a)[8], float* red, float* out, int w, int lane,
+                                                  int tid, int bid) {
+    const int sub = lane % LPR;
+    if (lane < LPR) {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) red[w * DH + sub * 8 + d] = a[d];
+    }
+    team_sync<NW>(bid);
+    for (int d = tid; d < DH; d += TEAM) {
+      float s = 0.f;
+      for (int i = 0; i < NW; ++i) s += red[i * DH + d];
+      out[d] = s;
+    }
+    team_sync<NW>(bid);
+  }
+
+  static __device__ __forceinline__ int team_int(int v, int* redi, int w, int lane, int bid) {
+    if (NW == 1) return v;
+    if (lane == 0) redi[w] = v;
+    team_sync<NW>(bid);
+    int s = 0;
+    for (int i = 0; i < NW; ++i) s += redi[i];
+    team_sync<NW>(bid);
+    return s;
+  }
+
+  static __device__ __forceinline__ unsigned long long team_kmax(unsigned long long v, unsigned long long* redk,
+                                                                 int w, int lane, int bid) {
+    if (NW == 1) return v;
+    if (lane == 0) redk[w] = v;
+    team_sync<NW>(bid);
+    unsigned long long m = 0;
+    for (int i = 0; i < NW; ++i) m = redk[i] > m ? redk[i] : m;
+    team_sync<NW>(bid);
+    return m;
+  }
+
+  // Load this lane's 8 dims of rows base + u*RPW + slot (u < U); rows past S or empty load as absent.
+  static __device__ __forceinline__ void load_rows(const float* keys, const int32_t* perm, const uint8_t* valid,
+                                                   int S, int base, int slot, int sub, float (&x)[U][8],
+                                                   bool (&ok)[U], int (&s_of)[U]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = base + u * RPW + slot;
+      s_of[u] = s;
+      ok[u] = s < S && valid[s];
+      if (ok[u]) {
+        const float4* r = reinterpret_cast<const float4*>(keys + (int64_t)perm[s] * DH + sub * 8);
+        const float4 a = r[0], b = r[1];
+        x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
+        x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
+      } else {
+#pragma unroll
+        for (int d = 0; d < 8; ++d) x[u][d] = 0.f;
+      }
     }
   }
 
-  // Order the S slots of one group and write the split (dyntree.py:6-31 and 58-73). tid = thread in team.
-  static __device__ void run(const LaneSplitParams& p, int64_t group, unsigned char* smem, int tid) {
+  static __device__ __forceinline__ void load_vec(const float* v, int sub, float (&r)[8]) {
+#pragma unroll
+    for (int d = 0; d < 8; ++d) r[d] = v[sub * 8 + d];
+  }
+
+  // Order the S slots of one group and write the split (dyntree.py:6-31 and 58-73). Slot s holds key row
+  // keys + perm[s] * DH (global or shared memory) when valid[s]; the split is written to po / vo (other arrays
+  // than perm / valid). tid = thread in team, bid = the team's barrier (see team_sync).
+  static __device__ void run(const float* keys, const int32_t* perm, const uint8_t* valid, int S, int iters,
+                             int32_t* po, uint8_t* vo, unsigned char* smem, int tid, int bid) {
     const int w = tid >> 5, lane = tid & 31;
-    const int G = 1 << p.lvl;
-    const int S = p.C >> p.lvl;
-    const int64_t lanep = group / G;
-    const int64_t base = lanep * p.C + (group % G) * (int64_t)S;
-    const float* keys = p.keys + (lanep / p.key_lane_div) * p.key_stride;
-    const int32_t* perm = p.perm_in + base;
-    const uint8_t* valid = p.valid_in + base;
+    const int slot = lane / LPR, sub = lane % LPR;
 
     unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem);
     float* mean = reinterpret_cast<float*>(smem + (size_t)S * 8);
@@ -136,120 +178,159 @@ struct TwoMeans {
     float* c1 = c0 + DH;
     float* diff = c1 + DH;
     float* red = diff + DH;                                   // 2 NW DH
-    int* redi = reinterpret_cast<int*>(red + 2 * NW * DH);    // NW
-    unsigned long long* redk = reinterpret_cast<unsigned long long*>(redi + 2 * NW);  // NW (8-byte aligned)
+    int* redi = reinterpret_cast<int*>(red + 2 * NW * DH);    // 2 NW
+    unsigned long long* redk = reinterpret_cast<unsigned long long*>(redi + 2 * NW);  // NW
 
-    // (1) count and mean of the valid keys
-    float acc[NJ];
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) acc[j] = 0.f;
+    float x[U][8];
+    bool ok[U];
+    int s_of[U];
+
+    // (0) count the valid keys. With at most two there is nothing to cluster: the split is one key per side (in
+    // either orientation, both keys being equally far from their mean) and the 2-means passes are skipped.
     int nv = 0;
-    for (int s = w; s < S; s += NW) {
-      if (!valid[s]) continue;
-      float x[NJ];
-      load_row(keys + (int64_t)perm[s] * DH, x, lane);
+    for (int r = tid; r < S; r += TEAM) nv += valid[r] ? 1 : 0;
+    const int ng = team_int(warp_isum(nv), redi, w, lane, bid);
+    if (ng <= 2) {
+      for (int r = tid; r < S; r += TEAM)
+        skey[r] = ((unsigned long long)(valid[r] ? 0u : 0xffffffffu) << 32) | (uint32_t)r;
+    } else {
+    // (1) mean of the valid keys
+    float acc[8];
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) acc[j] += x[j];
-      ++nv;
+    for (int d = 0; d < 8; ++d) acc[d] = 0.f;
+    for (int b = w * RPW * U; b < S; b += STEP) {
+      load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int d = 0; d < 8; ++d) acc[d] += x[u][d];
     }
-    const int ng = reduce_int(nv, redi, w, lane);
-    reduce_vec(acc, red, mean, w, lane, tid);
-    for (int d = tid; d < DH; d += TEAM) mean[d] = mean[d] / (float)(ng > 1 ? ng : 1);
-    team_sync<NW>();
+    slots_sum(acc);
+    team_vec(acc, red, mean, w, lane, tid, bid);
+    for (int d = tid; d < DH; d += TEAM) mean[d] = mean[d] / (float)ng;
+    team_sync<NW>(bid);
 
-    if (ng >= 1) {
+    {
       // (2) a = the valid key farthest from the mean, (3) b = the valid key farthest from a (first index on ties)
       for (int pass = 0; pass < 2; ++pass) {
-        const float* ref = pass == 0 ? mean : c0;
+        float ref[8];
+        load_vec(pass == 0 ? mean : c0, sub, ref);
         unsigned long long best = 0;
-        for (int s = w; s < S; s += NW) {
-          if (!valid[s]) continue;
-          float x[NJ];
-          load_row(keys + (int64_t)perm[s] * DH, x, lane);
-          float v = 0.f;
+        for (int b = w * RPW * U; b < S; b += STEP) {
+          load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
+          float v[U];
 #pragma unroll
-          for (int j = 0; j < NJ; ++j) {
-            const int d = lane + 32 * j;
-            const float e = d < DH ? x[j] - ref[d] : 0.f;
-            v = fmaf(e, e, v);
+          for (int u = 0; u < U; ++u) {
+            v[u] = 0.f;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) {
+              const float e = x[u][d] - ref[d];
+              v[u] = fmaf(e, e, v[u]);
+            }
           }
-          v = warp_sum(v);
-          const unsigned long long key = ((unsigned long long)asc_bits(v) << 32) | (uint32_t)(0xffffffffu - s);
-          best = key > best ? key : best;
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const float t = row_sum(v[u]);
+            if (ok[u]) {
+              const unsigned long long key =
+                  ((unsigned long long)asc_bits(t) << 32) | (uint32_t)(0xffffffffu - s_of[u]);
+              best = key > best ? key : best;
+            }
+          }
         }
-        best = reduce_max(best, redk, w, lane);
+        best = team_kmax(warp_kmax(best), redk, w, lane, bid);
         const int sel = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
         float* dst = pass == 0 ? c0 : c1;
         for (int d = tid; d < DH; d += TEAM) dst[d] = keys[(int64_t)perm[sel] * DH + d];
-        team_sync<NW>();
+        team_sync<NW>(bid);
       }
       // (4) 2-means rounds: nearer centre by |x|^2 - 2 x.c + |c|^2 (first centre on ties), centres to the means
-      for (int it = 0; it < p.iters; ++it) {
+      for (int it = 0; it < iters; ++it) {
+        float r0[8], r1[8];
+        load_vec(c0, sub, r0);
+        load_vec(c1, sub, r1);
         float q0 = 0.f, q1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          const int d = lane + 32 * j;
-          if (d < DH) { q0 = fmaf(c0[d], c0[d], q0); q1 = fmaf(c1[d], c1[d], q1); }
-        }
-        const float csq0 = warp_sum(q0), csq1 = warp_sum(q1);
-        float a0[NJ], a1[NJ];
+        for (int d = 0; d < 8; ++d) { q0 = fmaf(r0[d], r0[d], q0); q1 = fmaf(r1[d], r1[d], q1); }
+        const float csq0 = row_sum(q0), csq1 = row_sum(q1);
+        float a0[8], a1[8];
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) { a0[j] = 0.f; a1[j] = 0.f; }
-        int n1 = 0, n0 = 0;
-        for (int s = w; s < S; s += NW) {
-          if (!valid[s]) continue;
-          float x[NJ];
-          load_row(keys + (int64_t)perm[s] * DH, x, lane);
-          float xx = 0.f, d0 = 0.f, d1 = 0.f;
+        for (int d = 0; d < 8; ++d) { a0[d] = 0.f; a1[d] = 0.f; }
+        int n0 = 0, n1 = 0;
+        for (int b = w * RPW * U; b < S; b += STEP) {
+          load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
+          float xx[U], d0[U], d1[U];
 #pragma unroll
-          for (int j = 0; j < NJ; ++j) {
-            const int d = lane + 32 * j;
-            if (d < DH) { xx = fmaf(x[j], x[j], xx); d0 = fmaf(x[j], c0[d], d0); d1 = fmaf(x[j], c1[d], d1); }
+          for (int u = 0; u < U; ++u) {
+            xx[u] = 0.f; d0[u] = 0.f; d1[u] = 0.f;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) {
+              xx[u] = fmaf(x[u][d], x[u][d], xx[u]);
+              d0[u] = fmaf(x[u][d], r0[d], d0[u]);
+              d1[u] = fmaf(x[u][d], r1[d], d1[u]);
+            }
           }
-          xx = warp_sum(xx); d0 = warp_sum(d0); d1 = warp_sum(d1);
-          const float dist0 = (xx - 2.f * d0) + csq0, dist1 = (xx - 2.f * d1) + csq1;
-          if (dist1 < dist0) {
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) a1[j] += x[j];
-            ++n1;
-          } else {
+          for (int u = 0; u < U; ++u) {
+            const float sx = row_sum(xx[u]), s0 = row_sum(d0[u]), s1 = row_sum(d1[u]);
+            const float dist0 = (sx - 2.f * s0) + csq0, dist1 = (sx - 2.f * s1) + csq1;
+            const bool one = dist1 < dist0;
+            if (ok[u]) {
+              if (one) {
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) a0[j] += x[j];
-            ++n0;
+                for (int d = 0; d < 8; ++d) a1[d] += x[u][d];
+                n1 += sub == 0 ? 1 : 0;
+              } else {
+#pragma unroll
+                for (int d = 0; d < 8; ++d) a0[d] += x[u][d];
+                n0 += sub == 0 ? 1 : 0;
+              }
+            }
           }
         }
-        const int m0 = reduce_int(n0, redi, w, lane);
-        const int m1 = reduce_int(n1, redi, w, lane);
+        slots_sum(a0);
+        slots_sum(a1);
+        const int m0 = team_int(warp_isum(n0), redi, w, lane, bid);
+        const int m1 = team_int(warp_isum(n1), redi + NW, w, lane, bid);
         // the team sums land in diff (centre 0) and mean (centre 1; the mean is no longer needed)
-        reduce_vec(a0, red, diff, w, lane, tid);
-        reduce_vec(a1, red + NW * DH, mean, w, lane, tid);
+        team_vec(a0, red, diff, w, lane, tid, bid);
+        team_vec(a1, red + NW * DH, mean, w, lane, tid, bid);
         for (int d = tid; d < DH; d += TEAM) {
           if (m0 > 0) c0[d] = diff[d] / (float)m0;
           if (m1 > 0) c1[d] = mean[d] / (float)m1;
         }
-        team_sync<NW>();
+        team_sync<NW>(bid);
       }
       for (int d = tid; d < DH; d += TEAM) diff[d] = c0[d] - c1[d];
-      team_sync<NW>();
+      team_sync<NW>(bid);
     }
     // (5) projections (valid keys) -> ascending (projection, slot) keys; empty slots last
-    for (int s = w; s < S; s += NW) {
-      uint32_t hi = 0xffffffffu;
-      if (valid[s] && ng >= 1) {
-        float x[NJ];
-        load_row(keys + (int64_t)perm[s] * DH, x, lane);
-        float v = 0.f;
+    {
+      float df[8];
+      load_vec(diff, sub, df);
+      for (int b = w * RPW * U; b < S; b += STEP) {
+        load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
+        float v[U];
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          const int d = lane + 32 * j;
-          if (d < DH) v = fmaf(x[j], diff[d], v);
+        for (int u = 0; u < U; ++u) {
+          v[u] = 0.f;
+#pragma unroll
+          for (int d = 0; d < 8; ++d) v[u] = fmaf(x[u][d], df[d], v[u]);
         }
-        hi = asc_bits(warp_sum(v));
-        if (hi == 0xffffffffu) hi = 0xfffffffeu;  // a NaN projection still sorts before the empty slots
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const float t = row_sum(v[u]);
+          uint32_t hi = 0xffffffffu;
+          if (ok[u]) {
+            hi = asc_bits(t);
+            if (hi == 0xffffffffu) hi = 0xfffffffeu;  // a NaN projection still sorts before the empty slots
+          }
+          if (sub == 0 && s_of[u] < S) skey[s_of[u]] = ((unsigned long long)hi << 32) | (uint32_t)s_of[u];
+        }
       }
-      if (lane == 0) skey[s] = ((unsigned long long)hi << 32) | (uint32_t)s;
     }
-    team_sync<NW>();
+    }
+    team_sync<NW>(bid);
     // bitonic sort, ascending
     for (int kk = 2; kk <= S; kk <<= 1) {
       for (int j = kk >> 1; j > 0; j >>= 1) {
@@ -261,15 +342,13 @@ struct TwoMeans {
             if ((a > b) == up) { skey[i] = b; skey[ixj] = a; }
           }
         }
-        team_sync<NW>();
+        team_sync<NW>(bid);
       }
     }
     // (6) deal: sorted rank r < nl -> left half position r, nl <= r < ng -> right half position half + r - nl;
     // the free positions are empty and point at the last sorted slot (dyntree.py:66-71)
     const int nl = (ng + 1) / 2, nr = ng - nl, half = S >> 1;
     const int32_t last = perm[(int)(skey[S - 1] & 0xffffffffu)];
-    int32_t* po = p.perm_out + base;
-    uint8_t* vo = p.valid_out + base;
     for (int r = tid; r < S; r += TEAM) {
       if (r < ng) {
         const int s = (int)(skey[r] & 0xffffffffu);
@@ -286,22 +365,113 @@ struct TwoMeans {
   }
 };
 
-// Groups of > 256 slots: one group per CTA of 8 warps.
+// The group of one (lane, level) in global memory: slot rows of the lane's key array, in / out permutations.
+struct GroupRef {
+  const float* keys;
+  const int32_t* perm;
+  const uint8_t* valid;
+  int32_t* po;
+  uint8_t* vo;
+  int S;
+};
+
+__device__ __forceinline__ GroupRef group_ref(const LaneSplitParams& p, int64_t group) {
+  const int G = 1 << p.lvl;
+  const int S = p.C >> p.lvl;
+  const int64_t lanep = group / G;
+  const int64_t base = lanep * p.C + (group % G) * (int64_t)S;
+  return GroupRef{p.keys + (lanep / p.key_lane_div) * p.key_stride, p.perm_in + base, p.valid_in + base,
+                  p.perm_out + base, p.valid_out + base, S};
+}
+
+// Groups of more than SUBTREE_SLOTS slots: one group per CTA of 8 warps, rows read from global memory (L2).
 template <int DH>
 __global__ void __launch_bounds__(256) lane_split_cta_kernel(LaneSplitParams p) {
   extern __shared__ __align__(16) unsigned char split_smem[];
-  TwoMeans<8, DH>::run(p, blockIdx.x, split_smem, threadIdx.x);
+  const GroupRef g = group_ref(p, blockIdx.x);
+  TwoMeans<8, DH>::run(g.keys, g.perm, g.valid, g.S, p.iters, g.po, g.vo, split_smem, threadIdx.x, 0);
 }
 
-// Groups of <= 256 slots: one group per warp, 8 per CTA.
+// The remaining levels of a subtree of at most SUBTREE_SLOTS slots, in one CTA: its key rows are staged in shared
+// memory once, then every level's groups are split there (a level of n groups: min(n, 8) teams of 8 / min(n, 8)
+// warps, each team on its own named barrier), and the final slot order is written back.
+#ifndef TA_SUBTREE_SLOTS
+#define TA_SUBTREE_SLOTS 128
+#endif
+constexpr int SUBTREE_SLOTS = TA_SUBTREE_SLOTS;
+
 template <int DH>
-__global__ void __launch_bounds__(256) lane_split_warp_kernel(LaneSplitParams p, int64_t n_groups, int S) {
+struct Subtree {
+  static __host__ __device__ constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+  // per-team scratch at group size s with NW warps per team, for 8 / NW teams
+  static __host__ __device__ size_t scratch(int S0) {
+    size_t m = 0;
+    for (int s = S0; s >= 4; s >>= 1) {
+      const int groups = S0 / s, teams = groups < 8 ? groups : 8, nw = 8 / teams;
+      const size_t per = align16((size_t)s * 8 + 4 * DH * 4 + (size_t)2 * nw * DH * 4 + nw * 32);
+      m = per * teams > m ? per * teams : m;
+    }
+    return m;
+  }
+  static __host__ __device__ size_t bytes(int S0) {
+    return align16((size_t)S0 * DH * 4) + 2 * align16((size_t)S0 * 4) + 2 * align16((size_t)S0) + scratch(S0);
+  }
+};
+
+template <int NW, int DH>
+__device__ __forceinline__ void subtree_level(const float* stage, const int32_t* lp, const uint8_t* lv, int32_t* lpo,
+                                              uint8_t* lvo, int S0, int s, int iters, unsigned char* scratch) {
+  constexpr int TEAMS = 8 / NW;
+  const int team = threadIdx.x / (NW * 32), tid = threadIdx.x % (NW * 32);
+  const size_t per = Subtree<DH>::align16((size_t)s * 8 + 4 * DH * 4 + (size_t)2 * NW * DH * 4 + NW * 32);
+  const int bid = NW == 8 ? 0 : 1 + team;
+  for (int g = team; g < S0 / s; g += TEAMS) {
+    const int o = g * s;
+    TwoMeans<NW, DH>::run(stage, lp + o, lv + o, s, iters, lpo + o, lvo + o, scratch + per * team, tid, bid);
+    team_sync<NW>(bid);
+  }
+}
+
+template <int DH>
+__global__ void __launch_bounds__(256) lane_subtree_kernel(LaneSplitParams p, int levels) {
   extern __shared__ __align__(16) unsigned char split_smem[];
-  const int w = threadIdx.x >> 5;
-  const int64_t g = (int64_t)blockIdx.x * 8 + w;
-  if (g >= n_groups) return;
-  const size_t per = (SplitSmem<1, DH>::bytes(S) + 15) & ~(size_t)15;
-  TwoMeans<1, DH>::run(p, g, split_smem + per * w, threadIdx.x & 31);
+  const int S0 = p.C >> p.lvl;
+  const GroupRef g = group_ref(p, blockIdx.x);
+  float* stage = reinterpret_cast<float*>(split_smem);
+  unsigned char* q = split_smem + Subtree<DH>::align16((size_t)S0 * DH * 4);
+  int32_t* lpa = reinterpret_cast<int32_t*>(q);
+  int32_t* lpb = reinterpret_cast<int32_t*>(q + Subtree<DH>::align16((size_t)S0 * 4));
+  uint8_t* lva = q + 2 * Subtree<DH>::align16((size_t)S0 * 4);
+  uint8_t* lvb = lva + Subtree<DH>::align16((size_t)S0);
+  unsigned char* scratch = lvb + Subtree<DH>::align16((size_t)S0);
+  // stage the valid rows (row i of the stage = slot i of the subtree)
+  for (int e = threadIdx.x; e < S0 * (DH / 4); e += blockDim.x) {
+    const int i = e / (DH / 4), c = e - i * (DH / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g.valid[i]) v = *reinterpret_cast<const float4*>(g.keys + (int64_t)g.perm[i] * DH + c * 4);
+    *reinterpret_cast<float4*>(stage + (size_t)i * DH + c * 4) = v;
+  }
+  for (int i = threadIdx.x; i < S0; i += blockDim.x) {
+    lpa[i] = i;
+    lva[i] = g.valid[i];
+  }
+  __syncthreads();
+  int s = S0;
+  for (int l = 0; l < levels; ++l, s >>= 1) {
+    const int groups = S0 / s;
+    if (groups == 1) subtree_level<8, DH>(stage, lpa, lva, lpb, lvb, S0, s, p.iters, scratch);
+    else if (groups == 2) subtree_level<4, DH>(stage, lpa, lva, lpb, lvb, S0, s, p.iters, scratch);
+    else if (groups == 4) subtree_level<2, DH>(stage, lpa, lva, lpb, lvb, S0, s, p.iters, scratch);
+    else subtree_level<1, DH>(stage, lpa, lva, lpb, lvb, S0, s, p.iters, scratch);
+    __syncthreads();
+    int32_t* tp = lpa; lpa = lpb; lpb = tp;
+    uint8_t* tv = lva; lva = lvb; lvb = tv;
+  }
+  // slot i of the subtree now holds stage row lpa[i] = subtree slot lpa[i] of the input order
+  for (int i = threadIdx.x; i < S0; i += blockDim.x) {
+    g.po[i] = g.perm[lpa[i]];
+    g.vo[i] = lva[i];
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ build: sums

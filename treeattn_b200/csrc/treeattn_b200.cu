@@ -317,19 +317,22 @@ __global__ void lane_init_kernel(const int64_t* n, int first, int P, int C, int3
   valid[i] = (s >= first && s < n[i / C]) ? 1 : 0;
 }
 
+// One level of the 2-means build for groups of more than ta::SUBTREE_SLOTS slots (one group per CTA, rows from
+// L2), or, from the first level whose groups are that small, all the remaining levels at once (ta::Subtree).
 template <typename T, int DH>
 struct LaneSplit {
-  static int run(ta::LaneSplitParams p, cudaStream_t st) {
+  static int run(ta::LaneSplitParams p, int levels_left, cudaStream_t st) {
     const int S = p.C >> p.lvl;
     const int64_t groups = (int64_t)p.P << p.lvl;
     if (groups == 0) return TA_OK;
-    if (S > 256) {
+    if (S > ta::SUBTREE_SLOTS) {
       const size_t smem = ta::SplitSmem<8, DH>::bytes(S);
       cudaFuncSetAttribute(ta::lane_split_cta_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       ta::lane_split_cta_kernel<DH><<<(unsigned)groups, 256, smem, st>>>(p);
     } else {
-      const size_t per = (ta::SplitSmem<1, DH>::bytes(S) + 15) & ~(size_t)15;
-      ta::lane_split_warp_kernel<DH><<<(unsigned)((groups + 7) / 8), 256, 8 * per, st>>>(p, groups, S);
+      const size_t smem = ta::Subtree<DH>::bytes(S);
+      cudaFuncSetAttribute(ta::lane_subtree_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      ta::lane_subtree_kernel<DH><<<(unsigned)groups, 256, smem, st>>>(p, levels_left);
     }
     return check_launch("ta_lane_order");
   }
@@ -865,6 +868,8 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
   if (levels < 0 || levels > lc - 1) return fail(TA_ERR_ARG, "ta_lane_order: levels=%d outside [0, %d]", levels, lc - 1);
   if (iters < 0 || first < 0 || key_lane_div < 1) return fail(TA_ERR_ARG, "ta_lane_order: bad iters / first / lane divisor");
   if (!keys || !n || !perm || !valid || !perm_tmp || !valid_tmp) return fail(TA_ERR_ARG, "ta_lane_order: null pointer");
+  if (!aligned16(keys) || (key_stride * 4) % 16 != 0)
+    return fail(TA_ERR_ARG, "ta_lane_order: keys and the key array stride must be 16-byte aligned");
   if (P == 0) return TA_OK;
   cudaStream_t st = S(stream);
   const int64_t total = (int64_t)P * C;
@@ -874,9 +879,10 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
   int32_t* pb = perm_tmp; uint8_t* vb = valid_tmp;
   for (int lvl = 0; lvl < levels; ++lvl) {
     ta::LaneSplitParams p{keys, key_lane_div, key_stride, pa, va, pb, vb, P, C, lvl, iters};
-    if (int e = by_dh<LaneSplit, float>(dh, p, st)) return e;
+    if (int e = by_dh<LaneSplit, float>(dh, p, levels - lvl, st)) return e;
     std::swap(pa, pb);
     std::swap(va, vb);
+    if ((C >> lvl) <= ta::SUBTREE_SLOTS) break;  // the subtree kernel did every remaining level
   }
   if (pa != perm) {
     cudaMemcpyAsync(perm, pa, total * sizeof(int32_t), cudaMemcpyDeviceToDevice, st);
