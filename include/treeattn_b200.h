@@ -181,6 +181,32 @@ int ta_lane_select(const float* q, const float* k, const int64_t* lhat, int B, i
                    float* sums, int32_t* cnt, int32_t* slot, int64_t* tree_pos, uint8_t* leaf_ok, int64_t* nb_pos,
                    int64_t* n_tree, int64_t* nb_leaves, void* stream);
 
+/* Replaces the node sums of forest.build_forest (forest.py:68-75) and forest.soft_gate (forest.py:36-44): per block
+ * p of B keys (rows p B .. p B + B - 1 of k, dtype code `dtype`, dh wide; with zero_sink the key at position 0 of
+ * every (b, h) - the first row of blocks p % nb == 0 - counts as 0), ranks ordered by perm (P, B) int32 (from
+ * ta_lane_order with every slot valid), level l = 0..depth (depth = log2(B / 2)) holds 2^l nodes summing B / 2^l
+ * keys each; out[l] (P 2^l, dh) in k's dtype. gate != 0 applies the soft mean-log gate (gate_q, gate_temp). */
+int ta_forest_levels(const void* k, int dtype, int P, int B, int dh, int depth, int nb, int zero_sink,
+                     const int32_t* perm, int gate, float gate_q, float gate_temp, void* const* out, void* stream);
+
+/* Replaces forest.soft_gate (forest.py:36-44) on explicit nodes: sm (N, dh) node sums and grp (N, S, dh) their
+ * member keys, dtype code `dtype`; out (N, dh) = sm * g * (dh / max(sum g, 1)), g = sigmoid((ml - thr) / gate_temp)
+ * with ml the members' mean of log(|x| + 1e-6) per dimension and thr its gate_q quantile over the dimensions. */
+int ta_soft_gate(const void* sm, const void* grp, int dtype, int64_t N, int S, int dh, float gate_q,
+                 float gate_temp, void* out, void* stream);
+
+/* Replaces the forest descent and key-position step of TreeAttention.sparse_attend (attention.py:73-90, 112-118):
+ * per query t of (b, h) (q (Bn, H, T, dh) strided, dtype code `dtype`), the roots of the blocks before t's block
+ * scored q . sum (rounded to the dtype), the best min(wmax, width) kept per level with the first bq (per query, or
+ * bq_const when bq is NULL) valid, children of the valid kept nodes down to level depth. levels[l]: the level sums
+ * of ta_forest_levels; perm: its rank order. Outputs (Bn, H, T, wl) leaf ids / validity and (Bn, H, T, 2 wl) key
+ * positions (slot j wl + i: key j of leaf i) with tok = valid and not the sink / t-1 / t-2 of an earlier block.
+ * lsel / lselv (arrays of depth + 1 pointers, or NULL): every level's kept ids / validity (Bn, H, T, w_l). */
+int ta_forest_select(const void* q, int dtype, int Bn, int H, int T, int dh, int64_t q_sb, int64_t q_sh,
+                     int64_t q_st, const void* const* levels, const int32_t* perm, int B, int depth,
+                     const int64_t* bq, int bq_const, int wmax, int64_t* leaf, uint8_t* leafv, int64_t* tkey,
+                     uint8_t* tok, int32_t* const* lsel, uint8_t* const* lselv, void* stream);
+
 /* Replaces the backward of fastseg.sparse_attn (fastseg.py:80-110 _attn_bwd, 158-170 _SparseAttnFn.backward):
  * from the forward's o and lse (natural log) and the output gradient dout, dq (q's dtype) and the fp32 key / value
  * gradients dk, dv, which are ACCUMULATED (vector atomics, as the reference does; zero them first). All tensors

@@ -4,7 +4,7 @@ The reference (Dex8123/treeattn, pure Python/PyTorch) is importable only in the 
 mounted read-only; it is made importable as the package `treeattn` through a symlink in a temp directory.
 The GPU box never runs this script: the tests read the committed .npz files.
 
-    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate|dyn]
+    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate|dyn|forest]
 
 Leaf blocks of 2^L0 tokens (the benchmark configs use 32, 64 and 128) are produced with the reference's own
 functions on the level-shifted tree ("adapter"): seg.level_sums, then seg.tree_pass with
@@ -168,6 +168,43 @@ def dyn_goldens(R):
     return out
 
 
+def forest_goldens(R):
+    """The block forest (attn='block'): forest.build_forest (forest.py:47-75) with and without the soft gate,
+    TreeAttention.sparse_attend (attention.py:47-143) on random q, k, v at two sizes, and tiny GPTs with
+    TreeAttention (fixed budget; learned budget + global pool + gate): logits and statistics."""
+    forest, Config = R['forest'], R['config'].Config
+    from treeattn.attention import TreeAttention
+    out = {}
+    g = torch.Generator().manual_seed(41)
+    k = torch.randn(2, 2, 128, 16, generator=g)
+    cfg = Config(kmeans_iters=3, gate=False)
+    perm, sums = forest.build_forest(k, 32, 4, cfg)
+    cfg_g = Config(kmeans_iters=3, gate=True, gate_q=0.25, gate_temp=0.3)
+    _, sums_g = forest.build_forest(k, 32, 4, cfg_g)
+    out['forest_build'] = dict(k=np_(k), perm=np_(perm), **{'S%d' % l: np_(sums[l]) for l in range(5)},
+                               **{'G%d' % l: np_(sums_g[l]) for l in range(5)})
+    for name, (B, H, T, dh, blk, wmax, beam) in dict(tree_attn_a=(2, 2, 128, 16, 32, 4, 2),
+                                                     tree_attn_b=(1, 3, 512, 32, 64, 8, 4)).items():
+        cfg = Config(n_embd=H * dh, n_head=H, seq_len=T, tree_block=blk, wmax=wmax, beam=beam)
+        m = TreeAttention(cfg).eval()
+        q, kk, v = [torch.randn(B, H, T, dh, generator=g) for _ in range(3)]
+        with torch.no_grad():
+            o = m.sparse_attend(q, kk, v)
+        out[name] = dict(q=np_(q), k=np_(kk), v=np_(v), o=np_(o), tree_block=blk, wmax=wmax, beam=beam,
+                         **{'stat_' + kk_: float(vv) for kk_, vv in m.aux.items()})
+    for name, kw in dict(tiny_gpt_block=dict(), tiny_gpt_block_pred=dict(beam_mode='pred', global_pool=True,
+                                                                         gate=True)).items():
+        cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, tree_block=32, wmax=4, beam=2,
+                     beam_classes=(2, 3, 4), **kw)
+        torch.manual_seed(43)
+        m = R['model'].GPT(cfg).eval()
+        idx = torch.randint(0, 64, (2, 128), generator=torch.Generator().manual_seed(44))
+        with torch.no_grad():
+            logits, _, stats = m(idx)
+        out[name] = dict(idx=np_(idx), logits=np_(logits), **{'stat_' + kk: vv for kk, vv in stats.items()})
+    return out
+
+
 def main(ref_path, only=None):
     R = import_reference(ref_path)
     single = dict(lanetree=lanetree_golden, tiny_gpt_nb=tiny_gpt_nb_golden)
@@ -176,8 +213,8 @@ def main(ref_path, only=None):
         np.savez_compressed(os.path.join(HERE, only + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
         print('wrote', only)
         return
-    if only in ('gate', 'dyn'):
-        for name, d in (gate_goldens if only == 'gate' else dyn_goldens)(R).items():
+    if only in ('gate', 'dyn', 'forest'):
+        for name, d in dict(gate=gate_goldens, dyn=dyn_goldens, forest=forest_goldens)[only](R).items():
             np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
             print('wrote', name)
         return
@@ -316,6 +353,7 @@ def main(ref_path, only=None):
     out['tiny_gpt_nb'] = tiny_gpt_nb_golden(R)
     out.update(gate_goldens(R))
     out.update(dyn_goldens(R))
+    out.update(forest_goldens(R))
 
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})

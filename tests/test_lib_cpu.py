@@ -119,8 +119,21 @@ def test_config_fields_match_reference_defaults():
     assert Config(**c.to_dict()) == c
 
 
-def test_unsupported_paths_raise():
+def test_block_and_dyn_paths_need_cuda():
+    """The block forest and the dynamic tree have no CPU path: CPU tensors are refused before any kernel call."""
+    import torch
     from treeattn_b200.config import Config
+    from treeattn_b200.dyntree import LaneTree, select_keys
+    from treeattn_b200.forest import build_forest
     from treeattn_b200.model import GPT
-    with pytest.raises(NotImplementedError):
-        GPT(Config(attn='block'))
+    m = GPT(Config(attn='block', vocab_size=64, seq_len=128, n_layer=1, n_head=2, n_embd=32, tree_block=32)).eval()
+    with pytest.raises(ValueError, match='CUDA'):
+        with torch.no_grad():
+            m(torch.zeros(1, 128, dtype=torch.long))
+    k = torch.zeros(1, 2, 64, 16)
+    with pytest.raises(ValueError, match='CUDA'):
+        build_forest(k, 32, 4, Config())
+    with pytest.raises(ValueError, match='CUDA'):
+        select_keys(k, k, torch.ones(1, 2, 64, dtype=torch.long), Config(attn='dyn', seq_len=64, chunk=16))
+    with pytest.raises(ValueError, match='CUDA'):
+        LaneTree(torch.zeros(2, 64, 16), torch.tensor([0, 5]))

@@ -263,3 +263,47 @@ def test_tiny_gpt_dyn_golden(name, kw):
     np.testing.assert_allclose(logits, g['logits'], atol=1e-6)
     for key in ('keys_total', 'keys_tree', 'keys_nb', 'nb_leaves', 'leaves_used'):
         assert abs(st[key] - float(g['stat_' + key])) < 1e-6, key
+
+
+# ------------------------------------------------------------------------------------------------ block forest
+def test_forest_build_golden():
+    """forest.build_forest (forest.py:47-75): the oracle's rank order equals the reference's on every block (no
+    decision near a tie), level sums within fp32 rounding, with and without the soft gate (forest.py:36-44)."""
+    g = load('forest_build')
+    perm, sums, margin = oracle.build_forest(g['k'], 32, 4, 3)
+    assert (margin > 1e-6).all()
+    assert np.array_equal(perm, g['perm'])
+    for l in range(5):
+        np.testing.assert_allclose(sums[l], g['S%d' % l], atol=2e-5)
+    _, sums_g, _ = oracle.build_forest(g['k'], 32, 4, 3, gate=(0.25, 0.3))
+    for l in range(5):
+        np.testing.assert_allclose(sums_g[l], g['G%d' % l], atol=2e-5)
+
+
+@pytest.mark.parametrize('name', ['tree_attn_a', 'tree_attn_b'])
+def test_tree_attention_golden(name):
+    """TreeAttention.sparse_attend (attention.py:47-143) on random q, k, v: outputs within 1e-5, same statistics."""
+    g = load(name)
+    out, st, margin = oracle.tree_attention(g['q'], g['k'], g['v'], int(g['tree_block']), int(g['wmax']),
+                                            int(g['beam']))
+    np.testing.assert_allclose(out, g['o'], atol=1e-5)
+    for key in ('keys_tree', 'keys_total'):
+        assert abs(st[key] - float(g['stat_' + key])) < 1e-4, key
+
+
+@pytest.mark.parametrize('name,kw', [('tiny_gpt_block', dict()),
+                                     ('tiny_gpt_block_pred', dict(beam_mode='pred', global_pool=True, gate=True))])
+def test_tiny_gpt_block_golden(name, kw):
+    """A tiny GPT with TreeAttention (attn='block'): the oracle's logits within 1e-5 of the reference's and the same
+    statistics (the weights come from the same seeded init)."""
+    from treeattn_b200.config import Config
+    from treeattn_b200.model import GPT
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, tree_block=32, wmax=4, beam=2,
+                 beam_classes=(2, 3, 4), **kw)
+    torch.manual_seed(43)
+    m = GPT(cfg)
+    g = load(name)
+    logits, st = oracle.gpt_forward_block(m.state_dict(), cfg.to_dict(), g['idx'])
+    np.testing.assert_allclose(logits, g['logits'], atol=1e-5)
+    for key in ('keys_tree', 'keys_total'):
+        assert abs(st[key] - float(g['stat_' + key])) < 1e-4, key

@@ -42,6 +42,9 @@ SIGNATURES = {
     'ta_lane_sums': [P, L, L, P, P, I, I, I, P, P, P, P],
     'ta_lane_insert': [P, P, P, I, I, I, P, P, P, P],
     'ta_lane_select': [P, P, P, I, I, I, I, I, I, I, I, I, I, F, I, P, P, P, P, P, P, P, P, P],
+    'ta_forest_levels': [P, I, I, I, I, I, I, I, P, I, F, F, P, P],
+    'ta_soft_gate': [P, P, I, L, I, I, F, F, P, P],
+    'ta_forest_select': [P, I, I, I, I, I, L, L, L, P, P, I, I, P, I, I, P, P, P, P, P, P, P],
     'ta_sparse_attn_bwd': [P, P, P, P, P, P, I, I, I, I, I, I, P, I, I, F, P, P, P, P],
     'ta_gather_dot': [P, P, I, I, I, I, I, I, I, L, L, L, L, L, L, P, I, F, P, P],
     'ta_gather_dot_blocks': [P, P, I, I, I, I, I, L, L, L, L, L, P, I, I, I, F, P, P],

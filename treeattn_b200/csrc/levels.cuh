@@ -144,21 +144,15 @@ __global__ void build_upper_levels_kernel(float* __restrict__ nodes, int64_t n_s
 // in fp32, the values at floor / ceil of the rank by a stable rank count, torch's fused two-sided lerp); kept =
 // #{ml >= thr}; out = (raw * [ml >= thr]) * (dh / max(kept, 1)). NPL = ceil(dh / 32) values per lane; with
 // dh = 16 the upper half-warp holds no element (ranked last, never counted).
+// torch.quantile(ml, q) over the DH values of a warp (NPL per lane, element (i, lane) = index i * 32 + lane, absent
+// elements +inf): ranks q (DH - 1) in fp32, the values at floor / ceil of the rank by a stable rank count, torch's
+// fused two-sided lerp.
 template <int DH>
-__device__ __forceinline__ void gate_node_warp(const float* raw, const float* lg, float* out, float inv_size,
-                                               float gate_q, int lane) {
+__device__ __forceinline__ float warp_quantile(const float (&ml)[(DH + 31) / 32], float gate_q, int lane) {
   constexpr int NPL = (DH + 31) / 32;
-  float r[NPL], ml[NPL];
-#pragma unroll
-  for (int i = 0; i < NPL; ++i) {
-    const bool on = i * 32 + lane < DH;
-    r[i] = on ? raw[i * 32 + lane] : 0.f;
-    ml[i] = on ? lg[i * 32 + lane] * inv_size : INFINITY;  // size is a power of two: exact
-  }
   const float rank = __fmul_rn(gate_q, (float)(DH - 1));
   const int lo = (int)floorf(rank), hi = (int)ceilf(rank);
   const float w = __fsub_rn(rank, (float)lo);
-  // stable ranks: element e = (i, lane) has index i * 32 + lane
   int rk[NPL];
 #pragma unroll
   for (int i = 0; i < NPL; ++i) rk[i] = 0;
@@ -182,7 +176,21 @@ __device__ __forceinline__ void gate_node_warp(const float* raw, const float* lg
     if (bhi) vhi = __shfl_sync(0xffffffffu, ml[i], __ffs(bhi) - 1);
   }
   const float d = __fsub_rn(vhi, vlo);
-  const float thr = w < 0.5f ? fmaf(w, d, vlo) : fmaf(-__fsub_rn(1.f, w), d, vhi);
+  return w < 0.5f ? fmaf(w, d, vlo) : fmaf(-__fsub_rn(1.f, w), d, vhi);
+}
+
+template <int DH>
+__device__ __forceinline__ void gate_node_warp(const float* raw, const float* lg, float* out, float inv_size,
+                                               float gate_q, int lane) {
+  constexpr int NPL = (DH + 31) / 32;
+  float r[NPL], ml[NPL];
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) {
+    const bool on = i * 32 + lane < DH;
+    r[i] = on ? raw[i * 32 + lane] : 0.f;
+    ml[i] = on ? lg[i * 32 + lane] * inv_size : INFINITY;  // size is a power of two: exact
+  }
+  const float thr = warp_quantile<DH>(ml, gate_q, lane);
   int kept = 0;
 #pragma unroll
   for (int i = 0; i < NPL; ++i) kept += __popc(__ballot_sync(0xffffffffu, ml[i] >= thr && i * 32 + lane < DH));

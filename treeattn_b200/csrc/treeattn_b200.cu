@@ -12,6 +12,7 @@
 
 #include "decode.cuh"
 #include "dyn.cuh"
+#include "forest.cuh"
 #include "model_ops.cuh"
 #include "prefill.cuh"
 
@@ -335,6 +336,38 @@ struct LaneSplit {
       ta::lane_subtree_kernel<DH><<<(unsigned)groups, 256, smem, st>>>(p, levels_left);
     }
     return check_launch("ta_lane_order");
+  }
+};
+
+template <typename T, int DH>
+struct ForestLevels {
+  static int run(ta::ForestLevelsParams p, cudaStream_t st) {
+    if (p.P == 0) return TA_OK;
+    const size_t smem = (size_t)3 * p.B / 2 * DH * sizeof(float);
+    if (smem > 200 * 1024) return fail(TA_ERR_ARG, "ta_forest_levels: blocks of %d keys need %zu B of shared memory", p.B, smem);
+    cudaFuncSetAttribute(ta::forest_levels_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ta::forest_levels_kernel<T, DH><<<(unsigned)p.P, 256, smem, st>>>(p);
+    return check_launch("ta_forest_levels");
+  }
+};
+
+template <typename T, int DH>
+struct SoftGate {
+  static int run(const void* sm, const void* grp, void* out, int64_t N, int S, float q, float temp, cudaStream_t st) {
+    if (N == 0) return TA_OK;
+    ta::soft_gate_kernel<T, DH><<<(unsigned)((N + 3) / 4), 128, 0, st>>>(
+        reinterpret_cast<const T*>(sm), reinterpret_cast<const T*>(grp), reinterpret_cast<T*>(out), N, S, q, temp);
+    return check_launch("ta_soft_gate");
+  }
+};
+
+template <typename T, int DH>
+struct ForestSelect {
+  static int run(ta::ForestSelectParams p, cudaStream_t st) {
+    const int64_t nq = (int64_t)p.Bn * p.H * p.T;
+    if (nq == 0) return TA_OK;
+    ta::forest_select_kernel<T, DH><<<(unsigned)((nq + 3) / 4), 128, 0, st>>>(p);
+    return check_launch("ta_forest_select");
   }
 };
 
@@ -942,6 +975,63 @@ int ta_lane_select(const float* q, const float* k, const int64_t* lhat, int B, i
   p.neighbors = neighbors; p.rho = nb_rho;
   p.tree_pos = tree_pos; p.leaf_ok = leaf_ok; p.nb_pos = nb_pos; p.n_tree = n_tree; p.nb_leaves = nb_leaves;
   return by_dh<LaneSelect, float>(dh, p, S(stream));
+}
+
+int ta_forest_levels(const void* k, int dtype, int P, int B, int dh, int depth, int nb, int zero_sink,
+                     const int32_t* perm, int gate, float gate_q, float gate_temp, void* const* out, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_forest_levels: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_forest_levels: unsupported head dim %d", dh);
+  if (P < 0 || nb < 1 || B < 4 || (B & (B - 1)) || (2 << depth) != B || depth + 1 > ta::FOREST_MAX_LEVELS)
+    return fail(TA_ERR_ARG, "ta_forest_levels: B=%d must be a power of two in [4, 512] with depth=log2(B/2)", B);
+  if (!k || !perm || !out) return fail(TA_ERR_ARG, "ta_forest_levels: null pointer");
+  ta::ForestLevelsParams p{};
+  p.k = k; p.perm = perm; p.P = P; p.B = B; p.depth = depth; p.nb = nb; p.zero_sink = zero_sink; p.gate = gate;
+  p.gate_q = gate_q; p.gate_temp = gate_temp;
+  for (int l = 0; l <= depth; ++l) {
+    if (!out[l]) return fail(TA_ERR_ARG, "ta_forest_levels: null output level %d", l);
+    p.out[l] = out[l];
+  }
+  return by_type_dh<ForestLevels>(dtype, dh, p, S(stream));
+}
+
+int ta_soft_gate(const void* sm, const void* grp, int dtype, int64_t N, int members, int dh, float gate_q,
+                 float gate_temp, void* out, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_soft_gate: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_soft_gate: unsupported head dim %d", dh);
+  if (N < 0 || members < 1) return fail(TA_ERR_ARG, "ta_soft_gate: bad sizes N=%lld S=%d", (long long)N, members);
+  if (!sm || !grp || !out) return fail(TA_ERR_ARG, "ta_soft_gate: null pointer");
+  return by_type_dh<SoftGate>(dtype, dh, sm, grp, out, N, members, gate_q, gate_temp, S(stream));
+}
+
+int ta_forest_select(const void* q, int dtype, int Bn, int H, int T, int dh, int64_t q_sb, int64_t q_sh,
+                     int64_t q_st, const void* const* levels, const int32_t* perm, int B, int depth,
+                     const int64_t* bq, int bq_const, int wmax, int64_t* leaf, uint8_t* leafv, int64_t* tkey,
+                     uint8_t* tok, int32_t* const* lsel, uint8_t* const* lselv, void* stream) {
+  g_err.clear();
+  if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_forest_select: bad dtype %d", dtype);
+  if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_forest_select: unsupported head dim %d", dh);
+  if (Bn < 0 || H < 0 || B < 4 || (B & (B - 1)) || (2 << depth) != B || depth + 1 > ta::FOREST_MAX_LEVELS ||
+      T < B || T % B != 0)
+    return fail(TA_ERR_ARG, "ta_forest_select: T=%d must be a multiple of the block B=%d (a power of two >= 4)", T, B);
+  if (wmax < 1 || wmax > ta::WMAX_LIMIT) return fail(TA_ERR_ARG, "ta_forest_select: wmax=%d outside [1, 64]", wmax);
+  if (!q || !levels || !perm || !leaf || !leafv || !tkey || !tok) return fail(TA_ERR_ARG, "ta_forest_select: null pointer");
+  ta::ForestSelectParams p{};
+  p.q = q; p.q_sb = q_sb; p.q_sh = q_sh; p.q_st = q_st;
+  for (int l = 0; l <= depth; ++l) {
+    if (!levels[l]) return fail(TA_ERR_ARG, "ta_forest_select: null level %d", l);
+    p.lv[l] = levels[l];
+    p.lsel[l] = lsel ? lsel[l] : nullptr;
+    p.lselv[l] = lselv ? lselv[l] : nullptr;
+  }
+  p.perm = perm; p.bq = bq; p.bq_const = bq_const;
+  p.Bn = Bn; p.H = H; p.T = T; p.B = B; p.nb = T / B; p.depth = depth; p.wmax = wmax;
+  int w = std::min(wmax, T / B);
+  for (int l = 1; l <= depth; ++l) w = std::min(wmax, 2 * w);
+  p.wl = w;
+  p.leaf = leaf; p.leafv = leafv; p.tkey = tkey; p.tok = tok;
+  return by_type_dh<ForestSelect>(dtype, dh, p, S(stream));
 }
 
 int ta_sparse_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
