@@ -4,7 +4,7 @@ The reference (Dex8123/treeattn, pure Python/PyTorch) is importable only in the 
 mounted read-only; it is made importable as the package `treeattn` through a symlink in a temp directory.
 The GPU box never runs this script: the tests read the committed .npz files.
 
-    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate|dyn|forest]
+    python tests/golden/make_golden.py /path/to/reference [--only=lanetree|tiny_gpt_nb|gate|dyn|forest|interop]
 
 Leaf blocks of 2^L0 tokens (the benchmark configs use 32, 64 and 128) are produced with the reference's own
 functions on the level-shifted tree ("adapter"): seg.level_sums, then seg.tree_pass with
@@ -205,6 +205,36 @@ def forest_goldens(R):
     return out
 
 
+def interop_goldens(R):
+    """Checkpoint interop (engine.py:123-146, train.py:144): a tiny seg GPT with the learned budget head saved the way
+    the reference's training scripts save it (ckpt_tiny_seg.pt), its forward logits and the reference Decoder's
+    token-by-token logits; the same weights renamed to a nanoGPT state dict (ckpt_tiny_nanogpt.pt, torch.compile's
+    '_orig_mod.' prefix) and the reference's dense-mode Decoder logits over it."""
+    Config, engine = R['config'].Config, R['engine']
+    cfg = Config(vocab_size=64, seq_len=128, n_layer=2, n_head=2, n_embd=32, attn='seg', wmax=4, beam=3,
+                 beam_mode='pred', global_pool=True, beam_classes=(2, 3, 4), neighbors=True)
+    torch.manual_seed(51)
+    m = R['model'].GPT(cfg).eval()
+    sd = {kk: vv.clone() for kk, vv in m.state_dict().items()}
+    torch.save({'model': sd, 'cfg': cfg.to_dict()}, os.path.join(HERE, 'ckpt_tiny_seg.pt'))
+    idx = torch.randint(0, 64, (1, 128), generator=torch.Generator().manual_seed(52))
+    with torch.no_grad():
+        logits, _, _ = m(idx)
+        dec = engine.Decoder(engine.weights_from_ours(sd, cfg), 2, 2, 32, 128, 'seg', cfg, 'cpu')
+        seg_steps = np.stack([np_(dec.step(int(idx[0, t]), t)[0]) for t in range(128)])
+        names = dict(wte='transformer.wte.weight', wpe='transformer.wpe.weight', ln_f='transformer.ln_f.weight')
+        nano = {'_orig_mod.' + names[kk]: sd[kk + '.weight'] for kk in ('wte', 'wpe', 'ln_f')}
+        for i in range(2):
+            p, o = 'blocks.%d.' % i, '_orig_mod.transformer.h.%d.' % i
+            nano.update({o + 'ln_1.weight': sd[p + 'ln1.weight'], o + 'attn.c_attn.weight': sd[p + 'attn.c_attn.weight'],
+                         o + 'attn.c_proj.weight': sd[p + 'attn.c_proj.weight'], o + 'ln_2.weight': sd[p + 'ln2.weight'],
+                         o + 'mlp.c_fc.weight': sd[p + 'mlp.c_fc.weight'], o + 'mlp.c_proj.weight': sd[p + 'mlp.c_proj.weight']})
+        torch.save(nano, os.path.join(HERE, 'ckpt_tiny_nanogpt.pt'))
+        dd = engine.Decoder(engine.weights_from_nanogpt(nano, 2), 2, 2, 32, 128, 'dense', None, 'cpu')
+        dense_steps = np.stack([np_(dd.step(int(idx[0, t]), t)[0]) for t in range(128)])
+    return dict(interop=dict(idx=np_(idx), logits=np_(logits), seg_steps=seg_steps, dense_steps=dense_steps))
+
+
 def main(ref_path, only=None):
     R = import_reference(ref_path)
     single = dict(lanetree=lanetree_golden, tiny_gpt_nb=tiny_gpt_nb_golden)
@@ -213,8 +243,9 @@ def main(ref_path, only=None):
         np.savez_compressed(os.path.join(HERE, only + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
         print('wrote', only)
         return
-    if only in ('gate', 'dyn', 'forest'):
-        for name, d in dict(gate=gate_goldens, dyn=dyn_goldens, forest=forest_goldens)[only](R).items():
+    if only in ('gate', 'dyn', 'forest', 'interop'):
+        for name, d in dict(gate=gate_goldens, dyn=dyn_goldens, forest=forest_goldens,
+                            interop=interop_goldens)[only](R).items():
             np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})
             print('wrote', name)
         return
@@ -354,6 +385,7 @@ def main(ref_path, only=None):
     out.update(gate_goldens(R))
     out.update(dyn_goldens(R))
     out.update(forest_goldens(R))
+    out.update(interop_goldens(R))
 
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, name + '.npz'), **{kk: np.asarray(vv) for kk, vv in d.items()})

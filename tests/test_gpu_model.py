@@ -471,3 +471,46 @@ def test_gpt_gate_golden():
         assert abs(float(keys) - float(g['dec_keys'][t])) < 1e-4, t
     assert worst < 1e-4, worst
     _no_device_error()
+
+
+# ------------------------------------------------------------------------------------------------ checkpoint interop
+GOLDEN_DIR = __import__('os').path.join(__import__('os').path.dirname(__import__('os').path.abspath(__file__)),
+                                        'golden')
+
+
+def test_checkpoint_forward_and_decoder_golden():
+    """A checkpoint saved the way the reference's training scripts save it (train.py:144): the loaded GPT's logits and
+    the Decoder's token-by-token logits (learned budget, neighbours) within 1e-4 of the reference's."""
+    import os
+    from treeattn_b200.engine import Decoder
+    from treeattn_b200.model import load_checkpoint
+    g = load('interop')
+    path = os.path.join(GOLDEN_DIR, 'ckpt_tiny_seg.pt')
+    m, cfg = load_checkpoint(path, DEV)
+    with torch.no_grad():
+        logits, _, _ = m(torch.as_tensor(g['idx']).to(DEV))
+    assert (logits.cpu() - torch.as_tensor(g['logits'])).abs().max().item() < 1e-4
+    dec = Decoder.from_checkpoint(path, 128, DEV)
+    got = torch.stack([dec.step(int(g['idx'][0, t]), t)[0].float().cpu() for t in range(128)])
+    assert (got - torch.as_tensor(g['seg_steps'])).abs().max().item() < 1e-4
+    _no_device_error()
+
+
+def test_nanogpt_dense_decoder_golden():
+    """engine.weights_from_nanogpt (engine.py:137-146, torch.compile's '_orig_mod.' prefix) and the dense-mode
+    Decoder (engine.py:74-81 DenseState): token-by-token logits within 1e-4 of the reference's; a prefill of the
+    first 100 tokens continues to the same logits."""
+    import os
+    from treeattn_b200.engine import Decoder, weights_from_nanogpt
+    g = load('interop')
+    sd = torch.load(os.path.join(GOLDEN_DIR, 'ckpt_tiny_nanogpt.pt'), map_location='cpu', weights_only=True)
+    W = weights_from_nanogpt(sd, 2)
+    dec = Decoder(W, 2, 2, 32, 128, 'dense', None, DEV)
+    got = torch.stack([dec.step(int(g['idx'][0, t]), t)[0].float().cpu() for t in range(128)])
+    assert (got - torch.as_tensor(g['dense_steps'])).abs().max().item() < 1e-4
+    dec2 = Decoder(W, 2, 2, 32, 128, 'dense', None, DEV)
+    last = dec2.prefill(torch.as_tensor(g['idx'][:, :100]).to(DEV))
+    assert (last[0].float().cpu() - torch.as_tensor(g['dense_steps'][99])).abs().max().item() < 1e-4
+    nxt = dec2.step(int(g['idx'][0, 100]), 100)[0].float().cpu()
+    assert (nxt - torch.as_tensor(g['dense_steps'][100])).abs().max().item() < 1e-4
+    _no_device_error()

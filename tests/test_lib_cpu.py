@@ -137,3 +137,17 @@ def test_block_and_dyn_paths_need_cuda():
         select_keys(k, k, torch.ones(1, 2, 64, dtype=torch.long), Config(attn='dyn', seq_len=64, chunk=16))
     with pytest.raises(ValueError, match='CUDA'):
         LaneTree(torch.zeros(2, 64, 16), torch.tensor([0, 5]))
+
+
+def test_checkpoint_loads_unchanged():
+    """A checkpoint written by the reference's training script format loads into this package's GPT unchanged."""
+    import torch
+    from treeattn_b200.model import load_checkpoint
+    path = os.path.join(ROOT, 'tests', 'golden', 'ckpt_tiny_seg.pt')
+    m, cfg = load_checkpoint(path, 'cpu')
+    ck = torch.load(path, map_location='cpu', weights_only=True)
+    sd = m.state_dict()
+    assert sorted(sd) == sorted(ck['model'])
+    for name, t in ck['model'].items():
+        assert torch.equal(sd[name], t), name
+    assert cfg.beam_mode == 'pred' and tuple(cfg.beam_classes) == (2, 3, 4)

@@ -200,8 +200,33 @@ def weights_from_nanogpt(sd, n_layer):
     return W
 
 
+class DenseCache:
+    """engine.py:74-81 DenseState, batched: the key/value cache of one layer for the dense baseline decoder
+    ('dense' mode, nanoGPT weights); a step writes k, v at every sequence's position and attends over its prefix
+    (torch's scaled-dot-product attention over the whole cache, later positions masked)."""
+
+    def __init__(self, B, H, cap, dh, dev, dtype):
+        self.K = torch.zeros(B, H, cap, dh, device=dev, dtype=dtype)
+        self.V = torch.zeros(B, H, cap, dh, device=dev, dtype=dtype)
+        self.ar = torch.arange(cap, device=dev)
+        self.ksum = torch.zeros(1, device=dev)
+
+    def attend(self, qkv, pos, out, nkeys):
+        B, H, cap, dh = self.K.shape
+        C = H * dh
+        q, k, v = [qkv[:, j * C:(j + 1) * C].view(B, H, 1, dh) for j in range(3)]
+        idx = pos.long().view(B, 1, 1, 1).expand(B, H, 1, dh)
+        self.K.scatter_(2, idx, k)
+        self.V.scatter_(2, idx, v)
+        mask = (self.ar.view(1, 1, 1, cap) <= pos.view(B, 1, 1, 1))
+        o = F.scaled_dot_product_attention(q, self.K, self.V, attn_mask=mask)
+        out.view(B, H, 1, dh).copy_(o)
+        nkeys.copy_((pos + 1).view(B, 1).expand(B, H))
+
+
 class Decoder:
-    """Token-by-token decoding for a batch of sequences (reference engine.py:149-177, mode 'seg').
+    """Token-by-token decoding for a batch of sequences (reference engine.py:149-177): mode 'seg' (the segment-tree
+    attention) or 'dense' (ordinary attention over the whole prefix, the nanoGPT baseline; weights_from_nanogpt).
 
     Decoder(W, n_layer, n_head, n_embd, Tcap, 'seg', cfg, dev) keeps the reference's arguments; `batch`, `dtype`
     (weights / cache precision, default: the weights' dtype), `cap` (allocated positions) and `graphs` are
@@ -209,9 +234,9 @@ class Decoder:
 
     def __init__(self, W, n_layer, n_head, n_embd, Tcap, mode='seg', cfg=None, dev='cuda', batch=1, dtype=None,
                  cap=None, graphs=True, splits=0):
-        if mode != 'seg':
-            raise NotImplementedError("Decoder mode '%s' is not implemented in treeattn_b200 (only 'seg')" % mode)
-        if cfg is None:
+        if mode not in ('seg', 'dense'):
+            raise NotImplementedError("Decoder mode '%s' is not implemented in treeattn_b200 ('seg', 'dense')" % mode)
+        if mode == 'seg' and cfg is None:
             raise ValueError("mode 'seg' needs cfg")
         self.dev = torch.device(dev)
         self.dtype = dtype or W['wte'].dtype
@@ -222,27 +247,40 @@ class Decoder:
                                    c_fc=cast(L['c_fc']), c_mlp=cast(L['c_mlp'])) for L in W['layers'][:n_layer]])
         # general selection (learned budget, neighbour borrowing): per layer the separate kernels of
         # _general_step instead of the single fused decode kernel
-        self.general = cfg.neighbors or cfg.beam_mode == 'pred' or cfg.gate
-        if cfg.beam_mode == 'pred':
+        seg = mode == 'seg'
+        self.general = seg and (cfg.neighbors or cfg.beam_mode == 'pred' or cfg.gate)
+        if seg and cfg.beam_mode == 'pred':
             for Ld, L in zip(self.W['layers'], W['layers'][:n_layer]):
                 Ld['pw'] = {k_: (t.to(self.dev) if torch.is_tensor(t) else t) for k_, t in L['pw'].items()}
         self.nl, self.H, self.C, self.Tcap = n_layer, n_head, n_embd, Tcap
         self.dh, self.mode, self.cfg = n_embd // n_head, mode, cfg
         self.batch = batch
         self.cap = int(cap or Tcap)
-        self.wmax = cfg.wmax
-        self.n_tree = n_tree_fixed(cfg.beam, cfg.wmax)
-        self.Lw = max(cfg.local, 3)
+        self.wmax = cfg.wmax if seg else 0
+        self.n_tree = n_tree_fixed(cfg.beam, cfg.wmax) if seg else 0
+        self.Lw = max(cfg.local, 3) if seg else 0
         self.scale = 1.0 / math.sqrt(self.dh)
         self.use_graphs = graphs
-        self.splits = splits or _ops.default_splits(batch, n_head, self.dh, self.dtype)
+        self.splits = (splits or _ops.default_splits(batch, n_head, self.dh, self.dtype)) if seg else 0
         self.reset()
+
+    @classmethod
+    def from_checkpoint(cls, path, Tcap, dev='cuda', **kw):
+        """A Decoder (mode 'seg') over a checkpoint written by the reference's training scripts
+        ({'model': state_dict, 'cfg': Config.to_dict()}, train.py:144), through weights_from_ours (engine.py:123-134)."""
+        from .config import Config
+        ck = torch.load(path, map_location='cpu', weights_only=True)
+        cfg = Config(**ck['cfg'])
+        return cls(weights_from_ours(ck['model'], cfg), cfg.n_layer, cfg.n_head, cfg.n_embd, Tcap, 'seg', cfg, dev, **kw)
 
     # -------------------------------------------------------------- state
     def reset(self):
         B, C, dev = self.batch, self.C, self.dev
-        self.states = [SegState(self.cfg, self.Tcap, self.H, self.dh, dev, B, self.dtype, self.cap)
-                       for _ in range(self.nl)]
+        if self.mode == 'seg':
+            self.states = [SegState(self.cfg, self.Tcap, self.H, self.dh, dev, B, self.dtype, self.cap)
+                           for _ in range(self.nl)]
+        else:
+            self.states = [DenseCache(B, self.H, self.cap, self.dh, dev, self.dtype) for _ in range(self.nl)]
         self._tok = torch.zeros(B, device=dev, dtype=torch.int64)
         self._pos = torch.zeros(B, device=dev, dtype=torch.int32)
         dt = self.dtype
@@ -269,7 +307,9 @@ class Decoder:
         for i, Li in enumerate(L):
             st = self.states[i]
             torch.mm(self._h, Li['c_attn'].t(), out=self._qkv)
-            if self.general:
+            if self.mode == 'dense':
+                st.attend(self._qkv, self._pos, self._att, self._nkeys[i])
+            elif self.general:
                 B, C, H, dh = self.batch, self.C, self.H, self.dh
                 q, k, v = [self._qkv[:, j * C:(j + 1) * C].view(B, H, 1, dh) for j in range(3)]
                 _, nk = _general_step(st, Li.get('pw'), q, k, v, self._pos, out=self._att.view(B, H, 1, dh))
@@ -431,6 +471,11 @@ class Decoder:
                 Kc, Vc = st.K[b0:b1, :, :T0], st.V[b0:b1, :, :T0]
                 Kc.copy_(k)
                 Vc.copy_(v)
+                if self.mode == 'dense':  # the nanoGPT baseline: causal dense attention over the prompt
+                    o = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).contiguous()
+                    x = x + F.linear(o.view(nb, T0, C), L['c_proj']).float()
+                    x = x + F.linear(F.gelu(F.linear(_ln(x, L['ln2']).to(dt), L['c_fc'])), L['c_mlp']).float()
+                    continue
                 lv = Levels(st.levels.nodes[b0:b1], st.cap, st.L0, st.Lm)
                 _ops.build_levels(Kc, st.cap, st.L0, st.Lm, zero_sink=True, out=lv)
                 if self.cfg.gate:  # the descent scores the gated nodes (levels >= gate_min_level)

@@ -103,3 +103,18 @@ class GPT(nn.Module):
         loss = lm + self.cfg.route_weight * route / n + self.cfg.pred_weight * pred / n
         stats.update(lm=lm.detach(), route=_f(route) / n, pred=_f(pred) / n)
         return logits, loss, stats
+
+
+def load_checkpoint(path, device='cuda', dtype=None):
+    """A checkpoint as the reference's training scripts write it (train.py:144, long_train.py:
+    {'model': state_dict, 'cfg': Config.to_dict()}) -> (GPT on `device`, in `dtype` when given, eval mode; Config).
+    The state dict loads unchanged: parameter names and shapes are the reference's."""
+    from .config import Config
+    ck = torch.load(path, map_location='cpu', weights_only=True)
+    cfg = Config(**ck['cfg'])
+    model = GPT(cfg)
+    model.load_state_dict(ck['model'])
+    model = model.to(device)
+    if dtype is not None:
+        model = model.to(dtype)
+    return model.eval(), cfg
