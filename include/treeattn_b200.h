@@ -156,6 +156,12 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
                   int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, int32_t* perm_tmp,
                   uint8_t* valid_tmp, void* stream);
 
+/* ta_lane_order without caller scratch: the ping-pong slot order lives in a static device buffer of the library
+ * (2^21 slots, P * C at most), found with cudaGetSymbolAddress, so the call allocates nothing. The buffer is shared:
+ * calls must not overlap in time (one stream, or ordered by the caller). Same arguments and results otherwise. */
+int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first,
+                          int P, int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, void* stream);
+
 /* Completes a dyntree.LaneTree build (dyntree.py:74-80): from the ordered slots of ta_lane_order, the group slots
  * slot (P, C/2, 2) int32 (key position, -1 = empty) and the node sums (P, C - 1, dh) fp32 / counts (P, C - 1) int32
  * packed level by level (level l at rows 2^l - 1 .. 2^(l+1) - 2), formed bottom-up in adjacent pairs. */

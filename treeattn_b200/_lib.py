@@ -39,6 +39,7 @@ SIGNATURES = {
                          P],
     'ta_lane_search': [P, P, P, I, I, I, I, I, P, P, P, P],
     'ta_lane_order': [P, L, L, P, I, I, I, I, I, I, P, P, P, P, P],
+    'ta_lane_order_noalloc': [P, L, L, P, I, I, I, I, I, I, P, P, P],
     'ta_lane_sums': [P, L, L, P, P, I, I, I, P, P, P, P],
     'ta_lane_insert': [P, P, P, I, I, I, P, P, P, P],
     'ta_lane_select': [P, P, P, I, I, I, I, I, I, I, I, I, I, F, I, P, P, P, P, P, P, P, P, P],

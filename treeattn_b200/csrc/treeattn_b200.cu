@@ -606,6 +606,12 @@ int rows_dispatch(int dtype, int kind, const void* a0, const void* a1, const int
 }  // namespace
 
 // ================================================================================================== C ABI
+// Static scratch of ta_lane_order_noalloc: the ping-pong slot order of the 2-means build, in the module's own
+// device memory (no allocation per call). One build at a time may use it.
+constexpr int64_t kLaneScratchSlots = int64_t(1) << 21;
+__device__ int32_t g_lane_perm_scratch[kLaneScratchSlots];
+__device__ uint8_t g_lane_valid_scratch[kLaneScratchSlots];
+
 extern "C" {
 
 int ta_version(void) { return 100; }
@@ -923,6 +929,21 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
     return check_launch("ta_lane_order");
   }
   return TA_OK;
+}
+
+int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first,
+                          int P, int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, void* stream) {
+  g_err.clear();
+  if (P < 0 || C < 0 || (int64_t)P * C > kLaneScratchSlots)
+    return fail(TA_ERR_ARG, "ta_lane_order_noalloc: P*C=%lld slots exceed the static scratch of %lld",
+                (long long)P * C, (long long)kLaneScratchSlots);
+  void* pt = nullptr;
+  void* vt = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&pt, g_lane_perm_scratch);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&vt, g_lane_valid_scratch);
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: scratch address: %s", cudaGetErrorString(e));
+  return ta_lane_order(keys, key_lane_div, key_stride, n, first, P, C, dh, iters, levels, perm, valid,
+                       static_cast<int32_t*>(pt), static_cast<uint8_t*>(vt), stream);
 }
 
 int ta_lane_sums(const float* keys, int64_t key_lane_div, int64_t key_stride, const int32_t* perm,
