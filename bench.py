@@ -85,6 +85,9 @@ def parse():
     p.add_argument('--config1', action='store_true',
                    help='configuration 1 instead: the full forward of the 4-layer d=256 fp32 GPT (B=2, T=512, leaf 32, '
                         'top-4, window 64) on the GPU and on the CPU oracle, logits compared; prints one JSON line')
+    p.add_argument('--block', action='store_true',
+                   help="the block forest's TreeAttention (attn='block') at train.py's and a 4096-token configuration; "
+                        'prints one JSON line each')
     p.add_argument('--dyn', action='store_true',
                    help="the dynamic content tree's select_keys (attn='dyn') at train.py's and a 4096-token "
                         'configuration; prints one JSON line each')
@@ -444,6 +447,59 @@ def union_tile_pairs(ids, vld, n_tree, leaf, Lw, T, qt=128, kt=64):
     return int(occ.sum())
 
 
+def run_block(a, dev):
+    """The block forest's attention (attn='block', TreeAttention) at the reference's train.py configuration
+    (B=8, 6 heads, 512 tokens, dh 64, 64-key blocks, wmax 8, beam 4) and a 4096-token window at B=2, bf16 q, k, v
+    ~ N(0, 1): one layer's sparse_attend (build: ta_lane_order + ta_forest_levels; descent: ta_forest_select;
+    attention: ta_sparse_attn) and the 6-layer GPT's forward, CUDA events after warm-up; the CPU oracle on one
+    (b, h) as the baseline. Prints one JSON line per configuration."""
+    from treeattn_b200.attention import TreeAttention
+    from treeattn_b200.config import Config
+    from treeattn_b200.forest import build_forest_raw
+    from treeattn_b200.model import GPT
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = ev(), ev()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    for name, (B, H, T, dh, blk, wmax, beam) in dict(train=(8, 6, 512, 64, 64, 8, 4),
+                                                     long=(2, 6, 4096, 64, 64, 8, 4)).items():
+        cfg = Config(vocab_size=8192, seq_len=T, n_layer=6, n_head=H, n_embd=H * dh, attn='block', tree_block=blk,
+                     wmax=wmax, beam=beam)
+        g = torch.Generator(device=dev).manual_seed(13)
+        q, k, v = [torch.randn(B, H, T, dh, device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
+        m = TreeAttention(cfg).to(dev, torch.bfloat16).eval()
+        with torch.no_grad():
+            attn_ms = timed(lambda: m.sparse_attend(q, k, v))
+            depth = int(round(math.log2(blk // 2)))
+            build_ms = timed(lambda: build_forest_raw(k, blk, depth, cfg, zero_sink=True))
+            model = GPT(cfg).to(dev, torch.bfloat16).eval()
+            idx = torch.randint(0, cfg.vocab_size, (B, T), device=dev, generator=g)
+            fwd_ms = timed(lambda: model(idx), reps=5)
+        line = dict(block_attn=True, config='%s: B=%d H=%d T=%d dh=%d bf16, blocks of %d, wmax %d, beam %d' % (
+            name, B, H, T, dh, blk, wmax, beam), layer_ms=attn_ms, build_ms=build_ms,
+            queries_per_s=B * H * T / (attn_ms * 1e-3), gpt6_forward_ms=fwd_ms, gpt6_tokens_per_s=B * T / (fwd_ms * 1e-3),
+            keys_per_query=float(m.aux['keys_total']))
+        if not a.no_cpu_baseline:
+            import oracle
+            qn, kn, vn = [x[:1, :1].float().cpu().numpy() for x in (q, k, v)]
+            t0 = time.perf_counter()
+            oracle.tree_attention(qn, kn, vn, blk, wmax, beam)
+            dt = time.perf_counter() - t0
+            line['cpu_baseline'] = dict(value=T / dt, unit='queries/s', cores=1, kind='port',
+                                        sample='oracle.tree_attention on one (b, h) of %d queries' % T)
+        print(json.dumps(line), flush=True)
+
+
 def run_dyn(a, dev):
     """The dynamic content tree's key selection (attn='dyn', dyntree.select_keys) at the reference's training
     configurations: train.py's defaults (B=8, 6 heads, 512 tokens, dh 64, lanes of 64, wmax 8, neighbours on) and a
@@ -700,6 +756,9 @@ def main():
         return
     if a.dyn:
         run_dyn(a, dev)
+        return
+    if a.block:
+        run_block(a, dev)
         return
 
     run_engine(a, CFG5 if a.config5 else CFG4, dev, rank, world, local)
