@@ -478,6 +478,19 @@ def run_block(a, dev):
         g = torch.Generator(device=dev).manual_seed(13)
         q, k, v = [torch.randn(B, H, T, dh, device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
         m = TreeAttention(cfg).to(dev, torch.bfloat16).eval()
+        if a.profile_steps:
+            if name != 'long':
+                continue
+            with torch.no_grad():
+                for _ in range(3):
+                    m.sparse_attend(q, k, v)
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStart()
+                for _ in range(a.profile_steps):
+                    m.sparse_attend(q, k, v)
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStop()
+            return
         with torch.no_grad():
             attn_ms = timed(lambda: m.sparse_attend(q, k, v))
             depth = int(round(math.log2(blk // 2)))

@@ -158,13 +158,20 @@ struct ForestSelectParams {
   uint8_t* lselv[FOREST_MAX_LEVELS];
 };
 
+// q . row for one node row (16-byte loads through the read-only path), rounded to T as a T-typed einsum.
 template <typename T, int DH>
 __device__ __forceinline__ float forest_score(const float* qf, const T* row) {
+  constexpr int V = 16 / sizeof(T);
   float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-  for (int d = 0; d < DH; d += 2) {
-    a0 = fmaf(qf[d], to_f32(row[d]), a0);
-    a1 = fmaf(qf[d + 1], to_f32(row[d + 1]), a1);
+  for (int c = 0; c < DH; c += V) {
+    float x[V];
+    ldg_vec_f32<T>(row + c, x);
+#pragma unroll
+    for (int i = 0; i < V; i += 2) {
+      a0 = fmaf(qf[c + i], x[i], a0);
+      a1 = fmaf(qf[c + i + 1], x[i + 1], a1);
+    }
   }
   return to_f32(from_f32<T>(a0 + a1));
 }
