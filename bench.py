@@ -330,11 +330,12 @@ def run_kernel_only(a, dev):
     att = torch.empty(B, Cm, device=dev, dtype=torch.bfloat16)
     nk = torch.empty(B, Hh, device=dev, dtype=torch.int32)
     splits = a.splits or _ops.default_splits(B, Hh, dh, torch.bfloat16)
+    scratch = _ops.split_scratch(B, Hh, dh, dev)
 
     def run_all():
         for K, Vv, lv in layers:
             _ops.decode_step(qkv, K, Vv, lv, pos, Hh, topk, topk, window, 1 / math.sqrt(dh), att, nkeys=nk,
-                             splits=splits)
+                             splits=splits, scratch=scratch)
 
     run_all()
     torch.cuda.synchronize()
@@ -880,7 +881,7 @@ def run_engine(a, M, dev, rank, world, local):
     def layer_launches():
         for st in dec.states:
             _ops.decode_step(qkv, st.K, st.V, st.levels, pos, H, M.topk, M.topk, M.window, 1 / math.sqrt(dh), att,
-                             nkeys=nk, splits=dec.splits)
+                             nkeys=nk, splits=dec.splits, scratch=dec._split)
 
     layer_launches()
     torch.cuda.synchronize()

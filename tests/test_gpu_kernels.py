@@ -517,6 +517,49 @@ def test_decode_long_context_wide_heads(splits):
     _no_device_error()
 
 
+@pytest.mark.parametrize('B,H,steps', [(10, 16, 6), (20, 16, 3)])
+def test_decode_split_items_match_whole_items(B, H, steps):
+    """Persistent decode with 256-byte rows (dh 128 bf16, one CTA per SM) and the split scratch: items cut into parts
+    (windows and leaf rows shared out, partial states merged by the last part) give the outputs of whole items up to
+    the merge order, the same selections and key counts, and the same caches and tree (appended once), over steps
+    that complete leaf blocks."""
+    ops = _ops()
+    from treeattn_b200._ops import Levels
+    dt, dh, L0, wmax, local = torch.bfloat16, 128, 7, 32, 256
+    rng = np.random.default_rng(B)
+    C = H * dh
+    T0 = (rng.integers(3000, 6000, B) // 128 * 128 - 2).tolist()
+    cap = max(T0) + steps + 1
+    Lm = int(math.ceil(math.log2(cap)))
+    kc = torch.randn(B, H, cap, dh, device=DEV).to(dt)
+    vc = torch.randn(B, H, cap, dh, device=DEV).to(dt)
+    lv = Levels.empty(B, H, dh, cap, L0, Lm, DEV)
+    ops.build_levels(kc, cap, L0, Lm, zero_sink=True, out=lv)
+    kc2, vc2 = kc.clone(), vc.clone()
+    lv2 = Levels(lv.nodes.clone(), cap, L0, Lm)
+    scratch = ops.split_scratch(B, H, dh, DEV)
+    outs = [torch.empty(B, C, device=DEV, dtype=dt) for _ in range(2)]
+    lses = [torch.empty(B, H, device=DEV) for _ in range(2)]
+    nks = [torch.empty(B, H, device=DEV, dtype=torch.int32) for _ in range(2)]
+    sels = [torch.empty(B, H, wmax + 1, device=DEV, dtype=torch.int32) for _ in range(2)]
+    for s_i in range(steps):
+        pos = torch.tensor([T0[b] + s_i for b in range(B)], device=DEV, dtype=torch.int32)
+        qkv = torch.randn(B, 3 * C, device=DEV).to(dt)
+        ops.decode_step(qkv, kc, vc, lv, pos, H, wmax, wmax, local, 1 / math.sqrt(dh), outs[0], lse=lses[0],
+                        nkeys=nks[0], sel=sels[0], splits=-1)
+        ops.decode_step(qkv, kc2, vc2, lv2, pos, H, wmax, wmax, local, 1 / math.sqrt(dh), outs[1], lse=lses[1],
+                        nkeys=nks[1], sel=sels[1], splits=-1, scratch=scratch)
+        assert (outs[0].float() - outs[1].float()).abs().max().item() < 2e-2
+        # p is rounded to bf16 against the running maximum of the part that holds it: the sums differ at that
+        # precision (2^-9 relative at most)
+        assert (lses[0] - lses[1]).abs().max().item() < 2e-3
+        assert torch.equal(nks[0], nks[1]) and torch.equal(sels[0], sels[1])
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert torch.equal(lv.nodes, lv2.nodes)
+    assert int(scratch[1].abs().sum()) == 0  # every counter reset by its merging part
+    _no_device_error()
+
+
 def test_decode_bad_position_records_error():
     """A position outside the capacity is rejected inside the kernel (no memory access, error recorded)."""
     ops = _ops()

@@ -52,11 +52,11 @@ def test_argument_validation_without_gpu():
     assert rc == _lib.TA_ERR_ARG and 'wmax' in _lib.last_error()
     # top level below the leaf level
     rc = lib.ta_decode_step(None, 1, 1, 1, 64, 0, 0, 0, None, None, 0, 0, 0, None, 0, 0, 64, 6, 5, None, 16, 16, 128,
-                            ctypes.c_float(0.125), None, 0, None, None, None, 1, None)
+                            ctypes.c_float(0.125), None, 0, None, None, None, 1, None, None, None)
     assert rc == _lib.TA_ERR_ARG and 'Lm' in _lib.last_error()
     # cluster size limit
     rc = lib.ta_decode_step(None, 1, 1, 1, 64, 0, 0, 0, None, None, 0, 0, 0, None, 0, 0, 64, 3, 5, None, 16, 16, 128,
-                            ctypes.c_float(0.125), None, 0, None, None, None, 9, None)
+                            ctypes.c_float(0.125), None, 0, None, None, None, 9, None, None, None)
     assert rc == _lib.TA_ERR_ARG and 'splits' in _lib.last_error()
     # misaligned rows
     buf = (ctypes.c_char * 256)()

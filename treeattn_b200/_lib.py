@@ -52,7 +52,7 @@ SIGNATURES = {
     'ta_dedupe': [P, P, P, L, I, P],
     'ta_append': [P, P, I, I, I, I, L, L, L, L, P, P, L, L, L, P, L, L, I, I, I, P, P],
     'ta_decode_step': [P, I, I, I, I, L, L, L, P, P, L, L, L, P, L, L, I, I, I, P, I, I, I, F, P, L, P, P, P, I,
-                       P],
+                       P, P, P],
     'ta_decode_default_splits': [I, I, I, I],
     'ta_embed_ln': [P, P, I, P, P, I, I, I, I, P, F, P, P, P],
     'ta_add_ln': [P, P, I, I, I, P, F, P, P],

@@ -378,10 +378,17 @@ def append(k, v, kc, vc, levels, pos):
               levels.cap, levels.L0, levels.Lm, _p(pos), _stream(kc))
 
 
+def split_scratch(B, H, dh, device):
+    """Scratch for decode_step's split items: (B*H*4*(dh+4) fp32 partials, B*H int32 counters, zeroed)."""
+    return (torch.empty(B * H * 4 * (dh + 4), device=device, dtype=torch.float32),
+            torch.zeros(B * H, device=device, dtype=torch.int32))
+
+
 def decode_step(qkv, kc, vc, levels, pos, H, wmax, n_tree, Lw, scale, out, lse=None, nkeys=None, sel=None,
-                splits=0):
+                splits=0, scratch=None):
     """Fused decode step of one layer (seg_attend): qkv (B, 3*H*dh) rows, caches (B, H, cap, dh), pos (B,) int32.
-    Writes out (B, H*dh) and appends k/v + updates the tree in place."""
+    Writes out (B, H*dh) and appends k/v + updates the tree in place. scratch = split_scratch(...) lets the
+    persistent kernel cut items into parts when whole items would leave SMs idle."""
     B = qkv.shape[0]
     dh = kc.shape[-1]
     C = H * dh
@@ -389,7 +396,8 @@ def decode_step(qkv, kc, vc, levels, pos, H, wmax, n_tree, Lw, scale, out, lse=N
     _lib.call('ta_decode_step', _p(qkv), _code(qkv), B, H, dh, qkv.stride(0), C, 2 * C, _p(kc), _p(vc),
               kc.stride(0), kc.stride(1), kc.stride(2), _p(nd), nd.stride(0), nd.stride(1), levels.cap, levels.L0,
               levels.Lm, _p(pos), wmax, n_tree, Lw, float(scale), _p(out), out.stride(0), _p(lse), _p(nkeys),
-              _p(sel), int(splits), _stream(qkv))
+              _p(sel), int(splits), _p(scratch[0]) if scratch else None, _p(scratch[1]) if scratch else None,
+              _stream(qkv))
 
 
 def embed_ln(wte, wpe, tok, pos, w, x_out, h_out, eps=1e-5):

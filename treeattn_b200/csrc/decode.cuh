@@ -37,6 +37,13 @@ struct DecodeParams {
   int32_t* nkeys;         // (B, H) keys attended, may be null
   int32_t* sel;           // (B, H, wmax + 1): [count, leaf ids...] of the descent, may be null
   int splits;             // cluster size S (grid.x)
+  // persistent kernel, split items: every (b, h) item is cut into psplit parts (its window rows and its leaf rows
+  // each in psplit near-equal shares); a part's partial softmax state goes to part[(bh * psplit + j) * (DH + 4)]
+  // (m, l, keys, -, acc[DH]) and the part that finishes last (part_cnt[bh], reset to 0 by it) merges them, writes
+  // the output and appends the step's rows. psplit = 1: whole items, no scratch.
+  int psplit;
+  float* part;
+  int32_t* part_cnt;
 };
 
 template <typename T, int DH, int CH, int NST, int NCW>
@@ -466,7 +473,7 @@ struct __align__(16) PItem {
   T q[DH], k[DH], v[DH];  // this step's rows of the item's (b, h)
   RangeList rl;           // used leaf blocks cut at the window start, and the sink; the window is not listed
   int sel[WMAX_LIMIT];
-  int t, bh, nsel, active;
+  int t, bh, nsel, active, part;
 };
 
 template <typename T, int DH, int NST, int NCW, int NCG>
@@ -573,7 +580,9 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   const int n_all = p.B * p.H;
-  const int K = ((int)blockIdx.x < n_all) ? (n_all - (int)blockIdx.x + G - 1) / G : 0;  // items of this CTA
+  const int PS = p.psplit > 1 ? p.psplit : 1;
+  const int n_units = n_all * PS;  // work units: (item, part)
+  const int K = ((int)blockIdx.x < n_units) ? (n_units - (int)blockIdx.x + G - 1) / G : 0;  // units of this CTA
   const int leaf = 1 << p.lv.L0;
 
   if (tid == 0) {
@@ -605,7 +614,8 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         break;
       }
       PItem<T, DH>& it = sh.item[slot];
-      const int bh = (int)blockIdx.x + k * G;
+      const int unit = (int)blockIdx.x + k * G;
+      const int bh = unit / PS;
       const int b = bh / p.H, h = bh % p.H;
       int t = p.pos[b];
       const bool active = t >= 0 && t < p.lv.cap;
@@ -642,6 +652,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       if (lane == 0) {
         it.t = t;
         it.bh = bh;
+        it.part = unit - bh * PS;
         it.nsel = nk;
         it.active = active ? 1 : 0;
       }
@@ -661,12 +672,16 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       };
       for (int k = 0; k < K && ok; ++k) {
         const int slot = k % PSLOTS;
-        const int bh = (int)blockIdx.x + k * G;
+        const int unit = (int)blockIdx.x + k * G;
+        const int bh = unit / PS, part = unit - bh * PS;
         const int b = bh / p.H, h = bh % p.H;
         int t = p.pos[b];
         const bool active = t >= 0 && t < p.lv.cap;
         if (!active) t = 0;
-        const int w0 = max(t - p.Lw + 1, 0);
+        const int wa0 = max(t - p.Lw + 1, 0);
+        // this part's share of the window rows [wa0, t)
+        const int w0 = wa0 + (int)((int64_t)(t - wa0) * part / PS);
+        const int w1 = wa0 + (int)((int64_t)(t - wa0) * (part + 1) / PS);
         const T* kbase = reinterpret_cast<const T*>(p.kc) + b * p.c_sb + h * p.c_sh;
         const T* vbase = reinterpret_cast<const T*>(p.vc) + b * p.c_sb + h * p.c_sh;
         unsigned started = 0, lasted = 0;  // consumer groups that got a FIRST / LAST stage of item k
@@ -681,10 +696,10 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           }
           return f;
         };
-        for (int r0 = w0; active && r0 < t; r0 += CH) {  // window rows [w0, t) (their LAST is not known yet)
+        for (int r0 = w0; active && r0 < w1; r0 += CH) {  // window rows [w0, w1) (their LAST is not known yet)
           int s;
           if (!(ok = acquire(s))) break;
-          const int n = min(CH, t - r0);
+          const int n = min(CH, w1 - r0);
           sh.nrows[s] = n;
           sh.flags[s] = flags_for(false);
           sh.slot[s] = slot;
@@ -697,17 +712,24 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         if (!ok) break;
         if (!(ok = mbar_wait_bounded(&sh.ifull[slot], (k / PSLOTS) & 1, K_DECODE, 11))) break;
         const RangeList& rl = sh.item[slot].rl;
-        const int n_leaf_stages = ceil_div(rl.pref[rl.n], CH);
+        // this part's share [la, lb) of the leaf rows (flattened over the ranges)
+        const int R = rl.pref[rl.n];
+        const int la = (int)((int64_t)R * part / PS), lb = (int)((int64_t)R * (part + 1) / PS);
+        const int n_leaf_stages = ceil_div(lb - la, CH);
         int ri = 0, roff = 0;
+        while (ri < rl.n && rl.pref[ri + 1] <= la) ++ri;
+        if (ri < rl.n) roff = la - rl.pref[ri];
+        int left = lb - la;
         for (int j = 0; j < n_leaf_stages; ++j) {  // leaf blocks + sink, packed CH rows per stage
           int s;
           if (!(ok = acquire(s))) break;
+          const int cap_n = min(CH, left);
           int n = 0;
           {
             int ri2 = ri, roff2 = roff;
-            while (n < CH && ri2 < rl.n) {
+            while (n < cap_n && ri2 < rl.n) {
               const int len = rl.pref[ri2 + 1] - rl.pref[ri2];
-              const int take = min(CH - n, len - roff2);
+              const int take = min(cap_n - n, len - roff2);
               n += take;
               roff2 += take;
               if (roff2 == len) { ++ri2; roff2 = 0; }
@@ -730,6 +752,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
             roff += take;
             if (roff == len) { ++ri; roff = 0; }
           }
+          left -= n;
           ++it;
         }
         while (ok && lasted != (1u << NCG) - 1u) {  // groups still without a LAST: empty end-of-item stages
@@ -768,8 +791,9 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       }
       PItem<T, DH>& item = sh.item[slot];
       const float* pacc = part_acc + (size_t)par * NCW * DH;
+      bool finish = item.active != 0;
       if (item.active) {
-        const int b = item.bh / p.H, h = item.bh % p.H, t = item.t;
+        const int b = item.bh / p.H, h = item.bh % p.H;
         float m = -INFINITY;
         for (int w = 0; w < NCW; ++w) m = fmaxf(m, sh.part_m[par][w]);
         float l = 0.f;
@@ -778,15 +802,60 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           if (sh.part_m[par][w] != -INFINITY) l += sh.part_l[par][w] * exp2f(sh.part_m[par][w] - m);
           keys += sh.part_rows[par][w];
         }
-        const float inv = l > 0.f ? 1.f / l : 0.f;
         T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
-        for (int d = lane; d < DH; d += 32) {
-          float a = 0.f;
-          for (int w = 0; w < NCW; ++w)
-            if (sh.part_m[par][w] != -INFINITY) a += pacc[w * DH + d] * exp2f(sh.part_m[par][w] - m);
-          orow[d] = from_f32<T>(a * inv);
+        if (PS == 1) {
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          for (int d = lane; d < DH; d += 32) {
+            float a = 0.f;
+            for (int w = 0; w < NCW; ++w)
+              if (sh.part_m[par][w] != -INFINITY) a += pacc[w * DH + d] * exp2f(sh.part_m[par][w] - m);
+            orow[d] = from_f32<T>(a * inv);
+          }
+        } else {
+          // this part's state to the scratch; the part that arrives last merges all of them (no waiting)
+          float* prow = p.part + ((int64_t)item.bh * PS + item.part) * (DH + 4);
+          for (int d = lane; d < DH; d += 32) {
+            float a = 0.f;
+            for (int w = 0; w < NCW; ++w)
+              if (sh.part_m[par][w] != -INFINITY) a += pacc[w * DH + d] * exp2f(sh.part_m[par][w] - m);
+            prow[4 + d] = a;
+          }
+          if (lane == 0) {
+            prow[0] = m;
+            prow[1] = l;
+            prow[2] = __int_as_float(keys);
+          }
+          __threadfence();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) last = atomicAdd(&p.part_cnt[item.bh], 1) == PS - 1 ? 1 : 0;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          finish = last != 0;
+          if (finish) {
+            __threadfence();
+            const float* pb = p.part + (int64_t)item.bh * PS * (DH + 4);
+            m = -INFINITY;
+            for (int j = 0; j < PS; ++j) m = fmaxf(m, __ldcg(pb + j * (DH + 4)));
+            l = 0.f;
+            keys = 0;
+            for (int j = 0; j < PS; ++j) {
+              const float mj = __ldcg(pb + j * (DH + 4));
+              if (mj != -INFINITY) l += __ldcg(pb + j * (DH + 4) + 1) * exp2f(mj - m);
+              keys += __float_as_int(__ldcg(pb + j * (DH + 4) + 2));
+            }
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            for (int d = lane; d < DH; d += 32) {
+              float a = 0.f;
+              for (int j = 0; j < PS; ++j) {
+                const float mj = __ldcg(pb + j * (DH + 4));
+                if (mj != -INFINITY) a += __ldcg(pb + j * (DH + 4) + 4 + d) * exp2f(mj - m);
+              }
+              orow[d] = from_f32<T>(a * inv);
+            }
+            if (lane == 0) p.part_cnt[item.bh] = 0;
+          }
         }
-        if (lane == 0) {
+        if (finish && lane == 0) {
           if (p.lse) p.lse[item.bh] = l > 0.f ? (m + log2f(l)) * LN2 : -INFINITY;
           if (p.nkeys) p.nkeys[item.bh] = keys;
           if (p.sel) {
@@ -795,16 +864,21 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
             for (int i = 0; i < p.wmax; ++i) so[1 + i] = i < item.nsel ? item.sel[i] : -1;
           }
         }
-        // append this step's k / v rows at position t
-        T* kc = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh;
-        T* vc = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh;
-        for (int c = lane; c < DH / VEC; c += 32) {
-          *reinterpret_cast<uint4*>(kc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.k + c * VEC);
-          *reinterpret_cast<uint4*>(vc + (int64_t)t * p.c_st + c * VEC) = *reinterpret_cast<const uint4*>(item.v + c * VEC);
+        if (finish) {
+          // append this step's k / v rows at position t
+          const int t = item.t;
+          T* kc = reinterpret_cast<T*>(p.kc) + b * p.c_sb + h * p.c_sh;
+          T* vc = reinterpret_cast<T*>(p.vc) + b * p.c_sb + h * p.c_sh;
+          for (int c = lane; c < DH / VEC; c += 32) {
+            *reinterpret_cast<uint4*>(kc + (int64_t)t * p.c_st + c * VEC) =
+                *reinterpret_cast<const uint4*>(item.k + c * VEC);
+            *reinterpret_cast<uint4*>(vc + (int64_t)t * p.c_st + c * VEC) =
+                *reinterpret_cast<const uint4*>(item.v + c * VEC);
+          }
+          if (((t + 1) & (leaf - 1)) == 0)
+            tree_update_warp<T, DH>(kc, p.c_st, item.k, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, tu,
+                                    Cfg::TU_FLOATS, lane);
         }
-        if (((t + 1) & (leaf - 1)) == 0)
-          tree_update_warp<T, DH>(kc, p.c_st, item.k, t, p.nodes + b * p.lv.s_b + h * p.lv.s_h, p.lv, tu,
-                                  Cfg::TU_FLOATS, lane);
       }
       __syncwarp();
       if (lane == 0) {
@@ -838,7 +912,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         PItem<T, DH>& item = sh.item[slot];
         wa.init(item.q, p.scale * LOG2E, lane);
         rows = 0;
-        if (warp == 0 && item.active) {  // the new token, from this step's rows
+        if (warp == 0 && item.active && item.part == 0) {  // the new token, from this step's rows (part 0)
           wa.one_row(item.k, item.v);
           rows = 1;
         }

@@ -507,6 +507,9 @@ struct Decode {
 
   // Pipeline shape of the persistent kernel for 256-byte rows (bf16/f16 dh=128, f32 dh=64), which run one CTA
   // per SM: rows per stage, ring stages and consumer groups (compile-time; NST must be a multiple of NCG).
+#ifndef TA_MAX_PSPLIT
+#define TA_MAX_PSPLIT 2  // most parts per decode item (split items, persistent kernel); 1 turns splitting off
+#endif
 #ifndef TA_WIDE_CH
 #define TA_WIDE_CH 32
 #endif
@@ -543,8 +546,24 @@ struct Decode {
     }
     const int items = p.B * p.H;
     const int gmax = per_sm * num_sms();
-    const int per_cta = (items + gmax - 1) / gmax;  // items per CTA (equal for all but the last few)
-    const int grid = (items + per_cta - 1) / per_cta;
+    // With one CTA per SM (256-byte rows) a whole-item grid can leave SMs idle (e.g. 320 items: 3 per CTA on 107 of
+    // 148 SMs); cutting every item into S parts (window and leaf rows shared out, partials merged by the last
+    // part) spreads the same bytes over more SMs. S is the smallest of 1..TA_MAX_PSPLIT within 5 % of the best
+    // per-CTA load. Measured on the configuration-5 shape (320 items): S=1 204 us, S=2 177 us, S=3 195 us (every
+    // part repeats its item's descent and pipeline fill), hence the cap of 2.
+    p.psplit = 1;
+    if (p.part && p.part_cnt && per_sm == 1) {
+      double best = 1e30;
+      int bs = 1;
+      for (int S = 1; S <= TA_MAX_PSPLIT; ++S) {
+        const double load = (double)((int64_t)items * S + gmax - 1) / gmax / S;  // items per CTA, rounded up
+        if (load < best * 0.95) { best = load; bs = S; }
+      }
+      p.psplit = bs;
+    }
+    const int units = items * p.psplit;
+    const int per_cta = (units + gmax - 1) / gmax;  // units per CTA (equal for all but the last few)
+    const int grid = (units + per_cta - 1) / per_cta;
     kern<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
     return check_launch("ta_decode_step(persistent)");
   }
@@ -1193,7 +1212,7 @@ int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv
                    void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st, float* nodes, int64_t n_sb,
                    int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos, int wmax, int n_tree, int Lw,
                    float scale, void* out, int64_t o_sb, float* lse, int32_t* nkeys, int32_t* sel, int splits,
-                   void* stream) {
+                   float* part, int32_t* part_cnt, void* stream) {
   g_err.clear();
   if (!valid_dtype(dtype)) return fail(TA_ERR_ARG, "ta_decode_step: bad dtype %d", dtype);
   if (!valid_dh(dh)) return fail(TA_ERR_ARG, "ta_decode_step: unsupported head dim %d", dh);
@@ -1221,6 +1240,9 @@ int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv
   p.out = out; p.o_sb = o_sb;
   p.lse = lse; p.nkeys = nkeys; p.sel = sel;
   p.splits = splits;
+  p.psplit = 1;
+  p.part = part;
+  p.part_cnt = part_cnt;
   return by_type_dh<Decode>(dtype, dh, p, S(stream));
 }
 

@@ -293,6 +293,9 @@ class Decoder:
         self._mlp = torch.empty(B, C, device=dev, dtype=dt)
         self._logits = torch.empty(B, self.W['wte'].shape[0], device=dev, dtype=dt)
         self._nkeys = torch.zeros(self.nl, B, self.H, device=dev, dtype=torch.int32)
+        # partial-state scratch that lets the decode kernel cut items into parts when whole items would leave SMs
+        # idle (shared by the layers: their launches run in order on one stream)
+        self._split = _ops.split_scratch(B, self.H, self.dh, dev) if self.mode == 'seg' else None
         self._graph = None
         self._graph_greedy = None
 
@@ -316,7 +319,8 @@ class Decoder:
                 self._nkeys[i].copy_(nk.view(B, H))
             else:
                 _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree,
-                                 self.Lw, self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits)
+                                 self.Lw, self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits,
+                                 scratch=self._split)
             torch.mm(self._att, Li['c_proj'].t(), out=self._proj)
             _ops.add_ln(self._x, self._proj, Li['ln2'], self._h)
             torch.mm(self._h, Li['c_fc'].t(), out=self._fc)
