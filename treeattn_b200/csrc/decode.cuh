@@ -550,7 +550,8 @@ __device__ void tree_update_warp(const T* __restrict__ kbase, int64_t c_st, cons
   }
 }
 
-template <typename T, int DH, int CH, int NST, int NCG, int WPG>
+// SPLIT: items cut into p.psplit parts (a separate instantiation, so that whole items run the unsplit code).
+template <typename T, int DH, int CH, int NST, int NCG, int WPG, bool SPLIT>
 __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
   using Cfg = PCfg<T, DH, CH, NST, NCG, WPG>;
   constexpr int NCW = Cfg::NCW;
@@ -580,7 +581,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   const int n_all = p.B * p.H;
-  const int PS = p.psplit > 1 ? p.psplit : 1;
+  const int PS = SPLIT ? (p.psplit > 1 ? p.psplit : 1) : 1;
   const int n_units = n_all * PS;  // work units: (item, part)
   const int K = ((int)blockIdx.x < n_units) ? (n_units - (int)blockIdx.x + G - 1) / G : 0;  // units of this CTA
   const int leaf = 1 << p.lv.L0;
@@ -712,48 +713,86 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         if (!ok) break;
         if (!(ok = mbar_wait_bounded(&sh.ifull[slot], (k / PSLOTS) & 1, K_DECODE, 11))) break;
         const RangeList& rl = sh.item[slot].rl;
-        // this part's share [la, lb) of the leaf rows (flattened over the ranges)
-        const int R = rl.pref[rl.n];
-        const int la = (int)((int64_t)R * part / PS), lb = (int)((int64_t)R * (part + 1) / PS);
-        const int n_leaf_stages = ceil_div(lb - la, CH);
-        int ri = 0, roff = 0;
-        while (ri < rl.n && rl.pref[ri + 1] <= la) ++ri;
-        if (ri < rl.n) roff = la - rl.pref[ri];
-        int left = lb - la;
-        for (int j = 0; j < n_leaf_stages; ++j) {  // leaf blocks + sink, packed CH rows per stage
-          int s;
-          if (!(ok = acquire(s))) break;
-          const int cap_n = min(CH, left);
-          int n = 0;
-          {
-            int ri2 = ri, roff2 = roff;
-            while (n < cap_n && ri2 < rl.n) {
-              const int len = rl.pref[ri2 + 1] - rl.pref[ri2];
-              const int take = min(cap_n - n, len - roff2);
-              n += take;
-              roff2 += take;
-              if (roff2 == len) { ++ri2; roff2 = 0; }
+        if constexpr (!SPLIT) {
+          const int n_leaf_stages = ceil_div(rl.pref[rl.n], CH);
+          int ri = 0, roff = 0;
+          for (int j = 0; j < n_leaf_stages; ++j) {  // leaf blocks + sink, packed CH rows per stage
+            int s;
+            if (!(ok = acquire(s))) break;
+            int n = 0;
+            {
+              int ri2 = ri, roff2 = roff;
+              while (n < CH && ri2 < rl.n) {
+                const int len = rl.pref[ri2 + 1] - rl.pref[ri2];
+                const int take = min(CH - n, len - roff2);
+                n += take;
+                roff2 += take;
+                if (roff2 == len) { ++ri2; roff2 = 0; }
+              }
             }
+            sh.nrows[s] = n;
+            sh.flags[s] = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
+            sh.slot[s] = slot;
+            T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
+            mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+            int put = 0;
+            while (put < n) {
+              const int len = rl.pref[ri + 1] - rl.pref[ri];
+              const int take = min(n - put, len - roff);
+              const int64_t r0 = rl.start[ri] + roff;
+              bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
+              bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s],
+                            pol);
+              put += take;
+              roff += take;
+              if (roff == len) { ++ri; roff = 0; }
+            }
+            ++it;
           }
-          sh.nrows[s] = n;
-          sh.flags[s] = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
-          sh.slot[s] = slot;
-          T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
-          mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
-          int put = 0;
-          while (put < n) {
-            const int len = rl.pref[ri + 1] - rl.pref[ri];
-            const int take = min(n - put, len - roff);
-            const int64_t r0 = rl.start[ri] + roff;
-            bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
-            bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s],
-                          pol);
-            put += take;
-            roff += take;
-            if (roff == len) { ++ri; roff = 0; }
+        } else {
+          // this part's share [la, lb) of the leaf rows (flattened over the ranges)
+          const int R = rl.pref[rl.n];
+          const int la = (int)((int64_t)R * part / PS), lb = (int)((int64_t)R * (part + 1) / PS);
+          const int n_leaf_stages = ceil_div(lb - la, CH);
+          int ri = 0, roff = 0;
+          while (ri < rl.n && rl.pref[ri + 1] <= la) ++ri;
+          if (ri < rl.n) roff = la - rl.pref[ri];
+          int left = lb - la;
+          for (int j = 0; j < n_leaf_stages; ++j) {  // leaf blocks + sink, packed CH rows per stage
+            int s;
+            if (!(ok = acquire(s))) break;
+            const int cap_n = min(CH, left);
+            int n = 0;
+            {
+              int ri2 = ri, roff2 = roff;
+              while (n < cap_n && ri2 < rl.n) {
+                const int len = rl.pref[ri2 + 1] - rl.pref[ri2];
+                const int take = min(cap_n - n, len - roff2);
+                n += take;
+                roff2 += take;
+                if (roff2 == len) { ++ri2; roff2 = 0; }
+              }
+            }
+            sh.nrows[s] = n;
+            sh.flags[s] = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
+            sh.slot[s] = slot;
+            T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
+            mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+            int put = 0;
+            while (put < n) {
+              const int len = rl.pref[ri + 1] - rl.pref[ri];
+              const int take = min(n - put, len - roff);
+              const int64_t r0 = rl.start[ri] + roff;
+              bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
+              bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s],
+                            pol);
+              put += take;
+              roff += take;
+              if (roff == len) { ++ri; roff = 0; }
+            }
+            left -= n;
+            ++it;
           }
-          left -= n;
-          ++it;
         }
         while (ok && lasted != (1u << NCG) - 1u) {  // groups still without a LAST: empty end-of-item stages
           int s;
@@ -803,7 +842,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           keys += sh.part_rows[par][w];
         }
         T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
-        if (PS == 1) {
+        if constexpr (!SPLIT) {
           const float inv = l > 0.f ? 1.f / l : 0.f;
           for (int d = lane; d < DH; d += 32) {
             float a = 0.f;
@@ -912,7 +951,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         PItem<T, DH>& item = sh.item[slot];
         wa.init(item.q, p.scale * LOG2E, lane);
         rows = 0;
-        if (warp == 0 && item.active && item.part == 0) {  // the new token, from this step's rows (part 0)
+        if (warp == 0 && item.active && (!SPLIT || item.part == 0)) {  // the new token (part 0 of a split item)
           wa.one_row(item.k, item.v);
           rows = 1;
         }

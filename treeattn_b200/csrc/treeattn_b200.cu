@@ -525,7 +525,8 @@ struct Decode {
     constexpr int NST = ROWB == 256 ? TA_WIDE_NST : 4;                        // ring stages
     constexpr int NCG = ROWB == 256 ? TA_WIDE_NCG : 2, WPG = 4;               // consumer groups x warps
     using Cfg = ta::PCfg<T, DH, CH, NST, NCG, WPG>;
-    auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG>;
+    auto kern = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG, false>;
+    auto kern_split = ta::decode_persistent_kernel<T, DH, CH, NST, NCG, WPG, true>;
     // descent staging rows: whatever keeps two CTAs per SM (111 KiB each) when at least one full level
     // (2*wmax+1 rows) fits that way, else what one CTA per SM allows
     const size_t row_bytes = (size_t)ta::stage_row_floats<DH>() * 4;
@@ -540,6 +541,7 @@ struct Decode {
     static size_t per_sm_smem = 0;
     if (per_sm == 0 || per_sm_smem != smem) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+      cudaFuncSetAttribute(kern_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::NTHREADS, smem);
       if (per_sm < 1) per_sm = 1;
       per_sm_smem = smem;
@@ -564,7 +566,10 @@ struct Decode {
     const int units = items * p.psplit;
     const int per_cta = (units + gmax - 1) / gmax;  // units per CTA (equal for all but the last few)
     const int grid = (units + per_cta - 1) / per_cta;
-    kern<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
+    if (p.psplit > 1)
+      kern_split<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
+    else
+      kern<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
     return check_launch("ta_decode_step(persistent)");
   }
 };
