@@ -309,7 +309,7 @@ def run_kernel_only(a, dev):
     from treeattn_b200._ops import Levels
     if a.config5:
         Hh, dh, leaf, topk, window, tcap = 16, 128, 128, 32, 256, 65536
-        B, T0 = a.batch if a.batch != 64 else 32, 32768
+        B, T0 = a.batch if a.batch != 64 else 32, (32768 if a.prompt == 4096 else a.prompt)
     else:
         Hh, dh, leaf, topk, window, tcap = H, C // H, LEAF, TOPK, WINDOW, TCAP
         B, T0 = a.batch, a.prompt
