@@ -77,6 +77,28 @@ def test_argument_validation_without_gpu():
     assert rc == _lib.TA_ERR_ARG and 'wl' in _lib.last_error()
     rc = lib.ta_lane_search(addr, addr, addr, 4, 0, 64, 4, 4, addr, addr, None, None)
     assert rc == _lib.TA_ERR_ARG and 'D=' in _lib.last_error()
+    # dynamic tree: capacity not a power of two, too many levels, neighbour store above the beam
+    rc = lib.ta_lane_order(addr, 1, 1000 * 16, addr, 1, 2, 1000, 16, 3, 3, addr, addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'power of two' in _lib.last_error()
+    rc = lib.ta_lane_order(addr, 1, 1024 * 16, addr, 1, 2, 1024, 16, 3, 10, addr, addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'levels' in _lib.last_error()
+    rc = lib.ta_lane_order(addr + 4, 1, 1024 * 16, addr, 1, 2, 1024, 16, 3, 9, addr, addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'aligned' in _lib.last_error()
+    rc = lib.ta_lane_select(addr, addr, addr, 1, 1, 64, 16, 16, 4, 4, 8, 2, 1, ctypes.c_float(0.35), 1, addr, addr,
+                            addr, addr, addr, addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'nb_store' in _lib.last_error()
+    rc = lib.ta_lane_insert(addr, addr, addr, 2, 48, 16, addr, addr, addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'power of two' in _lib.last_error()
+    # block forest: depth not log2(B / 2), T not a multiple of the block, bad dtype
+    ptrs = (ctypes.c_void_p * 8)(*([addr] * 8))
+    rc = lib.ta_forest_levels(addr, 1, 4, 32, 16, 3, 2, 1, addr, 0, ctypes.c_float(0.25), ctypes.c_float(0.3),
+                              ptrs, None)
+    assert rc == _lib.TA_ERR_ARG and 'depth' in _lib.last_error()
+    rc = lib.ta_forest_select(addr, 1, 1, 1, 100, 16, 0, 0, 16, ptrs, addr, 32, 4, None, 4, 8, addr, addr, addr,
+                              addr, None, None, None)
+    assert rc == _lib.TA_ERR_ARG and 'multiple' in _lib.last_error()
+    rc = lib.ta_soft_gate(addr, addr, 7, 4, 8, 16, ctypes.c_float(0.25), ctypes.c_float(0.3), addr, None)
+    assert rc == _lib.TA_ERR_ARG and 'dtype' in _lib.last_error()
     # neighbour pass: more than 32 stored leaves per query
     rc = lib.ta_neighbor_pass(addr, 1, 1, 1, 4, 64, 0, 0, 64, addr, 0, 1, addr, 0, 0, 8, 3, addr, addr, addr, 16,
                               9, 4, ctypes.c_float(0.35), 3, 2, 1, addr, addr, addr, None)
