@@ -746,10 +746,14 @@ __global__ void __launch_bounds__(128) gather_dot_blocks_kernel(GatherDotBlocksP
   const int row_bytes = DH * (int)sizeof(T);
   const int32_t* bl = p.blocks + (int64_t)bh * p.nblk + j0;
   const T* kbase = reinterpret_cast<const T*>(p.k) + b * p.k_sb + h * p.k_sh;
+  // launched with programmatic stream serialization: wait (before the first global read) until the previous grid
+  // of the stream has completed and its writes are visible; the next grid may be scheduled once every CTA of this
+  // one has its rows in flight
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint64_t pol = l2_policy_evict_first();
@@ -772,6 +776,7 @@ __global__ void __launch_bounds__(128) gather_dot_blocks_kernel(GatherDotBlocksP
   const int sub = lane / LPR, c = lane % LPR;
   float qv[VEC];
   load_vec_f32<T>(reinterpret_cast<const T*>(p.q) + b * p.q_sb + h * p.q_sh + c * VEC, qv);
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const bool ok = mbar_wait_bounded(&bar, 0, K_GATHER_DOT_BLOCKS, 0);
   if (!ok) return;  // the wait gave up; an error is recorded (copies may still land in this CTA's smem)
   const int nrows = nb * p.blk;

@@ -415,7 +415,19 @@ struct GatherDotBlocks {
     const int groups = ta::ceil_div(p.nblk, p.nb_cta);
     const int64_t grid = (int64_t)p.B * p.H * groups;
     if (grid == 0) return TA_OK;
-    ta::gather_dot_blocks_kernel<T, DH><<<(unsigned)grid, 128, smem, st>>>(p);
+    // programmatic dependent launch: a chain of these short, latency-bound calls overlaps each launch with the
+    // previous call (the kernel waits for the previous grid before its first global read)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, ta::gather_dot_blocks_kernel<T, DH>, p);
     return check_launch("ta_gather_dot_blocks");
   }
 };
