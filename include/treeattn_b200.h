@@ -251,9 +251,11 @@ int ta_append(const void* k, const void* v, int dtype, int B, int H, int dh, int
  * qkv rows (B, 3*H*dh): q at 0, k at k_ofs, v at v_ofs (elements). out rows (B, H*dh). lse / nkeys /
  * sel (B, H, wmax+1) may be NULL. splits: 0 = choose; -1 = persistent pipelined kernel (a selector warp runs
  * the descent of the next (b, h) while the current one streams; for B*H >= #SMs); 1..8 = CTAs per (b, h) of
- * the cluster kernel (split KV merged through distributed shared memory; for small batches). * part / part_cnt (may be NULL): scratch of B*H*4*(dh+4) floats (room for 4 parts) and B*H int32 (zero before the first call; the kernel
- * leaves it zero) that lets the persistent form cut every (b, h) item into up to 2 parts when whole items would leave
- * SMs idle (one CTA per SM, e.g. dh 128 bf16 rows); the outputs are the same up to the fp32 merge order. */
+ * the cluster kernel (split KV merged through distributed shared memory; for small batches).
+ * part / part_cnt (may be NULL): scratch of B*H*4*(dh+4) floats and B*H int32 (zero before the first call; the
+ * kernel leaves it zero). With it the persistent form (one CTA per SM, e.g. dh 128 bf16 rows) cuts the items of its
+ * last, part-empty round into up to 8 parts spread over every CTA (partial states merged by the last part); the
+ * outputs are the same up to the fp32 merge order. */
 int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,
                    void* kc, void* vc, int64_t c_sb, int64_t c_sh, int64_t c_st, float* nodes, int64_t n_sb,
                    int64_t n_sh, int cap, int L0, int Lm, const int32_t* pos, int wmax, int n_tree, int Lw,

@@ -37,11 +37,11 @@ struct DecodeParams {
   int32_t* nkeys;         // (B, H) keys attended, may be null
   int32_t* sel;           // (B, H, wmax + 1): [count, leaf ids...] of the descent, may be null
   int splits;             // cluster size S (grid.x)
-  // persistent kernel, split items: every (b, h) item is cut into psplit parts (its window rows and its leaf rows
-  // each in psplit near-equal shares); a part's partial softmax state goes to part[(bh * psplit + j) * (DH + 4)]
-  // (m, l, keys, -, acc[DH]) and the part that finishes last (part_cnt[bh], reset to 0 by it) merges them, writes
-  // the output and appends the step's rows. psplit = 1: whole items, no scratch.
-  int psplit;
+  // persistent kernel, split items: the items [0, n_whole) run whole; every later item is cut into psplit parts
+  // (its window rows and its leaf rows each in psplit near-equal shares). A part's partial softmax state goes to
+  // part[((bh - n_whole) * psplit + j) * (DH + 4)] (m, l, keys, -, acc[DH]) and the part that finishes last
+  // (part_cnt[bh], reset to 0 by it) merges them, writes the output and appends the step's rows.
+  int psplit, n_whole;
   float* part;
   int32_t* part_cnt;
 };
@@ -473,7 +473,7 @@ struct __align__(16) PItem {
   T q[DH], k[DH], v[DH];  // this step's rows of the item's (b, h)
   RangeList rl;           // used leaf blocks cut at the window start, and the sink; the window is not listed
   int sel[WMAX_LIMIT];
-  int t, bh, nsel, active, part;
+  int t, bh, nsel, active, part, np;
 };
 
 template <typename T, int DH, int NST, int NCW, int NCG>
@@ -581,8 +581,17 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   const int n_all = p.B * p.H;
-  const int PS = SPLIT ? (p.psplit > 1 ? p.psplit : 1) : 1;
-  const int n_units = n_all * PS;  // work units: (item, part)
+  // work units: the whole items [0, NW), then PT parts of every later item
+  const int PT = SPLIT ? (p.psplit > 1 ? p.psplit : 1) : 1;
+  const int NW = SPLIT ? min(max(p.n_whole, 0), n_all) : n_all;
+  const int n_units = NW + (n_all - NW) * PT;
+  auto unit_item = [&](int u, int& part, int& np) -> int {
+    if (u < NW) { part = 0; np = 1; return u; }
+    const int v = u - NW;
+    part = v % PT;
+    np = PT;
+    return NW + v / PT;
+  };
   const int K = ((int)blockIdx.x < n_units) ? (n_units - (int)blockIdx.x + G - 1) / G : 0;  // units of this CTA
   const int leaf = 1 << p.lv.L0;
 
@@ -616,7 +625,8 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       }
       PItem<T, DH>& it = sh.item[slot];
       const int unit = (int)blockIdx.x + k * G;
-      const int bh = unit / PS;
+      int upart, unp;
+      const int bh = unit_item(unit, upart, unp);
       const int b = bh / p.H, h = bh % p.H;
       int t = p.pos[b];
       const bool active = t >= 0 && t < p.lv.cap;
@@ -653,7 +663,8 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       if (lane == 0) {
         it.t = t;
         it.bh = bh;
-        it.part = unit - bh * PS;
+        it.part = upart;
+        it.np = unp;
         it.nsel = nk;
         it.active = active ? 1 : 0;
       }
@@ -674,7 +685,8 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       for (int k = 0; k < K && ok; ++k) {
         const int slot = k % PSLOTS;
         const int unit = (int)blockIdx.x + k * G;
-        const int bh = unit / PS, part = unit - bh * PS;
+        int part, PS;
+        const int bh = unit_item(unit, part, PS);
         const int b = bh / p.H, h = bh % p.H;
         int t = p.pos[b];
         const bool active = t >= 0 && t < p.lv.cap;
@@ -842,7 +854,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           keys += sh.part_rows[par][w];
         }
         T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * DH;
-        if constexpr (!SPLIT) {
+        if (!SPLIT || item.np == 1) {
           const float inv = l > 0.f ? 1.f / l : 0.f;
           for (int d = lane; d < DH; d += 32) {
             float a = 0.f;
@@ -852,7 +864,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           }
         } else {
           // this part's state to the scratch; the part that arrives last merges all of them (no waiting)
-          float* prow = p.part + ((int64_t)item.bh * PS + item.part) * (DH + 4);
+          float* prow = p.part + ((int64_t)(item.bh - NW) * PT + item.part) * (DH + 4);
           for (int d = lane; d < DH; d += 32) {
             float a = 0.f;
             for (int w = 0; w < NCW; ++w)
@@ -867,17 +879,17 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           __threadfence();
           __syncwarp();
           int last = 0;
-          if (lane == 0) last = atomicAdd(&p.part_cnt[item.bh], 1) == PS - 1 ? 1 : 0;
+          if (lane == 0) last = atomicAdd(&p.part_cnt[item.bh], 1) == PT - 1 ? 1 : 0;
           last = __shfl_sync(0xffffffffu, last, 0);
           finish = last != 0;
           if (finish) {
             __threadfence();
-            const float* pb = p.part + (int64_t)item.bh * PS * (DH + 4);
+            const float* pb = p.part + (int64_t)(item.bh - NW) * PT * (DH + 4);
             m = -INFINITY;
-            for (int j = 0; j < PS; ++j) m = fmaxf(m, __ldcg(pb + j * (DH + 4)));
+            for (int j = 0; j < PT; ++j) m = fmaxf(m, __ldcg(pb + j * (DH + 4)));
             l = 0.f;
             keys = 0;
-            for (int j = 0; j < PS; ++j) {
+            for (int j = 0; j < PT; ++j) {
               const float mj = __ldcg(pb + j * (DH + 4));
               if (mj != -INFINITY) l += __ldcg(pb + j * (DH + 4) + 1) * exp2f(mj - m);
               keys += __float_as_int(__ldcg(pb + j * (DH + 4) + 2));
@@ -885,7 +897,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
             const float inv = l > 0.f ? 1.f / l : 0.f;
             for (int d = lane; d < DH; d += 32) {
               float a = 0.f;
-              for (int j = 0; j < PS; ++j) {
+              for (int j = 0; j < PT; ++j) {
                 const float mj = __ldcg(pb + j * (DH + 4));
                 if (mj != -INFINITY) a += __ldcg(pb + j * (DH + 4) + 4 + d) * exp2f(mj - m);
               }

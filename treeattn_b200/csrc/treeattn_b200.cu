@@ -520,7 +520,7 @@ struct Decode {
   // Pipeline shape of the persistent kernel for 256-byte rows (bf16/f16 dh=128, f32 dh=64), which run one CTA
   // per SM: rows per stage, ring stages and consumer groups (compile-time; NST must be a multiple of NCG).
 #ifndef TA_MAX_PSPLIT
-#define TA_MAX_PSPLIT 2  // most parts per decode item (split items, persistent kernel); 1 turns splitting off
+#define TA_MAX_PSPLIT 8  // most parts per split decode item (persistent kernel); 1 turns splitting off
 #endif
 #ifndef TA_WIDE_CH
 #define TA_WIDE_CH 32
@@ -560,24 +560,31 @@ struct Decode {
     }
     const int items = p.B * p.H;
     const int gmax = per_sm * num_sms();
-    // With one CTA per SM (256-byte rows) a whole-item grid can leave SMs idle (e.g. 320 items: 3 per CTA on 107 of
-    // 148 SMs); cutting every item into S parts (window and leaf rows shared out, partials merged by the last
-    // part) spreads the same bytes over more SMs. S is the smallest of 1..TA_MAX_PSPLIT within 5 % of the best
-    // per-CTA load. Measured on the configuration-5 shape (320 items): S=1 204 us, S=2 177 us, S=3 195 us (every
-    // part repeats its item's descent and pipeline fill), hence the cap of 2.
+    // With one CTA per SM (256-byte rows) whole items leave the last round of CTAs part-empty (e.g. 320 items on 148
+    // SMs: 3 rounds, the third for 24 items). The items of that last round are cut into parts (window and leaf rows
+    // shared out, partial states merged by the last part to finish) spread over every CTA. Measured on the
+    // configuration-5 shape: whole items 204 us; every item in 2 / 3 parts 177 / 195 us (each part repeats its
+    // item's descent and pipeline fill); 296 whole items + the 24 others in 6 parts: see the decode profile.
     p.psplit = 1;
-    if (p.part && p.part_cnt && per_sm == 1) {
-      double best = 1e30;
-      int bs = 1;
-      for (int S = 1; S <= TA_MAX_PSPLIT; ++S) {
-        const double load = (double)((int64_t)items * S + gmax - 1) / gmax / S;  // items per CTA, rounded up
-        if (load < best * 0.95) { best = load; bs = S; }
+    p.n_whole = items;
+    int grid;
+    if (p.part && p.part_cnt && per_sm == 1 && items % gmax != 0) {
+      // full rounds of whole items, then the remaining `tail` items cut into PT parts each so that the last round
+      // spreads them over (nearly) every CTA: per CTA R whole items and at most one part of 1/PT item
+      const int R = items / gmax, tail = items - R * gmax;
+      const int PT = std::min(TA_MAX_PSPLIT, gmax / tail);
+      if (PT > 1 && (int64_t)tail * PT <= (int64_t)items * 4) {  // the scratch holds 4 parts per item
+        p.psplit = PT;
+        p.n_whole = R * gmax;
       }
-      p.psplit = bs;
     }
-    const int units = items * p.psplit;
-    const int per_cta = (units + gmax - 1) / gmax;  // units per CTA (equal for all but the last few)
-    const int grid = (units + per_cta - 1) / per_cta;
+    const int units = p.n_whole + (items - p.n_whole) * p.psplit;
+    if (p.psplit > 1) {
+      grid = std::min(units, gmax);  // unit u runs on CTA u % grid
+    } else {
+      const int per_cta = (units + gmax - 1) / gmax;  // units per CTA (equal for all but the last few)
+      grid = (units + per_cta - 1) / per_cta;
+    }
     if (p.psplit > 1)
       kern_split<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
     else
