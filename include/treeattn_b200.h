@@ -156,9 +156,14 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
                   int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, int32_t* perm_tmp,
                   uint8_t* valid_tmp, void* stream);
 
-/* ta_lane_order without caller scratch: the ping-pong slot order lives in a static device buffer of the library
- * (2^21 slots, P * C at most), found with cudaGetSymbolAddress, so the call allocates nothing. The buffer is shared:
- * calls must not overlap in time (one stream, or ordered by the caller). Same arguments and results otherwise. */
+/* No counterpart in the reference: ta_lane_order for callers that cannot allocate device memory - for instance a
+ * host program that reserved the GPU's memory up front for its own pool and hands the library only views into it,
+ * so that a cudaMalloc would fail or break its accounting. The build's second slot-order buffer is a static array
+ * inside the library (2^21 slots: P * C at most, 10 MiB held on every GPU that loads the library); the call itself
+ * calls no allocator. Larger P * C is rejected with TA_ERR_ARG. The first call on each device looks up the array's
+ * device address (once, with that device current); make that first call before any stream capture. All calls share
+ * the array (it is fully rewritten by each call, nothing needs clearing): calls that overlap on the GPU race, so
+ * order them (one stream, or events). Same arguments and results as ta_lane_order otherwise. */
 int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first,
                           int P, int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, void* stream);
 

@@ -1,5 +1,10 @@
-"""ta_lane_order_noalloc: the 2-means build's slot ordering with its scratch in the library's static device memory
-(cudaGetSymbolAddress) instead of caller buffers. It must give exactly ta_lane_order's result and allocate nothing."""
+"""ta_lane_order_noalloc: the dynamic tree's slot ordering for callers that cannot allocate device memory (a program
+that reserved the GPU's memory for its own pool and gives the library only views into it). Its scratch is a static
+array inside the library instead of a caller buffer; it must give ta_lane_order's result, call after call, and leave
+torch's allocator untouched.
+
+This file is collected last on purpose, so that a run stopping at its first failure has already run every other
+test; it also passes when run alone in a fresh process."""
 import ctypes
 
 import numpy as np
@@ -8,7 +13,7 @@ import torch
 
 
 def test_noalloc_rejects_oversize_without_gpu():
-    """More slots than the static scratch holds: TA_ERR_ARG before any CUDA call."""
+    """More slots than the static scratch holds: TA_ERR_ARG with a message, before any CUDA call."""
     from treeattn_b200 import _lib
     lib = _lib.load()
     buf = (ctypes.c_char * 64)()
@@ -18,27 +23,35 @@ def test_noalloc_rejects_oversize_without_gpu():
     assert rc == _lib.TA_ERR_ARG and 'static scratch' in _lib.last_error()
 
 
+def _inputs(rng, P, C, dh, dev):
+    keys = torch.as_tensor(rng.standard_normal((P, C, dh)).astype(np.float32)).to(dev)
+    n = torch.as_tensor(rng.integers(0, C + 1, P)).to(dev)
+    return keys, n
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize('P,C,dh', [(8, 1024, 64), (96, 512, 32), (3, 16384, 16)])
-def test_noalloc_matches_lane_order(P, C, dh):
+def test_noalloc_matches_lane_order_twice(P, C, dh):
+    """Two calls in a row on different inputs (the second sees the scratch the first left behind), each equal to
+    ta_lane_order with caller scratch; no torch allocation during either call."""
     from treeattn_b200 import _lib, _ops
     dev = 'cuda'
     rng = np.random.default_rng(C + dh)
-    keys = torch.as_tensor(rng.standard_normal((P, C, dh)).astype(np.float32)).to(dev)
-    n = torch.as_tensor(rng.integers(0, C + 1, P)).to(dev)
     D = C.bit_length() - 2
-    perm = torch.empty(P, C, device=dev, dtype=torch.int32)
-    valid = torch.empty(P, C, device=dev, dtype=torch.uint8)
-    pt, vt = torch.empty_like(perm), torch.empty_like(valid)
-    _lib.call('ta_lane_order', _ops._p(keys), 1, C * dh, _ops._p(n), 1, P, C, dh, 3, D, _ops._p(perm),
-              _ops._p(valid), _ops._p(pt), _ops._p(vt), _ops._stream(keys))
-    perm2 = torch.empty_like(perm)
-    valid2 = torch.empty_like(valid)
-    torch.cuda.synchronize()
-    before = torch.cuda.memory_allocated()
-    _lib.call('ta_lane_order_noalloc', _ops._p(keys), 1, C * dh, _ops._p(n), 1, P, C, dh, 3, D, _ops._p(perm2),
-              _ops._p(valid2), _ops._stream(keys))
-    torch.cuda.synchronize()
-    assert torch.cuda.memory_allocated() == before
-    assert torch.equal(perm, perm2) and torch.equal(valid, valid2)
+    for _ in range(2):
+        keys, n = _inputs(rng, P, C, dh, dev)
+        perm = torch.empty(P, C, device=dev, dtype=torch.int32)
+        valid = torch.empty(P, C, device=dev, dtype=torch.uint8)
+        pt, vt = torch.empty_like(perm), torch.empty_like(valid)
+        _lib.call('ta_lane_order', _ops._p(keys), 1, C * dh, _ops._p(n), 1, P, C, dh, 3, D, _ops._p(perm),
+                  _ops._p(valid), _ops._p(pt), _ops._p(vt), _ops._stream(keys))
+        perm2 = torch.full_like(perm, -7)
+        valid2 = torch.full_like(valid, 9)
+        torch.cuda.synchronize()
+        before = torch.cuda.memory_allocated()
+        _lib.call('ta_lane_order_noalloc', _ops._p(keys), 1, C * dh, _ops._p(n), 1, P, C, dh, 3, D, _ops._p(perm2),
+                  _ops._p(valid2), _ops._stream(keys))
+        torch.cuda.synchronize()
+        assert torch.cuda.memory_allocated() == before
+        assert torch.equal(perm, perm2) and torch.equal(valid, valid2)
     assert _ops.device_error()[0] == 0

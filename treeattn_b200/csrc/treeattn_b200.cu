@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/treeattn_b200.h"
@@ -649,11 +650,44 @@ int rows_dispatch(int dtype, int kind, const void* a0, const void* a1, const int
 }  // namespace
 
 // ================================================================================================== C ABI
-// Static scratch of ta_lane_order_noalloc: the ping-pong slot order of the 2-means build, in the module's own
-// device memory (no allocation per call). One build at a time may use it.
+// Scratch of ta_lane_order_noalloc, in the library's own device memory: the second slot-order buffer that the
+// 2-means build ping-pongs with the caller's output. 2^21 slots (P * C at most): 8 MiB of int32 + 2 MiB of flags,
+// held by every GPU that loads the library until the process exits. Every slot of it is written before it is read in
+// a call, so it never needs clearing; all calls share it, so calls that overlap on the GPU race.
 constexpr int64_t kLaneScratchSlots = int64_t(1) << 21;
-__device__ int32_t g_lane_perm_scratch[kLaneScratchSlots];
-__device__ uint8_t g_lane_valid_scratch[kLaneScratchSlots];
+static __device__ __align__(256) int32_t g_lane_perm_scratch[kLaneScratchSlots];
+static __device__ __align__(256) uint8_t g_lane_valid_scratch[kLaneScratchSlots];
+
+namespace {
+// Device addresses of the scratch, looked up once per device (with that device current) by the first
+// ta_lane_order_noalloc call made on it. In host code the arrays' names stand for host-side shadows, never for the
+// device memory, so only these addresses may reach a kernel.
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+int32_t* g_scratch_perm[kMaxDevices];
+uint8_t* g_scratch_valid[kMaxDevices];
+
+int lane_scratch(int32_t** perm, uint8_t** valid) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: no current device: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(TA_ERR_ARG, "ta_lane_order_noalloc: device %d above %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_perm[dev] || !g_scratch_valid[dev]) {
+    void* pa = nullptr;
+    void* va = nullptr;
+    e = cudaGetSymbolAddress(&pa, g_lane_perm_scratch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&va, g_lane_valid_scratch);
+    if (e != cudaSuccess || !pa || !va)
+      return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: scratch address on device %d: %s", dev, cudaGetErrorString(e));
+    g_scratch_perm[dev] = static_cast<int32_t*>(pa);
+    g_scratch_valid[dev] = static_cast<uint8_t*>(va);
+  }
+  *perm = g_scratch_perm[dev];
+  *valid = g_scratch_valid[dev];
+  return TA_OK;
+}
+}  // namespace
 
 extern "C" {
 
@@ -974,19 +1008,19 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
   return TA_OK;
 }
 
+// ta_lane_order for callers that may not allocate device memory: the second ping-pong buffer is the library's
+// static scratch above instead of a caller buffer. The first call on a device looks the scratch up (once).
 int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first,
                           int P, int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, void* stream) {
   g_err.clear();
   if (P < 0 || C < 0 || (int64_t)P * C > kLaneScratchSlots)
     return fail(TA_ERR_ARG, "ta_lane_order_noalloc: P*C=%lld slots exceed the static scratch of %lld",
                 (long long)P * C, (long long)kLaneScratchSlots);
-  void* pt = nullptr;
-  void* vt = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(&pt, g_lane_perm_scratch);
-  if (e == cudaSuccess) e = cudaGetSymbolAddress(&vt, g_lane_valid_scratch);
-  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: scratch address: %s", cudaGetErrorString(e));
-  return ta_lane_order(keys, key_lane_div, key_stride, n, first, P, C, dh, iters, levels, perm, valid,
-                       static_cast<int32_t*>(pt), static_cast<uint8_t*>(vt), stream);
+  int32_t* pt = nullptr;
+  uint8_t* vt = nullptr;
+  if (int r = lane_scratch(&pt, &vt)) return r;
+  return ta_lane_order(keys, key_lane_div, key_stride, n, first, P, C, dh, iters, levels, perm, valid, pt, vt,
+                       stream);
 }
 
 int ta_lane_sums(const float* keys, int64_t key_lane_div, int64_t key_stride, const int32_t* perm,
