@@ -168,6 +168,33 @@ def test_greedy_graph_matches_eager():
     assert torch.equal(toks[0], toks[1])
 
 
+def test_serve_step_matches_greedy_steps():
+    """serve_step (tokens host -> device, the step's graph, next tokens device -> host; and the eager form without
+    graphs) returns the tokens the device greedy loop produces, step after step."""
+    from treeattn_b200.engine import Decoder, weights_from_ours
+    from treeattn_b200.model import GPT
+    cfg = tiny(seq_len=256, n_embd=64, wmax=4, beam=4, local=16, leaf=8)
+    torch.manual_seed(12)
+    m = GPT(cfg).eval()
+    W = weights_from_ours(m.state_dict(), cfg)
+    idx = torch.randint(0, 64, (4, 100), device=DEV)
+    ref = Decoder(W, cfg.n_layer, cfg.n_head, cfg.n_embd, 256, 'seg', cfg, DEV, batch=4)
+    ref.prefill(idx)
+    want = []
+    for _ in range(30):
+        ref.greedy_steps(1)
+        want.append(ref.tokens.cpu().clone())
+    for graphs in (True, False):
+        dec = Decoder(W, cfg.n_layer, cfg.n_head, cfg.n_embd, 256, 'seg', cfg, DEV, batch=4, graphs=graphs)
+        dec.prefill(idx)
+        host = torch.empty(4, dtype=torch.int64, pin_memory=True)
+        host.copy_(dec.tokens.cpu())
+        for i in range(30):
+            dec.serve_step(host, out=host)
+            assert torch.equal(host, want[i]), (graphs, i)
+        assert int(dec.positions[0]) == 130
+
+
 def test_past_is_covered_exactly():
     """Reference test_seg.test_past_is_covered_exactly: with a wide beam the tree keys plus the static keys
     cover [0, t] exactly and nothing later."""
