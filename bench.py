@@ -724,15 +724,18 @@ def run_reference(a, rank, world):
     if rank != 0:
         return
     warm = max(0, a.warmup)
-    value, steps, threads = cpu_decode_sample(max(5.0, a.cpu_seconds), seed=1)
+    value, steps, threads, how = cpu_decode_sample(max(5.0, a.cpu_seconds), seed=1)
+    M = CFG4
     line = dict(metric=METRIC, value=value, unit='tokens/s', n_gpus=world, steps=a.steps, warmup=warm,
                 ms_per_step=1000.0 / value, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
                 data='synthetic', impl='reference',
-                config=dict(workload='config 4 decode, CPU oracle (numpy restatement of the reference engine), '
-                                     'batch 1 sample', global_batch=1, seq_len=4096, parallelism='none'),
+                config=dict(workload='config %s: KV-cache decode, %dx%d GPT bf16 (%d heads, vocab %d), batch '
+                                     '%d/GPU, context %d, leaf %d, top-%d, window %d' % (
+                                         M.name, M.NL, M.C, M.H, M.V, M.batch, M.prompt, M.leaf, M.topk, M.window),
+                            global_batch=M.batch * world, seq_len=M.prompt,
+                            parallelism='the CPU oracle (numpy restatement of the reference engine) on rank 0'),
                 cpu_baseline=dict(value=value, unit='tokens/s', cores=threads, kind='port',
-                                  sample='%d greedy decode steps of 1 sequence at t~4096 (12 layers + lm_head), '
-                                         'fp32 numpy, cache filled with random K/V' % steps),
+                                  sample='%s (12 layers + lm_head), fp32 numpy, cache filled with random K/V' % how),
                 e2e=dict(value=value, unit='tokens/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
