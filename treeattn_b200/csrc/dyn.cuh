@@ -708,7 +708,7 @@ __global__ void __launch_bounds__(128) lane_select_kernel(LaneSelectParams p) {
     const int64_t floor_b = nL < lo ? 2 : 1;
     int64_t b_tree = nL >= L ? 0 : (need > floor_b ? need : floor_b);
     b_tree = b_tree < p.wmax ? b_tree : p.wmax;
-    const int nk = lane_descend<DH>(sums, cnt, p.D, p.wmax, sc, lane);
+    const int nk = lane_descend<DH, false>(sums, cnt, p.D, p.wmax, sc, lane);  // the tree changes as the loop runs
     for (int x = lane; x < wl; x += 32) {
       const bool ok = x < nk;
       int32_t s0 = -1, s1 = -1;

@@ -680,8 +680,9 @@ struct LaneSearchParams {
 };
 
 // The descent of one query (in sc.qf) over one lane's packed tree; the kept level-D nodes end in sc.kid / sc.ksc,
-// best first. Returns how many are valid.
-template <int DH>
+// best first. Returns how many are valid. NC: node rows through the read-only (non-coherent) path - only for a tree
+// that no thread writes while the kernel runs (the select loop updates its trees, so it reads them coherently).
+template <int DH, bool NC = true>
 __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cnt, int D, int wmax,
                                             DescentScratch& sc, int lane) {
   if (lane == 0) sc.kid[0] = 0;
@@ -715,7 +716,8 @@ __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cn
 #pragma unroll
         for (int cc = 0; cc < DH / 4; ++cc) {
           const float4 qv = *reinterpret_cast<const float4*>(sc.qf + cc * 4);
-          const float4 v = __ldg(reinterpret_cast<const float4*>(row + cc * 4));
+          const float4 v = NC ? __ldg(reinterpret_cast<const float4*>(row + cc * 4))
+                              : *reinterpret_cast<const float4*>(row + cc * 4);
           if (cc & 1) {
             a1 = fmaf(qv.x, v.x, a1); a1 = fmaf(qv.y, v.y, a1); a1 = fmaf(qv.z, v.z, a1); a1 = fmaf(qv.w, v.w, a1);
           } else {
