@@ -15,8 +15,9 @@
 //  * lane_sums_kernel: the slots of the built tree and its node sums / counts bottom-up in adjacent pairs.
 //  * lane_insert_kernel: dyntree.py:83-106, one warp per lane.
 //  * lane_select_kernel: dyntree.py:150-243 select_keys, one warp per lane walking the lane's tokens in order:
-//    neighbour rescoring, beam descent (lane_descend, shared with ta_lane_search), insertion; the tree stays in
-//    global memory (L2) and is updated in place.
+//    neighbour rescoring, beam descent (lane_descend_t, shared with ta_lane_search), insertion; the tree's upper
+//    levels are copied to shared memory for the loop and written back after it, the rest is updated in place in
+//    global memory (L2).
 #pragma once
 #include "select.cuh"
 
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(512) lane_sums_kernel(LaneSumsParams p) {
 // scores higher against it (kv . sum / count; -1e9 when empty, -inf when full; ties left), and the first free slot
 // of the last group. kv in shared memory (DH floats). The warp's writes are ordered before its later reads.
 template <int DH>
-__device__ __forceinline__ void lane_insert_warp(float* sums, int32_t* cnt, int32_t* slot, const float* kv, int D,
+__device__ __forceinline__ void lane_insert_warp(const LaneTreeRef<DH>& tr, int32_t* slot, const float* kv, int D,
                                                  int C, int32_t kpos, int lane) {
   constexpr int NJ = (DH + 31) / 32;
   float k[NJ];
@@ -536,18 +537,18 @@ __device__ __forceinline__ void lane_insert_warp(float* sums, int32_t* cnt, int3
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
     const int d = lane + 32 * j;
-    if (d < DH) sums[d] += k[j];
+    if (d < DH) tr.row(0)[d] += k[j];
   }
-  if (lane == 0) cnt[0] += 1;
+  if (lane == 0) *tr.cntp(0) += 1;
   __syncwarp();
   int node = 0;
   for (int lvl = 0; lvl < D; ++lvl) {
     const int o = (2 << lvl) - 1;
     const int left = 2 * node, right = left + 1;
     const int cap = C >> (lvl + 1);
-    const int cL = cnt[o + left], cR = cnt[o + right];
-    const float* SL = sums + (int64_t)(o + left) * DH;
-    const float* SR = sums + (int64_t)(o + right) * DH;
+    const int cL = tr.cnt(o + left), cR = tr.cnt(o + right);
+    const float* SL = tr.row(o + left);
+    const float* SR = tr.row(o + right);
     float pl = 0.f, pr = 0.f;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
@@ -565,13 +566,13 @@ __device__ __forceinline__ void lane_insert_warp(float* sums, int32_t* cnt, int3
     if (cR == 0) sR = -1e9f;
     if (cR >= cap) sR = -INFINITY;
     node = sR > sL ? right : left;
-    float* dst = sums + (int64_t)(o + node) * DH;
+    float* dst = tr.row(o + node);
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
       const int d = lane + 32 * j;
       if (d < DH) dst[d] += k[j];
     }
-    if (lane == 0) cnt[o + node] += 1;
+    if (lane == 0) *tr.cntp(o + node) += 1;
     __syncwarp();
   }
   if (lane == 0) {
@@ -600,8 +601,8 @@ __global__ void __launch_bounds__(128) lane_insert_kernel(LaneInsertParams p) {
   const int NN = (2 << p.D) - 1;
   for (int d = lane; d < DH; d += 32) kb[warp][d] = p.kv[pl * DH + d];
   __syncwarp();
-  lane_insert_warp<DH>(p.sums + pl * (int64_t)NN * DH, p.cnt + pl * (int64_t)NN, p.slot + pl * (int64_t)p.C,
-                       kb[warp], p.D, p.C, (int32_t)p.kpos[pl], lane);
+  const LaneTreeRef<DH> tr{p.sums + pl * (int64_t)NN * DH, p.cnt + pl * (int64_t)NN, nullptr, nullptr, 0};
+  lane_insert_warp<DH>(tr, p.slot + pl * (int64_t)p.C, kb[warp], p.D, p.C, (int32_t)p.kpos[pl], lane);
 }
 
 // ------------------------------------------------------------------------------------------------ select
@@ -621,8 +622,20 @@ struct LaneSelectParams {
   int64_t* nb_leaves;      // (B, H, T)
 };
 
+// Rows of a lane's tree that the select loop keeps in shared memory: the upper levels, about 16 KB per warp (every
+// token's descent and insertion passes through them, and the insertion rewrites one node per level).
+template <int DH>
+__host__ __device__ constexpr int lane_cache_rows() {
+  return DH <= 16 ? 255 : DH <= 32 ? 127 : DH <= 64 ? 63 : 31;
+}
+template <int DH>
+__host__ __device__ constexpr size_t lane_select_smem_bytes() {
+  return (size_t)4 * lane_cache_rows<DH>() * (DH * sizeof(float) + sizeof(int32_t));
+}
+
 template <int DH>
 __global__ void __launch_bounds__(128) lane_select_kernel(LaneSelectParams p) {
+  extern __shared__ __align__(16) unsigned char lane_cache_smem[];
   __shared__ DescentScratch scr[4];
   __shared__ __align__(16) float kb[4][DH];
   __shared__ int32_t ring_id[4][32];
@@ -641,6 +654,16 @@ __global__ void __launch_bounds__(128) lane_select_kernel(LaneSelectParams p) {
   int32_t* cnt = p.cnt + pl * (int64_t)NN;
   int32_t* slot = p.slot + pl * (int64_t)C;
   const int W = p.Wn * p.NS, wl = p.wl;
+  // the upper levels of this lane's tree move to shared memory for the loop and back to global memory after it
+  constexpr int NSR = lane_cache_rows<DH>();
+  const int ns = NN < NSR ? NN : NSR;
+  float* s_sums = reinterpret_cast<float*>(lane_cache_smem) + warp * NSR * DH;
+  int32_t* s_cnt = reinterpret_cast<int32_t*>(lane_cache_smem + (size_t)4 * NSR * DH * sizeof(float)) + warp * NSR;
+  for (int e = lane; e < ns * (DH / 4); e += 32)
+    reinterpret_cast<float4*>(s_sums)[e] = reinterpret_cast<const float4*>(sums)[e];
+  for (int r = lane; r < ns; r += 32) s_cnt[r] = cnt[r];
+  const LaneTreeRef<DH> tr{sums, cnt, s_sums, s_cnt, ns};
+  __syncwarp();
   ring_ok[warp][lane] = 0;
   ring_id[warp][lane] = 0;
   ring_sc[warp][lane] = 0.f;
@@ -668,8 +691,8 @@ __global__ void __launch_bounds__(128) lane_select_kernel(LaneSelectParams p) {
     }
     bool m = false;
     if (ok0) {
-      const int cn = cnt[offD + id];
-      const float* nrow = sums + (int64_t)(offD + id) * DH;
+      const int cn = tr.cnt(offD + id);
+      const float* nrow = tr.row(offD + id);
       float a0 = 0.f, a1 = 0.f;
 #pragma unroll
       for (int cc = 0; cc < DH / 4; ++cc) {
@@ -708,7 +731,7 @@ __global__ void __launch_bounds__(128) lane_select_kernel(LaneSelectParams p) {
     const int64_t floor_b = nL < lo ? 2 : 1;
     int64_t b_tree = nL >= L ? 0 : (need > floor_b ? need : floor_b);
     b_tree = b_tree < p.wmax ? b_tree : p.wmax;
-    const int nk = lane_descend<DH, false>(sums, cnt, p.D, p.wmax, sc, lane);  // the tree changes as the loop runs
+    const int nk = lane_descend_t<DH, false>(tr, p.D, p.wmax, sc, lane);  // the tree changes as the loop runs
     for (int x = lane; x < wl; x += 32) {
       const bool ok = x < nk;
       int32_t s0 = -1, s1 = -1;
@@ -731,9 +754,12 @@ __global__ void __launch_bounds__(128) lane_select_kernel(LaneSelectParams p) {
     }
     __syncwarp();
     // (3) the token's key joins the tree (the sink, position 0, never does)
-    if (t >= 1) lane_insert_warp<DH>(sums, cnt, slot, kb[warp], p.D, C, t, lane);
+    if (t >= 1) lane_insert_warp<DH>(tr, slot, kb[warp], p.D, C, t, lane);
     __syncwarp();
   }
+  for (int e = lane; e < ns * (DH / 4); e += 32)
+    reinterpret_cast<float4*>(sums)[e] = reinterpret_cast<const float4*>(s_sums)[e];
+  for (int r = lane; r < ns; r += 32) cnt[r] = s_cnt[r];
 }
 
 }  // namespace ta

@@ -679,15 +679,33 @@ struct LaneSearchParams {
   float* sct;          // (P, wl) scores (-inf invalid), may be null
 };
 
+// A lane's packed tree (row r = node r in level order): rows [0, ns) in shared memory (a cached copy of the upper
+// levels), the others in global memory. Rows and counts are reached through generic pointers.
+template <int DH>
+struct LaneTreeRef {
+  float* g;
+  int32_t* gc;
+  float* s;
+  int32_t* sc;
+  int ns;
+  __device__ __forceinline__ float* row(int r) const { return r < ns ? s + (size_t)r * DH : g + (int64_t)r * DH; }
+  __device__ __forceinline__ int32_t* cntp(int r) const { return r < ns ? sc + r : gc + r; }
+  __device__ __forceinline__ int cnt(int r) const { return *cntp(r); }
+};
+
 // The descent of one query (in sc.qf) over one lane's packed tree; the kept level-D nodes end in sc.kid / sc.ksc,
 // best first. Returns how many are valid. NC: node rows through the read-only (non-coherent) path - only for a tree
 // that no thread writes while the kernel runs (the select loop updates its trees, so it reads them coherently).
 template <int DH, bool NC = true>
 __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cnt, int D, int wmax,
-                                            DescentScratch& sc, int lane) {
+                                            DescentScratch& sc, int lane);
+
+template <int DH, bool NC>
+__device__ __forceinline__ int lane_descend_t(const LaneTreeRef<DH>& tr, int D, int wmax, DescentScratch& sc,
+                                              int lane) {
   if (lane == 0) sc.kid[0] = 0;
   __syncwarp();
-  int nk = cnt[0] > 0 ? 1 : 0;
+  int nk = tr.cnt(0) > 0 ? 1 : 0;
   int w = 1;
   for (int l = 1; l <= D; ++l) {
     const int off = (1 << l) - 1;
@@ -699,7 +717,7 @@ __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cn
       if (j < 2 * nk) {
         const int m = sc.kid[j >> 1];
         c = 2 * m + (j & 1);
-        if (cnt[off + c] <= 0) c = -1;
+        if (tr.cnt(off + c) <= 0) c = -1;
       }
       const unsigned mask = __ballot_sync(0xffffffffu, c >= 0);
       if (c >= 0) sc.cid[n + __popc(mask & ((1u << lane) - 1u))] = c;
@@ -711,7 +729,7 @@ __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cn
       const int j = base + lane;
       if (j < n) {
         const int c = sc.cid[j];
-        const float* row = sums + (int64_t)(off + c) * DH;
+        const float* row = tr.row(off + c);
         float a0 = 0.f, a1 = 0.f;
 #pragma unroll
         for (int cc = 0; cc < DH / 4; ++cc) {
@@ -724,7 +742,7 @@ __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cn
             a0 = fmaf(qv.x, v.x, a0); a0 = fmaf(qv.y, v.y, a0); a0 = fmaf(qv.z, v.z, a0); a0 = fmaf(qv.w, v.w, a0);
           }
         }
-        const float s = (a0 + a1) / (float)cnt[off + c];
+        const float s = (a0 + a1) / (float)tr.cnt(off + c);
         sc.csc[j] = s;
         sc.ckey[j] = order_key(s, c);
       }
@@ -735,6 +753,13 @@ __device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cn
   }
   __syncwarp();
   return nk;
+}
+
+template <int DH, bool NC>
+__device__ __forceinline__ int lane_descend(const float* sums, const int32_t* cnt, int D, int wmax,
+                                            DescentScratch& sc, int lane) {
+  const LaneTreeRef<DH> tr{const_cast<float*>(sums), const_cast<int32_t*>(cnt), nullptr, nullptr, 0};
+  return lane_descend_t<DH, NC>(tr, D, wmax, sc, lane);
 }
 
 template <int DH>

@@ -386,7 +386,15 @@ struct LaneSelect {
   static int run(ta::LaneSelectParams p, cudaStream_t st) {
     const int64_t P = (int64_t)p.B * p.H * p.nl;
     if (P == 0) return TA_OK;
-    ta::lane_select_kernel<DH><<<(unsigned)((P + 3) / 4), 128, 0, st>>>(p);
+    constexpr size_t smem = ta::lane_select_smem_bytes<DH>();
+    static bool attr_set = false;
+    if (!attr_set) {
+      if (cudaFuncSetAttribute(ta::lane_select_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+        return check_launch("ta_lane_select (shared memory attribute)");
+      attr_set = true;
+    }
+    ta::lane_select_kernel<DH><<<(unsigned)((P + 3) / 4), 128, smem, st>>>(p);
     return check_launch("ta_lane_select");
   }
 };
