@@ -186,11 +186,18 @@ struct TwoMeans {
     bool ok[U];
     int s_of[U];
 
-    // (0) count the valid keys. With at most two there is nothing to cluster: the split is one key per side (in
-    // either orientation, both keys being equally far from their mean) and the 2-means passes are skipped.
-    int nv = 0;
-    for (int r = tid; r < S; r += TEAM) nv += valid[r] ? 1 : 0;
+    // (0) count the valid keys and find the end of the last one: the passes below stop there (the builds keep each
+    // group's valid slots in front, so the slots past Se are empty). With at most two keys there is nothing to
+    // cluster: the split is one key per side (in either orientation, both keys being equally far from their mean)
+    // and the 2-means passes are skipped.
+    int nv = 0, vend = 0;
+    for (int r = tid; r < S; r += TEAM)
+      if (valid[r]) {
+        ++nv;
+        vend = r + 1;
+      }
     const int ng = team_int(warp_isum(nv), redi, w, lane, bid);
+    const int Se = (int)team_kmax(warp_kmax((unsigned long long)vend), redk, w, lane, bid);
     if (ng <= 2) {
       for (int r = tid; r < S; r += TEAM)
         skey[r] = ((unsigned long long)(valid[r] ? 0u : 0xffffffffu) << 32) | (uint32_t)r;
@@ -199,7 +206,7 @@ struct TwoMeans {
     float acc[8];
 #pragma unroll
     for (int d = 0; d < 8; ++d) acc[d] = 0.f;
-    for (int b = w * RPW * U; b < S; b += STEP) {
+    for (int b = w * RPW * U; b < Se; b += STEP) {
       load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
 #pragma unroll
       for (int u = 0; u < U; ++u)
@@ -217,7 +224,7 @@ struct TwoMeans {
         float ref[8];
         load_vec(pass == 0 ? mean : c0, sub, ref);
         unsigned long long best = 0;
-        for (int b = w * RPW * U; b < S; b += STEP) {
+        for (int b = w * RPW * U; b < Se; b += STEP) {
           load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
           float v[U];
 #pragma unroll
@@ -258,7 +265,7 @@ struct TwoMeans {
 #pragma unroll
         for (int d = 0; d < 8; ++d) { a0[d] = 0.f; a1[d] = 0.f; }
         int n0 = 0, n1 = 0;
-        for (int b = w * RPW * U; b < S; b += STEP) {
+        for (int b = w * RPW * U; b < Se; b += STEP) {
           load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
           float xx[U], d0[U], d1[U];
 #pragma unroll
@@ -309,7 +316,7 @@ struct TwoMeans {
     {
       float df[8];
       load_vec(diff, sub, df);
-      for (int b = w * RPW * U; b < S; b += STEP) {
+      for (int b = w * RPW * U; b < Se; b += STEP) {
         load_rows(keys, perm, valid, S, b, slot, sub, x, ok, s_of);
         float v[U];
 #pragma unroll
@@ -326,16 +333,20 @@ struct TwoMeans {
             hi = asc_bits(t);
             if (hi == 0xffffffffu) hi = 0xfffffffeu;  // a NaN projection still sorts before the empty slots
           }
-          if (sub == 0 && s_of[u] < S) skey[s_of[u]] = ((unsigned long long)hi << 32) | (uint32_t)s_of[u];
+          if (sub == 0 && s_of[u] < Se) skey[s_of[u]] = ((unsigned long long)hi << 32) | (uint32_t)s_of[u];
         }
       }
+      for (int r = Se + tid; r < S; r += TEAM) skey[r] = (0xffffffffull << 32) | (uint32_t)r;
     }
     }
     team_sync<NW>(bid);
-    // bitonic sort, ascending
-    for (int kk = 2; kk <= S; kk <<= 1) {
+    // bitonic sort, ascending, of the first Sp keys (the power of two that covers Se): the keys past it are empty
+    // slots in slot order, above every key before them, so they are in place already
+    int Sp = 2;
+    while (Sp < Se) Sp <<= 1;
+    for (int kk = 2; kk <= Sp; kk <<= 1) {
       for (int j = kk >> 1; j > 0; j >>= 1) {
-        for (int i = tid; i < S; i += TEAM) {
+        for (int i = tid; i < Sp; i += TEAM) {
           const int ixj = i ^ j;
           if (ixj > i) {
             const unsigned long long a = skey[i], b = skey[ixj];
@@ -433,8 +444,13 @@ __device__ __forceinline__ void subtree_level(const float* stage, const int32_t*
   }
 }
 
+// Three CTAs per SM: the register cap that keeps the 2-means passes at 80 registers (uncapped they take 128 and
+// only two CTAs fit, which costs more than it gains in this latency-bound kernel).
+#ifndef TA_SUBTREE_MINB
+#define TA_SUBTREE_MINB 3
+#endif
 template <int DH>
-__global__ void __launch_bounds__(256) lane_subtree_kernel(LaneSplitParams p, int levels) {
+__global__ void __launch_bounds__(256, TA_SUBTREE_MINB) lane_subtree_kernel(LaneSplitParams p, int levels) {
   extern __shared__ __align__(16) unsigned char split_smem[];
   const int S0 = p.C >> p.lvl;
   const GroupRef g = group_ref(p, blockIdx.x);
