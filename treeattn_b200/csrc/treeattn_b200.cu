@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -55,6 +56,51 @@ bool valid_dtype(int dtype) { return dtype == TA_F32 || dtype == TA_BF16 || dtyp
 bool valid_dh(int dh) { return dh == 16 || dh == 32 || dh == 64 || dh == 128; }
 
 cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Per-device state of one launcher. cudaFuncSetAttribute and the occupancy and SM-count queries answer for the
+// current device only, so a process that drives several GPUs keeps one entry per device (the first 64 devices
+// are cached; others are asked again on every call).
+constexpr int kDevCache = 64;
+
+int current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  return dev;
+}
+
+// The dynamic shared-memory size a call site has allowed for its kernel, per device (0 = not yet).
+struct SmemAttr {
+  std::atomic<size_t> bytes[kDevCache];
+};
+
+// Allow `bytes` of dynamic shared memory for kern on the current device. The attribute is always set to the most
+// the device gives one block beside the kernel's static shared memory: a kernel launched from several call sites
+// (or launcher instantiations) then never has its limit lowered by one of them under another's launch.
+template <typename K>
+int allow_smem(SmemAttr& a, K* kern, size_t bytes, const char* what) {
+  const int dev = current_device();
+  const bool cached = dev >= 0 && dev < kDevCache;
+  if (cached) {
+    const size_t have = a.bytes[dev].load(std::memory_order_relaxed);
+    if (have >= bytes) return TA_OK;
+    if (have != 0) return fail(TA_ERR_ARG, "%s: %zu B of dynamic shared memory, above the %zu B a block can have",
+                               what, bytes, have);
+  }
+  int optin = 0;
+  cudaFuncAttributes fa;
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev < 0 ? 0 : dev) != cudaSuccess ||
+      cudaFuncGetAttributes(&fa, kern) != cudaSuccess)
+    return check_launch(what);
+  const size_t most = (size_t)optin > fa.sharedSizeBytes ? (size_t)optin - fa.sharedSizeBytes : 0;
+  if (bytes > most)
+    return fail(TA_ERR_ARG, "%s: %zu B of dynamic shared memory, above the %zu B a block can have", what, bytes, most);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    return fail(TA_ERR_CUDA, "%s: dynamic shared memory limit of %zu B refused: %s", what, most, cudaGetErrorString(e));
+  }
+  if (cached) a.bytes[dev].store(most, std::memory_order_relaxed);
+  return TA_OK;
+}
 
 // Dispatch F<T, DH>::run(args...) over the runtime dtype and head dim.
 template <template <typename, int> class F, typename T, typename... Args>
@@ -121,12 +167,8 @@ struct BuildLevels {
       const bool aligned = (reinterpret_cast<uintptr_t>(nodes) & 15u) == 0 && (n_sb * 4) % 16 == 0 &&
                            (n_sh * 4) % 16 == 0;
       if (aligned && smem <= 200 * 1024 && (int64_t)B * H <= 0x7fffffff) {
-        static size_t smem_set = 0;
-        if (smem > 48 * 1024 && smem > smem_set) {
-          cudaFuncSetAttribute(ta::build_upper_levels_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               200 * 1024);
-          smem_set = 200 * 1024;
-        }
+        static SmemAttr smem_attr;
+        if (int r = allow_smem(smem_attr, ta::build_upper_levels_smem_kernel, smem, "ta_build_levels(upper)")) return r;
         if (B * H > 0)
           ta::build_upper_levels_smem_kernel<<<(unsigned)(B * H), 256, smem, st>>>(nodes, n_sb, n_sh, H, DH, lv, T_len);
       } else {
@@ -180,11 +222,8 @@ struct Select {
     while (warps > 1 && smem_for(warps) > 200 * 1024) warps >>= 1;
     const size_t smem = smem_for(warps);
     if (smem > 200 * 1024) return fail(TA_ERR_ARG, "ta_select: wmax %d too large for head dim %d", p.wmax, DH);
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(ta::select_kernel<QT, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      attr_set = true;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, ta::select_kernel<QT, DH>, smem, "ta_select")) return r;
     const int64_t nq = (int64_t)p.B * p.H * p.Nq;
     if (nq == 0) return TA_OK;
     ta::select_kernel<QT, DH><<<(unsigned)((nq + warps - 1) / warps), warps * 32, smem, st>>>(p);
@@ -195,12 +234,8 @@ struct Select {
   static int tile(ta::SelectParams p, cudaStream_t st, int rmax) {
     auto kern = ta::select_tile_kernel<QT, DH, W>;
     const size_t smem = ta::select_tile_smem_bytes<DH>(rmax);
-    static size_t smem_set = 0;
-    if (smem > smem_set) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return check_launch("ta_select (shared memory attribute)");
-      smem_set = smem;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, kern, smem, "ta_select")) return r;
     if ((int64_t)p.B * p.H == 0 || p.Nq == 0) return TA_OK;
     const dim3 grid((unsigned)((p.Nq + ta::TS_QT - 1) / ta::TS_QT), (unsigned)(p.B * p.H), 1);
     kern<<<grid, ta::TS_THREADS, smem, st>>>(p);
@@ -259,12 +294,8 @@ struct Prefill {
                  cudaStream_t st) {
     auto kern = ta::prefill_tile_kernel<T, DH, NS>;
     const size_t smem = ta::prefill_smem_bytes<DH, NS>(p.leaf_words, p.tile_words);
-    static size_t smem_set = 0;
-    if (smem > smem_set) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return check_launch("ta_prefill_attn (shared memory attribute)");
-      smem_set = smem;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, kern, smem, "ta_prefill_attn")) return r;
     const int64_t grid = (int64_t)p.B * p.H * p.n_qtiles;
     kern<<<(unsigned)grid, ta::PF_THREADS, smem, st>>>(mq, mk, mv, p);
     return check_launch("ta_prefill_attn");
@@ -329,11 +360,13 @@ struct LaneSplit {
     if (groups == 0) return TA_OK;
     if (S > ta::SUBTREE_SLOTS) {
       const size_t smem = ta::SplitSmem<8, DH>::bytes(S);
-      cudaFuncSetAttribute(ta::lane_split_cta_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      static SmemAttr smem_attr;
+      if (int r = allow_smem(smem_attr, ta::lane_split_cta_kernel<DH>, smem, "ta_lane_order")) return r;
       ta::lane_split_cta_kernel<DH><<<(unsigned)groups, 256, smem, st>>>(p);
     } else {
       const size_t smem = ta::Subtree<DH>::bytes(S);
-      cudaFuncSetAttribute(ta::lane_subtree_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      static SmemAttr smem_attr;
+      if (int r = allow_smem(smem_attr, ta::lane_subtree_kernel<DH>, smem, "ta_lane_order")) return r;
       ta::lane_subtree_kernel<DH><<<(unsigned)groups, 256, smem, st>>>(p, levels_left);
     }
     return check_launch("ta_lane_order");
@@ -346,7 +379,8 @@ struct ForestLevels {
     if (p.P == 0) return TA_OK;
     const size_t smem = (size_t)3 * p.B / 2 * DH * sizeof(float);
     if (smem > 200 * 1024) return fail(TA_ERR_ARG, "ta_forest_levels: blocks of %d keys need %zu B of shared memory", p.B, smem);
-    cudaFuncSetAttribute(ta::forest_levels_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, ta::forest_levels_kernel<T, DH>, smem, "ta_forest_levels")) return r;
     ta::forest_levels_kernel<T, DH><<<(unsigned)p.P, 256, smem, st>>>(p);
     return check_launch("ta_forest_levels");
   }
@@ -387,13 +421,8 @@ struct LaneSelect {
     const int64_t P = (int64_t)p.B * p.H * p.nl;
     if (P == 0) return TA_OK;
     constexpr size_t smem = ta::lane_select_smem_bytes<DH>();
-    static bool attr_set = false;
-    if (!attr_set) {
-      if (cudaFuncSetAttribute(ta::lane_select_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess)
-        return check_launch("ta_lane_select (shared memory attribute)");
-      attr_set = true;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, ta::lane_select_kernel<DH>, smem, "ta_lane_select")) return r;
     ta::lane_select_kernel<DH><<<(unsigned)((P + 3) / 4), 128, smem, st>>>(p);
     return check_launch("ta_lane_select");
   }
@@ -415,12 +444,8 @@ struct GatherDotBlocks {
     const size_t smem = (size_t)p.nb_cta * p.blk * DH * sizeof(T);
     if (smem > 200 * 1024)
       return fail(TA_ERR_ARG, "ta_gather_dot_blocks: nb_cta*blk rows need %zu B of shared memory (max 200 KiB)", smem);
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(ta::gather_dot_blocks_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           200 * 1024);
-      attr_set = true;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, ta::gather_dot_blocks_kernel<T, DH>, smem, "ta_gather_dot_blocks")) return r;
     const int groups = ta::ceil_div(p.nblk, p.nb_cta);
     const int64_t grid = (int64_t)p.B * p.H * groups;
     if (grid == 0) return TA_OK;
@@ -444,12 +469,9 @@ struct GatherDotBlocks {
 template <typename T, int DH>
 struct Append {
   static int run(ta::AppendParams p, cudaStream_t st) {
-    static bool attr_set = false;
     const size_t smem = ta::APPEND_SMEM_FLOATS * sizeof(float);
-    if (!attr_set) {
-      cudaFuncSetAttribute(ta::append_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_set = true;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, ta::append_kernel<T, DH>, smem, "ta_append")) return r;
     if (p.B * p.H == 0) return TA_OK;
     ta::append_kernel<T, DH><<<p.B * p.H, ta::APPEND_THREADS, smem, st>>>(p);
     return check_launch("ta_append");
@@ -465,16 +487,20 @@ struct DecodeShape {
   static constexpr int NCW = 4;
 };
 
-int g_num_sms = 0;
+std::atomic<int> g_num_sms[kDevCache];
 
 int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
+  const int dev = current_device();
+  const bool cached = dev >= 0 && dev < kDevCache;
+  int n = cached ? g_num_sms[dev].load(std::memory_order_relaxed) : 0;
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev < 0 ? 0 : dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    if (cached) g_num_sms[dev].store(n, std::memory_order_relaxed);
   }
-  return g_num_sms;
+  return n;
 }
 
 // Decode mode for B*H (b, h) pairs of row_bytes-wide K/V rows: -1 = persistent pipelined kernel (enough pairs
@@ -504,11 +530,8 @@ struct Decode {
     if (smem > 220 * 1024) return fail(TA_ERR_ARG, "ta_decode_step: %zu B of shared memory needed", smem);
     constexpr int RING_FLOATS = (int)(ta::DecodeCfg<T, DH, Sh::CH, Sh::NST, Sh::NCW>::RING_BYTES / sizeof(float));
     if ((1 << p.lv.L0) > RING_FLOATS) return fail(TA_ERR_ARG, "ta_decode_step: leaf block too large");
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      attr_set = true;
-    }
+    static SmemAttr smem_attr;
+    if (int r = allow_smem(smem_attr, kern, smem, "ta_decode_step")) return r;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)p.splits, (unsigned)(p.B * p.H), 1);
     cfg.blockDim = dim3((Sh::NCW + 1) * 32, 1, 1);
@@ -558,14 +581,22 @@ struct Decode {
     const size_t smem = Cfg::smem_bytes(stage_rows);
     if (smem > 220 * 1024) return fail(TA_ERR_ARG, "ta_decode_step: %zu B of shared memory needed", smem);
     if ((1 << p.lv.L0) > Cfg::TU_FLOATS) return fail(TA_ERR_ARG, "ta_decode_step: leaf block too large");
-    static int per_sm = 0;
-    static size_t per_sm_smem = 0;
-    if (per_sm == 0 || per_sm_smem != smem) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      cudaFuncSetAttribute(kern_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::NTHREADS, smem);
-      if (per_sm < 1) per_sm = 1;
-      per_sm_smem = smem;
+    static SmemAttr smem_attr, smem_attr_split;
+    if (int r = allow_smem(smem_attr, kern, smem, "ta_decode_step(persistent)")) return r;
+    if (int r = allow_smem(smem_attr_split, kern_split, smem, "ta_decode_step(persistent)")) return r;
+    // CTAs per SM at this shared-memory size, per device
+    static std::atomic<int64_t> occ[kDevCache];
+    const int dev = current_device();
+    const bool cached = dev >= 0 && dev < kDevCache;
+    int per_sm = 0;
+    const int64_t hit = cached ? occ[dev].load(std::memory_order_relaxed) : 0;
+    if (hit != 0 && (size_t)(hit >> 8) == smem) {
+      per_sm = (int)(hit & 0xff);
+    } else {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Cfg::NTHREADS, smem) != cudaSuccess)
+        return check_launch("ta_decode_step(persistent) occupancy");
+      per_sm = std::min(std::max(per_sm, 1), 255);
+      if (cached) occ[dev].store(((int64_t)smem << 8) | per_sm, std::memory_order_relaxed);
     }
     const int items = p.B * p.H;
     const int gmax = per_sm * num_sms();
