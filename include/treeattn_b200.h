@@ -43,6 +43,12 @@ const char* ta_last_error(void);
  * 3 = index out of range. */
 int ta_device_error(int* out4);
 
+/* No counterpart in the reference: a test of the kernels' bounded waits. One CTA waits on an mbarrier that no
+ * thread arrives at; after limit_ns (1 us .. 10 s) it gives up, records code 1 (bounded wait gave up) with
+ * kernel id 13 in the device-side error record and ends normally, so that the context stays usable. The
+ * library's own waits give up the same way, after 2 s. */
+int ta_wait_probe(int64_t limit_ns, void* stream);
+
 /* Nodes per (b, h) for a capacity and level range: sum over l in [L0, Lm] of cap >> l. */
 int64_t ta_level_nodes(int cap, int L0, int Lm);
 

@@ -580,6 +580,25 @@ def test_decode_bad_position_records_error():
         assert kc[0, :, 5].abs().sum() > 0  # the valid sequence was still processed
 
 
+def test_bounded_wait_gives_up_and_context_stays_usable():
+    """A wait that nothing completes (ta_wait_probe: an mbarrier no thread arrives at) gives up after its limit,
+    records code 1 (bounded wait gave up) for kernel 13 and ends; the next kernels run and give correct results."""
+    import time
+    from treeattn_b200 import _lib
+    from treeattn_b200 import _ops as ops_mod
+    _no_device_error()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    _lib.call('ta_wait_probe', 200 * 1000 * 1000, ops_mod._stream(torch.empty(1, device=DEV)))
+    assert ops_mod.device_error() == (1, 13, 7, 0)
+    assert 0.15 < time.time() - t0 < 30
+    g = load('levels')  # the context still works: the golden level build afterwards
+    lv = _ops().build_levels(to_dev(g['k']), 64, 1, 5, zero_sink=False)
+    for l in range(1, 6):
+        assert np.array_equal(lv.level(l).cpu().numpy(), g['S%d' % l]), l
+    _no_device_error()
+
+
 def test_bad_arguments_raise():
     ops = _ops()
     from treeattn_b200._lib import TreeAttnError

@@ -44,6 +44,10 @@ def test_argument_validation_without_gpu():
     """Rejected arguments return TA_ERR_ARG with a message; no CUDA call is made on these paths."""
     from treeattn_b200 import _lib
     lib = _lib.load()
+    # wait probe: limit outside [1 us, 10 s]
+    for limit in (0, 999, 10 ** 10 + 1):
+        rc = lib.ta_wait_probe(limit, None)
+        assert rc == _lib.TA_ERR_ARG and 'ta_wait_probe' in _lib.last_error()
     # bad head dim
     rc = lib.ta_build_levels(None, 1, 1, 1, 16, 48, 0, 0, 0, 16, 1, 3, 1, None, 0, 0, None)
     assert rc == _lib.TA_ERR_ARG and 'head dim' in _lib.last_error()

@@ -24,6 +24,7 @@ SIGNATURES = {
     'ta_last_error': [],
     'ta_device_error': [P],
     'ta_level_nodes': [I, I, I],
+    'ta_wait_probe': [L, P],
     'ta_build_levels': [P, I, I, I, I, I, L, L, L, I, I, I, I, P, L, L, P],
     'ta_build_log_levels': [P, I, I, I, I, I, L, L, L, I, I, I, I, P, L, L, P],
     'ta_gate_levels': [P, P, P, I, I, I, I, L, L, I, I, I, F, I, P],

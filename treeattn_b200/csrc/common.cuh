@@ -50,6 +50,7 @@ enum KernelId : int {
   K_FINISH = 10,
   K_ROWS = 11,
   K_PREFILL = 12,
+  K_WAIT_PROBE = 13,
 };
 
 // ------------------------------------------------------------------------------------------------ types
@@ -180,18 +181,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (after recording DEV_WAIT_TIMEOUT) if the phase does not complete in time.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int kernel, int where) {
+// Bounded wait: returns false (after recording DEV_WAIT_TIMEOUT) if the phase does not complete within limit_ns.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int kernel, int where,
+                                                  uint64_t limit_ns = TA_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 3u) == 0 && global_timer_ns() - t0 > TA_WAIT_LIMIT_NS) {
+    if ((++spins & 3u) == 0 && global_timer_ns() - t0 > limit_ns) {
       record_error(DEV_WAIT_TIMEOUT, kernel, where, (int)parity);
       return false;
     }
   }
+}
+
+// The bounded wait's failure path, on purpose: thread 0 waits on an mbarrier that no thread arrives at, gives up
+// after limit_ns and records DEV_WAIT_TIMEOUT (kernel K_WAIT_PROBE, where = 7). The kernel then ends normally.
+__global__ void wait_probe_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_bounded(&bar, 0, K_WAIT_PROBE, 7, limit_ns);
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (bytes multiple of 16,

@@ -746,6 +746,14 @@ int ta_device_error(int* out4) {
   return TA_OK;
 }
 
+int ta_wait_probe(int64_t limit_ns, void* stream) {
+  g_err.clear();
+  if (limit_ns < 1000 || limit_ns > 10000000000ll)
+    return fail(TA_ERR_ARG, "ta_wait_probe: limit %lld ns outside [1 us, 10 s]", (long long)limit_ns);
+  ta::wait_probe_kernel<<<1, 32, 0, S(stream)>>>((uint64_t)limit_ns);
+  return check_launch("ta_wait_probe");
+}
+
 int64_t ta_level_nodes(int cap, int L0, int Lm) {
   if (cap <= 0 || L0 < 0 || Lm < L0 || Lm > 30) return 0;
   int off[ta::MAX_LEVELS];
