@@ -62,7 +62,16 @@ struct SplitSmem {
   }
 };
 
-template <int NW, int DH>
+// Place of the 16-byte chunk c (head dims 4c .. 4c + 3) inside a staged key row: the even chunks first, then the
+// odd ones. Lane `sub` of a row reads chunks 2 sub and 2 sub + 1 (dims 8 sub .. 8 sub + 7), i.e. places sub and
+// DH / 8 + sub: consecutive 16-byte places across the lanes, on distinct banks (in natural order the lanes'
+// chunks are 32 bytes apart and two lanes of every eight meet on the same banks).
+template <int DH>
+__host__ __device__ constexpr int stage_chunk(int c) { return (c >> 1) + (DH / 8) * (c & 1); }
+
+// SWZ: the key rows are a shared-memory stage whose 16-byte chunks are placed by stage_chunk (below), so that the
+// two loads of the LPR lanes of a row each fall on distinct banks; otherwise rows are plain (global memory).
+template <int NW, int DH, bool SWZ = false>
 struct TwoMeans {
   // Each key row is read by LPR lanes holding 8 consecutive head dims each (two 16-byte loads), so a warp holds
   // RPW rows at once and U such steps are in flight per iteration; per-row dots reduce over the LPR lanes only.
@@ -149,8 +158,8 @@ struct TwoMeans {
       s_of[u] = s;
       ok[u] = s < S && valid[s];
       if (ok[u]) {
-        const float4* r = reinterpret_cast<const float4*>(keys + (int64_t)perm[s] * DH + sub * 8);
-        const float4 a = r[0], b = r[1];
+        const float4* r = reinterpret_cast<const float4*>(keys + (int64_t)perm[s] * DH);
+        const float4 a = SWZ ? r[sub] : r[2 * sub], b = SWZ ? r[LPR + sub] : r[2 * sub + 1];
         x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
         x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
       } else {
@@ -249,7 +258,8 @@ struct TwoMeans {
         best = team_kmax(warp_kmax(best), redk, w, lane, bid);
         const int sel = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
         float* dst = pass == 0 ? c0 : c1;
-        for (int d = tid; d < DH; d += TEAM) dst[d] = keys[(int64_t)perm[sel] * DH + d];
+        for (int d = tid; d < DH; d += TEAM)
+          dst[d] = keys[(int64_t)perm[sel] * DH + (SWZ ? stage_chunk<DH>(d >> 2) * 4 + (d & 3) : d)];
         team_sync<NW>(bid);
       }
       // (4) 2-means rounds: nearer centre by |x|^2 - 2 x.c + |c|^2 (first centre on ties), centres to the means
@@ -439,7 +449,7 @@ __device__ __forceinline__ void subtree_level(const float* stage, const int32_t*
   const int bid = NW == 8 ? 0 : 1 + team;
   for (int g = team; g < S0 / s; g += TEAMS) {
     const int o = g * s;
-    TwoMeans<NW, DH>::run(stage, lp + o, lv + o, s, iters, lpo + o, lvo + o, scratch + per * team, tid, bid);
+    TwoMeans<NW, DH, true>::run(stage, lp + o, lv + o, s, iters, lpo + o, lvo + o, scratch + per * team, tid, bid);
     team_sync<NW>(bid);
   }
 }
@@ -461,12 +471,12 @@ __global__ void __launch_bounds__(256, TA_SUBTREE_MINB) lane_subtree_kernel(Lane
   uint8_t* lva = q + 2 * Subtree<DH>::align16((size_t)S0 * 4);
   uint8_t* lvb = lva + Subtree<DH>::align16((size_t)S0);
   unsigned char* scratch = lvb + Subtree<DH>::align16((size_t)S0);
-  // stage the valid rows (row i of the stage = slot i of the subtree)
+  // stage the valid rows (row i of the stage = slot i of the subtree; chunks placed by stage_chunk)
   for (int e = threadIdx.x; e < S0 * (DH / 4); e += blockDim.x) {
     const int i = e / (DH / 4), c = e - i * (DH / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (g.valid[i]) v = *reinterpret_cast<const float4*>(g.keys + (int64_t)g.perm[i] * DH + c * 4);
-    *reinterpret_cast<float4*>(stage + (size_t)i * DH + c * 4) = v;
+    *reinterpret_cast<float4*>(stage + (size_t)i * DH + stage_chunk<DH>(c) * 4) = v;
   }
   for (int i = threadIdx.x; i < S0; i += blockDim.x) {
     lpa[i] = i;
