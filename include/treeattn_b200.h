@@ -166,8 +166,11 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
  * host program that reserved the GPU's memory up front for its own pool and hands the library only views into it,
  * so that a cudaMalloc would fail or break its accounting. The build's second slot-order buffer is a static array
  * inside the library (2^21 slots: P * C at most, 10 MiB held on every GPU that loads the library); the call itself
- * calls no allocator. Larger P * C is rejected with TA_ERR_ARG. The first call on each device looks up the array's
- * device address (once, with that device current); make that first call before any stream capture. All calls share
+ * calls no allocator. Larger P * C is rejected with TA_ERR_ARG. The array's device address belongs to one CUDA
+ * context: each call made outside stream capture looks it up with the calling thread's current context (so a
+ * cudaDeviceReset or another context made current in between is followed), and records it for that context; a call
+ * whose stream is capturing reuses the address recorded for the current context, so the first call in a context
+ * must come before any stream capture (otherwise TA_ERR_ARG). All calls share
  * the array (it is fully rewritten by each call, nothing needs clearing): calls that overlap on the GPU race, so
  * order them (one stream, or events). Same arguments and results as ta_lane_order otherwise. */
 int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first,

@@ -33,12 +33,14 @@ def _inputs(rng, P, C, dh, dev):
 @pytest.mark.parametrize('P,C,dh', [(8, 1024, 64), (96, 512, 32), (3, 16384, 16)])
 def test_noalloc_matches_lane_order_twice(P, C, dh):
     """Two calls in a row on different inputs (the second sees the scratch the first left behind), each equal to
-    ta_lane_order with caller scratch; no torch allocation during either call."""
+    ta_lane_order with caller scratch. Neither call allocates through torch; the second (after the first has loaded
+    the library's kernels and looked up the scratch) leaves the device's free memory unchanged as well, which also
+    catches an allocation inside the library that torch's counters cannot see."""
     from treeattn_b200 import _lib, _ops
     dev = 'cuda'
     rng = np.random.default_rng(C + dh)
     D = C.bit_length() - 2
-    for _ in range(2):
+    for call in range(2):
         keys, n = _inputs(rng, P, C, dh, dev)
         perm = torch.empty(P, C, device=dev, dtype=torch.int32)
         valid = torch.empty(P, C, device=dev, dtype=torch.uint8)
@@ -49,9 +51,12 @@ def test_noalloc_matches_lane_order_twice(P, C, dh):
         valid2 = torch.full_like(valid, 9)
         torch.cuda.synchronize()
         before = torch.cuda.memory_allocated()
+        free_before = torch.cuda.mem_get_info()[0]
         _lib.call('ta_lane_order_noalloc', _ops._p(keys), 1, C * dh, _ops._p(n), 1, P, C, dh, 3, D, _ops._p(perm2),
                   _ops._p(valid2), _ops._stream(keys))
         torch.cuda.synchronize()
         assert torch.cuda.memory_allocated() == before
+        if call == 1:
+            assert torch.cuda.mem_get_info()[0] == free_before
         assert torch.equal(perm, perm2) and torch.equal(valid, valid2)
     assert _ops.device_error()[0] == 0

@@ -161,6 +161,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Invalidates an mbarrier so its shared memory can be reused for something else; no thread may be waiting on it or
+// arrive at it afterwards.
+__device__ __forceinline__ void mbar_inval(uint64_t* bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -197,7 +203,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // The bounded wait's failure path, on purpose: thread 0 waits on an mbarrier that no thread arrives at, gives up
-// after limit_ns and records DEV_WAIT_TIMEOUT (kernel K_WAIT_PROBE, where = 7). The kernel then ends normally.
+// after limit_ns and records DEV_WAIT_TIMEOUT (kernel K_WAIT_PROBE, where = 7). Once no thread waits any more the
+// abandoned barrier is invalidated (what a give-up path must do before its shared memory is reused), and the
+// kernel ends normally.
 __global__ void wait_probe_kernel(uint64_t limit_ns) {
   __shared__ __align__(8) uint64_t bar;
   if (threadIdx.x == 0) {
@@ -206,6 +214,8 @@ __global__ void wait_probe_kernel(uint64_t limit_ns) {
   }
   __syncthreads();
   if (threadIdx.x == 0) mbar_wait_bounded(&bar, 0, K_WAIT_PROBE, 7, limit_ns);
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_inval(&bar);
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (bytes multiple of 16,

@@ -698,33 +698,70 @@ static __device__ __align__(256) int32_t g_lane_perm_scratch[kLaneScratchSlots];
 static __device__ __align__(256) uint8_t g_lane_valid_scratch[kLaneScratchSlots];
 
 namespace {
-// Device addresses of the scratch, looked up once per device (with that device current) by the first
-// ta_lane_order_noalloc call made on it. In host code the arrays' names stand for host-side shadows, never for the
+// Device addresses of the scratch. An address belongs to one CUDA context (the module is loaded per context), not
+// to a device number: after cudaDeviceReset, or with another context current (a driver-API caller with its own
+// context), the old address is stale. So every call made outside stream capture looks the address up again with
+// the calling thread's context current, and records it against that context; a call made while its stream is
+// capturing (where a lookup could load the module, which capture forbids) uses the address recorded for the current
+// context, and fails if there is none. In host code the arrays' names stand for host-side shadows, never for the
 // device memory, so only these addresses may reach a kernel.
-constexpr int kMaxDevices = 64;
+struct LaneScratch {
+  CUcontext ctx;
+  int32_t* perm;
+  uint8_t* valid;
+};
+constexpr int kMaxScratchContexts = 64;
 std::mutex g_scratch_mu;
-int32_t* g_scratch_perm[kMaxDevices];
-uint8_t* g_scratch_valid[kMaxDevices];
+LaneScratch g_scratch[kMaxScratchContexts];
+int g_scratch_n = 0;
+PFN_cuCtxGetCurrent_v4000 g_ctx_get_current = nullptr;
 
-int lane_scratch(int32_t** perm, uint8_t** valid) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: no current device: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return fail(TA_ERR_ARG, "ta_lane_order_noalloc: device %d above %d", dev, kMaxDevices);
+int current_context(CUcontext* ctx) {
+  if (!g_ctx_get_current) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr = cudaDriverEntryPointSymbolNotFound;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &qr);
+    if (e != cudaSuccess || qr != cudaDriverEntryPointSuccess || !fn)
+      return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: cuCtxGetCurrent unavailable (%s)", cudaGetErrorString(e));
+    g_ctx_get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  }
+  *ctx = nullptr;
+  const CUresult r = g_ctx_get_current(ctx);
+  if (r != CUDA_SUCCESS) return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: cuCtxGetCurrent failed (CUresult %d)", (int)r);
+  return TA_OK;
+}
+
+int lane_scratch(cudaStream_t st, int32_t** perm, uint8_t** valid) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cs);
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: stream state: %s", cudaGetErrorString(e));
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_perm[dev] || !g_scratch_valid[dev]) {
+  CUcontext ctx = nullptr;
+  if (cs == cudaStreamCaptureStatusNone) {
     void* pa = nullptr;
     void* va = nullptr;
-    e = cudaGetSymbolAddress(&pa, g_lane_perm_scratch);
+    e = cudaGetSymbolAddress(&pa, g_lane_perm_scratch);  // makes the device's primary context current if none is
     if (e == cudaSuccess) e = cudaGetSymbolAddress(&va, g_lane_valid_scratch);
     if (e != cudaSuccess || !pa || !va)
-      return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: scratch address on device %d: %s", dev, cudaGetErrorString(e));
-    g_scratch_perm[dev] = static_cast<int32_t*>(pa);
-    g_scratch_valid[dev] = static_cast<uint8_t*>(va);
+      return fail(TA_ERR_CUDA, "ta_lane_order_noalloc: scratch address: %s", cudaGetErrorString(e));
+    if (int r = current_context(&ctx)) return r;
+    int i = 0;
+    while (i < g_scratch_n && g_scratch[i].ctx != ctx) ++i;
+    if (i == g_scratch_n && g_scratch_n < kMaxScratchContexts) ++g_scratch_n;
+    if (i < kMaxScratchContexts) g_scratch[i] = {ctx, static_cast<int32_t*>(pa), static_cast<uint8_t*>(va)};
+    *perm = static_cast<int32_t*>(pa);
+    *valid = static_cast<uint8_t*>(va);
+    return TA_OK;
   }
-  *perm = g_scratch_perm[dev];
-  *valid = g_scratch_valid[dev];
-  return TA_OK;
+  if (int r = current_context(&ctx)) return r;
+  for (int i = 0; i < g_scratch_n; ++i)
+    if (g_scratch[i].ctx == ctx) {
+      *perm = g_scratch[i].perm;
+      *valid = g_scratch[i].valid;
+      return TA_OK;
+    }
+  return fail(TA_ERR_ARG, "ta_lane_order_noalloc: called during stream capture before any call outside capture in "
+              "this context (the scratch address is looked up outside capture)");
 }
 }  // namespace
 
@@ -1056,7 +1093,7 @@ int ta_lane_order(const float* keys, int64_t key_lane_div, int64_t key_stride, c
 }
 
 // ta_lane_order for callers that may not allocate device memory: the second ping-pong buffer is the library's
-// static scratch above instead of a caller buffer. The first call on a device looks the scratch up (once).
+// static scratch above instead of a caller buffer, its address looked up for the calling thread's current context.
 int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_stride, const int64_t* n, int first,
                           int P, int C, int dh, int iters, int levels, int32_t* perm, uint8_t* valid, void* stream) {
   g_err.clear();
@@ -1065,7 +1102,7 @@ int ta_lane_order_noalloc(const float* keys, int64_t key_lane_div, int64_t key_s
                 (long long)P * C, (long long)kLaneScratchSlots);
   int32_t* pt = nullptr;
   uint8_t* vt = nullptr;
-  if (int r = lane_scratch(&pt, &vt)) return r;
+  if (int r = lane_scratch(S(stream), &pt, &vt)) return r;
   return ta_lane_order(keys, key_lane_div, key_stride, n, first, P, C, dh, iters, levels, perm, valid, pt, vt,
                        stream);
 }
