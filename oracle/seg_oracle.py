@@ -540,7 +540,8 @@ class DecoderNP:
                         for _ in self.W['layers']] for _ in range(batch)]
 
     def step(self, toks, t):
-        """toks (B,) token ids at position t (an int or (B,) array). Returns (logits (B, V), keys read)."""
+        """toks (B,) token ids at position t (an int or (B,) array). Returns (logits (B, V), keys read); the final
+        hidden state (the layer-normed, rounded rows the lm_head multiplies) stays in self.last_h."""
         W, H, C, dh, r = self.W, self.H, self.C, self.dh, self.r
         toks = np.asarray(toks, np.int64)
         B = toks.shape[0]
@@ -558,4 +559,5 @@ class DecoderNP:
             x = (x + r((r(o) @ L['c_proj'].T).astype(F32))).astype(F32)
             f = r(gelu(r((r(layer_norm(x, L['ln2'])) @ L['c_fc'].T).astype(F32))))
             x = (x + r((f @ L['c_mlp'].T).astype(F32))).astype(F32)
-        return r((r(layer_norm(x, W['ln_f'])) @ W['wte'].T).astype(F32)), keys / len(W['layers'])
+        self.last_h = r(layer_norm(x, W['ln_f']))
+        return r((self.last_h @ W['wte'].T).astype(F32)), keys / len(W['layers'])

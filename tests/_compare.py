@@ -3,10 +3,22 @@
 The reference's torch.topk leaves the order of tied scores undefined, and two fp32 dot-product reductions
 round differently, so selected sets are compared only for queries with no near-tie at any cut: a query is
 excluded when, at some level, the best dropped valid candidate scores within TIE_REL (relative) of the last
-kept one. Only valid slots are compared (invalid slots of torch.topk carry arbitrary ids)."""
+kept one. Only valid slots are compared (invalid slots of torch.topk carry arbitrary ids).
+
+Every comparison is logged (test, queries compared, queries excluded as ties, mismatches) so that the exclusions
+can be audited: tests/conftest.py prints the log at the end of the run."""
+import os
+
 import numpy as np
 
 TIE_REL = 1e-6
+TIE_LOG = []
+
+
+def record(n_compared, n_excluded, n_mismatch=0, what=''):
+    """Adds one selection comparison to the run's log."""
+    test = os.environ.get('PYTEST_CURRENT_TEST', '?').split(' ')[0]
+    TIE_LOG.append((test, what, int(n_compared), int(n_excluded), int(n_mismatch)))
 
 
 def valid_sets(ids, vld):
@@ -27,7 +39,9 @@ def compare_sets(ids_a, vld_a, ids_b, vld_b, exclude=None):
     if exclude is None:
         exclude = np.zeros(eq.shape, bool)
     comp = ~exclude
-    return int((~eq & comp).sum()), int(comp.sum()), int(exclude.sum())
+    res = int((~eq & comp).sum()), int(comp.sum()), int(exclude.sum())
+    record(res[1], res[2], res[0])
+    return res
 
 
 def tied(margin):

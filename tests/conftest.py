@@ -24,3 +24,30 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if 'gpu' in it.keywords:
             it.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter):
+    """Selection comparisons of the run: per test, the queries compared, those excluded as fp32 ties at a cut
+    (tests/_compare.py) and the mismatches."""
+    try:
+        from tests._compare import TIE_LOG
+    except Exception:  # pragma: no cover
+        return
+    if not TIE_LOG:
+        return
+    agg = {}
+    for test, what, n, x, bad in TIE_LOG:
+        a = agg.setdefault((test, what), [0, 0, 0])
+        a[0] += n
+        a[1] += x
+        a[2] += bad
+    tr = terminalreporter
+    tr.section('selection comparisons (queries compared / excluded as fp32 ties / mismatches)')
+    tot = [0, 0, 0]
+    for (test, what), (n, x, bad) in sorted(agg.items()):
+        frac = x / max(n + x, 1)
+        tr.write_line('%-90s compared %8d  excluded %6d (%.4f%%)  mismatches %d' % (
+            test + (' [%s]' % what if what else ''), n, x, 100 * frac, bad))
+        tot = [tot[0] + n, tot[1] + x, tot[2] + bad]
+    tr.write_line('%-90s compared %8d  excluded %6d (%.4f%%)  mismatches %d' % (
+        'TOTAL', tot[0], tot[1], 100 * tot[1] / max(tot[0] + tot[1], 1), tot[2]))

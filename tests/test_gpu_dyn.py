@@ -11,6 +11,7 @@ import pytest
 import torch
 
 import oracle
+from tests._compare import record
 from tests._golden import load
 
 pytestmark = pytest.mark.gpu
@@ -41,6 +42,7 @@ def _compare_trees(tree, ref, min_frac):
     ex = ref.excluded(TIE)[ar, b[3]]  # in canonical rows
     offD = (1 << ref.D) - 1
     okg = ~ex[:, offD:]
+    record(int(okg.sum()), int((~okg).sum()), 0, 'tree groups')
     assert okg.mean() >= min_frac, okg.mean()
     assert np.array_equal(a[0][okg], b[0][okg])
     assert np.array_equal(a[2][~ex], b[2][~ex])
@@ -108,6 +110,7 @@ def _compare_select(sel, ref, Y, min_frac, build=True):
     ok = ref['query_margin'] > TIE
     if build:
         ok &= np.repeat(ref['build_margin'] > TIE, Y, axis=-1)
+    record(int(ok.sum()), int((~ok).sum()), 0, 'select_keys')
     assert ok.mean() >= min_frac, ok.mean()
     srt = lambda a: np.sort(np.asarray(a), -1)
     got = {k: v.cpu().numpy() for k, v in sel.items()}

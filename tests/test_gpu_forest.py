@@ -9,6 +9,7 @@ import pytest
 import torch
 
 import oracle
+from tests._compare import record
 from tests._golden import load
 
 pytestmark = pytest.mark.gpu
@@ -39,6 +40,7 @@ def test_two_means_order_vs_oracle(P, G, S, D):
     got = two_means_order(to_dev(X), 3).cpu().numpy()
     ref, margin = oracle.two_means_order(X, 3, with_margin=True)
     ok = margin > TIE
+    record(int(ok.sum()), int((~ok).sum()), 0, 'groups')
     assert ok.mean() >= 0.5, ok.mean()
     assert np.array_equal(got[ok], ref[ok])
     _no_device_error()
@@ -72,6 +74,7 @@ def test_build_forest_vs_oracle(dtype, dh):
     perm, sums = build_forest(k.to(DEV), 64, 5, cfg)
     rperm, rsums, margin = oracle.build_forest(kn, 64, 5, 3, gate=(0.25, 0.3), bf16=dtype == torch.bfloat16)
     ok = np.repeat(margin > TIE, 64, axis=-1)
+    record(int((margin > TIE).sum()), int((margin <= TIE).sum()), 0, 'blocks')
     assert ok.mean() >= 0.5
     assert np.array_equal(perm.cpu().numpy()[ok], rperm[ok])
     okb = margin > TIE
@@ -111,6 +114,7 @@ def test_tree_attention_golden(name):
     _, _, margin = oracle.tree_attention(g['q'], g['k'], g['v'], int(g['tree_block']), int(g['wmax']),
                                          int(g['beam']))
     ok = margin > TIE
+    record(int(ok.sum()), int((~ok).sum()), 0, 'queries')
     assert ok.mean() > 0.9
     np.testing.assert_allclose(out[ok], g['o'][ok], atol=1e-4)
     for key in ('keys_tree', 'keys_total'):
@@ -144,6 +148,7 @@ def test_forest_select_vs_oracle(T, B, dh, wmax, beam):
               None, beam, wmax, *[_ops._p(o) for o in out], None, None, _ops._stream(qd))
     gl, gv = out[0].cpu().numpy(), out[1].cpu().numpy()
     ok = margin > TIE
+    record(int(ok.sum()), int((~ok).sum()), 0, 'queries')
     assert ok.mean() > 0.9
     big = np.iinfo(np.int64).max
     sa = np.sort(np.where(gv, gl, big), -1)

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import oracle
-from tests._compare import compare_sets, tied
+from tests._compare import compare_sets, record, tied
 from tests._golden import load
 
 pytestmark = pytest.mark.gpu
@@ -357,7 +357,7 @@ def test_decode_step_vs_oracle(dt, dh, L0, wmax, beam, local, splits):
     sel = torch.empty(B, H, wmax + 1, device=DEV, dtype=torch.int32)
     lse = torch.empty(B, H, device=DEV, dtype=torch.float32)
     ntree = oracle.n_tree_fixed(beam, wmax)
-    n_cmp = n_bad = 0
+    n_cmp = n_bad = n_tie = 0
     for s_i in range(steps):
         pos = torch.tensor([T0[b] + s_i for b in range(B)], device=DEV, dtype=torch.int32)
         qkv_np = rnd(rng.standard_normal((B, 3 * C)).astype(np.float32))
@@ -371,6 +371,7 @@ def test_decode_step_vs_oracle(dt, dh, L0, wmax, beam, local, splits):
                                                                  with_sel=True)
             for h in range(H):
                 if margin[h] <= 1e-6:
+                    n_tie += 1
                     continue
                 n_cmp += 1
                 got = sorted(sel_n[b, h, 1:1 + sel_n[b, h, 0]].tolist())
@@ -383,6 +384,7 @@ def test_decode_step_vs_oracle(dt, dh, L0, wmax, beam, local, splits):
                 assert nk_n[b, h] == len(set(
                     [p for p in oracle.leaves_to_pos(rids[h], rused[h], leaf).tolist() if p >= 0] +
                     [0] + list(range(max(0, T0[b] + s_i - Lw + 1), T0[b] + s_i + 1)))), (b, h, s_i)
+    record(n_cmp, n_tie, n_bad)
     assert n_bad == 0 and n_cmp > 0.95 * steps * B * H, (n_bad, n_cmp)
     # caches and tree equal the oracle's after all appends (nodes bit-exact)
     for b in range(B):
@@ -443,6 +445,7 @@ def test_decode_persistent_many_items(dt, dh, L0):
             ro, _, (rids, rused, margin) = oracle.seg_attend(states[b], q, k, v, T0[b] + s_i, wmax, beam, local,
                                                              with_sel=True)
             ok = margin > 1e-6
+            record(int(ok.sum()), int((~ok).sum()), 0, 'outputs')
             d = np.abs(o_n[b].reshape(H, dh) - ro).max(-1)
             worst = max(worst, float(d[ok].max(initial=0)))
     assert worst < 2e-2, worst
@@ -493,7 +496,7 @@ def test_decode_long_context_wide_heads(splits):
     nkeys = torch.empty(B, H, device=DEV, dtype=torch.int32)
     sel = torch.empty(B, H, wmax + 1, device=DEV, dtype=torch.int32)
     ntree = oracle.n_tree_fixed(beam, wmax)
-    worst, n_cmp = 0.0, 0
+    worst, n_cmp, n_tie = 0.0, 0, 0
     for s_i in range(steps):
         pos = torch.tensor([T0[b] + s_i for b in range(B)], device=DEV, dtype=torch.int32)
         qkv_np = rnd(rng.standard_normal((B, 3 * C)).astype(np.float32))
@@ -506,6 +509,7 @@ def test_decode_long_context_wide_heads(splits):
                                                              with_sel=True)
             for h in range(H):
                 if margin[h] <= 1e-6:
+                    n_tie += 1
                     continue
                 n_cmp += 1
                 assert sorted(sel_n[b, h, 1:1 + sel_n[b, h, 0]].tolist()) == sorted(rids[h][rused[h]].tolist())
@@ -513,6 +517,7 @@ def test_decode_long_context_wide_heads(splits):
                 assert nk_n[b, h] == len(set(
                     [p for p in oracle.leaves_to_pos(rids[h], rused[h], leaf).tolist() if p >= 0] +
                     [0] + list(range(T0[b] + s_i - local + 1, T0[b] + s_i + 1)))), (b, h, s_i)
+    record(n_cmp, n_tie)
     assert worst < 2e-2 and n_cmp > 0.9 * steps * B * H, (worst, n_cmp)
     _no_device_error()
 

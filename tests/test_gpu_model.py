@@ -7,6 +7,7 @@ import pytest
 import torch
 
 import oracle
+from tests._compare import record
 from tests._golden import load
 
 pytestmark = pytest.mark.gpu
@@ -322,6 +323,7 @@ def test_neighbours_leaf_blocks_vs_oracle(dt):
     excl = near | (ref['nb_margin'] <= 1e-6)
     srt = lambda a: np.sort(a, -1)
     ok = ~excl
+    record(int(ok.sum()), int(excl.sum()), 0, 'descent + neighbours')
     for key in ('tree_pos', 'nb_pos'):
         eq = (srt(sel[key].cpu().numpy()) == srt(ref[key])).all(-1)
         assert eq[ok].all(), (key, int((~eq & ok).sum()))

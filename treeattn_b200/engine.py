@@ -13,6 +13,7 @@ import torch.nn.functional as F
 
 from . import _ops
 from ._ops import Levels
+from .budget import budget_features, mean_before
 from .fastseg import n_tree_fixed
 from .forest import gather_nodes
 
@@ -97,13 +98,8 @@ def pred_budget(pw, q, kmean, H):
     """The learned leaf budget (engine.py:89-94, fastseg.py:352-365): features [q, log |q|, one-hot head] (+ the
     mean of the earlier keys with cfg.global_pool) through the two-layer head, argmax over the budget classes.
     q (B, H, N, dh); kmean (B, H, N, dh) or None. Returns (B, H, N) int64 leaf budgets."""
-    qf = q.float()
-    B, _, N, dh = qf.shape
-    feats = [qf, torch.log(qf.norm(dim=-1, keepdim=True) + 1e-6),
-             torch.eye(H, device=q.device).view(1, H, 1, H).expand(B, H, N, H)]
-    if kmean is not None:
-        feats.append(kmean.float())
-    h = F.relu(F.linear(torch.cat(feats, -1), pw['w1'].float(), pw['b1'].float()))
+    feats = budget_features(q.float(), None if kmean is None else kmean.float())
+    h = F.relu(F.linear(feats, pw['w1'].float(), pw['b1'].float()))
     lg = F.linear(h, pw['w2'].float(), pw['b2'].float())
     return pw['classes'][lg.argmax(-1)]
 
@@ -300,15 +296,20 @@ class Decoder:
         self._graph_greedy = None
 
     # -------------------------------------------------------------- one model step on the static buffers
-    def _forward_step(self):
+    def _forward_step(self, record=None):
         """Logits (B, V) of the tokens in self._tok at positions self._pos; appends their K/V to every layer.
         Per layer: [x += mlp; h = ln1(x)] qkv-matmul, fused decode attention, c_proj-matmul, [x += proj;
-        h = ln2(x)], c_fc-matmul, GELU, c_mlp-matmul (the bracketed steps are single launches)."""
+        h = ln2(x)], c_fc-matmul, GELU, c_mlp-matmul (the bracketed steps are single launches).
+        `record` (a list; eager steps only) receives per layer copies of the residual entering it (x_in), its
+        q/k/v rows, its attention output, its selected leaves (fused decode only) and the residual leaving it
+        (x_out), for layer-by-layer checks."""
         W = self.W
         L = W['layers']
         _ops.embed_ln(W['wte'], W['wpe'], self._tok, self._pos, L[0]['ln1'], self._x, self._h)
         for i, Li in enumerate(L):
             st = self.states[i]
+            if record is not None:
+                record.append(dict(x_in=self._x.clone()))
             torch.mm(self._h, Li['c_attn'].t(), out=self._qkv)
             if self.mode == 'dense':
                 st.attend(self._qkv, self._pos, self._att, self._nkeys[i])
@@ -318,8 +319,12 @@ class Decoder:
                 _, nk = _general_step(st, Li.get('pw'), q, k, v, self._pos, out=self._att.view(B, H, 1, dh))
                 self._nkeys[i].copy_(nk.view(B, H))
             else:
+                sel = None
+                if record is not None:  # the selected leaves as well: (B, H, 1 + wmax) count, then leaf ids
+                    sel = torch.empty(self.batch, self.H, self.wmax + 1, device=self.dev, dtype=torch.int32)
+                    record[-1]['sel'] = sel
                 _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree,
-                                 self.Lw, self.scale, self._att, nkeys=self._nkeys[i], splits=self.splits,
+                                 self.Lw, self.scale, self._att, nkeys=self._nkeys[i], sel=sel, splits=self.splits,
                                  scratch=self._split)
             torch.mm(self._att, Li['c_proj'].t(), out=self._proj)
             _ops.add_ln(self._x, self._proj, Li['ln2'], self._h)
@@ -327,6 +332,8 @@ class Decoder:
             torch.mm(_ops.gelu_(self._fc), Li['c_mlp'].t(), out=self._mlp)
             nxt = L[i + 1]['ln1'] if i + 1 < len(L) else W['ln_f']
             _ops.add_ln(self._x, self._mlp, nxt, self._h)
+            if record is not None:
+                record[-1].update(qkv=self._qkv.clone(), att=self._att.clone(), x_out=self._x.clone())
         torch.mm(self._h, W['wte'].t(), out=self._logits)
         return self._logits
 
@@ -429,8 +436,7 @@ class Decoder:
         if cfg.beam_mode == 'pred':
             km = None
             if cfg.global_pool:
-                kf = k.float()
-                km = (kf.cumsum(2) - kf) / tq.clamp(min=1).view(1, 1, T0, 1).float()
+                km = mean_before(k.float(), 2)
             lhat = pred_budget(L['pw'], q, km, H)
         else:
             lhat = torch.full((nb, H, T0), cfg.beam, device=q.device, dtype=torch.int64)
