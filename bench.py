@@ -10,6 +10,11 @@ One step = one greedy decode step of the whole batch through all 12 layers + lm_
            device->host every step
   roofline the fused decode-attention kernel (ta_decode_step) timed alone with CUDA events: selected-KV bytes per
            launch / launch time vs the measured HBM copy bandwidth
+  strong   (under torchrun) the same 64 sequences split over the ranks, 64 / N each: tokens/s, speed-up and
+           efficiency against this run's own 1-GPU step time
+  kernels  (N=1) configurations 1, 2, 3 and 5: the whole configuration-1 forward, the configuration-2 gather-dot,
+           one configuration-3 prefill attention layer and the configuration-5 decode kernel, each against its
+           roofline with its own clock record
 Multi-GPU: one process per GPU (torchrun), each rank decodes its own 64 sequences; no collective in the timed
 region (weak scaling). `--impl reference` times the CPU oracle (numpy restatement of the reference's engine) on
 the host cores instead.
@@ -94,6 +99,11 @@ def parse():
     p.add_argument('--config3', action='store_true',
                    help='configuration 3 end to end: the 12-layer bf16 GPT forward (prefill) over 4 x 8192 tokens; '
                         'prints one JSON line')
+    p.add_argument('--no-kernels', action='store_true',
+                   help='default run: skip the kernels sub-record (configurations 1, 2, 3 and 5 measured after the '
+                        'decode loop)')
+    p.add_argument('--no-strong', action='store_true',
+                   help='default run under torchrun: skip the fixed-global-batch (strong scaling) decode loop')
     p.add_argument('--profile-steps', type=int, default=0,
                    help='profiling mode: after prefill and warm-up run this many eager decode steps between '
                         'cudaProfilerStart/Stop (for ncu --profile-from-start off) and exit')
@@ -301,7 +311,7 @@ def cpu_prefill_sample(q, k, v, leaf, topk, window):
                        'figure covers 48 (b, h)' % dt)
 
 
-def run_kernel_only(a, dev):
+def run_kernel_only(a, dev, emit=True):
     """Config-4 decode-attention kernel alone: batch a.batch x 12 heads, dh 64, bf16 caches holding a.prompt
     positions, leaf 64, top-16, window 128, position t = prompt (+ the launch index). With --profile-steps the
     launches are bracketed by cudaProfilerStart/Stop for ncu."""
@@ -366,13 +376,15 @@ def run_kernel_only(a, dev):
     byts = float(nk.sum()) * dh * 2 * 2
     peaks = measured_peaks()
     peak = peaks['hbm_gbs'] if peaks else 6650.0
-    print(json.dumps(dict(kernel_only=True, config='5' if a.config5 else '4', batch=B, heads=Hh, dh=dh, prompt=T0,
-                          splits=splits, kernel_us=us, bytes_per_launch=byts,
-                          achieved_gbs=byts / us / 1e3, frac=byts / us / 1e3 / peak,
-                          keys_per_head=float(nk.float().mean()))), flush=True)
+    line = dict(kernel_only=True, config='5' if a.config5 else '4', batch=B, heads=Hh, dh=dh, prompt=T0,
+                splits=splits, kernel_us=us, bytes_per_launch=byts, achieved_gbs=byts / us / 1e3,
+                frac=byts / us / 1e3 / peak, keys_per_head=float(nk.float().mean()))
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
-def run_gather_dot(a, dev):
+def run_gather_dot(a, dev, emit=True):
     """Configuration 2: per (b, h), scores of q against the 1024 keys of 16 selected 64-token blocks (fp32 out).
     The 13 MB working set fits in L2, so ROT independent copies of K (> L2 in total) are cycled through."""
     from treeattn_b200 import _ops
@@ -419,7 +431,9 @@ def run_gather_dot(a, dev):
                 rotated_copies=ROT)
     if not a.no_cpu_baseline:
         line['cpu_baseline'] = cpu_gather_dot_sample(q, Ks[0], blocks, blk, byts, seconds=min(a.cpu_seconds, 4.0))
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
 def union_tile_pairs(ids, vld, n_tree, leaf, Lw, T, qt=128, kt=64):
@@ -606,7 +620,7 @@ def run_config3(a, dev):
                           data='synthetic (uniform random tokens, N(0,0.02) random-init weights)')), flush=True)
 
 
-def run_prefill_attn(a, dev):
+def run_prefill_attn(a, dev, emit=True):
     """Configuration 3, one layer of prefill sparse attention: B=4, H=12, T=8192, dh=64 bf16, 64-token leaves,
     top-16, 128-token window. q / k / v random, the selection from build_levels + select (the model's own
     kernels). Each launch is timed alone with CUDA events after a 256 MB L2 flush."""
@@ -671,10 +685,12 @@ def run_prefill_attn(a, dev):
                 peak_tflops=peak)
     if not a.no_cpu_baseline:
         line['cpu_baseline'] = cpu_prefill_sample(q, k, v, leaf, topk, window)
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
-def run_config1(a, dev):
+def run_config1(a, dev, emit=True):
     """Configuration 1: GPT 4 layers, d=256, 4 heads, vocab 4096, T=512, leaf 32, top-4, window 64, fp32, batch 2,
     weights from torch.manual_seed(0) + GPT._init, tokens uniform from a seeded generator. The whole forward (our
     SegAttention path on the GPU) against the CPU oracle's forward (numpy fp32 restatement of model.py +
@@ -711,13 +727,40 @@ def run_config1(a, dev):
     cpu_ms = (time.perf_counter() - t0) * 1e3
     diff = float(np.abs(logits.float().cpu().numpy() - ref).max())
     toks = 2 * 512
-    print(json.dumps(dict(config1=True, config='1: GPT 4x256 fp32, B=2, T=512, leaf 32, top-4, window 64',
-                          gpu_forward_ms=gpu_ms, gpu_tokens_per_s=toks / (gpu_ms * 1e-3),
-                          max_abs_logit_diff=diff, keys_total=stats['keys_total'],
-                          ref_keys_total=rstats['keys_total'],
-                          cpu_baseline=dict(value=toks / (cpu_ms * 1e-3), unit='tokens/s', cores=_cpu_threads(),
-                                            kind='port', sample='one full forward (2 x 512 tokens) of the CPU oracle '
-                                            'in %.0f ms' % cpu_ms))), flush=True)
+    line = dict(config1=True, config='1: GPT 4x256 fp32, B=2, T=512, leaf 32, top-4, window 64',
+                gpu_forward_ms=gpu_ms, gpu_tokens_per_s=toks / (gpu_ms * 1e-3), max_abs_logit_diff=diff,
+                keys_total=stats['keys_total'], ref_keys_total=rstats['keys_total'],
+                cpu_baseline=dict(value=toks / (cpu_ms * 1e-3), unit='tokens/s', cores=_cpu_threads(), kind='port',
+                                  sample='one full forward (2 x 512 tokens) of the CPU oracle in %.0f ms' % cpu_ms))
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
+
+
+def measure_kernels(a, dev, local):
+    """The other configurations' hot kernels, measured after the configuration-4 decode loop so that one default
+    run records them all (each with CUDA events and its own clock record): configuration 2's gather-dot,
+    configuration 3's prefill attention layer (tensor-core tiles), configuration 5's decode kernel at the batch per
+    GPU its engine runs (20 sequences of 32768 tokens) and configuration 1's whole forward."""
+    import types
+    base = dict(vars(a), profile_steps=0, cpu_seconds=min(a.cpu_seconds, 2.0), splits=0)
+    out = {}
+
+    def clocked(name, fn, **kw):
+        ck = Clocks(local)
+        ck.start()
+        ck.mark_begin()
+        line = fn(types.SimpleNamespace(**dict(base, **kw)), dev, emit=False)
+        ck.mark_end()
+        line['clocks'] = ck.stop()
+        out[name] = line
+        torch.cuda.empty_cache()
+
+    clocked('config2_gather_dot', run_gather_dot)
+    clocked('config3_prefill_layer', run_prefill_attn, batch=4)
+    clocked('config5_decode_kernel', run_kernel_only, config5=True, batch=20, prompt=32768)
+    clocked('config1_forward', run_config1)
+    return out
 
 
 def run_reference(a, rank, world):
@@ -906,6 +949,43 @@ def run_engine(a, M, dev, rank, world, local):
     ms, ms_e2e, kern_ms = tdist.max_over_ranks([ms, ms_e2e, kern_ms], dev)
     if world > 1:
         tdist.gather_rows(dec.tokens.view(-1, 1))  # generated tokens gathered off the hot path
+
+    # ---------------------------------------------------------------- strong scaling: the global batch fixed
+    # The weak line above gives every rank the 1-GPU workload (B sequences); here the same B sequences are split
+    # over the ranks (B / world each, engine.py:22-33: every sequence is independent), so the step time is that
+    # of the smaller per-rank batch. Speed-up is against this run's own 1-GPU figure: each rank of the weak run is
+    # exactly the 1-GPU configuration.
+    strong = None
+    if M is CFG4 and not a.no_strong and B % world == 0:
+        if world == 1:
+            strong = dict(global_batch=B, batch_per_rank=B, ms_per_step=ms / K, value=B * K / (ms * 1e-3),
+                          unit='tokens/s', speedup=1.0, efficiency=1.0, note='the same run as value')
+        else:
+            del dec
+            torch.cuda.empty_cache()
+            Bs = B // world
+            dec = Decoder(W, NL, H, C, M.tcap, 'seg', cfg, dev, batch=Bs, dtype=torch.bfloat16, cap=cap,
+                          splits=a.splits)
+            g = torch.Generator(device=dev).manual_seed(100)
+            prompts = torch.randint(0, M.V, (B, T0), device=dev, generator=g)  # the global batch, same on all ranks
+            lo, hi = tdist.shard(B, rank, world)
+            dec.prefill(prompts[lo:hi])
+            dec._ensure_graphs()
+            dec.greedy_steps(Wm)
+            dist.barrier()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            dec.greedy_steps(K)
+            s1.record()
+            torch.cuda.synchronize()
+            ms_s = tdist.max_over_ranks([s0.elapsed_time(s1)], dev)[0]
+            v_s = B * K / (ms_s * 1e-3)
+            v_1 = B * K / (ms * 1e-3)  # every rank of the weak run decoded the whole 1-GPU batch
+            strong = dict(global_batch=B, batch_per_rank=Bs, ms_per_step=ms_s / K, value=v_s, unit='tokens/s',
+                          speedup=v_s / v_1, efficiency=v_s / v_1 / world, splits=dec.splits,
+                          note='1-GPU reference: this run\'s weak-scaling step time (each rank decodes the whole '
+                               '1-GPU batch of %d)' % B)
     if rank == 0:
         peaks = measured_peaks()
         peak = peaks['hbm_gbs'] if peaks else 6650.0
@@ -938,12 +1018,18 @@ def run_engine(a, M, dev, rank, world, local):
                                   kernel_us=kern_ms * 1e3, bytes_per_launch=sel_bytes,
                                   peak_source='MEASURED_PEAKS.json hbm_gbs (burst copy)' if peaks else 'fallback'),
                     clocks=ck)
+        if strong is not None:
+            line['strong'] = strong
         if world == 1 and not a.no_cpu_baseline:
             v, steps, threads, how = cpu_decode_sample(a.cpu_seconds, W_dev=W if M is CFG4 else None, M=M)
             line['cpu_baseline'] = dict(value=v, unit='tokens/s', cores=threads, kind='port',
                                         sample=how + ' on the CPU oracle (numpy fp32 restatement of the reference '
                                         'engine), %s weights, cache filled with random K/V' % (
                                             'same' if M is CFG4 else 'random'))
+        if world == 1 and M is CFG4 and not a.no_kernels:
+            del dec
+            torch.cuda.empty_cache()
+            line['kernels'] = measure_kernels(a, dev, local)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
