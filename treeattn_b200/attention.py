@@ -16,6 +16,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib, _ops
+from .budget import budget_features, budget_label
 from .fastseg import gather_dot, sparse_attn
 from .forest import _ptr_array, build_forest_raw, gather_nodes
 
@@ -54,7 +55,6 @@ class TreeAttention(nn.Module):
             fin = self.dh + 1 + self.H + (self.dh if cfg.global_pool else 0)
             self.pred = nn.Sequential(nn.Linear(fin, 64), nn.ReLU(), nn.Linear(64, len(cfg.beam_classes)))
             self.register_buffer('classes', torch.tensor(list(cfg.beam_classes)), persistent=False)
-            self.register_buffer('head_eye', torch.eye(self.H), persistent=False)
         self.aux = {}
         self._cands = {}
 
@@ -129,21 +129,14 @@ class TreeAttention(nn.Module):
                                                          cfg.wmax if pred_mode else cfg.beam, route_on)
         wl = leaf.shape[-1]
 
-        # (4) the learned budget head (attention.py:92-108)
+        # (4) the learned budget head (attention.py:92-108): a query keeps only its first `budget` valid leaves
         plog = None
         leafv_use = leafv
         if pred_mode:
-            feats = [qd, torch.log(qd.float().norm(dim=-1, keepdim=True) + 1e-6).to(qd.dtype),
-                     self.head_eye.to(qd.dtype)[None, :, None, :].expand(b, H, T, H)]
-            if cfg.global_pool:
-                cum = sums[0].cumsum(2)
-                prev = torch.cat([torch.zeros_like(cum[:, :, :1]), cum[:, :, :-1]], 2)
-                ar_nb = torch.arange(nb, device=dev)
-                denom = (ar_nb.clamp(min=1) * B).to(qd.dtype).view(1, 1, nb, 1)
-                feats.append((prev / denom)[:, :, blk, :])
-            plog = self.pred(torch.cat(feats, -1))
-            bq_pred = self.classes[plog.argmax(-1).detach()]
-            leafv_use = leafv & (torch.arange(wl, device=dev) < bq_pred.unsqueeze(-1))
+            kmean = self._earlier_blocks_mean(sums[0], B, blk, qd.dtype) if cfg.global_pool else None
+            plog = self.pred(budget_features(qd, kmean))
+            budget = self.classes[plog.argmax(-1).detach()]
+            leafv_use = leafv & (torch.arange(wl, device=dev) < budget.unsqueeze(-1))
 
         # (5)-(6) key positions of the used leaves, then exact attention over own block + static + tree keys
         tvalid = tok & torch.cat([leafv_use, leafv_use], -1)
@@ -156,36 +149,53 @@ class TreeAttention(nn.Module):
         self.aux['keys_total'] = ((t % B + 1).float().mean() + s_valid.float().sum(-1).mean()
                                   + tcount.mean()).detach()
 
-        # (7) training signals (attention.py:145-174): labels from the attention weights themselves
+        # (7) training signals (attention.py:145-174), both read off this layer's own attention weights
         if self.training:
             with torch.no_grad():
-                if pred_mode:
-                    cand_lab = torch.cat([st, torch.where(tok, tkey, torch.full_like(tkey, -1)).to(torch.int32)],
-                                         -1).contiguous()
-                    tv_lab = tok
-                else:
-                    cand_lab = cand
-                    tv_lab = tvalid
-                Sl = gather_dot(qd, kd, cand_lab, scale)
-                w_lab = torch.softmax(Sl.masked_fill(cand_lab < 0, float('-inf')), -1)
-                wt = w_lab[..., B + 3:]
-                best = wt.argmax(-1)
-                ok = tv_lab.gather(-1, best.unsqueeze(-1)).squeeze(-1) & (wt.max(-1).values > 0) \
-                    & (blk >= 1).view(1, 1, T)
-                leafnode = leaf.gather(-1, (best % wl).unsqueeze(-1)).squeeze(-1)
-                if pred_mode:
-                    leaf_mass = wt[..., :wl] + wt[..., wl:]
-                    total = leaf_mass.sum(-1, keepdim=True)
-                    need = (leaf_mass.cumsum(-1) < 0.9 * total).sum(-1) + 1
-                    label = (need.unsqueeze(-1) > self.classes).sum(-1).clamp(max=len(self.classes) - 1)
+                target = self._leaf_targets(qd, kd, st, cand, tkey, tok, tvalid, leaf, blk, scale, pred_mode)
             route = q.new_zeros(()).float()
+            leafnode, ok = target['leafnode'], target['ok']
             if route_on and bool(ok.any()):
                 route = self._route_loss(q, k, perm, B, depth, sel_lists, leafnode, ok, blk)
             self.aux['route'] = route
             if pred_mode:
-                prow = (blk >= 1).view(1, 1, T).expand(b, H, T)
-                self.aux['pred'] = F.cross_entropy(plog.float()[prow], label[prow])
+                rows = (blk >= 1).view(1, 1, T).expand(b, H, T)  # the first block has no earlier leaves
+                self.aux['pred'] = F.cross_entropy(plog.float()[rows], target['budget'][rows])
         return out
+
+    @staticmethod
+    def _earlier_blocks_mean(roots, B, blk, dtype):
+        """Global pooling input of the budget head: per query, the mean of the keys in the blocks before its own
+        (zero in the first block). roots (b, H, nb, dh): each block's key sum (the level-0 node)."""
+        nb = roots.shape[2]
+        before = F.pad(roots.cumsum(2), (0, 0, 1, 0))[:, :, :nb]  # key sums of blocks 0 .. j-1
+        n_keys = (torch.arange(nb, device=roots.device).clamp(min=1) * B).to(dtype).view(1, 1, nb, 1)
+        return (before / n_keys)[:, :, blk, :]
+
+    def _leaf_targets(self, qd, kd, st, cand, tkey, tok, tvalid, leaf, blk, scale, pred_mode):
+        """Targets of the two training losses from the softmax weights of each query over its keys: the leaf whose
+        key took the largest weight (the routing loss steers the descent toward its ancestors; `ok` marks the
+        queries where that key is a used tree key with weight, in blocks >= 1) and, with the budget head, the
+        budget class that covers 90 % of the weight on the leaves (budget.budget_label). In 'pred' mode the weights
+        come from attention over every found leaf, not only the budgeted ones, so the label does not depend on the
+        head's own choice."""
+        T = qd.shape[2]
+        wl = leaf.shape[-1]
+        nb_static = st.shape[-1]
+        if pred_mode:
+            tree = torch.where(tok, tkey, torch.full_like(tkey, -1)).to(torch.int32)
+            cand, counted = torch.cat([st, tree], -1).contiguous(), tok
+        else:
+            counted = tvalid
+        s = gather_dot(qd, kd, cand, scale).masked_fill(cand < 0, float('-inf'))
+        w_tree = torch.softmax(s, -1)[..., nb_static:]  # weights of the tree keys: [first keys | second keys]
+        top = w_tree.argmax(-1)
+        ok = counted.gather(-1, top.unsqueeze(-1)).squeeze(-1) & (w_tree.amax(-1) > 0) & (blk >= 1).view(1, 1, T)
+        target = dict(ok=ok, leafnode=leaf.gather(-1, (top % wl).unsqueeze(-1)).squeeze(-1))
+        if pred_mode:
+            per_leaf = w_tree.unflatten(-1, (2, wl)).sum(-2)  # a block-forest leaf holds two keys
+            target['budget'] = budget_label(per_leaf, self.classes)[0]
+        return target
 
     def _route_loss(self, q, k, perm, B, depth, sel_lists, leafnode, ok, blk):
         """attention.py:162-174: per level, cross entropy of the scaled node scores toward the ancestor of the leaf

@@ -10,6 +10,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib, _ops
+from .budget import budget_features, budget_label, mean_before
 from .seg import finish, gate_apply, neighbor_pass, select_seg, select_tree, tree_pass  # noqa: F401
 
 FAST = [True]  # kept for callers that toggle it; this package has only the CUDA path
@@ -121,7 +122,6 @@ class SegAttention(nn.Module):
             fin = self.dh + 1 + self.H + (self.dh if cfg.global_pool else 0)
             self.pred = nn.Sequential(nn.Linear(fin, 64), nn.ReLU(), nn.Linear(64, len(cfg.beam_classes)))
             self.register_buffer('classes', torch.tensor(list(cfg.beam_classes)), persistent=False)
-            self.register_buffer('head_eye', torch.eye(self.H), persistent=False)
         self.aux = {}
 
     def forward(self, x):
@@ -140,19 +140,12 @@ class SegAttention(nn.Module):
         return torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v))
 
     def _lhat(self, q, k, with_logits=False):
-        cfg = self.cfg
-        b, H, T, dh = q.shape
-        if cfg.beam_mode != 'pred':
+        """Leaf budget per query from the budget head (beam_mode 'pred', fastseg.py:352-365), or None."""
+        if self.cfg.beam_mode != 'pred':
             return (None, None) if with_logits else None
-        t = torch.arange(T, device=q.device)
         qd = q.detach()
-        feats = [qd, torch.log(qd.float().norm(dim=-1, keepdim=True) + 1e-6).to(qd.dtype),
-                 self.head_eye.to(qd.dtype)[None, :, None, :].expand(b, H, T, H)]
-        if cfg.global_pool:
-            kd = k.detach().float()
-            prefix_mean = (kd.cumsum(2) - kd) / t.clamp(min=1).view(1, 1, T, 1).float()
-            feats.append(prefix_mean.to(qd.dtype))
-        plog = self.pred(torch.cat(feats, -1))
+        kmean = mean_before(k.detach().float(), 2).to(qd.dtype) if self.cfg.global_pool else None
+        plog = self.pred(budget_features(qd, kmean))
         lhat = self.classes[plog.argmax(-1).detach()]
         return (lhat, plog) if with_logits else lhat
 
@@ -251,16 +244,21 @@ class SegAttention(nn.Module):
         self.aux['leaves_used'] = used.sum(-1).float().mean()
         if self.training and plog is not None:
             with torch.no_grad():
-                tv_full = torch.cat([leaf_ok] * leaf, -1) & (tree_pos >= 0)
-                keep_f = dedupe_fast(cand, torch.cat([tv_full, rest], -1))
-                Sf = gather_dot(q.detach(), k.detach(), cand, scale)
-                wf = torch.softmax(Sf.masked_fill(~keep_f, float('-inf')), -1)
-                wt = wf[..., :leaf * wl]
-                leaf_mass = sum(wt[..., j * wl:(j + 1) * wl] for j in range(leaf))
-                total = leaf_mass.sum(-1, keepdim=True)
-                need = (leaf_mass.cumsum(-1) < 0.9 * total).sum(-1) + 1
-                label = (need.unsqueeze(-1) > self.classes).sum(-1).clamp(max=len(self.classes) - 1)
-                rows = total.squeeze(-1) > 0
+                label, rows = self._budget_target(q.detach(), k.detach(), cand, tree_pos, leaf_ok, rest, leaf, scale)
             if bool(rows.any()):
                 self.aux['pred'] = F.cross_entropy(plog.float()[rows], label[rows])
         return out
+
+    def _budget_target(self, qd, kd, cand, tree_pos, leaf_ok, rest, leaf, scale):
+        """Budget-head target (fastseg.py:394-405): the attention weights a query would give ALL of its found leaves
+        (every valid one, not only the budgeted), summed per leaf block, through budget.budget_label. Returns
+        (label, rows): rows are the queries whose leaves take any weight."""
+        wl = leaf_ok.shape[-1]
+        every_leaf = torch.cat([leaf_ok] * leaf, -1) & (tree_pos >= 0)
+        keep = dedupe_fast(cand, torch.cat([every_leaf, rest], -1))
+        s = gather_dot(qd, kd, cand, scale).masked_fill(~keep, float('-inf'))
+        w_leaf_keys = torch.softmax(s, -1)[..., :leaf * wl]  # slot j * wl + i: key j of leaf i
+        per_leaf = w_leaf_keys[..., :wl]
+        for j in range(1, leaf):
+            per_leaf = per_leaf + w_leaf_keys[..., j * wl:(j + 1) * wl]
+        return budget_label(per_leaf, self.classes)
