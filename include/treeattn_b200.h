@@ -293,6 +293,37 @@ int ta_add_ln(float* x, const void* y, int dtype, int B, int C, const float* w, 
 int ta_gelu(void* x, int dtype, int64_t n, void* stream);
 int ta_argmax_advance(const void* logits, int dtype, int B, int V, int64_t* tok, int32_t* pos, void* stream);
 
+/* The decode step's linear layers on the tensor cores (callers of the hot path; reference model.py:21-44 c_attn,
+ * c_proj, c_fc + F.gelu, c_mlp; model.py:90 / engine.py:177 the lm_head on the tied embedding; phase2.py:61-62 the
+ * greedy argmax). Each replaces one torch matmul of the batched step, plus the elementwise work around it.
+ * ta_linear_rows: for rows act (B, K) (row stride act_ld, 16-byte aligned) and an nn.Linear weight w (N, K)
+ *   contiguous, both bf16 or both f16, 1 <= B <= 256, K a multiple of 64 x splits:
+ *     mode 0 STORE    out (B, N) (row stride out_ld) = act w^T rounded to the dtype, as F.linear;
+ *     mode 1 GELU     out = F.gelu of that rounded product (exact erf GELU), rounded;
+ *     mode 2 PARTIAL  part (splits, B, N) fp32: the product over each of `splits` K slices, unrounded;
+ *     mode 3 ARGMAX   STORE, plus keys (ceil(N / 128), B): per 128-feature tile and row the largest rounded value
+ *                     and its first index, packed as (order(value) << 32) | (0xffffffff - index).
+ *   Modes 0, 1 and 3 may split K too (more CTAs stream the weight): each split writes its fp32 sums to ws
+ *   (ceil(N / 128) x splits x B x 128 floats) and the last split of each 128-feature tile to arrive (counters,
+ *   ceil(N / 128) ints, zero before the first call and left zero by every call) adds them in split order and writes
+ *   the result, so it does not depend on the order of arrival. N a multiple of 8; outputs 16-byte aligned.
+ *   Launched with programmatic dependent launch: the weight stream starts before the previous kernel of the
+ *   stream has finished; the rows are read after it has.
+ * ta_linear_supported: 1 when ta_linear_rows takes (dtype, B, N, K, splits), else 0 (the caller then uses a
+ *   library GEMM).
+ * ta_add_splits_ln: x[b] += (sum of part[0 .. splits-1, b] in that order, rounded to `dtype`), then
+ *   h[b] = LayerNorm(x[b]) * w (engine.py:175-176: the residual add of a projection's output and the next layer
+ *   norm). C a multiple of 8, at most 2048.
+ * ta_argmax_finish: tok[b] = the index held by the largest keys[t, b] over the n_tiles tiles, pos[b] += 1. */
+int ta_linear_supported(int dtype, int B, int N, int K, int splits);
+int ta_linear_rows(const void* act, int64_t act_ld, int dtype, int B, int N, int K, const void* w, int splits, int mode,
+                   void* out, int64_t out_ld, float* part, unsigned long long* keys, float* ws, int* counters,
+                   void* stream);
+int ta_add_splits_ln(float* x, const float* part, int splits, int dtype, int B, int C, const float* w, float eps,
+                     void* h, void* stream);
+int ta_argmax_finish(const unsigned long long* keys, int n_tiles, int B, int V, int64_t* tok, int32_t* pos,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

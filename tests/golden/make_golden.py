@@ -395,4 +395,8 @@ def main(ref_path, only=None):
 if __name__ == '__main__':
     args = [x for x in sys.argv[1:] if not x.startswith('--only=')]
     only = next((x.split('=', 1)[1] for x in sys.argv[1:] if x.startswith('--only=')), None)
-    main(args[0] if args else os.environ.get('TREEATTN_REFERENCE', '/root/reference'), only)
+    ref = args[0] if args else os.environ.get('TREEATTN_REFERENCE')
+    if not ref:
+        sys.exit('usage: python tests/golden/make_golden.py <path of the treeattn checkout> [--only=name]  '
+                 '(or set TREEATTN_REFERENCE)')
+    main(ref, only)

@@ -59,6 +59,10 @@ SIGNATURES = {
     'ta_add_ln': [P, P, I, I, I, P, F, P, P],
     'ta_gelu': [P, I, L, P],
     'ta_argmax_advance': [P, I, I, I, P, P, P],
+    'ta_linear_supported': [I, I, I, I, I],
+    'ta_linear_rows': [P, L, I, I, I, I, P, I, I, P, L, P, P, P, P, P],
+    'ta_add_splits_ln': [P, P, I, I, I, I, P, F, P, P],
+    'ta_argmax_finish': [P, I, I, I, P, P, P],
 }
 _RESTYPES = {'ta_last_error': ctypes.c_char_p, 'ta_level_nodes': c_int64}
 

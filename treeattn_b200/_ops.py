@@ -425,6 +425,64 @@ def argmax_advance(logits, tok, pos):
     _lib.call('ta_argmax_advance', _p(logits), _code(logits), B, V, _p(tok), _p(pos), _stream(logits))
 
 
+LIN_STORE, LIN_GELU, LIN_PARTIAL, LIN_ARGMAX = 0, 1, 2, 3
+LIN_TILE = 128  # output features per CTA of ta_linear_rows
+
+
+def linear_supported(dtype, B, N, K, splits=1):
+    """Whether ta_linear_rows takes these rows: 16-bit, 1..256 rows, K a multiple of 64 x splits that fits."""
+    if dtype not in (torch.bfloat16, torch.float16):
+        return False
+    return bool(_lib.load().ta_linear_supported(_DT[dtype], B, N, K, splits))
+
+
+def linear_workspace(B, N, splits, device):
+    """(ws, counters) for ta_linear_rows' STORE / GELU / ARGMAX modes with K splits."""
+    tiles = -(-N // LIN_TILE)
+    return (torch.empty(tiles * splits * B * LIN_TILE, device=device, dtype=torch.float32),
+            torch.zeros(tiles, device=device, dtype=torch.int32))
+
+
+def linear_rows(act, w, mode=LIN_STORE, out=None, splits=1, part=None, keys=None, ws=None):
+    """Rows times an nn.Linear weight on the tensor cores (ta_linear_rows): act (B, K) with a contiguous last dim,
+    w (N, K) contiguous, same 16-bit dtype. mode STORE: out (B, N) = act w^T; GELU: exact GELU of it; PARTIAL: the
+    fp32 sums of each of `splits` K slices into part (splits, B, N); ARGMAX: STORE plus each 128-feature tile's best
+    (value, first index) per row in keys (ceil(N / 128), B) int64 for argmax_finish. STORE / GELU / ARGMAX with
+    splits > 1 use ws = linear_workspace(...) (allocated here when not given). Returns out / part."""
+    _need_cuda('linear_rows', act, w)
+    B, K = act.shape
+    N = w.shape[0]
+    if act.stride(1) != 1 or not w.is_contiguous() or w.shape[1] != K or w.dtype != act.dtype:
+        raise ValueError('linear_rows: act (B, K) with a unit inner stride and w (N, K) contiguous of its dtype')
+    if mode == LIN_PARTIAL:
+        if part is None:
+            part = torch.empty(splits, B, N, device=act.device, dtype=torch.float32)
+        res = part
+    else:
+        if out is None:
+            out = torch.empty(B, N, device=act.device, dtype=act.dtype)
+        res = out
+    if mode != LIN_PARTIAL and splits > 1 and ws is None:
+        ws = linear_workspace(B, N, splits, act.device)
+    _lib.call('ta_linear_rows', _p(act), act.stride(0), _code(act), B, N, K, _p(w), int(splits), int(mode),
+              _p(out) if mode != LIN_PARTIAL else None, out.stride(0) if mode != LIN_PARTIAL else 0,
+              _p(part) if mode == LIN_PARTIAL else None, _p(keys) if mode == LIN_ARGMAX else None,
+              _p(ws[0]) if ws is not None else None, _p(ws[1]) if ws is not None else None, _stream(act))
+    return res
+
+
+def add_splits_ln(x, part, w, h_out, eps=1e-5):
+    """x += (sum of the splits of part (S, B, C), rounded to h_out's dtype); h_out = LayerNorm(x) * w."""
+    B, C = x.shape
+    _lib.call('ta_add_splits_ln', _p(x), _p(part), part.shape[0], _code(h_out), B, C, _p(w), float(eps), _p(h_out),
+              _stream(x))
+
+
+def argmax_finish(keys, V, tok, pos):
+    """tok = the argmax packed in keys (tiles, B) by linear_rows' ARGMAX mode, pos += 1."""
+    _lib.call('ta_argmax_finish', _p(keys), keys.shape[0], keys.shape[1], int(V), _p(tok), _p(pos), _stream(keys))
+
+
 def default_splits(B, H, dh, dtype):
     """The decode mode ta_decode_step picks for B*H (b, h) pairs of head dim dh and element type dtype."""
     return _lib.load().ta_decode_default_splits(B, H, dh, _DT[dtype])

@@ -244,6 +244,13 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gm
       : "memory");
 }
 
+// ------------------------------------------------------------------------------------------------ dependent launch
+// Programmatic dependent launch: wait until the grid this one depends on has completed and its memory is visible
+// (a no-op when the kernel was launched without the attribute) / let the grids that depend on this one start
+// launching (they still wait for its completion before reading what it writes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------------ cluster
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -157,6 +157,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32) decode_kernel(DecodeParams p) 
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int leaf = 1 << p.lv.L0;
+  pdl_wait();  // every input (positions, q/k/v rows, caches, tree) may come from the grid this one follows
+  pdl_launch_dependents();
 
   int t = p.pos[b];
   bool active = true;
@@ -613,6 +615,8 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();  // every input (positions, q/k/v rows, caches, tree) may come from the grid this one follows
+  pdl_launch_dependents();
 
   if (warp == W_SEL) {
     // ------------------------------------------------------------------ selector warp

@@ -67,6 +67,8 @@ __global__ void __launch_bounds__(ROW_THREADS) embed_ln_kernel(const T* __restri
                                                                const float* __restrict__ w, float eps, float* x,
                                                                T* h) {
   __shared__ float2 red[ROW_THREADS / 32];
+  pdl_wait();  // tokens and positions come from the previous step's greedy argmax
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   int64_t tk = tok[b];
   int ps = pos[b];

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/treeattn_b200.h"
 #include <cudaTypedefs.h>
@@ -15,6 +16,7 @@
 #include "decode.cuh"
 #include "dyn.cuh"
 #include "forest.cuh"
+#include "linear.cuh"
 #include "model_ops.cuh"
 #include "prefill.cuh"
 
@@ -100,6 +102,23 @@ int allow_smem(SmemAttr& a, K* kern, size_t bytes, const char* what) {
   }
   if (cached) a.bytes[dev].store(most, std::memory_order_relaxed);
   return TA_OK;
+}
+
+// Launch with programmatic stream serialization: the kernel may start while the previous kernel of the stream is
+// still running (it calls griddepcontrol.wait before reading anything that kernel writes).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // Dispatch F<T, DH>::run(args...) over the runtime dtype and head dim.
@@ -537,13 +556,15 @@ struct Decode {
     cfg.blockDim = dim3((Sh::NCW + 1) * 32, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)p.splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // set up while the kernel before ends
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.splits;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = p.splits > 1 ? 1 : 0;
+    cfg.numAttrs = p.splits > 1 ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
     if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_decode_step: launch failed: %s", cudaGetErrorString(e));
     return check_launch("ta_decode_step");
@@ -625,10 +646,10 @@ struct Decode {
       const int per_cta = (units + gmax - 1) / gmax;  // units per CTA (equal for all but the last few)
       grid = (units + per_cta - 1) / per_cta;
     }
-    if (p.psplit > 1)
-      kern_split<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
-    else
-      kern<<<grid, Cfg::NTHREADS, smem, st>>>(p, stage_rows);
+    // programmatic dependent launch: the CTAs set up while the projection before them ends
+    const cudaError_t e = launch_pdl(p.psplit > 1 ? kern_split : kern, dim3(grid), dim3(Cfg::NTHREADS), smem, st, p,
+                                     stage_rows);
+    if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_decode_step(persistent): launch failed: %s", cudaGetErrorString(e));
     return check_launch("ta_decode_step(persistent)");
   }
 };
@@ -636,9 +657,10 @@ struct Decode {
 template <typename T, int MAXV>
 int launch_embed(const void* wte, const void* wpe, const int64_t* tok, const int32_t* pos, int B, int V, int P, int C,
                  const float* w, float eps, float* x, void* h, cudaStream_t st) {
-  ta::embed_ln_kernel<T, MAXV><<<B, ta::ROW_THREADS, 0, st>>>(reinterpret_cast<const T*>(wte),
-                                                                reinterpret_cast<const T*>(wpe), tok, pos, V, P, C, w,
-                                                                eps, x, reinterpret_cast<T*>(h));
+  const cudaError_t e = launch_pdl(ta::embed_ln_kernel<T, MAXV>, dim3(B), dim3(ta::ROW_THREADS), 0, st,
+                                   reinterpret_cast<const T*>(wte), reinterpret_cast<const T*>(wpe), tok, pos, V, P,
+                                   C, w, eps, x, reinterpret_cast<T*>(h));
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_embed_ln: launch failed: %s", cudaGetErrorString(e));
   return check_launch("ta_embed_ln");
 }
 
@@ -687,6 +709,72 @@ int rows_dispatch(int dtype, int kind, const void* a0, const void* a1, const int
 }
 
 }  // namespace
+
+// ---------------------------------------------------------------------------------------------- linear rows
+// Shared memory a linear_rows_kernel block may use (the B200's 227 KiB opt-in limit).
+constexpr size_t kLinearSmem = 227 * 1024;
+
+// Copy shape of a linear_rows_kernel CTA with BN rows and a Ks slice: nb K blocks per weight copy (large copies
+// stream faster), na per copy of the rows, nst ring stages. nst = 0 when nothing fits in shared memory.
+struct LinShape {
+  int nb, na, nst;
+};
+
+LinShape linear_shape(int BN, int Ks) {
+  const int nkb = Ks / ta::LIN_KB;
+  LinShape sh{1, 1, 0};
+  for (int d = 8; d >= 1; --d)
+    if (nkb % d == 0) { sh.na = d; break; }
+  for (int nb = 4; nb >= 1; --nb) {
+    if (nkb % nb != 0) continue;
+    const int nstage = nkb / nb;
+    for (int nst = std::min(nstage, ta::LIN_MAX_NST); nst >= 1; --nst)
+      if (ta::linear_smem_bytes(BN, Ks, nst, nb) <= kLinearSmem && (nst >= 2 || nstage == 1)) {
+        sh.nb = nb;
+        sh.nst = nst;
+        return sh;
+      }
+  }
+  return sh;
+}
+
+// 3-D tensor map viewing a (rows, K) 16-bit matrix with a row stride of ld elements as (64, rows, K / 64): box
+// (64, box_rows, nblk) = nblk consecutive 64-wide K blocks of box_rows rows; 128-byte swizzle, zeros outside.
+int make_blocks_map(CUtensorMap* m, const void* ptr, int dtype, int rows, int K, int64_t ld, int box_rows, int nblk,
+                    const char* what) {
+  if (int r = get_encode_tiled()) return r;
+  const cuuint64_t dims[3] = {(cuuint64_t)ta::LIN_KB, (cuuint64_t)rows, (cuuint64_t)(K / ta::LIN_KB)};
+  const cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)ta::LIN_KB * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)ta::LIN_KB, (cuuint32_t)box_rows, (cuuint32_t)nblk};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode_tiled(m, dtype == TA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                    3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TA_ERR_ARG, "ta_linear_rows: tensor map of the %s rejected (CUresult %d)", what, (int)r);
+  return TA_OK;
+}
+
+template <typename T, int MODE>
+int launch_linear(const CUtensorMap& tw, const CUtensorMap& ta_, const ta::LinearParams& p, dim3 grid, size_t smem,
+                  cudaStream_t st) {
+  static SmemAttr attr;
+  if (int r = allow_smem(attr, ta::linear_rows_kernel<T, MODE>, smem, "ta_linear_rows")) return r;
+  const cudaError_t e = launch_pdl(ta::linear_rows_kernel<T, MODE>, grid, dim3(ta::LIN_THREADS), smem, st, tw, ta_, p);
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_linear_rows: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("ta_linear_rows");
+}
+
+template <typename T>
+int launch_linear_mode(int mode, const CUtensorMap& tw, const CUtensorMap& ta_, const ta::LinearParams& p, dim3 grid,
+                       size_t smem, cudaStream_t st) {
+  switch (mode) {
+    case ta::LIN_STORE: return launch_linear<T, ta::LIN_STORE>(tw, ta_, p, grid, smem, st);
+    case ta::LIN_GELU: return launch_linear<T, ta::LIN_GELU>(tw, ta_, p, grid, smem, st);
+    case ta::LIN_PARTIAL: return launch_linear<T, ta::LIN_PARTIAL>(tw, ta_, p, grid, smem, st);
+    default: return launch_linear<T, ta::LIN_ARGMAX>(tw, ta_, p, grid, smem, st);
+  }
+}
 
 // ================================================================================================== C ABI
 // Scratch of ta_lane_order_noalloc, in the library's own device memory: the second slot-order buffer that the
@@ -1348,6 +1436,97 @@ int ta_argmax_advance(const void* logits, int dtype, int B, int V, int64_t* tok,
     default: return fail(TA_ERR_ARG, "ta_argmax_advance: bad dtype %d", dtype);
   }
   return check_launch("ta_argmax_advance");
+}
+
+int ta_linear_supported(int dtype, int B, int N, int K, int splits) {
+  if (dtype != TA_BF16 && dtype != TA_F16) return 0;
+  if (B < 1 || B > ta::LIN_MAX_BN || N < 8 || N % 8 != 0 || K < ta::LIN_KB || splits < 1) return 0;
+  if (K % (ta::LIN_KB * splits) != 0) return 0;
+  return linear_shape((B + 15) / 16 * 16, K / splits).nst > 0 ? 1 : 0;
+}
+
+int ta_linear_rows(const void* act, int64_t act_ld, int dtype, int B, int N, int K, const void* w, int splits, int mode,
+                   void* out, int64_t out_ld, float* part, unsigned long long* keys, float* ws, int* counters,
+                   void* stream) {
+  g_err.clear();
+  if (dtype != TA_BF16 && dtype != TA_F16) return fail(TA_ERR_ARG, "ta_linear_rows: bf16 or f16 operands only");
+  if (B < 1 || B > ta::LIN_MAX_BN || N < 8 || N % 8 != 0 || K < ta::LIN_KB || splits < 1)
+    return fail(TA_ERR_ARG, "ta_linear_rows: bad sizes B=%d (1..%d) N=%d (a multiple of 8) K=%d splits=%d", B,
+                ta::LIN_MAX_BN, N, K, splits);
+  if (K % (ta::LIN_KB * splits) != 0)
+    return fail(TA_ERR_ARG, "K=%d is not a multiple of %d x splits (splits=%d)", K, ta::LIN_KB, splits);
+  if (mode < ta::LIN_STORE || mode > ta::LIN_ARGMAX) return fail(TA_ERR_ARG, "ta_linear_rows: bad mode %d", mode);
+  if (mode != ta::LIN_PARTIAL && splits > 1 && (!ws || !counters || !aligned16(ws)))
+    return fail(TA_ERR_ARG, "ta_linear_rows: mode %d with %d K splits needs the workspace and counters", mode, splits);
+  if (!act || !w) return fail(TA_ERR_ARG, "ta_linear_rows: null pointer");
+  if (!aligned16(act) || act_ld < K || act_ld % 8 != 0 || !aligned16(w))
+    return fail(TA_ERR_ARG, "ta_linear_rows: rows and weight must be 16-byte aligned with a row stride of >= K, a "
+                "multiple of 8 elements");
+  if (mode == ta::LIN_PARTIAL ? (!part || !aligned16(part)) : (!out || out_ld < N || out_ld % 8 != 0 || !aligned16(out)))
+    return fail(TA_ERR_ARG, "ta_linear_rows: missing, short or unaligned output for mode %d (16-byte aligned rows)",
+                mode);
+  if (mode == ta::LIN_ARGMAX && !keys) return fail(TA_ERR_ARG, "ta_linear_rows: ARGMAX needs the key buffer");
+  const int BN = (B + 15) / 16 * 16, Ks = K / splits;
+  const LinShape sh = linear_shape(BN, Ks);
+  if (sh.nst == 0)
+    return fail(TA_ERR_ARG, "ta_linear_rows: %d rows x %d of K per CTA do not fit in shared memory (use more splits)",
+                B, Ks);
+  const size_t smem = ta::linear_smem_bytes(BN, Ks, sh.nst, sh.nb);
+  CUtensorMap tw, trows;
+  if (int r = make_blocks_map(&tw, w, dtype, N, K, K, ta::LIN_MT, sh.nb, "weight")) return r;
+  if (int r = make_blocks_map(&trows, act, dtype, B, K, act_ld, BN, sh.na, "rows")) return r;
+  ta::LinearParams p{};
+  p.B = B;
+  p.BN = BN;
+  p.N = N;
+  p.K = K;
+  p.Ks = Ks;
+  p.nb = sh.nb;
+  p.na = sh.na;
+  p.nst = sh.nst;
+  p.out = out;
+  p.out_ld = out_ld;
+  p.part = part;
+  p.keys = keys;
+  p.ws = ws;
+  p.counters = counters;
+  const dim3 grid((unsigned)ta::ceil_div(N, ta::LIN_MT), (unsigned)splits);
+  return dtype == TA_BF16 ? launch_linear_mode<__nv_bfloat16>(mode, tw, trows, p, grid, smem, S(stream))
+                          : launch_linear_mode<__half>(mode, tw, trows, p, grid, smem, S(stream));
+}
+
+int ta_add_splits_ln(float* x, const float* part, int splits, int dtype, int B, int C, const float* w, float eps,
+                     void* h, void* stream) {
+  g_err.clear();
+  if (!x || !part || !w || !h) return fail(TA_ERR_ARG, "ta_add_splits_ln: null pointer");
+  if (dtype != TA_BF16 && dtype != TA_F16) return fail(TA_ERR_ARG, "ta_add_splits_ln: bf16 or f16 rows only");
+  if (B < 0 || C < 8 || C % 8 != 0 || splits < 1 || !aligned16(x) || !aligned16(part) || !aligned16(h))
+    return fail(TA_ERR_ARG, "ta_add_splits_ln: bad sizes or alignment (C a multiple of 8, 16-byte aligned rows)");
+  if (B == 0) return TA_OK;
+  if (C > 8 * 1024) return fail(TA_ERR_ARG, "ta_add_splits_ln: row width %d above 8192", C);
+  const dim3 grid((unsigned)B), block((unsigned)(((C / 8) + 31) / 32 * 32));
+  cudaStream_t st = S(stream);
+  cudaError_t e;
+  if (dtype == TA_BF16)
+    e = launch_pdl(ta::add_splits_ln_kernel<__nv_bfloat16>, grid, block, 0, st, x, part, splits, B, C, w, eps,
+                   reinterpret_cast<__nv_bfloat16*>(h));
+  else
+    e = launch_pdl(ta::add_splits_ln_kernel<__half>, grid, block, 0, st, x, part, splits, B, C, w, eps,
+                   reinterpret_cast<__half*>(h));
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_add_splits_ln: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("ta_add_splits_ln");
+}
+
+int ta_argmax_finish(const unsigned long long* keys, int n_tiles, int B, int V, int64_t* tok, int32_t* pos,
+                     void* stream) {
+  g_err.clear();
+  if (!keys || !tok || !pos) return fail(TA_ERR_ARG, "ta_argmax_finish: null pointer");
+  if (B < 0 || n_tiles < 1 || V < 1) return fail(TA_ERR_ARG, "ta_argmax_finish: bad sizes");
+  if (B == 0) return TA_OK;
+  const cudaError_t e = launch_pdl(ta::argmax_finish_kernel, dim3((unsigned)((B + 3) / 4)), dim3(128), 0, S(stream),
+                                   keys, n_tiles, B, V, tok, pos);
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_argmax_finish: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("ta_argmax_finish");
 }
 
 int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,

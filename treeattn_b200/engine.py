@@ -28,6 +28,20 @@ def _positions(t, B, device):
     return torch.full((B,), int(t), device=device, dtype=torch.int32)
 
 
+def _pick_splits(N, K, target=36, min_k=128):
+    """K splits of an (N, K) projection for ta_linear_rows: the fewest that give `target` CTAs (N / 128 feature
+    tiles each) with slices of at least min_k, a whole number of 64-wide blocks each."""
+    tiles, blocks = -(-N // _ops.LIN_TILE), K // 64
+    best = 1
+    for sp in range(1, blocks + 1):
+        if blocks % sp or (K // sp) < min_k:
+            continue
+        best = sp
+        if tiles * sp >= target:
+            break
+    return best
+
+
 class SegState:
     """Per-layer cache for a batch of sequences: keys, values and the tree levels L0..Lm (reference
     engine.py:18-71; a node is formed the moment its last position is added).
@@ -229,7 +243,7 @@ class Decoder:
     additions. The residual stream is kept in fp32; matmuls run in `dtype` on cuBLAS."""
 
     def __init__(self, W, n_layer, n_head, n_embd, Tcap, mode='seg', cfg=None, dev='cuda', batch=1, dtype=None,
-                 cap=None, graphs=True, splits=0):
+                 cap=None, graphs=True, splits=0, fused_linear=None):
         if mode not in ('seg', 'dense'):
             raise NotImplementedError("Decoder mode '%s' is not implemented in treeattn_b200 ('seg', 'dense')" % mode)
         if mode == 'seg' and cfg is None:
@@ -258,6 +272,20 @@ class Decoder:
         self.scale = 1.0 / math.sqrt(self.dh)
         self.use_graphs = graphs
         self.splits = (splits or _ops.default_splits(batch, n_head, self.dh, self.dtype)) if seg else 0
+        # fused_linear=True: the linear layers on the library's tensor-core kernel (ta_linear_rows: 16-bit weights,
+        # K slices of 64) instead of torch matmuls; K splits of c_proj and c_mlp so that enough CTAs stream their
+        # weights. Off by default: measured slower than cuBLAS at the configuration-4 shapes so far.
+        V = self.W['wte'].shape[0]
+        C = n_embd
+        # per projection: K splits on ta_linear_rows, or 0 = torch's matmul (cuBLAS) where that measured faster
+        self.lin_splits = dict(qkv=0, proj=_pick_splits(C, C), fc=0, mlp=_pick_splits(C, 4 * C, target=96), lm=0)
+        shapes = dict(qkv=(3 * C, C), proj=(C, C), fc=(4 * C, C), mlp=(C, 4 * C), lm=(V, C))
+        ok = all(sp == 0 or _ops.linear_supported(self.dtype, batch, shapes[k][0], shapes[k][1], sp)
+                 for k, sp in self.lin_splits.items())
+        self.fused_linear = False if fused_linear is None else bool(fused_linear)
+        if self.fused_linear and not ok:
+            raise ValueError('fused_linear: ta_linear_rows does not take this model (16-bit weights, width and '
+                             'batch it supports)')
         self.reset()
 
     @classmethod
@@ -292,10 +320,89 @@ class Decoder:
         # partial-state scratch that lets the decode kernel cut items into parts when whole items would leave SMs
         # idle (shared by the layers: their launches run in order on one stream)
         self._split = _ops.split_scratch(B, self.H, self.dh, dev) if self.mode == 'seg' else None
+        if self.fused_linear:  # K-split sums of c_proj / c_mlp, the lm_head's per-tile argmax keys, split workspace
+            ls = self.lin_splits
+            self._part = torch.empty(max(ls['proj'], ls['mlp'], 1), B, C, device=dev, dtype=torch.float32)
+            V = self.W['wte'].shape[0]
+            self._keys = torch.zeros(-(-V // _ops.LIN_TILE), B, device=dev, dtype=torch.int64)
+            n_ws = max([ls[k] * -(-N // _ops.LIN_TILE) for k, N in (('qkv', 3 * C), ('fc', 4 * C), ('lm', V))
+                        if ls[k] > 1] + [1])
+            self._ws = (torch.empty(n_ws * B * _ops.LIN_TILE, device=dev, dtype=torch.float32),
+                        torch.zeros(-(-V // _ops.LIN_TILE), device=dev, dtype=torch.int32))
         self._graph = None
         self._graph_greedy = None
 
     # -------------------------------------------------------------- one model step on the static buffers
+    def _attend(self, i, record):
+        """Layer i's attention for the step: q/k/v rows in self._qkv -> self._att (and the cache / tree update)."""
+        st = self.states[i]
+        if self.mode == 'dense':
+            st.attend(self._qkv, self._pos, self._att, self._nkeys[i])
+        elif self.general:
+            B, C, H, dh = self.batch, self.C, self.H, self.dh
+            q, k, v = [self._qkv[:, j * C:(j + 1) * C].view(B, H, 1, dh) for j in range(3)]
+            _, nk = _general_step(st, self.W['layers'][i].get('pw'), q, k, v, self._pos,
+                                  out=self._att.view(B, H, 1, dh))
+            self._nkeys[i].copy_(nk.view(B, H))
+        else:
+            sel = None
+            if record is not None:  # the selected leaves as well: (B, H, 1 + wmax) count, then leaf ids
+                sel = torch.empty(self.batch, self.H, self.wmax + 1, device=self.dev, dtype=torch.int32)
+                record[-1]['sel'] = sel
+            _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree, self.Lw,
+                             self.scale, self._att, nkeys=self._nkeys[i], sel=sel, splits=self.splits,
+                             scratch=self._split)
+
+    def _linear(self, name, act, w, mode, out=None, part=None):
+        """One projection of the step: ta_linear_rows with self.lin_splits[name] K splits, or torch's matmul (and
+        the GELU kernel) when that is 0."""
+        sp = self.lin_splits[name]
+        if sp == 0:
+            torch.mm(act, w.t(), out=out)
+            if mode == _ops.LIN_GELU:
+                _ops.gelu_(out)
+            return
+        _ops.linear_rows(act, w, mode, out=out, splits=sp, part=part, keys=self._keys, ws=self._ws)
+
+    def _forward_step_fused(self, record=None, greedy=False):
+        """_forward_step on the library's linear kernel: per layer [h] qkv = h Wa^T, attention, part = att Wp^T
+        (K split), [x += sum(part); h = ln2(x)], fc = gelu(h Wf^T), part = fc Wm^T (K split), [x += sum(part);
+        h = ln1'(x)]; then the lm_head, with the greedy argmax and the position advance when `greedy`. The library's
+        launches are chained by programmatic dependent launch; projections marked 0 in lin_splits stay on cuBLAS."""
+        W = self.W
+        L = W['layers']
+        sp, sm = self.lin_splits['proj'], self.lin_splits['mlp']
+        _ops.embed_ln(W['wte'], W['wpe'], self._tok, self._pos, L[0]['ln1'], self._x, self._h)
+        for i, Li in enumerate(L):
+            if record is not None:
+                record.append(dict(x_in=self._x.clone()))
+            self._linear('qkv', self._h, Li['c_attn'], _ops.LIN_STORE, out=self._qkv)
+            self._attend(i, record)
+            if sp:
+                _ops.linear_rows(self._att, Li['c_proj'], _ops.LIN_PARTIAL, splits=sp, part=self._part[:sp])
+                _ops.add_splits_ln(self._x, self._part[:sp], Li['ln2'], self._h)
+            else:
+                torch.mm(self._att, Li['c_proj'].t(), out=self._proj)
+                _ops.add_ln(self._x, self._proj, Li['ln2'], self._h)
+            self._linear('fc', self._h, Li['c_fc'], _ops.LIN_GELU, out=self._fc)
+            nxt = L[i + 1]['ln1'] if i + 1 < len(L) else W['ln_f']
+            if sm:
+                _ops.linear_rows(self._fc, Li['c_mlp'], _ops.LIN_PARTIAL, splits=sm, part=self._part[:sm])
+                _ops.add_splits_ln(self._x, self._part[:sm], nxt, self._h)
+            else:
+                torch.mm(self._fc, Li['c_mlp'].t(), out=self._mlp)
+                _ops.add_ln(self._x, self._mlp, nxt, self._h)
+            if record is not None:
+                record[-1].update(qkv=self._qkv.clone(), att=self._att.clone(), x_out=self._x.clone())
+        if greedy and self.lin_splits['lm']:
+            self._linear('lm', self._h, W['wte'], _ops.LIN_ARGMAX, out=self._logits)
+            _ops.argmax_finish(self._keys, W['wte'].shape[0], self._tok, self._pos)
+        else:
+            self._linear('lm', self._h, W['wte'], _ops.LIN_STORE, out=self._logits)
+            if greedy:
+                _ops.argmax_advance(self._logits, self._tok, self._pos)
+        return self._logits
+
     def _forward_step(self, record=None):
         """Logits (B, V) of the tokens in self._tok at positions self._pos; appends their K/V to every layer.
         Per layer: [x += mlp; h = ln1(x)] qkv-matmul, fused decode attention, c_proj-matmul, [x += proj;
@@ -303,29 +410,16 @@ class Decoder:
         `record` (a list; eager steps only) receives per layer copies of the residual entering it (x_in), its
         q/k/v rows, its attention output, its selected leaves (fused decode only) and the residual leaving it
         (x_out), for layer-by-layer checks."""
+        if self.fused_linear:
+            return self._forward_step_fused(record)
         W = self.W
         L = W['layers']
         _ops.embed_ln(W['wte'], W['wpe'], self._tok, self._pos, L[0]['ln1'], self._x, self._h)
         for i, Li in enumerate(L):
-            st = self.states[i]
             if record is not None:
                 record.append(dict(x_in=self._x.clone()))
             torch.mm(self._h, Li['c_attn'].t(), out=self._qkv)
-            if self.mode == 'dense':
-                st.attend(self._qkv, self._pos, self._att, self._nkeys[i])
-            elif self.general:
-                B, C, H, dh = self.batch, self.C, self.H, self.dh
-                q, k, v = [self._qkv[:, j * C:(j + 1) * C].view(B, H, 1, dh) for j in range(3)]
-                _, nk = _general_step(st, Li.get('pw'), q, k, v, self._pos, out=self._att.view(B, H, 1, dh))
-                self._nkeys[i].copy_(nk.view(B, H))
-            else:
-                sel = None
-                if record is not None:  # the selected leaves as well: (B, H, 1 + wmax) count, then leaf ids
-                    sel = torch.empty(self.batch, self.H, self.wmax + 1, device=self.dev, dtype=torch.int32)
-                    record[-1]['sel'] = sel
-                _ops.decode_step(self._qkv, st.K, st.V, st.levels, self._pos, self.H, self.wmax, self.n_tree,
-                                 self.Lw, self.scale, self._att, nkeys=self._nkeys[i], sel=sel, splits=self.splits,
-                                 scratch=self._split)
+            self._attend(i, record)
             torch.mm(self._att, Li['c_proj'].t(), out=self._proj)
             _ops.add_ln(self._x, self._proj, Li['ln2'], self._h)
             torch.mm(self._h, Li['c_fc'].t(), out=self._fc)
@@ -338,6 +432,8 @@ class Decoder:
         return self._logits
 
     def _greedy_step(self):
+        if self.fused_linear:
+            return self._forward_step_fused(greedy=True)
         logits = self._forward_step()
         _ops.argmax_advance(logits, self._tok, self._pos)
         return logits
