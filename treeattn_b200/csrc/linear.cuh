@@ -351,9 +351,9 @@ __global__ void __launch_bounds__(128) argmax_finish_kernel(const unsigned long 
 
 // x[b] += round_T(sum over the splits s = 0 .. S-1 of part[s, b]) (the projection's output rounded to the model
 // dtype, as F.linear returns it, added to the fp32 residual), h[b] = LN(x[b]) * w (T). One CTA per row, one thread
-// per 8 features (C a multiple of 8, at most 8 x 1024), 16-byte accesses; each thread requests the splits' pieces
+// per 8 features (C a multiple of 8, at most 8 x 256), 16-byte accesses; each thread requests the splits' pieces
 // eight at a time before adding them, in split order.
-constexpr int ASL_MAX_WARPS = 32;
+constexpr int ASL_MAX_WARPS = 8;
 
 __device__ __forceinline__ float block_sum_rows(float v, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
@@ -367,7 +367,7 @@ __device__ __forceinline__ float block_sum_rows(float v, float* red) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(1024) add_splits_ln_kernel(float* x, const float* __restrict__ part, int S, int B,
+__global__ void __launch_bounds__(256) add_splits_ln_kernel(float* x, const float* __restrict__ part, int S, int B,
                                                              int C, const float* __restrict__ w, float eps, T* h) {
   __shared__ float red[ASL_MAX_WARPS];
   pdl_wait();

@@ -1503,7 +1503,7 @@ int ta_add_splits_ln(float* x, const float* part, int splits, int dtype, int B, 
   if (B < 0 || C < 8 || C % 8 != 0 || splits < 1 || !aligned16(x) || !aligned16(part) || !aligned16(h))
     return fail(TA_ERR_ARG, "ta_add_splits_ln: bad sizes or alignment (C a multiple of 8, 16-byte aligned rows)");
   if (B == 0) return TA_OK;
-  if (C > 8 * 1024) return fail(TA_ERR_ARG, "ta_add_splits_ln: row width %d above 8192", C);
+  if (C > 8 * 256) return fail(TA_ERR_ARG, "ta_add_splits_ln: row width %d above 2048", C);
   const dim3 grid((unsigned)B), block((unsigned)(((C / 8) + 31) / 32 * 32));
   cudaStream_t st = S(stream);
   cudaError_t e;

@@ -274,11 +274,12 @@ class Decoder:
         self.splits = (splits or _ops.default_splits(batch, n_head, self.dh, self.dtype)) if seg else 0
         # fused_linear=True: the linear layers on the library's tensor-core kernel (ta_linear_rows: 16-bit weights,
         # K slices of 64) instead of torch matmuls; K splits of c_proj and c_mlp so that enough CTAs stream their
-        # weights. Off by default: measured slower than cuBLAS at the configuration-4 shapes so far.
+        # weights. Off by default: whole configuration-4 steps measured 0.948 ms with it against 0.937 on cuBLAS.
         V = self.W['wte'].shape[0]
         C = n_embd
         # per projection: K splits on ta_linear_rows, or 0 = torch's matmul (cuBLAS) where that measured faster
-        self.lin_splits = dict(qkv=0, proj=_pick_splits(C, C), fc=0, mlp=_pick_splits(C, 4 * C, target=96), lm=0)
+        # (configuration 4, whole steps: c_fc with its GELU, c_proj and c_mlp here, c_attn and the lm_head on cuBLAS)
+        self.lin_splits = dict(qkv=0, proj=_pick_splits(C, C), fc=1, mlp=_pick_splits(C, 4 * C, target=96), lm=0)
         shapes = dict(qkv=(3 * C, C), proj=(C, C), fc=(4 * C, C), mlp=(C, 4 * C), lm=(V, C))
         ok = all(sp == 0 or _ops.linear_supported(self.dtype, batch, shapes[k][0], shapes[k][1], sp)
                  for k, sp in self.lin_splits.items())
