@@ -493,7 +493,10 @@ struct __align__(16) PShared {
 template <typename T, int DH, int CH, int NST, int NCG, int WPG>
 struct PCfg {
   static constexpr int NCW = NCG * WPG;
-  static constexpr int NTHREADS = (NCW + 3) * 32;  // consumers, producer, selector, finalizer
+  // two producer warps for 256-byte rows (keys and values issued separately: measured faster there), one for
+  // narrower rows (no gain measured)
+  static constexpr int NPROD = (DH * (int)sizeof(T) >= 256) ? 2 : 1;
+  static constexpr int NTHREADS = (NCW + 2 + NPROD) * 32;  // consumers, producer(s), selector, finalizer
   static constexpr int STAGE_ELEMS = 2 * CH * DH;
   static constexpr size_t RING_BYTES = (size_t)NST * STAGE_ELEMS * sizeof(T);
   static constexpr int TU_FLOATS = 2048;
@@ -554,7 +557,8 @@ __device__ void tree_update_warp(const T* __restrict__ kbase, int64_t c_st, cons
 
 // SPLIT: items cut into p.psplit parts (a separate instantiation, so that whole items run the unsplit code).
 template <typename T, int DH, int CH, int NST, int NCG, int WPG, bool SPLIT>
-__global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel(DecodeParams p, int stage_rows) {
+__global__ void __launch_bounds__(PCfg<T, DH, CH, NST, NCG, WPG>::NTHREADS) decode_persistent_kernel(DecodeParams p,
+                                                                                                   int stage_rows) {
   using Cfg = PCfg<T, DH, CH, NST, NCG, WPG>;
   constexpr int NCW = Cfg::NCW;
   using Sh = typename Cfg::Sh;
@@ -567,7 +571,10 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
   // could reach a slot whose previous phase (the other group's stage) is still in flight, and a parity wait would
   // take the older completed phase of the same parity for the new one.
   static_assert(NCW >= 2 && NST <= 16 && NST % NCG == 0, "pipeline shape");
-  constexpr int W_PROD = NCW, W_SEL = NCW + 1, W_FIN = NCW + 2;
+  // with two producer warps W_PROD issues every stage's key copies (and writes the stage descriptors), W_PROD_V the
+  // value copies: one thread's bulk copies proceed one after another, so two issuers keep more in flight
+  constexpr int NPROD = Cfg::NPROD;
+  constexpr int W_PROD = NCW, W_SEL = NCW + 1, W_FIN = NCW + 2, W_PROD_V = NPROD == 2 ? NCW + 3 : -1;
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Sh& sh = *reinterpret_cast<Sh*>(smem_raw);
@@ -599,7 +606,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
-      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.full[s], NPROD);  // one arrival per producer warp
       mbar_init(&sh.empty[s], WPG);
     }
     for (int s = 0; s < PSLOTS; ++s) {
@@ -675,8 +682,13 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.ifull[slot]);
     }
-  } else if (warp == W_PROD) {
-    // ------------------------------------------------------------------ producer warp (lane 0 issues)
+  } else if (warp == W_PROD || warp == W_PROD_V) {
+    // ------------------------------------------------------------------ producer warps (lane 0 issues)
+    // Both run the same stage sequence; the key producer writes each stage's descriptor before its arrival, and
+    // a stage is complete (full[s]) once both producers have arrived and all of its bytes have landed.
+    const bool vrole = warp == W_PROD_V;
+    const bool kcopy = !vrole, vcopy = vrole || NPROD == 1;  // which copies this warp issues
+    const uint32_t nsides = (kcopy ? 1u : 0u) + (vcopy ? 1u : 0u);
     int it = 0;
     bool ok = true;
     if (lane == 0) {
@@ -717,13 +729,16 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
           int s;
           if (!(ok = acquire(s))) break;
           const int n = min(CH, w1 - r0);
-          sh.nrows[s] = n;
-          sh.flags[s] = flags_for(false);
-          sh.slot[s] = slot;
+          const int f = flags_for(false);
+          if (!vrole) {
+            sh.nrows[s] = n;
+            sh.flags[s] = f;
+            sh.slot[s] = slot;
+          }
           T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
-          mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
-          bulk_g2s_hint(kd, kbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
-          bulk_g2s_hint(kd + CH * DH, vbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
+          mbar_arrive_expect_tx(&sh.full[s], nsides * (uint32_t)(n * ROWB));
+          if (kcopy) bulk_g2s_hint(kd, kbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
+          if (vcopy) bulk_g2s_hint(kd + CH * DH, vbase + (int64_t)r0 * p.c_st, (uint32_t)(n * ROWB), &sh.full[s], pol);
           ++it;
         }
         if (!ok) break;
@@ -746,19 +761,24 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
                 if (roff2 == len) { ++ri2; roff2 = 0; }
               }
             }
-            sh.nrows[s] = n;
-            sh.flags[s] = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
-            sh.slot[s] = slot;
+            const int f = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
+            if (!vrole) {
+              sh.nrows[s] = n;
+              sh.flags[s] = f;
+              sh.slot[s] = slot;
+            }
             T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
-            mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+            mbar_arrive_expect_tx(&sh.full[s], nsides * (uint32_t)(n * ROWB));
             int put = 0;
             while (put < n) {
               const int len = rl.pref[ri + 1] - rl.pref[ri];
               const int take = min(n - put, len - roff);
               const int64_t r0 = rl.start[ri] + roff;
-              bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
-              bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s],
-                            pol);
+              if (kcopy)
+                bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
+              if (vcopy)
+                bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB),
+                              &sh.full[s], pol);
               put += take;
               roff += take;
               if (roff == len) { ++ri; roff = 0; }
@@ -789,19 +809,24 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
                 if (roff2 == len) { ++ri2; roff2 = 0; }
               }
             }
-            sh.nrows[s] = n;
-            sh.flags[s] = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
-            sh.slot[s] = slot;
+            const int f = flags_for(j >= n_leaf_stages - NCG);  // the last stage of each group ends the item
+            if (!vrole) {
+              sh.nrows[s] = n;
+              sh.flags[s] = f;
+              sh.slot[s] = slot;
+            }
             T* kd = ring + (size_t)s * Cfg::STAGE_ELEMS;
-            mbar_arrive_expect_tx(&sh.full[s], (uint32_t)(2 * n * ROWB));
+            mbar_arrive_expect_tx(&sh.full[s], nsides * (uint32_t)(n * ROWB));
             int put = 0;
             while (put < n) {
               const int len = rl.pref[ri + 1] - rl.pref[ri];
               const int take = min(n - put, len - roff);
               const int64_t r0 = rl.start[ri] + roff;
-              bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
-              bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s],
-                            pol);
+              if (kcopy)
+                bulk_g2s_hint(kd + (size_t)put * DH, kbase + r0 * p.c_st, (uint32_t)(take * ROWB), &sh.full[s], pol);
+              if (vcopy)
+                bulk_g2s_hint(kd + (size_t)(CH + put) * DH, vbase + r0 * p.c_st, (uint32_t)(take * ROWB),
+                              &sh.full[s], pol);
               put += take;
               roff += take;
               if (roff == len) { ++ri; roff = 0; }
@@ -813,9 +838,12 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
         while (ok && lasted != (1u << NCG) - 1u) {  // groups still without a LAST: empty end-of-item stages
           int s;
           if (!(ok = acquire(s))) break;
-          sh.nrows[s] = 0;
-          sh.flags[s] = flags_for(true);
-          sh.slot[s] = slot;
+          const int f = flags_for(true);
+          if (!vrole) {
+            sh.nrows[s] = 0;
+            sh.flags[s] = f;
+            sh.slot[s] = slot;
+          }
           mbar_arrive(&sh.full[s]);
           ++it;
         }
@@ -823,7 +851,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       for (int g = 0; g < NCG && ok; ++g) {  // one sentinel per consumer group
         int s;
         if ((ok = acquire(s))) {
-          sh.nrows[s] = -1;
+          if (!vrole) sh.nrows[s] = -1;
           mbar_arrive(&sh.full[s]);
           ++it;
         }
@@ -831,7 +859,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
       if (!ok) atomicExch(&sh.abort_flag, 1);
     }
     __syncwarp();
-    named_bar_sync(2, (NCW + 1) * 32);
+    named_bar_sync(2, (NCW + NPROD) * 32);
     if (lane == 0) {  // no bulk copy of this CTA may still be in flight when it exits
       for (int i = 0; i < it; ++i)
         if (i >= sh.consumed[i % NCG]) mbar_wait_bounded(&sh.full[i % NST], (i / NST) & 1, K_DECODE, 2);
@@ -1009,7 +1037,7 @@ __global__ void __launch_bounds__((NCG * WPG + 3) * 32) decode_persistent_kernel
     }
     if (!ok) atomicExch(&sh.abort_flag, 1);
     if (wig == 0 && lane == 0) sh.consumed[cg] = it;
-    named_bar_sync(2, (NCW + 1) * 32);
+    named_bar_sync(2, (NCW + NPROD) * 32);
   }
 }
 

@@ -470,17 +470,8 @@ struct GatherDotBlocks {
     if (grid == 0) return TA_OK;
     // programmatic dependent launch: a chain of these short, latency-bound calls overlaps each launch with the
     // previous call (the kernel waits for the previous grid before its first global read)
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, ta::gather_dot_blocks_kernel<T, DH>, p);
+    const cudaError_t e = launch_pdl(ta::gather_dot_blocks_kernel<T, DH>, dim3((unsigned)grid), dim3(128), smem, st, p);
+    if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_gather_dot_blocks: launch failed: %s", cudaGetErrorString(e));
     return check_launch("ta_gather_dot_blocks");
   }
 };
