@@ -522,18 +522,20 @@ def test_decode_long_context_wide_heads(splits):
     _no_device_error()
 
 
-@pytest.mark.parametrize('B,H,steps', [(10, 16, 6), (20, 16, 3)])
-def test_decode_split_items_match_whole_items(B, H, steps):
-    """Persistent decode with 256-byte rows (dh 128 bf16, one CTA per SM) and the split scratch: items cut into parts
-    (windows and leaf rows shared out, partial states merged by the last part) give the outputs of whole items up to
-    the merge order, the same selections and key counts, and the same caches and tree (appended once), over steps
-    that complete leaf blocks."""
+@pytest.mark.parametrize('B,H,steps,dh', [(10, 16, 6, 128), (20, 16, 3, 128), (8, 12, 4, 64), (3, 12, 3, 64)])
+def test_decode_split_items_match_whole_items(B, H, steps, dh):
+    """Persistent decode with the split scratch: items cut into parts (windows and leaf rows shared out, partial
+    states merged by the last part) give the outputs of whole items up to the merge order, the same selections and
+    key counts, and the same caches and tree (appended once), over steps that complete leaf blocks. 256-byte rows
+    (dh 128 bf16, one CTA per SM) split the last round's items; 128-byte rows split every item when there are fewer
+    items than CTA slots (small batches: 96 and 36 items)."""
     ops = _ops()
     from treeattn_b200._ops import Levels
-    dt, dh, L0, wmax, local = torch.bfloat16, 128, 7, 32, 256
+    dt = torch.bfloat16
+    L0, wmax, local = (7, 32, 256) if dh == 128 else (6, 16, 128)
     rng = np.random.default_rng(B)
     C = H * dh
-    T0 = (rng.integers(3000, 6000, B) // 128 * 128 - 2).tolist()
+    T0 = (rng.integers(3000, 6000, B) // (1 << L0) * (1 << L0) - 2).tolist()
     cap = max(T0) + steps + 1
     Lm = int(math.ceil(math.log2(cap)))
     kc = torch.randn(B, H, cap, dh, device=DEV).to(dt)

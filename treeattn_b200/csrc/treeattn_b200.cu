@@ -513,8 +513,8 @@ int num_sms() {
   return n;
 }
 
-// Decode mode for B*H (b, h) pairs of row_bytes-wide K/V rows: -1 = persistent pipelined kernel (enough pairs
-// for every SM, rows of at most 128 bytes so that two CTAs share an SM), otherwise the number of CTAs per (b, h)
+// Decode mode for B*H (b, h) pairs of row_bytes-wide K/V rows: -1 = persistent pipelined kernel (rows of at most
+// 128 bytes, so that two CTAs share an SM, or enough pairs for every SM), otherwise the number of CTAs per (b, h)
 // of the cluster kernel (~4 resident CTAs per SM). With wider rows the persistent kernel runs one CTA per SM and
 // its consumer warps cannot hide their latency, so the cluster kernel (several CTAs per SM) streams faster once
 // there are about three pairs per SM; below that (e.g. 320 pairs of 32768-token contexts, dh 128: 0.54 vs 0.47
@@ -523,6 +523,10 @@ int default_splits(int B, int H, int row_bytes) {
   const int pairs = B * H;
   if (pairs <= 0) return 1;
   if (pairs >= num_sms()) return (row_bytes <= 128 || pairs < 3 * num_sms()) ? -1 : 1;
+  // fewer pairs than SMs with narrow rows: the persistent kernel cutting every item into parts (given the split
+  // scratch) descends from one round trip of node rows; the cluster kernel descends level by level (configuration-4
+  // rows, 96 pairs: 19.9 us against 35.8 us)
+  if (row_bytes <= 128) return -1;
   const int target = 4 * num_sms();
   int s = 1;
   while (s < 8 && pairs * s < target) s <<= 1;
@@ -628,6 +632,14 @@ struct Decode {
       if (PT > 1 && (int64_t)tail * PT <= (int64_t)items * 4) {  // the scratch holds 4 parts per item
         p.psplit = PT;
         p.n_whole = R * gmax;
+      }
+    } else if (p.part && p.part_cnt && items < gmax) {
+      // fewer items than CTA slots (small batches): every item in PT parts, so that each CTA streams a share of one
+      // item and the items' descents run side by side (the scratch holds 4 parts per item)
+      const int PT = std::min(std::min(TA_MAX_PSPLIT, 4), gmax / items);
+      if (PT > 1) {
+        p.psplit = PT;
+        p.n_whole = 0;
       }
     }
     const int units = p.n_whole + (items - p.n_whole) * p.psplit;
