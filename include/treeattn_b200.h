@@ -324,6 +324,31 @@ int ta_add_splits_ln(float* x, const float* part, int splits, int dtype, int B, 
 int ta_argmax_finish(const unsigned long long* keys, int n_tiles, int B, int V, int64_t* tok, int32_t* pos,
                      void* stream);
 
+/* The rest of a decode step's transformer block after its attention, and the next block's projection, in ONE
+ * launch (reference model.py:21-44 Block.forward after attn: x + c_proj(y), ln_2, c_fc, F.gelu, mlp c_proj,
+ * x + mlp; the next block's ln_1 and c_attn; engine.py:161-177 runs this once per decoded token per layer):
+ *   x += round(att w_proj^T);            h2 = LayerNorm(x) * ln2_w
+ *   fc = round(gelu(round(h2 w_fc^T)));  x += round(fc w_mlp^T)
+ *   h = LayerNorm(x) * ln_next_w;        qkv = round(h w_qkv^T)          (when w_qkv is given)
+ * att (B, C), h (B, C) and qkv (B, 3C) contiguous in `dtype` (bf16 or f16), x (B, C) fp32 in place; weights as
+ * nn.Linear stores them: w_proj (C, C), w_fc (4C, C), w_mlp (C, 4C), w_qkv (3C, C), contiguous 16-bit; ln2_w and
+ * ln_next_w (C,) fp32 (LayerNorm without bias, as ta_add_ln). w_qkv and qkv are both NULL after the last block
+ * (ln_next_w is then ln_f). 1 <= B <= 128, C a multiple of 128 up to 2048. The layer norms, roundings and GELU are
+ * those of ta_add_splits_ln / ta_linear_rows; the fp32 sums of each projection run in a fixed order, so repeated
+ * calls give identical results.
+ * One CTA per SM; all CTAs are resident together and order the phases through `sync` (sync_words int32, zero
+ * before the first call; every call leaves them zero). ws (ws_bytes) holds the projections' fp32 partial sums and
+ * the 16-bit rows between phases. Calls that share `sync` or `ws` must not overlap on the GPU. Every wait is
+ * bounded: a CTA that gives up records a device error (ta_device_error) and the others end early.
+ * Launched with programmatic dependent launch: the weight stream starts before the previous kernel of the stream
+ * has finished.
+ * ta_block_tail_plan: ws_bytes and sync_words for (dtype, B, C, with_qkv) on the current device, or TA_ERR_ARG
+ *   (with the reason) when ta_block_tail does not take the shape. */
+int ta_block_tail_plan(int dtype, int B, int C, int with_qkv, int64_t* ws_bytes, int* sync_words);
+int ta_block_tail(const void* att, float* x, const void* w_proj, const float* ln2_w, const void* w_fc,
+                  const void* w_mlp, const float* ln_next_w, const void* w_qkv, float eps, int dtype, int B, int C,
+                  void* h, void* qkv, void* ws, int64_t ws_bytes, int* sync, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

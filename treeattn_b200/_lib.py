@@ -63,6 +63,8 @@ SIGNATURES = {
     'ta_linear_rows': [P, L, I, I, I, I, P, I, I, P, L, P, P, P, P, P],
     'ta_add_splits_ln': [P, P, I, I, I, I, P, F, P, P],
     'ta_argmax_finish': [P, I, I, I, P, P, P],
+    'ta_block_tail_plan': [I, I, I, I, P, P],
+    'ta_block_tail': [P, P, P, P, P, P, P, P, F, I, I, I, P, P, P, L, P, P],
 }
 _RESTYPES = {'ta_last_error': ctypes.c_char_p, 'ta_level_nodes': c_int64}
 

@@ -4,6 +4,7 @@ Every function here takes CUDA tensors, checks shapes / dtypes / layouts, alloca
 library itself allocates nothing) and enqueues the kernel on the current torch stream of the tensors' device.
 CPU tensors are rejected: there is no CPU, Triton or eager-PyTorch fallback.
 """
+import ctypes
 import math
 
 import torch
@@ -481,6 +482,47 @@ def add_splits_ln(x, part, w, h_out, eps=1e-5):
 def argmax_finish(keys, V, tok, pos):
     """tok = the argmax packed in keys (tiles, B) by linear_rows' ARGMAX mode, pos += 1."""
     _lib.call('ta_argmax_finish', _p(keys), keys.shape[0], keys.shape[1], int(V), _p(tok), _p(pos), _stream(keys))
+
+
+def block_tail_plan(dtype, B, C, with_qkv=True):
+    """(workspace bytes, sync words) of ta_block_tail for B rows of width C on the current device, or None when it
+    does not take the shape."""
+    if dtype not in (torch.bfloat16, torch.float16):
+        return None
+    ws, ns = ctypes.c_int64(0), ctypes.c_int(0)
+    if _lib.load().ta_block_tail_plan(_DT[dtype], int(B), int(C), int(bool(with_qkv)), ctypes.byref(ws),
+                                      ctypes.byref(ns)) != 0:
+        return None
+    return int(ws.value), int(ns.value)
+
+
+def block_tail_buffers(dtype, B, C, device, with_qkv=True):
+    """(ws, sync) for block_tail: a byte workspace and zeroed int32 sync words (one pair per stream of calls)."""
+    plan = block_tail_plan(dtype, B, C, with_qkv)
+    if plan is None:
+        raise ValueError('block_tail: %d rows of width %d are not taken' % (B, C))
+    return (torch.empty(plan[0], device=device, dtype=torch.uint8),
+            torch.zeros(plan[1], device=device, dtype=torch.int32))
+
+
+def block_tail(att, x, w_proj, ln2, w_fc, w_mlp, ln_next, h_out, w_qkv=None, qkv_out=None, bufs=None, eps=1e-5):
+    """The rest of a block after its attention and the next block's projection, one launch (ta_block_tail):
+    x += c_proj(att); h2 = ln_2(x); x += c_mlp(gelu(c_fc(h2))); h_out = ln_next(x); qkv_out = c_attn'(h_out) when
+    w_qkv is given. att, h_out, qkv_out (B, *) 16-bit contiguous, x (B, C) fp32 in place, weights (out, in)
+    contiguous, ln weights fp32. bufs = block_tail_buffers(...) (allocated here when not given)."""
+    _need_cuda('block_tail', att, x, w_proj, w_fc, w_mlp, h_out)
+    B, C = x.shape
+    with_qkv = w_qkv is not None
+    if bufs is None:
+        bufs = block_tail_buffers(att.dtype, B, C, att.device, with_qkv)
+    for t in (att, x, w_proj, w_fc, w_mlp, h_out) + ((w_qkv, qkv_out) if with_qkv else ()):
+        if not t.is_contiguous():
+            raise ValueError('block_tail: contiguous tensors only')
+    ws, sync = bufs
+    _lib.call('ta_block_tail', _p(att), _p(x), _p(w_proj), _p(ln2), _p(w_fc), _p(w_mlp), _p(ln_next),
+              _p(w_qkv) if with_qkv else None, float(eps), _code(att), B, C, _p(h_out),
+              _p(qkv_out) if with_qkv else None, _p(ws), ws.numel(), _p(sync), _stream(x))
+    return h_out
 
 
 def default_splits(B, H, dh, dtype):

@@ -37,6 +37,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Order this thread's generic-proxy global accesses against its async-proxy ones (a TMA copy that reads rows that
+// generic stores wrote: the writer fences after its stores, the reader after it has observed them).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane (lane = 32 * (warp % 4) + lane id, encoded in taddr's
 // upper 16 bits by the caller), waited for before returning.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {

@@ -4,15 +4,20 @@
 
 #include <algorithm>
 #include <atomic>
+#include <climits>
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <utility>
+#include <vector>
 
 #include "../../include/treeattn_b200.h"
 #include <cudaTypedefs.h>
 
+#include "block.cuh"
 #include "decode.cuh"
 #include "dyn.cuh"
 #include "forest.cuh"
@@ -754,7 +759,7 @@ int make_blocks_map(CUtensorMap* m, const void* ptr, int dtype, int rows, int K,
                                     3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(TA_ERR_ARG, "ta_linear_rows: tensor map of the %s rejected (CUresult %d)", what, (int)r);
+  if (r != CUDA_SUCCESS) return fail(TA_ERR_ARG, "tensor map of the %s rejected (CUresult %d)", what, (int)r);
   return TA_OK;
 }
 
@@ -776,6 +781,179 @@ int launch_linear_mode(int mode, const CUtensorMap& tw, const CUtensorMap& ta_, 
     case ta::LIN_GELU: return launch_linear<T, ta::LIN_GELU>(tw, ta_, p, grid, smem, st);
     case ta::LIN_PARTIAL: return launch_linear<T, ta::LIN_PARTIAL>(tw, ta_, p, grid, smem, st);
     default: return launch_linear<T, ta::LIN_ARGMAX>(tw, ta_, p, grid, smem, st);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- block tail
+// Launch plan of block_tail_kernel for B rows of width C on G CTAs (one per SM): K splits per GEMM, the CTA offset of
+// each GEMM's units, the shared memory of the busiest CTA and the caller's workspace layout.
+struct TailPlan {
+  int BN = 0, maxc = 0, nslot = 0;
+  ta::TailGemm g[4] = {};
+  int off_ln = 0, nsync = 0;
+  size_t smem = 0;
+  size_t o_part_proj = 0, o_ws_fc = 0, o_part_mlp = 0, o_ws_qkv = 0, o_h2 = 0, o_fc = 0, ws_bytes = 0;
+};
+
+// Shared memory a block_tail_kernel block may use (the B200's 227 KiB opt-in limit).
+constexpr size_t kTailSmem = 227 * 1024;
+
+// Units of GEMM g that land on CTA c when its first unit sits on CTA `off`.
+int tail_units_on(const ta::TailGemm& g, int c, int off, int G) {
+  const int first = ((c - off) % G + G) % G;
+  return first < g.n ? (g.n - first + G - 1) / G : 0;
+}
+
+// Place every GEMM's units (largest units first) at the CTA offset that keeps the busiest CTA's weight bytes lowest
+// (ties: the most even spread), so that units of one phase land on different CTAs where they can. Returns the
+// busiest CTA's weight bytes, or SIZE_MAX if some CTA would hold more than BT_MAXU units.
+size_t place_tail_units(ta::TailGemm (&g)[4], int G) {
+  std::vector<size_t> bytes(G, 0);
+  std::vector<int> units(G, 0);
+  int order[4] = {0, 1, 2, 3};
+  std::sort(order, order + 4, [&](int a, int b) { return g[a].kc > g[b].kc || (g[a].kc == g[b].kc && a < b); });
+  for (int oi = 0; oi < 4; ++oi) {
+    ta::TailGemm& t = g[order[oi]];
+    t.off = 0;
+    if (t.n == 0) continue;
+    const size_t ub = (size_t)t.kc * ta::LIN_W_BYTES;
+    size_t best_max = SIZE_MAX;
+    double best_sq = 0.0;
+    for (int off = 0; off < G; ++off) {
+      size_t mx = 0;
+      double sq = 0.0;
+      for (int c = 0; c < G; ++c) {
+        const size_t b = bytes[c] + (size_t)tail_units_on(t, c, off, G) * ub;
+        mx = std::max(mx, b);
+        sq += (double)b * (double)b;
+      }
+      if (mx < best_max || (mx == best_max && sq < best_sq)) {
+        best_max = mx;
+        best_sq = sq;
+        t.off = off;
+      }
+    }
+    for (int c = 0; c < G; ++c) {
+      const int k = tail_units_on(t, c, t.off, G);
+      bytes[c] += (size_t)k * ub;
+      units[c] += k;
+    }
+  }
+  size_t mx = 0;
+  for (int c = 0; c < G; ++c) {
+    if (units[c] > ta::BT_MAXU) return SIZE_MAX;
+    mx = std::max(mx, bytes[c]);
+  }
+  return mx;
+}
+
+// Smallest K split of nk 64-wide blocks whose units hold at most kc_cap blocks.
+int split_for(int nk, int kc_cap) {
+  for (int d = 1; d <= nk; ++d)
+    if (nk % d == 0 && nk / d <= kc_cap) return d;
+  return nk;
+}
+
+bool make_tail_plan(int B, int C, bool with_qkv, int G, int esize, TailPlan& pl) {
+  pl = TailPlan{};
+  if (B < 1 || C < 128 || C % 128 != 0 || C > ta::BT_MAX_C || G < 1) return false;
+  pl.BN = (B + 15) / 16 * 16;
+  if (pl.BN > ta::BT_MAX_BN) return false;
+  pl.maxc = pl.BN <= 32 ? 32 : (pl.BN <= 64 ? 64 : 128);
+  const int F = 4 * C;
+  const int N[4] = {C, F, C, 3 * C}, K[4] = {C, C, F, C};
+  const int T[4] = {C / 128, F / 128, C / 128, 3 * C / 128};
+  // K splits: c_proj and c_mlp in slices of at most 6 / 8 blocks (their partial sums meet in the layer norm's
+  // rows); c_fc and c_attn whole when the rows' stage fits (no partial sums to exchange), else split with the
+  // tile's last split adding the others' sums
+  const int s_proj = split_for(K[0] / 64, 6), s_mlp = split_for(K[2] / 64, 8);
+  const int whole_opts[] = {1, 2, 3, 4, 6};
+  for (int sf : whole_opts)
+    for (int sq : whole_opts) {
+      const int S[4] = {s_proj, sf, s_mlp, with_qkv ? sq : 1};
+      bool ok = true;
+      for (int i = 0; i < 4 && ok; ++i) ok = (K[i] / 64) % S[i] == 0;
+      if (!ok) continue;
+      ta::TailGemm g[4];
+      int kc_max = 1;
+      for (int i = 0; i < 4; ++i) {
+        g[i].N = N[i];
+        g[i].K = K[i];
+        g[i].S = S[i];
+        g[i].kc = K[i] / 64 / S[i];
+        g[i].n = (i == ta::TG_QKV && !with_qkv) ? 0 : T[i] * S[i];
+        if (g[i].n > 0) kc_max = std::max(kc_max, g[i].kc);
+      }
+      if (place_tail_units(g, G) == SIZE_MAX) continue;
+      const size_t fixed = 1024 + ta::tail_stage_bytes(pl.BN, kc_max, C, std::max(S[0], S[2])) +
+                           sizeof(ta::TailBars) + 16;
+      if (fixed + 2 * (size_t)ta::LIN_W_BYTES > kTailSmem) continue;
+      const int nslot = (int)std::min<size_t>(ta::BT_MAX_SLOTS, (kTailSmem - fixed) / ta::LIN_W_BYTES);
+      std::copy(g, g + 4, pl.g);
+      pl.nslot = nslot;
+      pl.smem = fixed + (size_t)nslot * ta::LIN_W_BYTES;
+      pl.off_ln = 0;
+      pl.nsync = ta::TW_FIXED + 2 * T[1] + T[3];
+      // workspace: fp32 sums, then the 16-bit layer-norm and GELU rows (each piece 256-byte aligned)
+      size_t o = 0;
+      auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o += (bytes + 255) / 256 * 256;
+        return at;
+      };
+      pl.o_part_proj = take((size_t)S[0] * B * C * 4);
+      pl.o_ws_fc = take(S[1] > 1 ? (size_t)T[1] * S[1] * pl.BN * 128 * 4 : 0);
+      pl.o_part_mlp = take((size_t)S[2] * B * C * 4);
+      pl.o_ws_qkv = take(with_qkv && S[3] > 1 ? (size_t)T[3] * S[3] * pl.BN * 128 * 4 : 0);
+      pl.o_h2 = take((size_t)B * C * esize);
+      pl.o_fc = take((size_t)B * F * esize);
+      pl.ws_bytes = o;
+      return true;
+    }
+  return false;
+}
+
+// Plans are cached per (rows, width, with c_attn, CTAs, element size).
+std::mutex g_tail_mu;
+std::map<std::tuple<int, int, int, int, int>, TailPlan> g_tail_plans;
+
+bool tail_plan(int B, int C, bool with_qkv, int esize, TailPlan& pl) {
+  const int G = num_sms();
+  const auto key = std::make_tuple(B, C, (int)with_qkv, G, esize);
+  std::lock_guard<std::mutex> lk(g_tail_mu);
+  auto it = g_tail_plans.find(key);
+  if (it != g_tail_plans.end()) {
+    pl = it->second;
+    return pl.BN > 0;
+  }
+  const bool ok = make_tail_plan(B, C, with_qkv, G, esize, pl);
+  if (!ok) pl = TailPlan{};
+  g_tail_plans[key] = pl;
+  return ok;
+}
+
+template <typename T, int MAXC>
+int launch_tail(const ta::TailMaps& m, const ta::BlockTailParams& p, size_t smem, cudaStream_t st) {
+  auto kern = ta::block_tail_kernel<T, MAXC>;
+  static SmemAttr attr;
+  if (int r = allow_smem(attr, kern, smem, "ta_block_tail")) return r;
+  // every CTA must be resident at once (the phases wait on each other's counters)
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, ta::BT_THREADS, smem) != cudaSuccess)
+    return check_launch("ta_block_tail");
+  if ((int64_t)per_sm * num_sms() < p.G)
+    return fail(TA_ERR_ARG, "ta_block_tail: %d CTAs cannot all be resident (%d per SM)", p.G, per_sm);
+  const cudaError_t e = launch_pdl(kern, dim3((unsigned)p.G), dim3(ta::BT_THREADS), smem, st, m, p);
+  if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_block_tail: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("ta_block_tail");
+}
+
+template <typename T>
+int launch_tail_by_c(int maxc, const ta::TailMaps& m, const ta::BlockTailParams& p, size_t smem, cudaStream_t st) {
+  switch (maxc) {
+    case 32: return launch_tail<T, 32>(m, p, smem, st);
+    case 64: return launch_tail<T, 64>(m, p, smem, st);
+    default: return launch_tail<T, 128>(m, p, smem, st);
   }
 }
 
@@ -1530,6 +1708,85 @@ int ta_argmax_finish(const unsigned long long* keys, int n_tiles, int B, int V, 
                                    keys, n_tiles, B, V, tok, pos);
   if (e != cudaSuccess) return fail(TA_ERR_CUDA, "ta_argmax_finish: launch failed: %s", cudaGetErrorString(e));
   return check_launch("ta_argmax_finish");
+}
+
+#ifdef TA_TAIL_TRACE
+// Profiling build only: the block tail's phase timestamps (256 x 32 uint64) to host memory.
+int ta_tail_trace_read(void* host) {
+  const cudaError_t e = cudaMemcpyFromSymbol(host, ta::g_tail_trace, sizeof(ta::g_tail_trace));
+  return e == cudaSuccess ? TA_OK : fail(TA_ERR_CUDA, "ta_tail_trace_read: %s", cudaGetErrorString(e));
+}
+#endif
+
+int ta_block_tail_plan(int dtype, int B, int C, int with_qkv, int64_t* ws_bytes, int* sync_words) {
+  g_err.clear();
+  if (dtype != TA_BF16 && dtype != TA_F16) return fail(TA_ERR_ARG, "ta_block_tail: bf16 or f16 weights only");
+  TailPlan pl;
+  if (!tail_plan(B, C, with_qkv != 0, 2, pl))
+    return fail(TA_ERR_ARG, "ta_block_tail: %d rows of width %d not taken (1..%d rows, width a multiple of 128 up to "
+                "%d whose weight slices fit one CTA per SM)", B, C, ta::BT_MAX_BN, ta::BT_MAX_C);
+  if (ws_bytes) *ws_bytes = (int64_t)pl.ws_bytes;
+  if (sync_words) *sync_words = pl.nsync;
+  return TA_OK;
+}
+
+int ta_block_tail(const void* att, float* x, const void* w_proj, const float* ln2_w, const void* w_fc,
+                  const void* w_mlp, const float* ln_next_w, const void* w_qkv, float eps, int dtype, int B, int C,
+                  void* h, void* qkv, void* ws, int64_t ws_bytes, int* sync, void* stream) {
+  g_err.clear();
+  if (dtype != TA_BF16 && dtype != TA_F16) return fail(TA_ERR_ARG, "ta_block_tail: bf16 or f16 weights only");
+  if (!att || !x || !w_proj || !ln2_w || !w_fc || !w_mlp || !ln_next_w || !h || !ws || !sync)
+    return fail(TA_ERR_ARG, "ta_block_tail: null pointer");
+  if ((w_qkv == nullptr) != (qkv == nullptr))
+    return fail(TA_ERR_ARG, "ta_block_tail: the next block's c_attn weight and its output go together");
+  const bool with_qkv = w_qkv != nullptr;
+  TailPlan pl;
+  if (!tail_plan(B, C, with_qkv, 2, pl))
+    return fail(TA_ERR_ARG, "ta_block_tail: %d rows of width %d not taken (1..%d rows, width a multiple of 128 up to "
+                "%d whose weight slices fit one CTA per SM)", B, C, ta::BT_MAX_BN, ta::BT_MAX_C);
+  if (ws_bytes < (int64_t)pl.ws_bytes)
+    return fail(TA_ERR_ARG, "ta_block_tail: workspace of %lld B, the plan needs %zu B", (long long)ws_bytes,
+                pl.ws_bytes);
+  for (const void* q : {att, (const void*)x, w_proj, w_fc, w_mlp, (const void*)h, (const void*)ws})
+    if (!aligned16(q)) return fail(TA_ERR_ARG, "ta_block_tail: rows, weights and workspace must be 16-byte aligned");
+  if (with_qkv && (!aligned16(qkv) || !aligned16(w_qkv)))
+    return fail(TA_ERR_ARG, "ta_block_tail: rows, weights and workspace must be 16-byte aligned");
+  ta::TailMaps m;
+  unsigned char* wsb = reinterpret_cast<unsigned char*>(ws);
+  const void* wts[4] = {w_proj, w_fc, w_mlp, with_qkv ? w_qkv : w_proj};
+  const void* rows[4] = {att, wsb + pl.o_h2, wsb + pl.o_fc, with_qkv ? h : att};
+  const char* names[4] = {"c_proj weight", "c_fc weight", "c_mlp weight", "c_attn weight"};
+  const char* rnames[4] = {"attention rows", "ln_2 rows", "GELU rows", "ln_1 rows"};
+  for (int i = 0; i < 4; ++i) {
+    const ta::TailGemm& g = pl.g[i == 3 && !with_qkv ? 0 : i];
+    if (int r = make_blocks_map(&m.w[i], wts[i], dtype, g.N, g.K, g.K, ta::LIN_MT, 1, names[i])) return r;
+    if (int r = make_blocks_map(&m.a[i], rows[i], dtype, B, g.K, g.K, pl.BN, 1, rnames[i])) return r;
+  }
+  ta::BlockTailParams p{};
+  p.B = B;
+  p.BN = pl.BN;
+  p.C = C;
+  p.G = num_sms();
+  p.nslot = pl.nslot;
+  for (int i = 0; i < 4; ++i) p.g[i] = pl.g[i];
+  p.off_ln = pl.off_ln;
+  p.nsync = pl.nsync;
+  p.att = att;
+  p.x = x;
+  p.ln2 = ln2_w;
+  p.ln_next = ln_next_w;
+  p.eps = eps;
+  p.part_proj = reinterpret_cast<float*>(wsb + pl.o_part_proj);
+  p.ws_fc = reinterpret_cast<float*>(wsb + pl.o_ws_fc);
+  p.part_mlp = reinterpret_cast<float*>(wsb + pl.o_part_mlp);
+  p.ws_qkv = reinterpret_cast<float*>(wsb + pl.o_ws_qkv);
+  p.h2 = wsb + pl.o_h2;
+  p.fc = wsb + pl.o_fc;
+  p.h = h;
+  p.qkv = qkv;
+  p.sync = sync;
+  return dtype == TA_BF16 ? launch_tail_by_c<__nv_bfloat16>(pl.maxc, m, p, pl.smem, S(stream))
+                          : launch_tail_by_c<__half>(pl.maxc, m, p, pl.smem, S(stream));
 }
 
 int ta_decode_step(const void* qkv, int dtype, int B, int H, int dh, int64_t qkv_sb, int64_t k_ofs, int64_t v_ofs,

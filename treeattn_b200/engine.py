@@ -243,7 +243,7 @@ class Decoder:
     additions. The residual stream is kept in fp32; matmuls run in `dtype` on cuBLAS."""
 
     def __init__(self, W, n_layer, n_head, n_embd, Tcap, mode='seg', cfg=None, dev='cuda', batch=1, dtype=None,
-                 cap=None, graphs=True, splits=0, fused_linear=None):
+                 cap=None, graphs=True, splits=0, fused_linear=None, block_tail=None):
         if mode not in ('seg', 'dense'):
             raise NotImplementedError("Decoder mode '%s' is not implemented in treeattn_b200 ('seg', 'dense')" % mode)
         if mode == 'seg' and cfg is None:
@@ -287,6 +287,15 @@ class Decoder:
         if self.fused_linear and not ok:
             raise ValueError('fused_linear: ta_linear_rows does not take this model (16-bit weights, width and '
                              'batch it supports)')
+        # block_tail=True: per layer, everything after the attention and the next layer's c_attn in one launch
+        # (ta_block_tail) instead of four matmuls and three row kernels
+        plans = [_ops.block_tail_plan(self.dtype, batch, C, q) for q in (True, False)]
+        tail_ok = self.dev.type == 'cuda' and all(pl is not None for pl in plans)
+        self.block_tail = False if block_tail is None else bool(block_tail)
+        if self.block_tail and not tail_ok:
+            raise ValueError('block_tail: ta_block_tail does not take this model (16-bit weights, width a multiple '
+                             'of 128, at most 128 sequences)')
+        self._tail_plans = plans
         self.reset()
 
     @classmethod
@@ -330,6 +339,9 @@ class Decoder:
                         if ls[k] > 1] + [1])
             self._ws = (torch.empty(n_ws * B * _ops.LIN_TILE, device=dev, dtype=torch.float32),
                         torch.zeros(-(-V // _ops.LIN_TILE), device=dev, dtype=torch.int32))
+        if self.block_tail:  # one workspace and one set of sync words, shared by the layers' launches (in order)
+            self._tail_bufs = (torch.empty(max(pl[0] for pl in self._tail_plans), device=dev, dtype=torch.uint8),
+                               torch.zeros(self._tail_plans[0][1], device=dev, dtype=torch.int32))
         self._graph = None
         self._graph_greedy = None
 
@@ -404,6 +416,36 @@ class Decoder:
                 _ops.argmax_advance(self._logits, self._tok, self._pos)
         return self._logits
 
+    def _forward_step_tail(self, record=None, greedy=False):
+        """_forward_step with the block tail: embedding + ln_1 and layer 0's c_attn, then per layer the attention
+        and ONE ta_block_tail launch (c_proj, residual, ln_2, c_fc + GELU, c_mlp, residual, the next layer's ln_1 and
+        c_attn - or ln_f after the last layer); then the lm_head (and the greedy argmax with the position advance)."""
+        W = self.W
+        L = W['layers']
+        _ops.embed_ln(W['wte'], W['wpe'], self._tok, self._pos, L[0]['ln1'], self._x, self._h)
+        self._linear('qkv', self._h, L[0]['c_attn'], _ops.LIN_STORE, out=self._qkv)
+        for i, Li in enumerate(L):
+            if record is not None:
+                record.append(dict(x_in=self._x.clone()))
+            self._attend(i, record)
+            if record is not None:
+                record[-1].update(qkv=self._qkv.clone(), att=self._att.clone())
+            nxt = L[i + 1] if i + 1 < len(L) else None
+            _ops.block_tail(self._att, self._x, Li['c_proj'], Li['ln2'], Li['c_fc'], Li['c_mlp'],
+                            nxt['ln1'] if nxt is not None else W['ln_f'], self._h,
+                            w_qkv=nxt['c_attn'] if nxt is not None else None,
+                            qkv_out=self._qkv if nxt is not None else None, bufs=self._tail_bufs)
+            if record is not None:
+                record[-1].update(x_out=self._x.clone())
+        if greedy and self.fused_linear and self.lin_splits['lm']:
+            self._linear('lm', self._h, W['wte'], _ops.LIN_ARGMAX, out=self._logits)
+            _ops.argmax_finish(self._keys, W['wte'].shape[0], self._tok, self._pos)
+        else:
+            self._linear('lm', self._h, W['wte'], _ops.LIN_STORE, out=self._logits)
+            if greedy:
+                _ops.argmax_advance(self._logits, self._tok, self._pos)
+        return self._logits
+
     def _forward_step(self, record=None):
         """Logits (B, V) of the tokens in self._tok at positions self._pos; appends their K/V to every layer.
         Per layer: [x += mlp; h = ln1(x)] qkv-matmul, fused decode attention, c_proj-matmul, [x += proj;
@@ -411,6 +453,8 @@ class Decoder:
         `record` (a list; eager steps only) receives per layer copies of the residual entering it (x_in), its
         q/k/v rows, its attention output, its selected leaves (fused decode only) and the residual leaving it
         (x_out), for layer-by-layer checks."""
+        if self.block_tail:
+            return self._forward_step_tail(record)
         if self.fused_linear:
             return self._forward_step_fused(record)
         W = self.W
@@ -433,6 +477,8 @@ class Decoder:
         return self._logits
 
     def _greedy_step(self):
+        if self.block_tail:
+            return self._forward_step_tail(greedy=True)
         if self.fused_linear:
             return self._forward_step_fused(greedy=True)
         logits = self._forward_step()
