@@ -99,9 +99,10 @@ def parse():
     p.add_argument('--config3', action='store_true',
                    help='configuration 3 end to end: the 12-layer bf16 GPT forward (prefill) over 4 x 8192 tokens; '
                         'prints one JSON line')
-    p.add_argument('--fused-linear', type=int, default=0,
+    p.add_argument('--fused-linear', type=int, default=-1,
                    help='1: the decode step\'s projections on the library\'s tensor-core kernel where Decoder.lin_splits '
-                        'says so (ta_linear_rows, K-split c_proj / c_mlp); 0: every projection on cuBLAS')
+                        'says so (ta_linear_rows, K-split c_proj / c_mlp); 0: every projection on cuBLAS; -1 (default): '
+                        'the Decoder\'s choice (the library kernel for batches of at most 32 sequences)')
     p.add_argument('--no-kernels', action='store_true',
                    help='default run: skip the kernels sub-record (configurations 1, 2, 3 and 5 measured after the '
                         'decode loop)')
@@ -857,7 +858,7 @@ def run_engine(a, M, dev, rank, world, local):
     cfg = make_cfg(M)
     W = make_weights(dev, 1234, torch.bfloat16, M)
     dec = Decoder(W, NL, H, C, M.tcap, 'seg', cfg, dev, batch=B, dtype=torch.bfloat16, cap=cap, splits=a.splits,
-                  fused_linear=bool(a.fused_linear))
+                  fused_linear=None if a.fused_linear < 0 else bool(a.fused_linear))
     torch.cuda.synchronize()
     t_pf = time.time()
     if M.fill == 'prefill':
@@ -969,7 +970,7 @@ def run_engine(a, M, dev, rank, world, local):
             torch.cuda.empty_cache()
             Bs = B // world
             dec = Decoder(W, NL, H, C, M.tcap, 'seg', cfg, dev, batch=Bs, dtype=torch.bfloat16, cap=cap,
-                          splits=a.splits, fused_linear=bool(a.fused_linear))
+                          splits=a.splits, fused_linear=None if a.fused_linear < 0 else bool(a.fused_linear))
             g = torch.Generator(device=dev).manual_seed(100)
             prompts = torch.randint(0, M.V, (B, T0), device=dev, generator=g)  # the global batch, same on all ranks
             lo, hi = tdist.shard(B, rank, world)

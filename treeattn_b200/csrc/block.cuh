@@ -84,9 +84,9 @@ struct BlockTailParams {
   void* h;                  // (B, C) T: ln_next output
   void* qkv;                // (B, 3C) T: the next block's projection (g[3].n == 0: none)
   float* part_proj;         // (S_proj, B, C)
-  float* ws_fc;             // (4C / 128, S_fc, 128, BN): per tile and split, feature-major
+  float* ws_fc;             // (4C / 128, S_fc, BN, 128): per tile and split, its fp32 tile row-major
   float* part_mlp;          // (S_mlp, B, C)
-  float* ws_qkv;            // (3C / 128, S_qkv, 128, BN)
+  float* ws_qkv;            // (3C / 128, S_qkv, BN, 128)
   int* sync;
 };
 
@@ -477,7 +477,8 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             float v[32];
             tmem_ld32(lane_base + c0, v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) tl[(c0 + i) * LIN_MT + fl] = v[i];
+            for (int i = 0; i < 32; ++i)
+              if (c0 + i < p.BN) tl[(c0 + i) * LIN_MT + fl] = v[i];  // the tile holds BN rows
           }
         tc_fence_before();
         named_bar_sync(1, 128);

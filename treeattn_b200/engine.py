@@ -28,6 +28,9 @@ def _positions(t, B, device):
     return torch.full((B,), int(t), device=device, dtype=torch.int32)
 
 
+FUSED_LINEAR_MAX_BATCH = 32  # Decoder's default: projections on ta_linear_rows up to this many sequences
+
+
 def _pick_splits(N, K, target=36, min_k=128):
     """K splits of an (N, K) projection for ta_linear_rows: the fewest that give `target` CTAs (N / 128 feature
     tiles each) with slices of at least min_k, a whole number of 64-wide blocks each."""
@@ -274,7 +277,9 @@ class Decoder:
         self.splits = (splits or _ops.default_splits(batch, n_head, self.dh, self.dtype)) if seg else 0
         # fused_linear=True: the linear layers on the library's tensor-core kernel (ta_linear_rows: 16-bit weights,
         # K slices of 64) instead of torch matmuls; K splits of c_proj and c_mlp so that enough CTAs stream their
-        # weights. Off by default: whole configuration-4 steps measured 0.948 ms with it against 0.937 on cuBLAS.
+        # weights. Default (None): on for batches of at most FUSED_LINEAR_MAX_BATCH sequences, where cuBLAS's small-row
+        # GEMMs are slowest (whole configuration-4 steps: 8 sequences 0.652 -> 0.590 ms, 16: 0.658 -> 0.567 ms, 32:
+        # 0.789 -> 0.724 ms); off above (64 sequences: 0.948 ms with it against 0.937 on cuBLAS).
         V = self.W['wte'].shape[0]
         C = n_embd
         # per projection: K splits on ta_linear_rows, or 0 = torch's matmul (cuBLAS) where that measured faster
@@ -283,7 +288,10 @@ class Decoder:
         shapes = dict(qkv=(3 * C, C), proj=(C, C), fc=(4 * C, C), mlp=(C, 4 * C), lm=(V, C))
         ok = all(sp == 0 or _ops.linear_supported(self.dtype, batch, shapes[k][0], shapes[k][1], sp)
                  for k, sp in self.lin_splits.items())
-        self.fused_linear = False if fused_linear is None else bool(fused_linear)
+        if fused_linear is None:
+            self.fused_linear = ok and batch <= FUSED_LINEAR_MAX_BATCH and self.dev.type == 'cuda'
+        else:
+            self.fused_linear = bool(fused_linear)
         if self.fused_linear and not ok:
             raise ValueError('fused_linear: ta_linear_rows does not take this model (16-bit weights, width and '
                              'batch it supports)')
