@@ -640,8 +640,10 @@ struct Decode {
       }
     } else if (p.part && p.part_cnt && items < gmax) {
       // fewer items than CTA slots (small batches): every item in PT parts, so that each CTA streams a share of one
-      // item and the items' descents run side by side (the scratch holds 4 parts per item)
-      const int PT = std::min(std::min(TA_MAX_PSPLIT, 4), gmax / items);
+      // item and the items' descents run side by side. Two parts measured best (every part repeats its item's
+      // descent): 8-sequence configuration-4 steps 0.563 ms with 2 parts, 0.574 with 3, 0.607 with 4; with 16 or
+      // 24 sequences (under 2 items per CTA slot) whole items stay faster (0.566 / 0.601 ms vs 0.663 / 0.707)
+      const int PT = std::min(std::min(TA_MAX_PSPLIT, 2), gmax / items);
       if (PT > 1) {
         p.psplit = PT;
         p.n_whole = 0;
