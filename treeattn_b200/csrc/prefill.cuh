@@ -11,11 +11,13 @@
 //                   which is exactly the deduplicated key set of the reference (every position once).
 // Warp roles (192 threads):
 //   warps 0-3  softmax: thread r owns query row r = TMEM lane r. Reads S = Q K^T of a tile from TMEM, masks,
-//              online softmax in the log2 domain, writes P (16-bit, 128-byte-swizzled K-major) to shared memory,
-//              and folds O_tile = P V (read back from TMEM) into its fp32 output row.
+//              softmax in the log2 domain against a per-row reference max, writes P (16-bit, 128-byte-swizzled
+//              K-major) to shared memory. The reference max moves only when a tile's max exceeds it by more than
+//              TAU (P then stays below 2^TAU); only then does the warp wait for the last P V and rescale its O rows
+//              in TMEM. The output row is read from TMEM once, at the end.
 //   warp 4     TMA producer: the Q tile once, then K and V tiles into an NS-stage ring.
 //   warp 5     allocates TMEM; one thread issues tcgen05.mma: S(n) = Q K(n)^T into S[n % 2], then
-//              O_tile(n-1) = P(n-1) V(n-1) into O[(n-1) % 2], committing to mbarriers.
+//              O += P(n-1) V(n-1) into the one O accumulator, committing to mbarriers.
 // Every wait is a bounded mbarrier wait; on a timeout the CTA records the error, stops, waits (bounded) for its
 // copies and MMAs in flight and frees its TMEM.
 #pragma once
@@ -54,9 +56,9 @@ struct PfCfg {
   static constexpr int KT_BYTES = PF_KT * DH * 2;       // one K or V tile
   static constexpr int STAGE_BYTES = 2 * KT_BYTES;      // K then V
   static constexpr int P_BYTES = PF_QT * PF_KT * 2;     // one P buffer
-  static constexpr int TM_S = 0;                        // TMEM columns: S[2] (64 each) then O[2] (DH each)
+  static constexpr int TM_S = 0;                        // TMEM columns: S[2] (64 each) then the O accumulator
   static constexpr int TM_O = 2 * PF_KT;
-  static constexpr int TM_COLS = (2 * PF_KT + 2 * DH) <= 256 ? 256 : 512;
+  static constexpr int TM_COLS = (2 * PF_KT + DH) <= 256 ? 256 : 512;
   static constexpr uint32_t IDESC_QK_BF16 = umma_idesc_f16(PF_QT, PF_KT, true, false);
   static constexpr uint32_t IDESC_QK_F16 = umma_idesc_f16(PF_QT, PF_KT, false, false);
   static constexpr uint32_t IDESC_PV_BF16 = umma_idesc_f16(PF_QT, DH, true, true);
@@ -68,7 +70,7 @@ template <int NS>
 struct PfBars {
   uint64_t q_full, mma_done;
   uint64_t kv_full[NS], kv_empty[NS];
-  uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
+  uint64_t s_full[2], s_free[2], p_full[2], o_full[2];  // o_full[j % 2]: P(j) V(j) has been added to O
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -185,7 +187,6 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       mbar_init(&bar.s_free[s], 4);
       mbar_init(&bar.p_full[s], 4);
       mbar_init(&bar.o_full[s], 1);
-      mbar_init(&bar.o_free[s], 4);
     }
     bar.abort_flag = 0;
     tmeta[0] = 0;
@@ -280,15 +281,15 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       const uint32_t aQ = smem_u32(sQ), aKV = smem_u32(sKV), aP = smem_u32(sP);
       bool ok = mbar_wait_bounded(&bar.q_full, 0, K_PREFILL, 23);
       auto issue_pv = [&](int j) -> bool {
+        // P(j) written (and any rescale of O the softmax warps made before it, ordered by their arrival)
         if (!mbar_wait_bounded(&bar.p_full[j & 1], (j >> 1) & 1, K_PREFILL, 24)) return false;
-        if (j >= 2 && !mbar_wait_bounded(&bar.o_free[j & 1], ((j >> 1) - 1) & 1, K_PREFILL, 25)) return false;
         tc_fence_after();
         const uint32_t pa = aP + (j & 1) * C::P_BYTES;
         const uint32_t va = aKV + (j % NS) * C::STAGE_BYTES + C::KT_BYTES;
 #pragma unroll
         for (int k = 0; k < PF_KT / 16; ++k)
-          umma_f16(tO + (j & 1) * DH, sw128_desc(pa + k * 32, 16, 1024), sw128_desc(va + k * 2048, PF_KT * 128, 1024),
-                   IDESC_PV, k > 0);
+          umma_f16(tO, sw128_desc(pa + k * 32, 16, 1024), sw128_desc(va + k * 2048, PF_KT * 128, 1024), IDESC_PV,
+                   j > 0 || k > 0);
         umma_commit(&bar.o_full[j & 1]);
         umma_commit(&bar.kv_empty[j % NS]);
         return true;
@@ -320,36 +321,17 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
   } else {
     // ---------------------------------------------------------------- softmax warps (thread = query row)
     const uint32_t lane_base = bar.tmem_base + ((uint32_t)(warp * 32) << 16);
-    float oacc[DH];
-#pragma unroll
-    for (int i = 0; i < DH; ++i) oacc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, m_acc = -INFINITY, m_h0 = -INFINITY, m_h1 = -INFINITY;
+    // a row's weights are p = 2^(s * scale_log2 - m_ref); m_ref follows the row's running max lazily: it moves to a
+    // tile's max only when that exceeds it by more than TAU, so p < 2^TAU (far inside the 16-bit and fp32 ranges)
+    constexpr float TAU = 8.f;
+    float m_ref = -INFINITY, l_run = 0.f;
     int keys = 0;
     bool ok = true;
     unsigned char* prow_base = sP + (tid >> 3) * 1024 + (tid & 7) * 128;
     const uint32_t* qb = qbits + tid;
-
-    auto consume = [&](int j) -> bool {
-      // warp-uniform outcome: the tcgen05.ld below is executed by the whole warp
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bar.o_full[j & 1], (j >> 1) & 1, K_PREFILL, 30))) return false;
-      tc_fence_after();
-      const float mj = (j & 1) ? m_h1 : m_h0;
-      const bool live = mj != -INFINITY;
-      const float f = live ? ex2_approx(m_acc - mj) : 1.f;
-#pragma unroll
-      for (int c = 0; c < DH / 32; ++c) {
-        float v[32];
-        tmem_ld32(lane_base + C::TM_O + (j & 1) * DH + c * 32, v);
-        if (live) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = fmaf(oacc[c * 32 + i], f, v[i]);
-        }
-      }
-      if (live) m_acc = mj;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar.o_free[j & 1]);
-      return true;
+    // warp-uniform: every lane waits for the same phase
+    auto pv_done = [&](int j, int where) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait_bounded(&bar.o_full[j & 1], (j >> 1) & 1, K_PREFILL, where));
     };
 
     TileIter it(tbits, p.tile_words);
@@ -396,14 +378,10 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       }
       keys += __popcll(vm);
       // warp-uniform shortcut: a tile masked for all 32 queries of the warp contributes nothing (its P rows are
-      // zero and the running max is unchanged)
+      // zero and the reference max is unchanged)
       const bool none = __all_sync(0xffffffffu, vm == 0ull);
-      unsigned char* prow = prow_base + (n & 1) * C::P_BYTES;
-      float m_new = m_run;
-      if (none) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
-      } else {
+      float mt = -INFINITY;  // this tile's max in the log2 domain
+      if (!none) {
         // max over the raw scores (scaling by a positive constant is monotone under rounding: max commutes)
         float mx = -INFINITY;
 #pragma unroll
@@ -411,9 +389,37 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
           s[i] = ((vm >> i) & 1ull) ? s[i] : -INFINITY;
           mx = fmaxf(mx, s[i]);
         }
-        m_new = fmaxf(m_run, mx * p.scale_log2);
-        const float mu = m_new == -INFINITY ? 0.f : m_new;
-        l_run *= ex2_approx(m_run - mu);
+        mt = mx * p.scale_log2;
+      }
+      const bool bump = mt > m_ref + TAU;            // a new reference (never for a masked row)
+      const bool resc = bump && m_ref != -INFINITY;  // O and l hold weights of the old reference
+      const float m_new = bump ? mt : m_ref;
+      const float f = resc ? ex2_approx(m_ref - m_new) : 1.f;
+      if (__any_sync(0xffffffffu, resc)) {
+        // rescale this warp's O rows once the last P V has landed in them (factor 1 for the other lanes)
+        if (n >= 1 && !(ok = pv_done(n - 1, 30))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          float v[32];
+          tmem_ld32(lane_base + C::TM_O + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= f;
+          tmem_st32(lane_base + C::TM_O + c * 32, v);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+      }
+      l_run *= f;
+      m_ref = m_new;
+      // P buffer n % 2 was last read by P(n-2) V(n-2)
+      if (n >= 2 && !(ok = pv_done(n - 2, 32))) break;
+      unsigned char* prow = prow_base + (n & 1) * C::P_BYTES;
+      if (none) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        const float mu = m_ref == -INFINITY ? 0.f : m_ref;
         // P row (16-bit, rounded for the tensor-core P.V) into the swizzled K-major P buffer; the denominator l sums
         // the fp32 weights p = 2^(s * scale_log2 - mu) (the scaling fused into one FMA)
 #pragma unroll
@@ -432,24 +438,39 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.p_full[n & 1]);
-      if (n & 1) m_h1 = m_new; else m_h0 = m_new;
-      m_run = m_new;
-      if (n >= 1 && !(ok = consume(n - 1))) break;
       if (__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&bar.abort_flag) != 0)) { ok = false; break; }
     }
-    if (ok && n > 0) ok = consume(n - 1);
+    // the output row: O / l once the last P V has landed
+    if (ok && n > 0) ok = pv_done(n - 1, 33);
     if (!ok) atomicExch(&bar.abort_flag, 1);
-    if (t >= 0) {
-      const float fin = (ok && l_run > 0.f) ? exp2f(m_acc - m_run) / l_run : 0.f;
+    if (ok && n > 0) {
+      tc_fence_after();
+      const float fin = l_run > 0.f ? 1.f / l_run : 0.f;
       T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + (int64_t)qi * p.o_st;
 #pragma unroll
-      for (int c = 0; c < DH / 8; ++c) {
-        float v8[8];
+      for (int c = 0; c < DH / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_base + C::TM_O + c * 32, v);  // the whole warp (a lane without a query discards its row)
+        if (t >= 0) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v8[e] = oacc[c * 8 + e] * fin;
-        if constexpr (sizeof(T) == 2) store_vec_from_f32<T>(orow + c * 8, v8);
+          for (int q8 = 0; q8 < 4; ++q8) {
+            float v8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v8[e] = v[q8 * 8 + e] * fin;
+            if constexpr (sizeof(T) == 2) store_vec_from_f32<T>(orow + c * 32 + q8 * 8, v8);
+          }
+        }
       }
-      if (p.lse) p.lse[qid] = l_run > 0.f ? (m_run + log2f(l_run)) * LN2 : -INFINITY;
+    }
+    if (t >= 0) {
+      if (!(ok && n > 0)) {  // nothing attended (a failed launch): zero rows
+        T* orow = reinterpret_cast<T*>(p.o) + b * p.o_sb + h * p.o_sh + (int64_t)qi * p.o_st;
+        float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < DH / 8; ++c)
+          if constexpr (sizeof(T) == 2) store_vec_from_f32<T>(orow + c * 8, z);
+      }
+      if (p.lse) p.lse[qid] = l_run > 0.f ? (m_ref + log2f(l_run)) * LN2 : -INFINITY;
       if (p.nkeys) p.nkeys[qid] = keys;
     }
   }
