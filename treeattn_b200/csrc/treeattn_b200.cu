@@ -313,7 +313,7 @@ int make_rows_map(CUtensorMap* m, const void* ptr, int dtype, int dh, int rows, 
 
 template <typename T, int DH>
 struct Prefill {
-  static constexpr int NS = DH == 64 ? 2 : 3;  // K/V ring stages (dh 64: two CTAs per SM)
+  static constexpr int NS = 3;  // K/V ring stages (dh 64: still two CTAs per SM)
   static int run(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const ta::PrefillParams& p,
                  cudaStream_t st) {
     auto kern = ta::prefill_tile_kernel<T, DH, NS>;
