@@ -383,13 +383,14 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       float mt = -INFINITY;  // this tile's max in the log2 domain
       if (!none) {
         // max over the raw scores (scaling by a positive constant is monotone under rounding: max commutes)
-        float mx = -INFINITY;
+        // (four independent chains: the max is exact in any order)
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           s[i] = ((vm >> i) & 1ull) ? s[i] : -INFINITY;
-          mx = fmaxf(mx, s[i]);
+          m4[i & 3] = fmaxf(m4[i & 3], s[i]);
         }
-        mt = mx * p.scale_log2;
+        mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
       }
       const bool bump = mt > m_ref + TAU;            // a new reference (never for a masked row)
       const bool resc = bump && m_ref != -INFINITY;  // O and l hold weights of the old reference
@@ -421,7 +422,9 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
       } else {
         const float mu = m_ref == -INFINITY ? 0.f : m_ref;
         // P row (16-bit, rounded for the tensor-core P.V) into the swizzled K-major P buffer; the denominator l sums
-        // the fp32 weights p = 2^(s * scale_log2 - mu) (the scaling fused into one FMA)
+        // the fp32 weights p = 2^(s * scale_log2 - mu) (the scaling fused into one FMA), as the reference's _attn_fwd
+        // sums them, in four independent chains
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint32_t w[4];
@@ -429,11 +432,12 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
           for (int e = 0; e < 4; ++e) {
             const float p0 = ex2_approx(fmaf(s[c * 8 + 2 * e], p.scale_log2, -mu));
             const float p1 = ex2_approx(fmaf(s[c * 8 + 2 * e + 1], p.scale_log2, -mu));
-            l_run += p0 + p1;  // the fp32 weights, as the reference's _attn_fwd sums them
+            l4[e] += p0 + p1;
             w[e] = pack2<T>(p0, p1);
           }
           *reinterpret_cast<uint4*>(prow + ((c ^ (tid & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
