@@ -46,7 +46,7 @@ def _keys(t, ids, vld, ntree, L0, Lw):
     return sorted(ks)
 
 
-def _run(B, H, T, dh, leaf, Lw, wl, dt, seed, Nq=None, t_off=0, n_check=64, strided=True):
+def _run(B, H, T, dh, leaf, Lw, wl, dt, seed, Nq=None, t_off=0, n_check=64, strided=True, k_growth=None):
     ops = _ops()
     rng = np.random.default_rng(seed)
     L0 = int(math.log2(leaf))
@@ -58,7 +58,10 @@ def _run(B, H, T, dh, leaf, Lw, wl, dt, seed, Nq=None, t_off=0, n_check=64, stri
         q = qkv[:, :, 0].permute(0, 2, 1, 3)
     else:
         q = torch.randn(B, H, Nq, dh, device=DEV, generator=g).to(dt)
-    k = (torch.randn(B, H, T, dh, device=DEV, generator=g) * 0.7).to(dt)
+    k = torch.randn(B, H, T, dh, device=DEV, generator=g) * 0.7
+    if k_growth:  # key norms grow with position: a row's max rises tile after tile
+        k = k * (1.0 + torch.arange(T, device=DEV, dtype=torch.float32) / k_growth).view(1, 1, T, 1)
+    k = k.to(dt)
     v = torch.randn(B, H, T, dh, device=DEV, generator=g).to(dt)
     tq_np = np.tile(np.arange(t_off, t_off + Nq, dtype=np.int64), (B, 1))
     ids_np, vld_np, nt_np = _selection(rng, B, H, tq_np, wl, L0, Lw)
@@ -117,6 +120,14 @@ def test_prefill_leaf2_min_window():
 def test_prefill_chunk_offset():
     """A chunk of 200 queries at positions 1300..1499 over a 1500-row cache (chunked prefill)."""
     _run(2, 2, 1500, 64, 32, 64, 8, torch.bfloat16, 5, Nq=200, t_off=1300, strided=False)
+
+
+@pytest.mark.parametrize('dh,leaf,Lw,wl', [(64, 64, 128, 16), (128, 128, 256, 32)])
+def test_prefill_rising_scores_rescale(dh, leaf, Lw, wl):
+    """Key norms growing with position, so that a row's running max rises by more than 2^8 (log2 domain) again and
+    again over its key tiles: the tile kernel's in-place rescale of the O accumulator (its reference max moves only
+    then) must give the same rows as the warp kernel and the fp64 evaluation."""
+    _run(2, 2, 1200, dh, leaf, Lw, wl, torch.bfloat16, 7, strided=False, k_growth=16.0)
 
 
 def test_prefill_rejects_unsupported():
