@@ -202,6 +202,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// The same bounded wait by polling (mbarrier.test_wait: the thread never suspends), for a wait on the critical path
+// whose phase completes within microseconds.
+__device__ __forceinline__ bool mbar_poll_bounded(uint64_t* bar, uint32_t parity, int kernel, int where,
+                                                  uint64_t limit_ns = TA_WAIT_LIMIT_NS) {
+  uint32_t ok;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t spins = 0;; ++spins) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((spins & 63u) == 63u && global_timer_ns() - t0 > limit_ns) {
+      record_error(DEV_WAIT_TIMEOUT, kernel, where, (int)parity);
+      return false;
+    }
+  }
+}
+
 // The bounded wait's failure path, on purpose: thread 0 waits on an mbarrier that no thread arrives at, gives up
 // after limit_ns and records DEV_WAIT_TIMEOUT (kernel K_WAIT_PROBE, where = 7). Once no thread waits any more the
 // abandoned barrier is invalidated (what a give-up path must do before its shared memory is reused), and the

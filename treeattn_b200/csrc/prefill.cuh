@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(PF_THREADS, DH == 64 ? 2 : 1)
     TileIter it(tbits, p.tile_words);
     int n = 0;
     for (int kt; ok && (kt = it.next()) >= 0; ++n) {
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar.s_full[n & 1], (n >> 1) & 1, K_PREFILL, 31)))) break;
+      if (!(ok = __all_sync(0xffffffffu, mbar_poll_bounded(&bar.s_full[n & 1], (n >> 1) & 1, K_PREFILL, 31)))) break;
       tc_fence_after();
       float s[64];
       {
