@@ -177,3 +177,34 @@ def test_checkpoint_loads_unchanged():
     for name, t in ck['model'].items():
         assert torch.equal(sd[name], t), name
     assert cfg.beam_mode == 'pred' and tuple(cfg.beam_classes) == (2, 3, 4)
+
+
+def test_block_tail_plan_and_linear_shapes_without_gpu():
+    """The host-side planning of the decode step's fused callers: ta_block_tail_plan sizes the workspace and sync
+    words for the shapes the block tail takes (and names why it refuses the others), ta_block_tail refuses missing
+    pointers and a short workspace before any CUDA call, ta_linear_supported answers from the shapes alone."""
+    from treeattn_b200 import _lib
+    lib = _lib.load()
+    ws, ns = ctypes.c_int64(0), ctypes.c_int(0)
+    for B, C, q in [(64, 768, 1), (64, 768, 0), (8, 768, 1), (128, 768, 1), (3, 128, 1), (20, 2048, 1)]:
+        assert lib.ta_block_tail_plan(1, B, C, q, ctypes.byref(ws), ctypes.byref(ns)) == _lib.TA_OK, _lib.last_error()
+        # sync words: 8 fixed, two per c_fc tile, one per c_attn tile
+        assert ns.value == 8 + 2 * (4 * C // 128) + 3 * C // 128
+        # the workspace holds at least the 16-bit ln_2 and GELU rows, each piece 256-byte aligned
+        assert ws.value >= B * C * 2 + B * 4 * C * 2 and ws.value % 256 == 0
+    for dt, B, C in [(0, 64, 768), (1, 64, 96), (1, 129, 768), (1, 20, 4096), (1, 0, 768)]:
+        rc = lib.ta_block_tail_plan(dt, B, C, 1, ctypes.byref(ws), ctypes.byref(ns))
+        assert rc == _lib.TA_ERR_ARG and 'ta_block_tail' in _lib.last_error()
+    f = ctypes.c_float(1e-5)
+    rc = lib.ta_block_tail(None, None, None, None, None, None, None, None, f, 1, 64, 768, None, None, None, 0, None, None)
+    assert rc == _lib.TA_ERR_ARG and 'null' in _lib.last_error()
+    fake = 1 << 20  # aligned addresses that are never dereferenced: the workspace check comes first
+    rc = lib.ta_block_tail(fake, fake, fake, fake, fake, fake, fake, fake, f, 1, 64, 768, fake, fake, fake, 256, fake,
+                           None)
+    assert rc == _lib.TA_ERR_ARG and 'workspace' in _lib.last_error()
+    assert lib.ta_linear_supported(1, 64, 2304, 768, 1) == 1
+    assert lib.ta_linear_supported(1, 64, 768, 3072, 16) == 1
+    assert lib.ta_linear_supported(0, 64, 2304, 768, 1) == 0   # fp32 operands
+    assert lib.ta_linear_supported(1, 300, 2304, 768, 1) == 0  # more than 256 rows
+    assert lib.ta_linear_supported(1, 64, 2300, 768, 1) == 0   # N not a multiple of 8
+    assert lib.ta_linear_supported(1, 64, 768, 768, 5) == 0    # K not a multiple of 64 x splits
