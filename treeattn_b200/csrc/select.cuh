@@ -156,7 +156,10 @@ struct Descent {
     int lp;     // lowest level whose whole reachable range is prefetched
   };
 
-  static __device__ __forceinline__ Plan plan(const LevelView& lv, int t, int wmax, int stage_rows) {
+  // max_levels: how many levels from l* down may be prefetched (the rest are gathered level by level, only the
+  // children the descent keeps)
+  static __device__ __forceinline__ Plan plan(const LevelView& lv, int t, int wmax, int stage_rows,
+                                              int max_levels = 64) {
     const int Lm = lv.Lm, L0 = lv.L0;
     const int eLm = t >> Lm;
     const int aLm = eLm - (eLm & 1);
@@ -172,7 +175,7 @@ struct Descent {
     if (pl.lstar >= 0) {
       int rows = 0;
       pl.lp = pl.lstar;
-      for (int l = pl.lstar; l >= L0; --l) {
+      for (int l = pl.lstar; l >= L0 && l > pl.lstar - max_levels; --l) {
         const int n_l = (t >> l) - (pl.astar << (pl.lstar - l));
         if (rows + n_l > stage_rows) break;
         rows += n_l;
