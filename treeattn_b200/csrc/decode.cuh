@@ -656,10 +656,13 @@ __global__ void __launch_bounds__(PCfg<T, DH, CH, NST, NCG, WPG>::NTHREADS) deco
         cp_async16(dst, row + src);
       }
       const float* nodes_bh = p.lv.nodes + b * p.lv.s_b + h * p.lv.s_h;
-      // only level l* is prefetched: the levels below are gathered child by child (this selector runs an item
-      // ahead of the streaming, so the extra round trips hide; configuration 4: 46.1 -> 45.1 us per launch, the
-      // ~6 MB of never-scored leaf-level rows no longer read)
-      const typename Descent<DH>::Plan pl = Descent<DH>::plan(p.lv, t, p.wmax, stage_rows, 1);
+      // when CTAs hold several units, only level l* is prefetched and the levels below are gathered child by child:
+      // this selector runs a unit ahead of the streaming, so the extra round trips hide (configuration 4:
+      // 46.1 -> 45.1 us per launch, the ~6 MB of never-scored leaf-level rows no longer read). With one unit per
+      // CTA (small batches) nothing would hide them: the whole reachable range is prefetched in one round trip
+      // (8 / 16 sequences: 0.565 / 0.562 ms per step against 0.571 / 0.571 with one level)
+      const typename Descent<DH>::Plan pl =
+          Descent<DH>::plan(p.lv, t, p.wmax, stage_rows, n_units > G ? 1 : 64);
       if (active) Descent<DH>::prefetch(nodes_bh, p.lv, t, pl, keep < (t >> p.lv.L0), dstage, lane);
       cp_async_wait_all();
       __syncwarp();
