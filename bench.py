@@ -401,12 +401,12 @@ def run_gather_dot(a, dev, emit=True):
                           for _ in range(B * H)]).view(B, H, nblk).int()
     out = torch.empty(B, H, nblk * blk, device=dev, dtype=torch.float32)
     for K in Ks:
-        _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=2, out=out)
+        _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=1, out=out)
     torch.cuda.synchronize()
     if a.profile_steps:
         torch.cuda.cudart().cudaProfilerStart()
         for K in Ks[:a.profile_steps]:
-            _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=2, out=out)
+            _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=1, out=out)
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
         return
@@ -415,7 +415,7 @@ def run_gather_dot(a, dev, emit=True):
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s), torch.cuda.graph(gr, stream=s):
         for K in Ks:
-            _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=2, out=out)
+            _ops.gather_dot_blocks(q, K, blocks, blk, 0.125, nb_cta=1, out=out)
     torch.cuda.current_stream(dev).wait_stream(s)
     gr.replay()
     torch.cuda.synchronize()

@@ -341,7 +341,7 @@ def gather_dot(q, S, cand, scale):
     return out
 
 
-def gather_dot_blocks(q, k, blocks, blk, scale, nb_cta=2, out=None):
+def gather_dot_blocks(q, k, blocks, blk, scale, nb_cta=1, out=None):
     """Block form: q (B, H, dh), k (B, H, T, dh) with contiguous rows, blocks (B, H, nblk) int32 block ids.
     Returns (B, H, nblk*blk) fp32 scores."""
     _need_cuda('gather_dot_blocks', q, k, blocks)
